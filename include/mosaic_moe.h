@@ -1,0 +1,179 @@
+/*
+ * mosaic_moe.h — C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Plain pointers and sizes only.  Every pointer argument is a DEVICE pointer
+ * unless stated otherwise; every call is asynchronous on the given stream,
+ * performs no host synchronisation and allocates nothing (the caller passes
+ * outputs and a workspace sized by the matching *_workspace_bytes call), so
+ * a whole layer can be captured in a CUDA graph.  Shapes, alignment and
+ * ranges are checked on the host before anything is launched; a failed check
+ * returns a MOSAIC_ERR_* code and launches nothing.  Errors found on the
+ * device (an expert id out of range, a pipeline wait that timed out) are
+ * recorded in an error word inside the workspace: read it with
+ * mosaic_read_error().
+ *
+ * Reference interfaces replaced (paths inside fazin-ahamed/Mosaic):
+ *   mosaic_router            <- mosaicvm/model/layers.py:118-150 (Router.forward) with the
+ *                               sigmoid score of .mosaicvm/source/inference_model.py:569-589 (Gate)
+ *   mosaic_layout_assignments<- mosaicvm/kernels/moe_layout.py:8-27 (layout_assignments)
+ *   mosaic_emit_tiles        <- mosaicvm/kernels/w4a16_grouped.py:151-169 (emit_tiles)
+ *   mosaic_act_quant         <- mosaicvm/kernels/fp4_source.py:110-129 (act_quant_ref)
+ *   mosaic_pack_mxfp4        <- mosaicvm/kernels/fp4_source.py:35-64 (pack_mxfp4_nk)
+ *   mosaic_prepack_scales    <- mosaicvm/kernels/qpa_mma.py:577-613 (prepack_expert_bank_qpa:
+ *                               an invertible re-layout of the expert bank, scales only here)
+ *   mosaic_moe_routed        <- mosaicvm/kernels/exact_moe.py:12-19 (exact_moe) /
+ *                               mosaicvm/kernels/qpa_mma.py:681-784 (fused_moe_qpa)
+ *   mosaic_moe_forward       <- mosaicvm/model/layers.py:284-303 (MoELayer.forward)
+ *   mosaic_ep_*              <- .mosaicvm/source/inference_model.py:614-650 (MoE.forward,
+ *                               expert-sharded; all_reduce replaced by all-to-all)
+ */
+#ifndef MOSAIC_MOE_H_
+#define MOSAIC_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOSAIC_API __attribute__((visibility("default")))
+#else
+#define MOSAIC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* mosaic_stream_t;
+
+enum mosaic_status {
+  MOSAIC_OK = 0,
+  MOSAIC_ERR_SHAPE = 1,       /* dimension contract violated (ValueError in the reference) */
+  MOSAIC_ERR_DTYPE = 2,       /* unsupported number format */
+  MOSAIC_ERR_ALIGN = 3,       /* pointer alignment contract violated */
+  MOSAIC_ERR_RANGE = 4,       /* value out of range (expert id, scale byte) */
+  MOSAIC_ERR_CUDA = 5,        /* CUDA runtime / driver error */
+  MOSAIC_ERR_TIMEOUT = 6,     /* a device pipeline wait gave up (kernel returned early) */
+  MOSAIC_ERR_UNSUPPORTED = 7, /* configuration outside what the kernels implement */
+  MOSAIC_ERR_WORKSPACE = 8    /* workspace too small */
+};
+
+/* Activation formats of the expert GEMMs.
+ * MOSAIC_ACT_BF16: bf16 activations (decode).  Each bf16 value is carried
+ *   into the block-scaled MMA as the sum of two E4M3 values with their own
+ *   per-32 power-of-two scales (hi + lo), which represents it to ~2^-8.
+ * MOSAIC_ACT_FP8: the reference's source semantics — act_quant_ref (E4M3,
+ *   power-of-two scale per 1x128 block) on the expert inputs, bf16 outputs
+ *   of every expert linear. */
+enum mosaic_act_mode { MOSAIC_ACT_BF16 = 0, MOSAIC_ACT_FP8 = 1 };
+
+typedef struct mosaic_moe_dims {
+  int32_t tokens;         /* T: rows of x */
+  int32_t hidden;         /* H: multiple of 128 */
+  int32_t inter;          /* I: moe_intermediate_size, multiple of 128 */
+  int32_t n_experts;      /* E routed experts, 1..256 */
+  int32_t top_k;          /* 1..8, <= E */
+  int32_t n_group;        /* router groups (1 = no group limit); divides E */
+  int32_t topk_group;     /* groups kept per token */
+  int32_t act_mode;       /* enum mosaic_act_mode */
+  int32_t norm_topk_prob; /* 1: weights /= sum(weights).clamp_min(1e-9) */
+  int32_t has_shared;     /* 1: the bank holds the shared expert as expert E and y includes it */
+  float route_scale;      /* routed_scaling_factor */
+  float swiglu_limit;     /* 0 = no clamp; else gate <= limit, |up| <= limit */
+} mosaic_moe_dims;
+
+/* Expert bank (device memory).  n_bank = E + has_shared; the shared expert,
+ * when present, is the last one.  Weights stay in the reference layout
+ * (mosaicvm/kernels/exact_moe.py:12: packed_gate_up uint8 [E, 2I, H/2], gate
+ * rows then up rows, low nibble = even K; packed_down [E, H, I/2]); the E8M0
+ * scales are re-laid out once by mosaic_prepack_scales. */
+typedef struct mosaic_expert_bank {
+  const uint8_t* gu_packed; /* [n_bank][2I][H/2], 32-B aligned */
+  const uint8_t* gu_sf;     /* [n_bank][2I/128][H/128][512] from mosaic_prepack_scales */
+  const uint8_t* dn_packed; /* [n_bank][H][I/2], 32-B aligned */
+  const uint8_t* dn_sf;     /* [n_bank][H/128][I/128][512] */
+} mosaic_expert_bank;
+
+MOSAIC_API int mosaic_version(void);
+MOSAIC_API const char* mosaic_status_string(int status);
+/* Number of SMs of the current device (0 when no device). */
+MOSAIC_API int mosaic_device_sm_count(void);
+
+/* Router: logits = x @ W^T in fp32, s = sigmoid(logits), selection on s + bias
+ * (fp32, selection only), optional group limit (sum of the top-2 biased
+ * scores per group, keep topk_group groups), top_k in descending order of the
+ * biased score, weights gathered from the unbiased s, normalised and scaled.
+ * x bf16 [T, H]; weight fp32 [E, H]; bias fp32 [E] (NULL = zeros);
+ * weights_out fp32 [T, top_k]; idx_out int64 [T, top_k].
+ * Equal biased scores are broken towards the lower expert id. */
+MOSAIC_API size_t mosaic_router_workspace_bytes(int32_t T, int32_t H, int32_t E);
+MOSAIC_API int mosaic_router(const void* x, const float* weight, const float* bias, int32_t T, int32_t H, int32_t E,
+                  int32_t top_k, int32_t n_group, int32_t topk_group, float route_scale, int32_t norm_topk_prob,
+                  float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
+                  mosaic_stream_t stream);
+
+/* ids int64 [A] -> sorted_ids int64 [A], perm int64 [A] (stable: ascending
+ * flat index inside each expert segment), offsets int32 [E+1], counts int32 [E].
+ * Single-CTA histogram / prefix scan / stable scatter; A <= 1<<20. */
+MOSAIC_API int mosaic_layout_assignments(const int64_t* expert_ids, int32_t A, int32_t E, int64_t* sorted_ids,
+                              int64_t* perm, int32_t* offsets, int32_t* counts, mosaic_stream_t stream);
+
+/* counts int32 [E] -> tiles (expert_index, m_start, tile_rows) int32 [max_tiles]
+ * in expert order and n_tiles int32 [1]; tiles beyond max_tiles are dropped
+ * and flagged by n_tiles > max_tiles. */
+MOSAIC_API int mosaic_emit_tiles(const int32_t* counts, int32_t E, int32_t block_m, int32_t max_tiles,
+                      int32_t* expert_index, int32_t* m_start, int32_t* n_tiles, int32_t* tile_rows,
+                      mosaic_stream_t stream);
+
+/* act_quant_ref: x bf16 [M, K] -> q e4m3fn bytes [M, K], scale fp32 [M, K/128]. */
+MOSAIC_API int mosaic_act_quant(const void* x, int32_t M, int32_t K, uint8_t* q, float* scale, mosaic_stream_t stream);
+
+/* pack_mxfp4_nk: w fp32 [N, K] -> packed uint8 [N, K/2], E8M0 scale uint8 [N, K/32]
+ * (FLOOR E8M0, RNE E2M1 with saturation; bit-identical to the reference packer). */
+MOSAIC_API int mosaic_pack_mxfp4(const float* w, int32_t N, int32_t K, uint8_t* packed, uint8_t* scale,
+                      mosaic_stream_t stream);
+
+/* Re-lay E8M0 scales [n_mats][rows][K/32] into the chunks the block-scaled MMA
+ * consumes: [n_mats][rows/128][K/128][512] with byte (r%32)*16 + ((r%128)/32)*4 + kb
+ * of a chunk holding row r, K32 block kb.  rows % 128 == 0, K % 128 == 0. */
+MOSAIC_API int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, uint8_t* sf_chunks,
+                          mosaic_stream_t stream);
+
+/* Workspace for mosaic_moe_forward / mosaic_moe_routed (256-B aligned pointer). */
+MOSAIC_API size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims);
+
+/* Full MoE layer: router -> layout -> expert gate/up (+SwiGLU, x route weight)
+ * -> down -> ordered combine (+ shared expert).  x, y bf16 [T, H].
+ * weights_out fp32 [T, top_k] and idx_out int64 [T, top_k] receive the routing. */
+MOSAIC_API int mosaic_moe_forward(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
+                       const float* router_bias, const mosaic_expert_bank* bank, void* y, float* weights_out,
+                       int64_t* idx_out, void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
+
+/* mosaic_moe_forward that also records caller-created CUDA events
+ * (cudaEvent_t handles, any slot may be NULL) on the stream at the stage
+ * boundaries: [0] start, [1] after the router, [2] after the layout, [3]
+ * after quantisation, [4] after the gate/up GEMM, [5] after the down GEMM,
+ * [6] after the combine.  For per-kernel timing. */
+MOSAIC_API int mosaic_moe_forward_profiled(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
+                                           const float* router_bias, const mosaic_expert_bank* bank, void* y,
+                                           float* weights_out, int64_t* idx_out, void* workspace,
+                                           size_t workspace_bytes, mosaic_stream_t stream,
+                                           void* const* stage_events);
+
+/* Routed experts only, routing given (exact_moe contract): x bf16 [T, H];
+ * expert_ids int64 [T, top_k]; expert_weights fp32 [T, top_k] (NULL = 1.0);
+ * y bf16 [T, H].  dims->has_shared selects whether the bank's last expert
+ * (the shared one) is added too. */
+MOSAIC_API int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,
+                      const float* expert_weights, const mosaic_expert_bank* bank, void* y, void* workspace,
+                      size_t workspace_bytes, mosaic_stream_t stream);
+
+/* Device error word of a workspace used by mosaic_moe_* (0 = none).
+ * Synchronises the stream.  reset != 0 clears it afterwards. */
+MOSAIC_API int mosaic_read_error(const void* workspace, int32_t reset, int32_t* code_out, mosaic_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOSAIC_MOE_H_ */

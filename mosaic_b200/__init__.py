@@ -1,0 +1,29 @@
+"""mosaic_b200 — B200-native (sm_100a) MoE-layer hot path of Mosaic.
+
+Router (sigmoid, group-limited top-k, selection-only bias), histogram / scan
+permutation, MXFP4 x E4M3 block-scaled tcgen05 expert GEMMs with a fused
+SwiGLU epilogue, shared expert and ordered combine, behind the reference's
+MoE module / operator API.  The CUDA library is loaded lazily; building it is
+``python -m mosaic_b200.build``.
+"""
+from .moe import (  # noqa: F401
+    ExactContractError,
+    ExpertBank,
+    MoEConfig,
+    MoELayer,
+    Router,
+    exact_moe,
+    exact_target,
+    grouped_expert_forward,
+)
+
+__all__ = [
+    "ExactContractError",
+    "ExpertBank",
+    "MoEConfig",
+    "MoELayer",
+    "Router",
+    "exact_moe",
+    "exact_target",
+    "grouped_expert_forward",
+]

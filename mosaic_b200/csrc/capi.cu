@@ -1,0 +1,403 @@
+// C ABI of the Mosaic B200 MoE hot path (see include/mosaic_moe.h).
+//
+// Host side only: argument validation, workspace planning, TMA tensor-map
+// encoding and kernel launches.  Nothing here allocates device memory or
+// synchronises a stream (except mosaic_read_error, which exists to do so).
+// cuTensorMapEncodeTiled is resolved through cudaGetDriverEntryPoint so the
+// library does not link libcuda and loads on hosts without a GPU.
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace mosaic;
+
+namespace {
+
+constexpr int kVersion = 1;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess) return nullptr;
+    if (q != cudaDriverEntryPointSuccess) return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Weights: 3-D map {K, rows, n_bank} over packed E2M1 codes, unpacked by TMA
+// into the 16-byte-per-16-values smem layout that kind::mxf8f6f4 reads.
+int make_weight_map(CUtensorMap* map, const uint8_t* packed, int n_bank, int rows, int K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return MOSAIC_ERR_CUDA;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(n_bank)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows) * (K / 2)};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<uint8_t*>(packed), dims, strides, box,
+                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+// Activations: 2-D map {K, rows} over E4M3 bytes, 16-row boxes.
+int make_act_map(CUtensorMap* map, const uint8_t* q, int rows, int K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return MOSAIC_ERR_CUDA;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {128, 16};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+struct WsPlan {
+  int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32;
+  size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, tiles, n_tiles;
+  size_t xq, xsf, zq, zsf, partial, total;
+};
+
+int check_dims(const mosaic_moe_dims* d) {
+  if (!d) return MOSAIC_ERR_SHAPE;
+  if (d->tokens < 1 || d->tokens > (1 << 20)) return MOSAIC_ERR_SHAPE;
+  if (d->hidden < 128 || d->hidden % 128 || d->inter < 128 || d->inter % 128) return MOSAIC_ERR_SHAPE;
+  if (d->n_experts < 1 || d->n_experts > 256) return MOSAIC_ERR_UNSUPPORTED;
+  if (d->top_k < 1 || d->top_k > 8 || d->top_k > d->n_experts) return MOSAIC_ERR_SHAPE;
+  if (d->n_group < 1 || d->n_group > 32 || d->n_experts % d->n_group) return MOSAIC_ERR_SHAPE;
+  if (d->topk_group < 1 || d->topk_group > d->n_group) return MOSAIC_ERR_SHAPE;
+  if (d->topk_group * (d->n_experts / d->n_group) < d->top_k) return MOSAIC_ERR_SHAPE;
+  if (d->act_mode != MOSAIC_ACT_BF16 && d->act_mode != MOSAIC_ACT_FP8) return MOSAIC_ERR_DTYPE;
+  if (!(d->swiglu_limit >= 0.f)) return MOSAIC_ERR_RANGE;
+  return MOSAIC_OK;
+}
+
+WsPlan plan_ws(const mosaic_moe_dims* d) {
+  WsPlan w{};
+  const int T = d->tokens, H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
+  const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
+  w.n_bank = E + (d->has_shared ? 1 : 0);
+  w.R = T * k + (d->has_shared ? T : 0);
+  w.R_pad = (w.R + 15) & ~15;
+  w.planes = hilo ? 2 : 1;
+  w.tt = hilo ? 64 : 128;
+  w.max_tiles = (T * k) / w.tt + w.n_bank + T / w.tt + 2;
+  const int sms = sm_count();
+  w.splits = router_splits(T, H, E, sms > 0 ? sms : 148);
+  w.partial_f32 = hilo ? 1 : 0;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = up256(o + bytes);
+    return at;
+  };
+  w.err = take(16);
+  w.router_part = take(sizeof(float) * static_cast<size_t>(w.splits) * T * E);
+  w.counts = take(sizeof(int) * (E + 1));
+  w.offsets = take(sizeof(int) * (E + 2));
+  w.row_of = take(sizeof(int) * static_cast<size_t>(T) * k);
+  w.row_sorted = take(sizeof(int) * static_cast<size_t>(T) * k);
+  w.row_token = take(sizeof(int) * static_cast<size_t>(w.R));
+  w.row_weight = take(sizeof(float) * static_cast<size_t>(w.R));
+  w.tiles = take(sizeof(int) * 3 * static_cast<size_t>(w.max_tiles));
+  w.n_tiles = take(sizeof(int) * 4);
+  w.xq = take(static_cast<size_t>(w.planes) * w.R_pad * H);
+  w.xsf = take(sizeof(uint32_t) * static_cast<size_t>(w.planes) * (H / 128) * w.R_pad);
+  w.zq = take(static_cast<size_t>(w.planes) * w.R_pad * I);
+  w.zsf = take(sizeof(uint32_t) * static_cast<size_t>(w.planes) * (I / 128) * w.R_pad);
+  w.partial = take(static_cast<size_t>(w.R) * H * (w.partial_f32 ? 4 : 2));
+  w.total = o;
+  return w;
+}
+
+int check_bank(const mosaic_expert_bank* b) {
+  if (!b || !b->gu_packed || !b->gu_sf || !b->dn_packed || !b->dn_sf) return MOSAIC_ERR_SHAPE;
+  if (!aligned(b->gu_packed, 32) || !aligned(b->dn_packed, 32)) return MOSAIC_ERR_ALIGN;
+  if (!aligned(b->gu_sf, 16) || !aligned(b->dn_sf, 16)) return MOSAIC_ERR_ALIGN;
+  return MOSAIC_OK;
+}
+
+// Layout -> quantise -> gate/up -> down -> combine, with routing in
+// (idx, weights) already on the device.
+// ev (optional) = 7 events: before router, after router, layout, quantise,
+// gate/up, down, combine; slots 0-1 are recorded by the caller of run_experts.
+inline bool rec(void* const* ev, int i, cudaStream_t s) {
+  return !ev || !ev[i] || cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s) == cudaSuccess;
+}
+
+int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const void* x, const int64_t* idx,
+                const float* weights, const mosaic_expert_bank* bank, void* y, cudaStream_t stream,
+                void* const* ev = nullptr) {
+  const int T = d->tokens, H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
+  const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
+  int* err = reinterpret_cast<int*>(ws + w.err);
+  const int shared_base = d->has_shared ? T * k : -1;
+
+  LayoutParams lp{};
+  lp.idx = idx;
+  lp.weights = weights;
+  lp.T = T;
+  lp.k = k;
+  lp.E = E;
+  lp.with_shared = d->has_shared ? 1 : 0;
+  lp.tt_routed = w.tt;
+  lp.tt_shared = w.tt;
+  lp.max_tiles = w.max_tiles;
+  lp.counts = reinterpret_cast<int*>(ws + w.counts);
+  lp.offsets = reinterpret_cast<int*>(ws + w.offsets);
+  lp.row_of = reinterpret_cast<int*>(ws + w.row_of);
+  lp.row_sorted = reinterpret_cast<int*>(ws + w.row_sorted);
+  lp.row_token = reinterpret_cast<int*>(ws + w.row_token);
+  lp.row_weight = reinterpret_cast<float*>(ws + w.row_weight);
+  lp.tiles = reinterpret_cast<int*>(ws + w.tiles);
+  lp.n_tiles = reinterpret_cast<int*>(ws + w.n_tiles);
+  lp.err = err;
+  if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
+
+  uint8_t* xq = ws + w.xq;
+  uint32_t* xsf = reinterpret_cast<uint32_t*>(ws + w.xsf);
+  if (launch_rows_quant(x, T, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, xq, xsf, stream) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
+
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  CUtensorMap tw, tx;
+  GemmParams gp{};
+  gp.hilo = hilo ? 1 : 0;
+  gp.fp8 = hilo ? 0 : 1;
+  gp.I = I;
+  gp.H = H;
+  gp.R = w.R;
+  gp.R_pad = w.R_pad;
+  gp.shared_expert = d->has_shared ? E : -1;
+  gp.tiles = lp.tiles;
+  gp.n_tiles = lp.n_tiles;
+  gp.max_tiles = w.max_tiles;
+  gp.row_weight = lp.row_weight;
+  gp.swiglu_limit = d->swiglu_limit;
+  gp.err = err;
+
+  // gate/up
+  int st = make_weight_map(&tw, bank->gu_packed, w.n_bank, 2 * I, H);
+  if (st) return st;
+  st = make_act_map(&tx, xq, w.planes * w.R_pad, H);
+  if (st) return st;
+  gp.mode = 0;
+  gp.K = H;
+  gp.n_blocks = I / 128;
+  gp.x_sf = xsf;
+  gp.x_sf_plane = static_cast<size_t>(H / 128) * w.R_pad;
+  gp.w_sf = bank->gu_sf;
+  gp.w_rowtiles = 2 * I / 128;
+  gp.zq = ws + w.zq;
+  gp.zsf = reinterpret_cast<uint32_t*>(ws + w.zsf);
+  gp.z_sf_plane = static_cast<size_t>(I / 128) * w.R_pad;
+  if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
+
+  // down
+  st = make_weight_map(&tw, bank->dn_packed, w.n_bank, H, I);
+  if (st) return st;
+  st = make_act_map(&tx, gp.zq, w.planes * w.R_pad, I);
+  if (st) return st;
+  gp.mode = 1;
+  gp.K = I;
+  gp.n_blocks = H / 128;
+  gp.x_sf = gp.zsf;
+  gp.x_sf_plane = gp.z_sf_plane;
+  gp.w_sf = bank->dn_sf;
+  gp.w_rowtiles = H / 128;
+  gp.out = ws + w.partial;
+  gp.out_f32 = w.partial_f32;
+  if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 5, stream)) return MOSAIC_ERR_CUDA;
+
+  if (launch_combine(ws + w.partial, w.partial_f32, lp.row_sorted, T, k, H, shared_base, y, stream) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 6, stream)) return MOSAIC_ERR_CUDA;
+  return MOSAIC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mosaic_version(void) { return kVersion; }
+
+const char* mosaic_status_string(int status) {
+  switch (status) {
+    case MOSAIC_OK: return "ok";
+    case MOSAIC_ERR_SHAPE: return "shape contract violated";
+    case MOSAIC_ERR_DTYPE: return "unsupported number format";
+    case MOSAIC_ERR_ALIGN: return "pointer alignment contract violated";
+    case MOSAIC_ERR_RANGE: return "value out of range";
+    case MOSAIC_ERR_CUDA: return "CUDA error";
+    case MOSAIC_ERR_TIMEOUT: return "device pipeline wait timed out";
+    case MOSAIC_ERR_UNSUPPORTED: return "configuration not supported";
+    case MOSAIC_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int mosaic_device_sm_count(void) { return sm_count(); }
+
+size_t mosaic_router_workspace_bytes(int32_t T, int32_t H, int32_t E) {
+  if (T < 1 || H < 1 || E < 1) return 0;
+  const int sms = sm_count();
+  const int splits = router_splits(T, H, E, sms > 0 ? sms : 148);
+  return up256(16) + up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
+}
+
+int mosaic_router(const void* x, const float* weight, const float* bias, int32_t T, int32_t H, int32_t E,
+                  int32_t top_k, int32_t n_group, int32_t topk_group, float route_scale, int32_t norm_topk_prob,
+                  float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
+                  mosaic_stream_t stream) {
+  if (!x || !weight || !weights_out || !idx_out || !workspace) return MOSAIC_ERR_SHAPE;
+  if (T < 1 || H < 32 || H % 32 || E < 1 || E > 256 || top_k < 1 || top_k > 8 || top_k > E) return MOSAIC_ERR_SHAPE;
+  if (n_group < 1 || n_group > 32 || E % n_group || topk_group < 1 || topk_group > n_group) return MOSAIC_ERR_SHAPE;
+  if (topk_group * (E / n_group) < top_k) return MOSAIC_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  if (workspace_bytes < mosaic_router_workspace_bytes(T, H, E)) return MOSAIC_ERR_WORKSPACE;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  const int splits = router_splits(T, H, E, sms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
+                                weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
+                                reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_layout_assignments(const int64_t* expert_ids, int32_t A, int32_t E, int64_t* sorted_ids, int64_t* perm,
+                              int32_t* offsets, int32_t* counts, mosaic_stream_t stream) {
+  if (!expert_ids || !sorted_ids || !perm || !offsets || !counts) return MOSAIC_ERR_SHAPE;
+  if (A < 1 || A > (1 << 20) || E < 1 || E > 256) return MOSAIC_ERR_SHAPE;
+  cudaError_t e = launch_layout_assignments(expert_ids, A, E, sorted_ids, perm, offsets, counts,
+                                            reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_emit_tiles(const int32_t* counts, int32_t E, int32_t block_m, int32_t max_tiles, int32_t* expert_index,
+                      int32_t* m_start, int32_t* n_tiles, int32_t* tile_rows, mosaic_stream_t stream) {
+  if (!counts || !expert_index || !m_start || !n_tiles || !tile_rows) return MOSAIC_ERR_SHAPE;
+  if (E < 1 || E > 4096 || block_m < 1 || max_tiles < 0) return MOSAIC_ERR_SHAPE;
+  cudaError_t e = launch_emit_tiles(counts, E, block_m, max_tiles, expert_index, m_start, n_tiles, tile_rows,
+                                    reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_act_quant(const void* x, int32_t M, int32_t K, uint8_t* q, float* scale, mosaic_stream_t stream) {
+  if (!x || !q || !scale) return MOSAIC_ERR_SHAPE;
+  if (M < 1 || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(q, 8)) return MOSAIC_ERR_ALIGN;
+  cudaError_t e = launch_act_quant(x, M, K, q, scale, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_pack_mxfp4(const float* w, int32_t N, int32_t K, uint8_t* packed, uint8_t* scale,
+                      mosaic_stream_t stream) {
+  if (!w || !packed || !scale) return MOSAIC_ERR_SHAPE;
+  if (N < 1 || K < 32 || K % 32) return MOSAIC_ERR_SHAPE;
+  if (!aligned(w, 16) || !aligned(packed, 16)) return MOSAIC_ERR_ALIGN;
+  cudaError_t e = launch_pack_mxfp4(w, N, K, packed, scale, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, uint8_t* sf_chunks,
+                          mosaic_stream_t stream) {
+  if (!scale || !sf_chunks) return MOSAIC_ERR_SHAPE;
+  if (n_mats < 1 || rows < 128 || rows % 128 || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
+  cudaError_t e = launch_prepack_scales(scale, n_mats, rows, K, sf_chunks, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims) {
+  if (check_dims(dims) != MOSAIC_OK) return 0;
+  return plan_ws(dims).total;
+}
+
+int mosaic_moe_forward_profiled(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
+                                const float* router_bias, const mosaic_expert_bank* bank, void* y,
+                                float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
+                                mosaic_stream_t stream, void* const* stage_events) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!x || !router_weight || !y || !weights_out || !idx_out || !workspace) return MOSAIC_ERR_SHAPE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(router_weight, 16) || !aligned(workspace, 256))
+    return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!rec(stage_events, 0, s)) return MOSAIC_ERR_CUDA;
+  cudaError_t e = launch_router(x, router_weight, router_bias, dims->tokens, dims->hidden, dims->n_experts,
+                                dims->top_k, dims->n_group, dims->topk_group, dims->route_scale,
+                                dims->norm_topk_prob, weights_out, idx_out,
+                                reinterpret_cast<float*>(ws + w.router_part), w.splits,
+                                reinterpret_cast<int*>(ws + w.err), s);
+  if (e != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!rec(stage_events, 1, s)) return MOSAIC_ERR_CUDA;
+  return run_experts(dims, w, ws, x, idx_out, weights_out, bank, y, s, stage_events);
+}
+
+int mosaic_moe_forward(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
+                       const float* router_bias, const mosaic_expert_bank* bank, void* y, float* weights_out,
+                       int64_t* idx_out, void* workspace, size_t workspace_bytes, mosaic_stream_t stream) {
+  return mosaic_moe_forward_profiled(dims, x, router_weight, router_bias, bank, y, weights_out, idx_out, workspace,
+                                     workspace_bytes, stream, nullptr);
+}
+
+int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,
+                      const float* expert_weights, const mosaic_expert_bank* bank, void* y, void* workspace,
+                      size_t workspace_bytes, mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!x || !expert_ids || !y || !workspace) return MOSAIC_ERR_SHAPE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  return run_experts(dims, w, ws, x, expert_ids, expert_weights, bank, y, s);
+}
+
+int mosaic_read_error(const void* workspace, int32_t reset, int32_t* code_out, mosaic_stream_t stream) {
+  if (!workspace || !code_out) return MOSAIC_ERR_SHAPE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (reset && cudaMemsetAsync(const_cast<void*>(workspace), 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  *code_out = v;
+  return MOSAIC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,86 @@
+// Internal launch interfaces of the Mosaic B200 MoE kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mosaic {
+
+// ---- grouped block-scaled expert GEMM (gemm_bs.cu)
+struct GemmParams {
+  int mode;           // 0 = gate/up (+SwiGLU, re-quantise), 1 = down (partials)
+  int hilo;           // 1: activation rows come as hi and lo E4M3 planes
+  int fp8;            // 1: reference FP8 semantics (act_quant per 128, bf16-rounded linears)
+  int K;              // reduction length (H for gate/up, I for down)
+  int n_blocks;       // 128-row output blocks (I/128 for gate/up, H/128 for down)
+  int I, H;
+  int R, R_pad;       // packed activation rows (routed + shared) and padded row count
+  int shared_expert;  // bank index of the shared expert, or -1
+  const int* tiles;   // [max_tiles][3] = (expert, first row, rows)
+  const int* n_tiles;
+  int max_tiles;
+  const uint32_t* x_sf;  // activation scales [plane][K/128][R_pad], 4 E8M0 bytes per word
+  size_t x_sf_plane;
+  const uint8_t* w_sf;   // weight scale chunks [bank][rows/128][K/128][512]
+  int w_rowtiles;
+  const float* row_weight;  // [R] route weight of each packed row
+  float swiglu_limit;
+  uint8_t* zq;        // gate/up output rows [plane][R_pad][I] (E4M3)
+  uint32_t* zsf;      // their scales [plane][I/128][R_pad]
+  size_t z_sf_plane;
+  void* out;          // down partials [R][H]
+  int out_f32;
+  int* err;
+};
+size_t gemm_smem_bytes(int mode);
+cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmParams& p, int grid,
+                            cudaStream_t stream);
+
+// ---- router (router.cu)
+int router_splits(int T, int H, int E, int num_sms);
+cudaError_t launch_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
+                          int n_group, int topk_group, float route_scale, int norm, float* weights_out,
+                          int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream);
+
+// ---- layout (layout.cu)
+struct LayoutParams {
+  const int64_t* idx;     // [T][k]
+  const float* weights;   // [T][k] or null (1.0)
+  int T, k, E;
+  int with_shared;
+  int tt_routed, tt_shared;  // token rows per GEMM tile
+  int max_tiles;
+  int* counts;            // [E+1]
+  int* offsets;           // [E+2]
+  int* row_of;            // [T][k]
+  int* row_sorted;        // [T][k] rows of each token in ascending expert id
+  int* row_token;         // [R]
+  float* row_weight;      // [R]
+  int* tiles;             // [max_tiles][3]
+  int* n_tiles;
+  int* err;
+};
+cudaError_t launch_layout(const LayoutParams& p, cudaStream_t stream);
+cudaError_t launch_layout_assignments(const int64_t* ids, int A, int E, int64_t* sorted_ids, int64_t* perm,
+                                      int32_t* offsets, int32_t* counts, cudaStream_t stream);
+cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max_tiles, int32_t* expert_index,
+                              int32_t* m_start, int32_t* n_tiles, int32_t* tile_rows, cudaStream_t stream);
+
+// ---- quantisation (quant.cu)
+// x bf16 [T][H] -> packed activation rows: row_of[t][s] (s < k) and, when
+// shared_base >= 0, row shared_base + t.  hilo: hi/lo planes with per-32
+// scales; else act_quant_ref per 128.
+cudaError_t launch_rows_quant(const void* x, int T, int H, int k, const int* row_of, int shared_base, int hilo,
+                              int R_pad, uint8_t* xq, uint32_t* xsf, cudaStream_t stream);
+cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
+cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
+cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, uint8_t* chunks,
+                                  cudaStream_t stream);
+
+// ---- combine (combine.cu)
+cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,
+                           int shared_base, void* y, cudaStream_t stream);
+
+}  // namespace mosaic

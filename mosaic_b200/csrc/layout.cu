@@ -1,0 +1,254 @@
+// Assignment layout: histogram -> prefix scan -> stable scatter -> GEMM tile list.
+//
+// Reference behaviour: mosaicvm/kernels/moe_layout.py:8-27 (layout_assignments:
+// bincount, cumsum offsets, a permutation that groups assignments by expert)
+// and mosaicvm/kernels/w4a16_grouped.py:41-61,151-169 (emit_tiles: per-expert
+// tiles (expert, m_start, rows), tile count kept on the device).  Inside an
+// expert segment rows are ordered by flat assignment index (token-major), the
+// stable order; the reference's argsort leaves that order unspecified.
+//
+// One CTA of 1024 threads does everything in shared memory, so the layer
+// needs no host round trip.  Ranks inside a 1024-token chunk come from
+// per-warp bit masks (one bit per lane, per expert) and a scan over the 32
+// warps; chunks are processed in order and carry per-expert running bases.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mosaic {
+
+namespace {
+
+// Exclusive scan of n ints by warp 0 (n small); out[n] receives the total.
+__device__ void warp0_exclusive_scan(const int* in, int* out, int n) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  int carry = 0;
+  for (int b = 0; b < n; b += 32) {
+    const int i = b + lane;
+    int v = (i < n) ? in[i] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (i < n) out[i] = carry + incl - v;
+    carry += __shfl_sync(0xFFFFFFFFu, incl, 31);
+  }
+  if (lane == 0) out[n] = carry;
+}
+
+struct LayoutExtra {
+  int64_t* perm;        // optional: packed row -> flat assignment index
+  int64_t* sorted_ids;  // optional: packed row -> expert id
+};
+
+__global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtra x) {
+  extern __shared__ int sm[];
+  const int E = p.E, T = p.T, k = p.k;
+  const int NE = E + (p.with_shared ? 1 : 0);
+  int* hist = sm;                      // NE
+  int* offs = hist + NE;               // NE + 1
+  int* base = offs + NE + 1;           // E
+  int* ntile = base + E;               // NE
+  int* toff = ntile + NE;              // NE + 1
+  unsigned* masks = reinterpret_cast<unsigned*>(toff + NE + 1);  // 32 * E
+  int* pre = reinterpret_cast<int*>(masks + 32 * E);             // 32 * E
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  for (int i = tid; i < NE; i += 1024) hist[i] = 0;
+  for (int i = tid; i < E; i += 1024) base[i] = 0;
+  __syncthreads();
+  const int A = T * k;
+  for (int a = tid; a < A; a += 1024) {
+    const int64_t e = p.idx[a];
+    if (e < 0 || e >= E) {
+      set_error(p.err, MOSAIC_ERR_RANGE);
+      continue;
+    }
+    atomicAdd(&hist[static_cast<int>(e)], 1);
+  }
+  __syncthreads();
+  if (tid == 0 && p.with_shared) hist[E] = T;
+  __syncthreads();
+  warp0_exclusive_scan(hist, offs, NE);
+  __syncthreads();
+
+  for (int c0 = 0; c0 < T; c0 += 1024) {
+    const int t = c0 + tid;
+    for (int i = tid; i < 32 * E; i += 1024) masks[i] = 0u;
+    __syncthreads();
+    int ev[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      ev[s] = -1;
+      if (s < k && t < T) {
+        const int64_t e = p.idx[static_cast<size_t>(t) * k + s];
+        if (e >= 0 && e < E) {
+          ev[s] = static_cast<int>(e);
+          atomicOr(&masks[warp * E + ev[s]], 1u << lane);
+        }
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += 1024) {
+      int run = base[e];
+      for (int w = 0; w < 32; ++w) {
+        pre[w * E + e] = run;
+        run += __popc(masks[w * E + e]);
+      }
+      base[e] = run;
+    }
+    __syncthreads();
+    if (t < T) {
+      int rows[8];
+      const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s >= k) break;
+        const int e = ev[s];
+        int row = -1;
+        if (e >= 0) {
+          const int rank = pre[warp * E + e] + __popc(masks[warp * E + e] & lt);
+          row = offs[e] + rank;
+          if (p.row_token) p.row_token[row] = t;
+          if (p.row_weight) p.row_weight[row] = p.weights ? p.weights[static_cast<size_t>(t) * k + s] : 1.0f;
+          if (x.perm) x.perm[row] = static_cast<int64_t>(t) * k + s;
+          if (x.sorted_ids) x.sorted_ids[row] = e;
+        }
+        rows[s] = row;
+        if (p.row_of) p.row_of[static_cast<size_t>(t) * k + s] = row;
+      }
+      if (p.row_sorted) {
+        // ascending expert id (ids of one token are distinct)
+        int ke[8], kr[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          ke[s] = (s < k) ? ev[s] : 0x7FFFFFFF;
+          kr[s] = (s < k) ? rows[s] : 0;
+        }
+        for (int i = 1; i < k; ++i) {
+          const int ce = ke[i], cr = kr[i];
+          int j = i - 1;
+          while (j >= 0 && ke[j] > ce) {
+            ke[j + 1] = ke[j];
+            kr[j + 1] = kr[j];
+            --j;
+          }
+          ke[j + 1] = ce;
+          kr[j + 1] = cr;
+        }
+        for (int s = 0; s < k; ++s) p.row_sorted[static_cast<size_t>(t) * k + s] = kr[s];
+      }
+    }
+    __syncthreads();
+  }
+  if (p.with_shared && p.row_token && p.row_weight) {
+    for (int t = tid; t < T; t += 1024) {
+      const int row = offs[E] + t;
+      p.row_token[row] = t;
+      p.row_weight[row] = 1.0f;
+    }
+  }
+  for (int i = tid; i < NE; i += 1024) {
+    if (p.counts) p.counts[i] = hist[i];
+    const int tt = (p.with_shared && i == E) ? p.tt_shared : p.tt_routed;
+    ntile[i] = (tt > 0) ? (hist[i] + tt - 1) / tt : 0;
+  }
+  for (int i = tid; i <= NE; i += 1024)
+    if (p.offsets) p.offsets[i] = offs[i];
+  __syncthreads();
+  if (p.tiles) {
+    warp0_exclusive_scan(ntile, toff, NE);
+    __syncthreads();
+    for (int e = tid; e < NE; e += 1024) {
+      const int tt = (p.with_shared && e == E) ? p.tt_shared : p.tt_routed;
+      for (int i = 0; i < ntile[e]; ++i) {
+        const int j = toff[e] + i;
+        if (j < p.max_tiles) {
+          p.tiles[3 * j + 0] = e;
+          p.tiles[3 * j + 1] = offs[e] + i * tt;
+          p.tiles[3 * j + 2] = min(tt, hist[e] - i * tt);
+        }
+      }
+    }
+    if (tid == 0) {
+      *p.n_tiles = toff[NE];
+      if (toff[NE] > p.max_tiles) set_error(p.err, MOSAIC_ERR_WORKSPACE);
+    }
+  }
+}
+
+size_t layout_smem(int E, int with_shared) {
+  const int NE = E + (with_shared ? 1 : 0);
+  return sizeof(int) * (static_cast<size_t>(NE) * 4 + 2 + E + 64 * static_cast<size_t>(E));
+}
+
+__global__ void emit_tiles_kernel(const int32_t* counts, int E, int block_m, int max_tiles, int32_t* expert_index,
+                                  int32_t* m_start, int32_t* n_tiles, int32_t* tile_rows) {
+  extern __shared__ int sm[];
+  int* nt = sm;
+  int* off = sm + E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) nt[e] = (counts[e] + block_m - 1) / block_m;
+  __syncthreads();
+  warp0_exclusive_scan(nt, off, E);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int c = counts[e];
+    for (int i = 0; i < nt[e]; ++i) {
+      const int j = off[e] + i;
+      if (j < max_tiles) {
+        expert_index[j] = e;
+        m_start[j] = i * block_m;
+        tile_rows[j] = min(block_m, c - i * block_m);
+      }
+    }
+  }
+  if (threadIdx.x == 0) *n_tiles = off[E];
+}
+
+}  // namespace
+
+cudaError_t launch_layout(const LayoutParams& p, cudaStream_t stream) {
+  const size_t smem = layout_smem(p.E, p.with_shared);
+  cudaError_t err = cudaFuncSetAttribute(layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  layout_kernel<<<1, 1024, smem, stream>>>(p, LayoutExtra{nullptr, nullptr});
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layout_assignments(const int64_t* ids, int A, int E, int64_t* sorted_ids, int64_t* perm,
+                                      int32_t* offsets, int32_t* counts, cudaStream_t stream) {
+  LayoutParams p{};
+  p.idx = ids;
+  p.weights = nullptr;
+  p.T = A;
+  p.k = 1;
+  p.E = E;
+  p.with_shared = 0;
+  p.counts = counts;
+  p.offsets = offsets;
+  p.row_token = nullptr;
+  p.row_weight = nullptr;
+  p.row_of = nullptr;
+  p.row_sorted = nullptr;
+  p.tiles = nullptr;
+  p.n_tiles = nullptr;
+  p.err = nullptr;
+  const size_t smem = layout_smem(E, 0);
+  cudaError_t err = cudaFuncSetAttribute(layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  layout_kernel<<<1, 1024, smem, stream>>>(p, LayoutExtra{perm, sorted_ids});
+  return cudaGetLastError();
+}
+
+cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max_tiles, int32_t* expert_index,
+                              int32_t* m_start, int32_t* n_tiles, int32_t* tile_rows, cudaStream_t stream) {
+  emit_tiles_kernel<<<1, 256, sizeof(int) * (2 * E + 1), stream>>>(counts, E, block_m, max_tiles, expert_index,
+                                                                  m_start, n_tiles, tile_rows);
+  return cudaGetLastError();
+}
+
+}  // namespace mosaic

@@ -1,0 +1,271 @@
+// Activation quantisation into packed expert rows, the reference act_quant,
+// the MXFP4 weight packer and the weight-scale re-layout.
+//
+// Reference behaviour:
+//   act_quant_ref         mosaicvm/kernels/fp4_source.py:110-129
+//   pack_mxfp4_nk         mosaicvm/kernels/fp4_source.py:35-64 with the FLOOR E8M0
+//                         scale of mosaicvm/kernels/mxfp4.py:32-43 and the RNE E2M1
+//                         rounding of mosaicvm/kernels/mxfp4.py:46-82
+//   bank re-layout        mosaicvm/kernels/qpa_mma.py:577-613 (prepack_expert_bank_qpa)
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mosaic {
+
+namespace {
+
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h2[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ uint2 pack8(const uint8_t (&b)[8]) {
+  uint2 r;
+  r.x = b[0] | (b[1] << 8) | (b[2] << 16) | (static_cast<uint32_t>(b[3]) << 24);
+  r.y = b[4] | (b[5] << 8) | (b[6] << 16) | (static_cast<uint32_t>(b[7]) << 24);
+  return r;
+}
+
+// act_quant_ref on 8 values held by this lane; the 128-block spans 16 lanes.
+// Returns the scale exponent and fills q.
+__device__ __forceinline__ int quant_block128(const float (&v)[8], uint8_t (&q)[8]) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  const int e = pow2_scale_exp(m, 1e-4f);
+  const float inv = exp2i(-e);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = f32_to_e4m3(fminf(fmaxf(v[i] * inv, -448.f), 448.f));
+  return e;
+}
+
+// hi + lo split on 8 values; the 32-block spans 4 lanes.
+__device__ __forceinline__ void split_block32(const float (&v)[8], uint8_t (&hi)[8], uint8_t (&lo)[8], int& eh,
+                                              int& el) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+  m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+  eh = max(-126, min(127, pow2_scale_exp(m, 1e-30f)));
+  const float ih = exp2i(-eh), sh = exp2i(eh);
+  float r[8];
+  float m2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    hi[i] = f32_to_e4m3(v[i] * ih);
+    r[i] = v[i] - e4m3_to_f32(hi[i]) * sh;
+    m2 = fmaxf(m2, fabsf(r[i]));
+  }
+  m2 = fmaxf(m2, __shfl_xor_sync(0xFFFFFFFFu, m2, 2));
+  m2 = fmaxf(m2, __shfl_xor_sync(0xFFFFFFFFu, m2, 1));
+  el = max(-126, min(127, pow2_scale_exp(m2, fmaxf(m * 1e-7f, 1e-30f))));
+  const float il = exp2i(-el);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) lo[i] = f32_to_e4m3(r[i] * il);
+}
+
+// Gather the four per-32 exponents of a 128-block (lanes g, g+4, g+8, g+12 of
+// each 16-lane half) into one scale word on the half's first lane.
+__device__ __forceinline__ uint32_t gather_word(int e) {
+  const int lane = threadIdx.x & 31;
+  const int src = lane & ~15;
+  uint32_t w = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int eg = __shfl_sync(0xFFFFFFFFu, e, src + 4 * g);
+    w |= (static_cast<uint32_t>(eg + 127) & 0xFFu) << (8 * g);
+  }
+  return w;
+}
+
+// grid (T, ceil(H / 1024)), 128 threads: each warp quantises 256 values of one token.
+__global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
+                                                         const int* __restrict__ row_of, int shared_base, int hilo,
+                                                         int R_pad, uint8_t* __restrict__ xq,
+                                                         uint32_t* __restrict__ xsf) {
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int k0 = blockIdx.y * 1024 + (threadIdx.x >> 5) * 256 + lane * 8;
+  const bool valid = k0 < H;
+  float v[8];
+  if (valid) {
+    load8_bf16(x + static_cast<size_t>(t) * H + k0, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  const int nrows = k + (shared_base >= 0 ? 1 : 0);
+  const size_t plane_w = static_cast<size_t>(H / 128) * R_pad;
+  if (!hilo) {
+    uint8_t q[8];
+    const int e = quant_block128(v, q);
+    if (!valid) return;
+    const uint2 pq = pack8(q);
+    const uint32_t word = (static_cast<uint32_t>(e + 127) & 0xFFu) * 0x01010101u;
+    for (int s = 0; s < nrows; ++s) {
+      const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
+      if (r < 0) continue;
+      *reinterpret_cast<uint2*>(xq + static_cast<size_t>(r) * H + k0) = pq;
+      if ((lane & 15) == 0) xsf[static_cast<size_t>(k0 / 128) * R_pad + r] = word;
+    }
+  } else {
+    uint8_t hi[8], lo[8];
+    int eh, el;
+    split_block32(v, hi, lo, eh, el);
+    const uint32_t wh = gather_word(eh);
+    const uint32_t wl = gather_word(el);
+    if (!valid) return;
+    const uint2 ph = pack8(hi), pl = pack8(lo);
+    for (int s = 0; s < nrows; ++s) {
+      const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
+      if (r < 0) continue;
+      *reinterpret_cast<uint2*>(xq + static_cast<size_t>(r) * H + k0) = ph;
+      *reinterpret_cast<uint2*>(xq + (static_cast<size_t>(R_pad) + r) * H + k0) = pl;
+      if ((lane & 15) == 0) {
+        xsf[static_cast<size_t>(k0 / 128) * R_pad + r] = wh;
+        xsf[plane_w + static_cast<size_t>(k0 / 128) * R_pad + r] = wl;
+      }
+    }
+  }
+}
+
+// act_quant_ref: grid (M, ceil(K / 1024)), 128 threads.
+__global__ void __launch_bounds__(128) act_quant_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                                                        uint8_t* __restrict__ q, float* __restrict__ scale) {
+  const int m = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int k0 = blockIdx.y * 1024 + (threadIdx.x >> 5) * 256 + lane * 8;
+  const bool valid = k0 < K;
+  float v[8];
+  if (valid) {
+    load8_bf16(x + static_cast<size_t>(m) * K + k0, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  uint8_t b[8];
+  const int e = quant_block128(v, b);
+  if (!valid) return;
+  *reinterpret_cast<uint2*>(q + static_cast<size_t>(m) * K + k0) = pack8(b);
+  if ((lane & 15) == 0) scale[static_cast<size_t>(m) * (K / 128) + k0 / 128] = exp2i(e);
+}
+
+// fp32 -> E2M1 code, round to nearest even, saturating at 6.0.
+__device__ __forceinline__ uint32_t f32_to_e2m1(float v) {
+  const uint32_t sign = (__float_as_uint(v) >> 28) & 0x8u;
+  const float a = fabsf(v);
+  uint32_t code;
+  if (a >= 6.0f) {
+    code = 7u;
+  } else if (a < 1.0f) {
+    // ulp(2^22) == 0.5: the fp32 add rounds a to the 0.5 grid (RNE)
+    const float big = 4194304.0f;
+    code = __float_as_uint(__fadd_rn(a, big)) - __float_as_uint(big);
+  } else {
+    const uint32_t b = __float_as_uint(a);
+    const uint32_t odd = (b >> 22) & 1u;
+    code = (b - (126u << 23) + ((1u << 21) - 1u) + odd) >> 22;
+  }
+  return (code & 0x7u) | sign;
+}
+
+// One thread per 32-element block of a row.
+__global__ void pack_mxfp4_kernel(const float* __restrict__ w, int N, int K, uint8_t* __restrict__ packed,
+                                  uint8_t* __restrict__ scale) {
+  const size_t blk = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t nblk = static_cast<size_t>(N) * (K / 32);
+  if (blk >= nblk) return;
+  const float* src = w + blk * 32;
+  float v[32];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = reinterpret_cast<const float4*>(src)[i];
+    v[4 * i] = f.x;
+    v[4 * i + 1] = f.y;
+    v[4 * i + 2] = f.z;
+    v[4 * i + 3] = f.w;
+  }
+  bool nan = false;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    amax = fmaxf(amax, fabsf(v[i]));
+    nan |= isnan(v[i]);
+  }
+  int unb = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 - 2;
+  unb = max(-127, min(128, unb));
+  uint32_t sb = static_cast<uint32_t>(unb + 127);
+  if (nan) sb = 255u;
+  float sf = __uint_as_float(sb << 23);
+  sf = fmaxf(sf, __uint_as_float(1u << 23));  // clamp to 2^-126
+  uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t c = f32_to_e2m1(__fdiv_rn(v[i], sf));
+    words[i / 8] |= c << (4 * (i % 8));
+  }
+  *reinterpret_cast<uint4*>(packed + blk * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+  scale[blk] = static_cast<uint8_t>(sb);
+}
+
+// One thread per output byte of the chunked scale layout.
+__global__ void prepack_scales_kernel(const uint8_t* __restrict__ in, int n_mats, int rows, int K,
+                                      uint8_t* __restrict__ out) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int RT = rows / 128, KT = K / 128, KB = K / 32;
+  const size_t total = static_cast<size_t>(n_mats) * RT * KT * 512;
+  if (i >= total) return;
+  const int b = static_cast<int>(i % 512);
+  size_t c = i / 512;
+  const int kt = static_cast<int>(c % KT);
+  c /= KT;
+  const int rt = static_cast<int>(c % RT);
+  const int m = static_cast<int>(c / RT);
+  const int r_local = (b >> 4) + 32 * ((b & 15) >> 2);
+  const int kb = b & 3;
+  out[i] = in[(static_cast<size_t>(m) * rows + rt * 128 + r_local) * KB + kt * 4 + kb];
+}
+
+}  // namespace
+
+cudaError_t launch_rows_quant(const void* x, int T, int H, int k, const int* row_of, int shared_base, int hilo,
+                              int R_pad, uint8_t* xq, uint32_t* xsf, cudaStream_t stream) {
+  dim3 grid(T, (H + 1023) / 1024);
+  rows_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, k, row_of, shared_base,
+                                               hilo, R_pad, xq, xsf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream) {
+  dim3 grid(M, (K + 1023) / 1024);
+  act_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, q, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream) {
+  const size_t nblk = static_cast<size_t>(N) * (K / 32);
+  const int threads = 256;
+  const unsigned grid = static_cast<unsigned>((nblk + threads - 1) / threads);
+  pack_mxfp4_kernel<<<grid, threads, 0, stream>>>(w, N, K, packed, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, uint8_t* chunks,
+                                  cudaStream_t stream) {
+  const size_t total = static_cast<size_t>(n_mats) * (rows / 128) * (K / 128) * 512;
+  const int threads = 256;
+  const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+  prepack_scales_kernel<<<grid, threads, 0, stream>>>(scale, n_mats, rows, K, chunks);
+  return cudaGetLastError();
+}
+
+}  // namespace mosaic

@@ -1,0 +1,78 @@
+"""Seeded input recipes shared by the golden generator and the tests.
+
+Everything is drawn from ``torch.Generator`` on the CPU, so the same seed gives
+the same tensors here and on the GPU box.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+# Small MoE cases (the BASELINE small config S and variants of it).
+MOE_CASES = {
+    # S: H 512, 32 routed + 1 shared, I 256, 4 groups / top-2 groups, top-4, 64 tokens
+    "S": dict(T=64, H=512, I=256, E=32, k=4, n_group=4, topk_group=2, scale=2.5,
+              swiglu_limit=0.0, seed=11),
+    # same with the SwiGLU clamp the reference exercises (layers.py:213-216)
+    "S_clamp": dict(T=24, H=512, I=256, E=32, k=4, n_group=4, topk_group=2, scale=2.5,
+                    swiglu_limit=10.0, seed=12, x_mult=6.0, w_std=0.2),
+    # tiny ragged case: few tokens, many experts
+    "tiny": dict(T=3, H=256, I=128, E=16, k=2, n_group=1, topk_group=1, scale=1.0,
+                 swiglu_limit=0.0, seed=13),
+}
+
+
+def edge_weight_matrix() -> torch.Tensor:
+    """[16, 64] weights hitting E2M1 rounding ties, saturation and scale edges."""
+    rows = []
+    base = torch.tensor([0.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0,
+                         6.0, 7.0, 0.1, 0.3, 0.6, 0.9, 1.1, 2.9])
+    for r in range(16):
+        v = torch.cat([base, -base]) * (2.0 ** (r - 8))
+        if r == 3:
+            v = torch.zeros(32)
+        if r == 5:
+            v = v * 1e-30
+        rows.append(torch.cat([v, v.flip(0) * 3.0]))
+    return torch.stack(rows).float()
+
+
+GATE_CASES = {"gate_s": (64, 512, 32, 4, 2.5), "gate_v3": (16, 7168, 256, 8, 2.5)}
+
+
+def make_gate_case(t, h, e, seed):
+    """Seeded router inputs: W U(-1/sqrt(h), 1/sqrt(h)) fp32 [e, h], bias N(0, 0.01), x bf16 [t, h]."""
+    g = torch.Generator().manual_seed(seed)
+    bound = 1.0 / math.sqrt(h)
+    wt = (torch.rand(e, h, generator=g) * 2 - 1) * bound
+    bias = torch.randn(e, generator=g) * 0.01
+    x = torch.randn(t, h, generator=g).to(torch.bfloat16)
+    return x, wt, bias
+
+
+def make_moe_case(T, H, I, E, k, n_group, topk_group, scale, swiglu_limit, seed,
+                  x_mult: float = 1.0, w_std: float = 0.02):
+    """Seeded MoE-layer inputs: router, expert weights (fp32, unpacked) and tokens.
+
+    Returns a dict with ``cfg``, ``x`` (bf16 [T, H]), ``router_w`` (fp32 [E, H],
+    U(-1/sqrt(H), 1/sqrt(H))), ``bias`` (fp32 [E], N(0, 0.01)), ``w_gu``
+    (list of E+1 fp32 [2I, H], gate rows then up rows; index E is the shared
+    expert), ``w_dn`` (list of E+1 fp32 [H, I]) and the routing ``weights``/``idx``
+    computed by the oracle router.
+    """
+    g = torch.Generator().manual_seed(seed)
+    bound = 1.0 / math.sqrt(H)
+    router_w = (torch.rand(E, H, generator=g) * 2 - 1) * bound
+    bias = torch.randn(E, generator=g) * 0.01
+    w_gu = [torch.randn(2 * I, H, generator=g) * w_std for _ in range(E + 1)]
+    w_dn = [torch.randn(H, I, generator=g) * w_std for _ in range(E + 1)]
+    x = (torch.randn(T, H, generator=g) * x_mult).to(torch.bfloat16)
+    from oracle.router import route
+
+    weights, idx = route(x, router_w, bias, top_k=k, n_group=n_group, topk_group=topk_group,
+                         route_scale=scale)
+    cfg = dict(T=T, H=H, I=I, E=E, k=k, n_group=n_group, topk_group=topk_group, scale=scale,
+               swiglu_limit=swiglu_limit)
+    return dict(cfg=cfg, x=x, router_w=router_w, bias=bias, w_gu=w_gu, w_dn=w_dn,
+                weights=weights, idx=idx)

@@ -1,0 +1,129 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, and host-side validation rejects bad calls before any launch."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from mosaic_b200 import _capi as C
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "mosaic_moe.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return set(re.findall(r"MOSAIC_API[^;(]*?\b(mosaic_\w+)\s*\(", text, flags=re.S))
+
+
+def test_library_loads_and_exports_all_declared_symbols():
+    lib = C.lib()
+    declared = _declared()
+    assert declared == set(C.EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.mosaic_version() >= 1
+
+
+def test_status_strings():
+    lib = C.lib()
+    for code in range(0, 9):
+        assert lib.mosaic_status_string(code)
+    assert lib.mosaic_status_string(0) == b"ok"
+
+
+def _dims(**kw):
+    d = C.MoEDims()
+    base = dict(tokens=8, hidden=512, inter=256, n_experts=32, top_k=4, n_group=4, topk_group=2, act_mode=0,
+                norm_topk_prob=1, has_shared=1, route_scale=2.5, swiglu_limit=0.0)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("bad", [dict(hidden=500), dict(inter=100), dict(n_experts=300), dict(top_k=9),
+                                 dict(n_group=3), dict(topk_group=5), dict(n_group=8, topk_group=1, top_k=8),
+                                 dict(act_mode=7), dict(tokens=0)])
+def test_workspace_bytes_rejects_bad_dims(bad):
+    assert C.lib().mosaic_moe_workspace_bytes(ctypes.byref(_dims(**bad))) == 0
+
+
+def test_workspace_bytes_grows_with_tokens():
+    lib = C.lib()
+    a = lib.mosaic_moe_workspace_bytes(ctypes.byref(_dims(tokens=8)))
+    b = lib.mosaic_moe_workspace_bytes(ctypes.byref(_dims(tokens=64)))
+    assert 0 < a < b
+
+
+def test_forward_validation_before_launch():
+    lib = C.lib()
+    bank = C.ExpertBankC()
+    fake = 1 << 20  # aligned, never dereferenced: validation fails first
+    bank.gu_packed = bank.gu_sf = bank.dn_packed = bank.dn_sf = fake
+    d = _dims()
+    args = [ctypes.byref(d), fake, fake, fake, ctypes.byref(bank), fake, fake, fake, fake, 1 << 40, None]
+    # null x
+    a = list(args)
+    a[1] = None
+    assert lib.mosaic_moe_forward(*a) == C.MOSAIC_ERR_SHAPE
+    # misaligned y
+    a = list(args)
+    a[5] = fake + 2
+    assert lib.mosaic_moe_forward(*a) == C.MOSAIC_ERR_ALIGN
+    # misaligned weight bank (TMA needs 32 B)
+    bank.gu_packed = fake + 16
+    assert lib.mosaic_moe_forward(*args) == C.MOSAIC_ERR_ALIGN
+    bank.gu_packed = fake
+    # workspace too small
+    a = list(args)
+    a[9] = 16
+    assert lib.mosaic_moe_forward(*a) == C.MOSAIC_ERR_WORKSPACE
+    # bad dims
+    bad = _dims(n_group=3)
+    a = list(args)
+    a[0] = ctypes.byref(bad)
+    assert lib.mosaic_moe_forward(*a) == C.MOSAIC_ERR_SHAPE
+
+
+def test_router_validation_before_launch():
+    lib = C.lib()
+    fake = 1 << 20
+    st = lib.mosaic_router(fake, fake, None, 4, 512, 32, 9, 1, 1, 1.0, 1, fake, fake, fake, 1 << 30, None)
+    assert st == C.MOSAIC_ERR_SHAPE
+    st = lib.mosaic_router(fake + 4, fake, None, 4, 512, 32, 4, 1, 1, 1.0, 1, fake, fake, fake, 1 << 30, None)
+    assert st == C.MOSAIC_ERR_ALIGN
+
+
+def test_check_maps_status_to_reference_exceptions():
+    with pytest.raises(ValueError):
+        C.check(C.MOSAIC_ERR_SHAPE, "x")
+    with pytest.raises(TypeError):
+        C.check(C.MOSAIC_ERR_DTYPE, "x")
+    with pytest.raises(C.MosaicError):
+        C.check(C.MOSAIC_ERR_TIMEOUT, "x")
+    C.check(C.MOSAIC_OK, "x")
+
+
+def test_host_api_mirrors_reference_names():
+    import mosaic_b200 as m
+
+    for name in ("MoELayer", "Router", "grouped_expert_forward", "exact_moe", "exact_target", "ExactContractError"):
+        assert hasattr(m, name)
+    from mosaic_b200 import ops
+
+    for name in ("layout_assignments", "emit_tiles", "act_quant", "pack_mxfp4_nk"):
+        assert hasattr(ops, name)
+
+
+def test_ops_reject_cpu_tensors():
+    import torch
+
+    from mosaic_b200 import ops
+
+    with pytest.raises(ValueError):
+        ops.layout_assignments(torch.tensor([0, 1, 2]), 4)
+    with pytest.raises(ValueError):
+        ops.act_quant(torch.zeros(2, 100))
