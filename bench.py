@@ -47,8 +47,9 @@ def parse():
     p.add_argument("--tokens", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true", help="skip the T sweep and the prefill line")
+    p.add_argument("--experts", type=int, default=256, help="routed experts in the bank (V3: 256)")
     p.add_argument("--profile-small", action="store_true",
-                   help="small case for ncu captures: 16 routed experts, 2 steps, no extras")
+                   help="small case for ncu captures: no extras, no CPU baseline, 2 profiled stage runs")
     return p.parse_args()
 
 
@@ -300,7 +301,7 @@ def main():
     if dist_on:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, bf16_tf, peak_src = peaks()
-    n_exp = 16 if args.profile_small else 256
+    n_exp = args.experts
     t = args.tokens
     layer, x = synthetic.make_layer(tokens=t, seed=1234 + rank, act_mode="bf16", n_experts=n_exp)
 

@@ -83,14 +83,17 @@ typedef struct mosaic_moe_dims {
 } mosaic_moe_dims;
 
 /* Expert bank (device memory).  n_bank = E + has_shared; the shared expert,
- * when present, is the last one.  Weights stay in the reference layout
+ * when present, is the last one.  The reference layout
  * (mosaicvm/kernels/exact_moe.py:12: packed_gate_up uint8 [E, 2I, H/2], gate
- * rows then up rows, low nibble = even K; packed_down [E, H, I/2]); the E8M0
- * scales are re-laid out once by mosaic_prepack_scales. */
+ * rows then up rows, low nibble = even K; packed_down [E, H, I/2]; E8M0
+ * scales [E, rows, K/32]) is re-laid out once, invertibly (the role of
+ * mosaicvm/kernels/qpa_mma.py:577-613 prepack_expert_bank_qpa): codes by
+ * mosaic_repack_weights into contiguous 8 KB tiles, scales by
+ * mosaic_prepack_scales into the 512-byte chunks the MMA reads. */
 typedef struct mosaic_expert_bank {
-  const uint8_t* gu_packed; /* [n_bank][2I][H/2], 32-B aligned */
+  const uint8_t* gu_tiled;  /* [n_bank][2I/128][H/128][128][64] from mosaic_repack_weights, 32-B aligned */
   const uint8_t* gu_sf;     /* [n_bank][2I/128][H/128][512] from mosaic_prepack_scales */
-  const uint8_t* dn_packed; /* [n_bank][H][I/2], 32-B aligned */
+  const uint8_t* dn_tiled;  /* [n_bank][H/128][I/128][128][64], 32-B aligned */
   const uint8_t* dn_sf;     /* [n_bank][H/128][I/128][512] */
 } mosaic_expert_bank;
 
@@ -132,6 +135,12 @@ MOSAIC_API int mosaic_act_quant(const void* x, int32_t M, int32_t K, uint8_t* q,
  * (FLOOR E8M0, RNE E2M1 with saturation; bit-identical to the reference packer). */
 MOSAIC_API int mosaic_pack_mxfp4(const float* w, int32_t N, int32_t K, uint8_t* packed, uint8_t* scale,
                       mosaic_stream_t stream);
+
+/* Re-lay packed E2M1 codes [n_mats][rows][K/2] (the reference layout) into
+ * [n_mats][rows/128][K/128][128][64]: each 128-row x 128-value tile becomes one
+ * contiguous 8 KB block.  rows % 128 == 0, K % 128 == 0, 16-B aligned pointers. */
+MOSAIC_API int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int32_t rows, int32_t K,
+                                     uint8_t* tiled, mosaic_stream_t stream);
 
 /* Re-lay E8M0 scales [n_mats][rows][K/32] into the chunks the block-scaled MMA
  * consumes: [n_mats][rows/128][K/128][512] with byte (r%32)*16 + ((r%128)/32)*4 + kb

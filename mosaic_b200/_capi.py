@@ -36,6 +36,7 @@ EXPORTED = (
     "mosaic_emit_tiles",
     "mosaic_act_quant",
     "mosaic_pack_mxfp4",
+    "mosaic_repack_weights",
     "mosaic_prepack_scales",
     "mosaic_moe_workspace_bytes",
     "mosaic_moe_forward",
@@ -64,9 +65,9 @@ class MoEDims(ctypes.Structure):
 
 class ExpertBankC(ctypes.Structure):
     _fields_ = [
-        ("gu_packed", ctypes.c_void_p),
+        ("gu_tiled", ctypes.c_void_p),
         ("gu_sf", ctypes.c_void_p),
-        ("dn_packed", ctypes.c_void_p),
+        ("dn_tiled", ctypes.c_void_p),
         ("dn_sf", ctypes.c_void_p),
     ]
 
@@ -89,6 +90,7 @@ _SIGS = {
     "mosaic_emit_tiles": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_act_quant": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
     "mosaic_pack_mxfp4": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
+    "mosaic_repack_weights": ([_P, _I, _I, _I, _P, _P], ctypes.c_int),
     "mosaic_prepack_scales": ([_P, _I, _I, _I, _P, _P], ctypes.c_int),
     "mosaic_moe_workspace_bytes": ([ctypes.POINTER(MoEDims)], _SZ),
     "mosaic_moe_forward": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _P, _P, _SZ, _P],

@@ -12,6 +12,16 @@
 
 using namespace mosaic;
 
+#ifndef MOSAIC_DECODE_TILE_ROWS
+#define MOSAIC_DECODE_TILE_ROWS 16
+#endif
+#ifndef MOSAIC_DECODE_CHAINS_GU
+#define MOSAIC_DECODE_CHAINS_GU 2
+#endif
+#ifndef MOSAIC_DECODE_CHAINS_DN
+#define MOSAIC_DECODE_CHAINS_DN 3
+#endif
+
 namespace {
 
 constexpr int kVersion = 1;
@@ -43,16 +53,18 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Weights: 3-D map {K, rows, n_bank} over packed E2M1 codes, unpacked by TMA
-// into the 16-byte-per-16-values smem layout that kind::mxf8f6f4 reads.
-int make_weight_map(CUtensorMap* map, const uint8_t* packed, int n_bank, int rows, int K) {
+// Weights: 3-D map {128 values, 128 rows, tiles} over the tiled E2M1 codes (one
+// box = one contiguous 8 KB tile), unpacked by TMA into the 16-byte-per-16-values
+// smem layout that kind::mxf8f6f4 reads.  Tile index = (expert*RT + rt)*KT + kt.
+int make_weight_map(CUtensorMap* map, const uint8_t* tiled, int n_bank, int rows, int K) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return MOSAIC_ERR_CUDA;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(n_bank)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows) * (K / 2)};
+  const cuuint64_t n_tiles = static_cast<cuuint64_t>(n_bank) * (rows / 128) * (K / 128);
+  cuuint64_t dims[3] = {128, 128, n_tiles};
+  cuuint64_t strides[2] = {64, 8192};
   cuuint32_t box[3] = {128, 128, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<uint8_t*>(packed), dims, strides, box,
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<uint8_t*>(tiled), dims, strides, box,
                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
@@ -73,9 +85,10 @@ int make_act_map(CUtensorMap* map, const uint8_t* q, int rows, int K) {
 }
 
 struct WsPlan {
-  int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32;
-  size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, tiles, n_tiles;
-  size_t xq, xsf, zq, zsf, partial, total;
+  int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32, max_n, nbuf, chains_gu, chains_dn;
+  size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, row_tile, row_pos, tiles,
+      n_tiles;
+  size_t xq, x_sft, zq, z_sft, partial, total;
 };
 
 int check_dims(const mosaic_moe_dims* d) {
@@ -96,11 +109,22 @@ WsPlan plan_ws(const mosaic_moe_dims* d) {
   WsPlan w{};
   const int T = d->tokens, H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
+  (void)I;
   w.n_bank = E + (d->has_shared ? 1 : 0);
   w.R = T * k + (d->has_shared ? T : 0);
   w.R_pad = (w.R + 15) & ~15;
   w.planes = hilo ? 2 : 1;
-  w.tt = hilo ? 64 : 128;
+  // Token rows per tile.  bf16 (decode) tiles carry hi + lo planes: MMA N = 2 * rows.
+  // Small-N tiles are latency-bound in the tensor pipe, so they get several
+  // independent accumulation chains and two TMEM buffers; FP8 (prefill) tiles take
+  // 128 rows in one buffer and one chain (512 TMEM columns in all).
+  w.tt = hilo ? MOSAIC_DECODE_TILE_ROWS : 128;
+  w.max_n = hilo ? 2 * w.tt : w.tt;
+  w.nbuf = hilo ? 2 : 1;
+  w.chains_gu = hilo ? MOSAIC_DECODE_CHAINS_GU : 1;
+  w.chains_dn = hilo ? MOSAIC_DECODE_CHAINS_DN : 1;
+  if (w.chains_gu > H / 128) w.chains_gu = H / 128;  // every chain needs at least one K tile
+  if (w.chains_dn > d->inter / 128) w.chains_dn = d->inter / 128;
   w.max_tiles = (T * k) / w.tt + w.n_bank + T / w.tt + 2;
   const int sms = sm_count();
   w.splits = router_splits(T, H, E, sms > 0 ? sms : 148);
@@ -119,20 +143,22 @@ WsPlan plan_ws(const mosaic_moe_dims* d) {
   w.row_sorted = take(sizeof(int) * static_cast<size_t>(T) * k);
   w.row_token = take(sizeof(int) * static_cast<size_t>(w.R));
   w.row_weight = take(sizeof(float) * static_cast<size_t>(w.R));
+  w.row_tile = take(sizeof(int) * static_cast<size_t>(w.R));
+  w.row_pos = take(sizeof(int) * static_cast<size_t>(w.R));
   w.tiles = take(sizeof(int) * 3 * static_cast<size_t>(w.max_tiles));
   w.n_tiles = take(sizeof(int) * 4);
   w.xq = take(static_cast<size_t>(w.planes) * w.R_pad * H);
-  w.xsf = take(sizeof(uint32_t) * static_cast<size_t>(w.planes) * (H / 128) * w.R_pad);
+  w.x_sft = take(static_cast<size_t>(w.max_tiles) * (H / 128) * 512);
   w.zq = take(static_cast<size_t>(w.planes) * w.R_pad * I);
-  w.zsf = take(sizeof(uint32_t) * static_cast<size_t>(w.planes) * (I / 128) * w.R_pad);
+  w.z_sft = take(static_cast<size_t>(w.max_tiles) * (I / 128) * 512);
   w.partial = take(static_cast<size_t>(w.R) * H * (w.partial_f32 ? 4 : 2));
   w.total = o;
   return w;
 }
 
 int check_bank(const mosaic_expert_bank* b) {
-  if (!b || !b->gu_packed || !b->gu_sf || !b->dn_packed || !b->dn_sf) return MOSAIC_ERR_SHAPE;
-  if (!aligned(b->gu_packed, 32) || !aligned(b->dn_packed, 32)) return MOSAIC_ERR_ALIGN;
+  if (!b || !b->gu_tiled || !b->gu_sf || !b->dn_tiled || !b->dn_sf) return MOSAIC_ERR_SHAPE;
+  if (!aligned(b->gu_tiled, 32) || !aligned(b->dn_tiled, 32)) return MOSAIC_ERR_ALIGN;
   if (!aligned(b->gu_sf, 16) || !aligned(b->dn_sf, 16)) return MOSAIC_ERR_ALIGN;
   return MOSAIC_OK;
 }
@@ -169,6 +195,8 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   lp.row_sorted = reinterpret_cast<int*>(ws + w.row_sorted);
   lp.row_token = reinterpret_cast<int*>(ws + w.row_token);
   lp.row_weight = reinterpret_cast<float*>(ws + w.row_weight);
+  lp.row_tile = reinterpret_cast<int*>(ws + w.row_tile);
+  lp.row_pos = reinterpret_cast<int*>(ws + w.row_pos);
   lp.tiles = reinterpret_cast<int*>(ws + w.tiles);
   lp.n_tiles = reinterpret_cast<int*>(ws + w.n_tiles);
   lp.err = err;
@@ -176,8 +204,8 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
 
   uint8_t* xq = ws + w.xq;
-  uint32_t* xsf = reinterpret_cast<uint32_t*>(ws + w.xsf);
-  if (launch_rows_quant(x, T, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, xq, xsf, stream) != cudaSuccess)
+  if (launch_rows_quant(x, T, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos, xq,
+                        reinterpret_cast<uint32_t*>(ws + w.x_sft), stream) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
   if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
 
@@ -196,37 +224,38 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   gp.n_tiles = lp.n_tiles;
   gp.max_tiles = w.max_tiles;
   gp.row_weight = lp.row_weight;
+  gp.max_n = w.max_n;
+  gp.nbuf = w.nbuf;
   gp.swiglu_limit = d->swiglu_limit;
   gp.err = err;
 
   // gate/up
-  int st = make_weight_map(&tw, bank->gu_packed, w.n_bank, 2 * I, H);
+  int st = make_weight_map(&tw, bank->gu_tiled, w.n_bank, 2 * I, H);
   if (st) return st;
   st = make_act_map(&tx, xq, w.planes * w.R_pad, H);
   if (st) return st;
   gp.mode = 0;
+  gp.chains = w.chains_gu;
   gp.K = H;
   gp.n_blocks = I / 128;
-  gp.x_sf = xsf;
-  gp.x_sf_plane = static_cast<size_t>(H / 128) * w.R_pad;
+  gp.x_sft = ws + w.x_sft;
   gp.w_sf = bank->gu_sf;
   gp.w_rowtiles = 2 * I / 128;
   gp.zq = ws + w.zq;
-  gp.zsf = reinterpret_cast<uint32_t*>(ws + w.zsf);
-  gp.z_sf_plane = static_cast<size_t>(I / 128) * w.R_pad;
+  gp.z_sft = reinterpret_cast<uint32_t*>(ws + w.z_sft);
   if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
 
   // down
-  st = make_weight_map(&tw, bank->dn_packed, w.n_bank, H, I);
+  st = make_weight_map(&tw, bank->dn_tiled, w.n_bank, H, I);
   if (st) return st;
   st = make_act_map(&tx, gp.zq, w.planes * w.R_pad, I);
   if (st) return st;
   gp.mode = 1;
+  gp.chains = w.chains_dn;
   gp.K = I;
   gp.n_blocks = H / 128;
-  gp.x_sf = gp.zsf;
-  gp.x_sf_plane = gp.z_sf_plane;
+  gp.x_sft = ws + w.z_sft;
   gp.w_sf = bank->dn_sf;
   gp.w_rowtiles = H / 128;
   gp.out = ws + w.partial;
@@ -322,6 +351,15 @@ int mosaic_pack_mxfp4(const float* w, int32_t N, int32_t K, uint8_t* packed, uin
   if (N < 1 || K < 32 || K % 32) return MOSAIC_ERR_SHAPE;
   if (!aligned(w, 16) || !aligned(packed, 16)) return MOSAIC_ERR_ALIGN;
   cudaError_t e = launch_pack_mxfp4(w, N, K, packed, scale, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int32_t rows, int32_t K, uint8_t* tiled,
+                          mosaic_stream_t stream) {
+  if (!packed || !tiled) return MOSAIC_ERR_SHAPE;
+  if (n_mats < 1 || rows < 128 || rows % 128 || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
+  if (!aligned(packed, 16) || !aligned(tiled, 16)) return MOSAIC_ERR_ALIGN;
+  cudaError_t e = launch_repack_weights(packed, n_mats, rows, K, tiled, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 

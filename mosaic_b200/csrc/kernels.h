@@ -21,20 +21,21 @@ struct GemmParams {
   const int* tiles;   // [max_tiles][3] = (expert, first row, rows)
   const int* n_tiles;
   int max_tiles;
-  const uint32_t* x_sf;  // activation scales [plane][K/128][R_pad], 4 E8M0 bytes per word
-  size_t x_sf_plane;
+  const uint8_t* x_sft;  // activation scale chunks per token tile: [tile][K/128][512]
+  int max_n;             // largest MMA N of the launch (token rows x planes), <= 128
+  int nbuf;              // TMEM accumulator buffers
+  int chains;            // independent K accumulation chains per buffer (1..4)
   const uint8_t* w_sf;   // weight scale chunks [bank][rows/128][K/128][512]
   int w_rowtiles;
   const float* row_weight;  // [R] route weight of each packed row
   float swiglu_limit;
   uint8_t* zq;        // gate/up output rows [plane][R_pad][I] (E4M3)
-  uint32_t* zsf;      // their scales [plane][I/128][R_pad]
-  size_t z_sf_plane;
+  uint32_t* z_sft;    // their scale chunks per token tile [tile][I/128][128 words]
   void* out;          // down partials [R][H]
   int out_f32;
   int* err;
 };
-size_t gemm_smem_bytes(int mode);
+size_t gemm_smem_bytes(int mode, int max_n);
 cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmParams& p, int grid,
                             cudaStream_t stream);
 
@@ -58,6 +59,8 @@ struct LayoutParams {
   int* row_sorted;        // [T][k] rows of each token in ascending expert id
   int* row_token;         // [R]
   float* row_weight;      // [R]
+  int* row_tile;          // [R] token tile holding the row
+  int* row_pos;           // [R] (rpad of that tile << 8) | position of the row in it
   int* tiles;             // [max_tiles][3]
   int* n_tiles;
   int* err;
@@ -71,11 +74,15 @@ cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max
 // ---- quantisation (quant.cu)
 // x bf16 [T][H] -> packed activation rows: row_of[t][s] (s < k) and, when
 // shared_base >= 0, row shared_base + t.  hilo: hi/lo planes with per-32
-// scales; else act_quant_ref per 128.
+// scales; else act_quant_ref per 128.  Scales go straight into the token
+// tile's MMA scale chunks sft [tile][H/128][128 words].
 cudaError_t launch_rows_quant(const void* x, int T, int H, int k, const int* row_of, int shared_base, int hilo,
-                              int R_pad, uint8_t* xq, uint32_t* xsf, cudaStream_t stream);
+                              int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
+                              cudaStream_t stream);
 cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
 cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
+cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, int K, uint8_t* tiled,
+                                  cudaStream_t stream);
 cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, uint8_t* chunks,
                                   cudaStream_t stream);
 

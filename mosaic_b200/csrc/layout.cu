@@ -72,6 +72,12 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
   if (tid == 0 && p.with_shared) hist[E] = T;
   __syncthreads();
   warp0_exclusive_scan(hist, offs, NE);
+  for (int i = tid; i < NE; i += 1024) {
+    const int tt = (p.with_shared && i == E) ? p.tt_shared : p.tt_routed;
+    ntile[i] = (tt > 0) ? (hist[i] + tt - 1) / tt : 0;
+  }
+  __syncthreads();
+  warp0_exclusive_scan(ntile, toff, NE);
   __syncthreads();
 
   for (int c0 = 0; c0 < T; c0 += 1024) {
@@ -112,6 +118,13 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
           const int rank = pre[warp * E + e] + __popc(masks[warp * E + e] & lt);
           row = offs[e] + rank;
           if (p.row_token) p.row_token[row] = t;
+          if (p.row_tile) {
+            const int tt = p.tt_routed;
+            const int ti = rank / tt;
+            const int rows_t = min(tt, hist[e] - ti * tt);
+            p.row_tile[row] = toff[e] + ti;
+            p.row_pos[row] = (((rows_t + 15) & ~15) << 8) | (rank - ti * tt);
+          }
           if (p.row_weight) p.row_weight[row] = p.weights ? p.weights[static_cast<size_t>(t) * k + s] : 1.0f;
           if (x.perm) x.perm[row] = static_cast<int64_t>(t) * k + s;
           if (x.sorted_ids) x.sorted_ids[row] = e;
@@ -148,19 +161,20 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
       const int row = offs[E] + t;
       p.row_token[row] = t;
       p.row_weight[row] = 1.0f;
+      if (p.row_tile) {
+        const int tt = p.tt_shared;
+        const int ti = t / tt;
+        const int rows_t = min(tt, T - ti * tt);
+        p.row_tile[row] = toff[E] + ti;
+        p.row_pos[row] = (((rows_t + 15) & ~15) << 8) | (t - ti * tt);
+      }
     }
   }
-  for (int i = tid; i < NE; i += 1024) {
+  for (int i = tid; i < NE; i += 1024)
     if (p.counts) p.counts[i] = hist[i];
-    const int tt = (p.with_shared && i == E) ? p.tt_shared : p.tt_routed;
-    ntile[i] = (tt > 0) ? (hist[i] + tt - 1) / tt : 0;
-  }
   for (int i = tid; i <= NE; i += 1024)
     if (p.offsets) p.offsets[i] = offs[i];
-  __syncthreads();
   if (p.tiles) {
-    warp0_exclusive_scan(ntile, toff, NE);
-    __syncthreads();
     for (int e = tid; e < NE; e += 1024) {
       const int tt = (p.with_shared && e == E) ? p.tt_shared : p.tt_routed;
       for (int i = 0; i < ntile[e]; ++i) {

@@ -87,11 +87,15 @@ __device__ __forceinline__ uint32_t gather_word(int e) {
   return w;
 }
 
-// grid (T, ceil(H / 1024)), 128 threads: each warp quantises 256 values of one token.
+// grid (T, ceil(H / 1024)), 128 threads: each warp quantises 256 values of one token
+// and writes them to every packed row of the token; the scale words go into the
+// row's token-tile chunk (word (n%32)*4 + n/32 of chunk [tile][kt]; the lo plane
+// of a bf16 tile sits at rows rpad + n of the same chunk).
 __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, int k,
                                                          const int* __restrict__ row_of, int shared_base, int hilo,
-                                                         int R_pad, uint8_t* __restrict__ xq,
-                                                         uint32_t* __restrict__ xsf) {
+                                                         int R_pad, const int* __restrict__ row_tile,
+                                                         const int* __restrict__ row_pos, uint8_t* __restrict__ xq,
+                                                         uint32_t* __restrict__ sft) {
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31;
   const int k0 = blockIdx.y * 1024 + (threadIdx.x >> 5) * 256 + lane * 8;
@@ -104,7 +108,8 @@ __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __
     for (int i = 0; i < 8; ++i) v[i] = 0.f;
   }
   const int nrows = k + (shared_base >= 0 ? 1 : 0);
-  const size_t plane_w = static_cast<size_t>(H / 128) * R_pad;
+  const int KT = H / 128;
+  const int kt = k0 / 128;
   if (!hilo) {
     uint8_t q[8];
     const int e = quant_block128(v, q);
@@ -115,7 +120,10 @@ __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __
       const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
       if (r < 0) continue;
       *reinterpret_cast<uint2*>(xq + static_cast<size_t>(r) * H + k0) = pq;
-      if ((lane & 15) == 0) xsf[static_cast<size_t>(k0 / 128) * R_pad + r] = word;
+      if ((lane & 15) == 0) {
+        const int n = row_pos[r] & 0xFF;
+        sft[(static_cast<size_t>(row_tile[r]) * KT + kt) * 128 + (n & 31) * 4 + (n >> 5)] = word;
+      }
     }
   } else {
     uint8_t hi[8], lo[8];
@@ -131,8 +139,11 @@ __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __
       *reinterpret_cast<uint2*>(xq + static_cast<size_t>(r) * H + k0) = ph;
       *reinterpret_cast<uint2*>(xq + (static_cast<size_t>(R_pad) + r) * H + k0) = pl;
       if ((lane & 15) == 0) {
-        xsf[static_cast<size_t>(k0 / 128) * R_pad + r] = wh;
-        xsf[plane_w + static_cast<size_t>(k0 / 128) * R_pad + r] = wl;
+        const int pos = row_pos[r];
+        const int n = pos & 0xFF, rp = pos >> 8, n2 = rp + n;
+        uint32_t* c = sft + (static_cast<size_t>(row_tile[r]) * KT + kt) * 128;
+        c[(n & 31) * 4 + (n >> 5)] = wh;
+        c[(n2 & 31) * 4 + (n2 >> 5)] = wl;
       }
     }
   }
@@ -235,13 +246,45 @@ __global__ void prepack_scales_kernel(const uint8_t* __restrict__ in, int n_mats
   out[i] = in[(static_cast<size_t>(m) * rows + rt * 128 + r_local) * KB + kt * 4 + kb];
 }
 
+// Weight re-layout: packed codes [n][rows][K/2] -> [n][rows/128][K/128][128][64 B],
+// so every 128-row x 128-value MMA tile is one contiguous 8 KB block.
+// One thread per 16-byte piece.
+__global__ void repack_weights_kernel(const uint4* __restrict__ in, int n_mats, int rows, int K,
+                                      uint4* __restrict__ out) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int RT = rows / 128, KT = K / 128;
+  const size_t total = static_cast<size_t>(n_mats) * rows * (K / 32);  // 16-byte pieces
+  if (i >= total) return;
+  const int c = static_cast<int>(i & 3);             // piece in the 64-byte row segment
+  size_t rest = i >> 2;
+  const int r = static_cast<int>(rest % 128);
+  rest /= 128;
+  const int kt = static_cast<int>(rest % KT);
+  rest /= KT;
+  const int rt = static_cast<int>(rest % RT);
+  const int m = static_cast<int>(rest / RT);
+  const size_t src = ((static_cast<size_t>(m) * rows + rt * 128 + r) * (K / 2) + kt * 64 + c * 16) / 16;
+  out[i] = in[src];
+}
+
 }  // namespace
 
+cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, int K, uint8_t* tiled,
+                                  cudaStream_t stream) {
+  const size_t total = static_cast<size_t>(n_mats) * rows * (K / 32);
+  const int threads = 256;
+  const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
+  repack_weights_kernel<<<grid, threads, 0, stream>>>(reinterpret_cast<const uint4*>(packed), n_mats, rows, K,
+                                                      reinterpret_cast<uint4*>(tiled));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_rows_quant(const void* x, int T, int H, int k, const int* row_of, int shared_base, int hilo,
-                              int R_pad, uint8_t* xq, uint32_t* xsf, cudaStream_t stream) {
+                              int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
+                              cudaStream_t stream) {
   dim3 grid(T, (H + 1023) / 1024);
   rows_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, k, row_of, shared_base,
-                                               hilo, R_pad, xq, xsf);
+                                               hilo, R_pad, row_tile, row_pos, xq, sft);
   return cudaGetLastError();
 }
 

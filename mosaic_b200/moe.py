@@ -94,12 +94,14 @@ class ExpertBank:
 
     ``gu_packed`` uint8 [n, 2I, H/2] (gate rows then up rows), ``gu_scale`` E8M0
     bytes [n, 2I, H/32], ``dn_packed`` [n, H, I/2], ``dn_scale`` [n, H, I/32];
-    with a shared expert it is the last of the n.  The scale chunks the MMA
-    reads are built once here (the bank re-layout of
-    mosaicvm/kernels/qpa_mma.py:577-613).
+    with a shared expert it is the last of the n.  The layouts the MMA reads
+    are built once here, invertibly (the bank re-layout of
+    mosaicvm/kernels/qpa_mma.py:577-613): codes in contiguous 8 KB tiles
+    (``gu_tiled``, ``dn_tiled``), scales in 512-byte chunks (``gu_sf``,
+    ``dn_sf``).  ``keep_packed=False`` drops the reference-layout copies.
     """
 
-    def __init__(self, gu_packed, gu_scale, dn_packed, dn_scale, *, has_shared: bool):
+    def __init__(self, gu_packed, gu_scale, dn_packed, dn_scale, *, has_shared: bool, keep_packed: bool = True):
         for t in (gu_packed, gu_scale, dn_packed, dn_scale):
             if t.device.type != "cuda":
                 raise ValueError("ExpertBank tensors must be on a CUDA device")
@@ -118,6 +120,10 @@ class ExpertBank:
         self.has_shared = bool(has_shared)
         self.gu_sf = ops.prepack_scales(self.gu_scale)
         self.dn_sf = ops.prepack_scales(self.dn_scale)
+        self.gu_tiled = ops.repack_weights(self.gu_packed)
+        self.dn_tiled = ops.repack_weights(self.dn_packed)
+        if not keep_packed:
+            self.gu_packed = self.dn_packed = None
 
     @classmethod
     def from_dense(cls, w_gu, w_dn, *, has_shared: bool, device="cuda"):
@@ -129,14 +135,15 @@ class ExpertBank:
 
     def c_struct(self) -> C.ExpertBankC:
         b = C.ExpertBankC()
-        b.gu_packed = self.gu_packed.data_ptr()
+        b.gu_tiled = self.gu_tiled.data_ptr()
         b.gu_sf = self.gu_sf.data_ptr()
-        b.dn_packed = self.dn_packed.data_ptr()
+        b.dn_tiled = self.dn_tiled.data_ptr()
         b.dn_sf = self.dn_sf.data_ptr()
         return b
 
     def nbytes(self) -> int:
-        return sum(t.numel() for t in (self.gu_packed, self.gu_scale, self.dn_packed, self.dn_scale))
+        """Device bytes the kernels read from (tiled codes + scale chunks)."""
+        return sum(t.numel() for t in (self.gu_tiled, self.gu_sf, self.dn_tiled, self.dn_sf))
 
 
 class _Workspace:

@@ -146,6 +146,21 @@ def prepack_scales(scale: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def repack_weights(packed: torch.Tensor) -> torch.Tensor:
+    """Packed E2M1 codes [n_mats, rows, K/2] -> contiguous 8 KB MMA tiles [n_mats, rows/128, K/128, 128, 64]."""
+    packed = _u8(packed).contiguous()
+    if packed.dim() == 2:
+        packed = packed.unsqueeze(0)
+    _need_cuda(packed, what="repack_weights")
+    n, rows, half_k = packed.shape
+    k = half_k * 2
+    if rows % 128 or k % 128:
+        raise ValueError("repack_weights needs rows % 128 == 0 and K % 128 == 0")
+    out = torch.empty(n, rows // 128, k // 128, 128, 64, dtype=torch.uint8, device=packed.device)
+    C.check(C.lib().mosaic_repack_weights(_ptr(packed), n, rows, k, _ptr(out), _stream()), "mosaic_repack_weights")
+    return out
+
+
 def read_error(workspace: torch.Tensor, reset: bool = True) -> int:
     """Device error word of a layer workspace (synchronises the stream)."""
     code = ctypes.c_int32(0)

@@ -62,7 +62,7 @@ def test_forward_validation_before_launch():
     lib = C.lib()
     bank = C.ExpertBankC()
     fake = 1 << 20  # aligned, never dereferenced: validation fails first
-    bank.gu_packed = bank.gu_sf = bank.dn_packed = bank.dn_sf = fake
+    bank.gu_tiled = bank.gu_sf = bank.dn_tiled = bank.dn_sf = fake
     d = _dims()
     args = [ctypes.byref(d), fake, fake, fake, ctypes.byref(bank), fake, fake, fake, fake, 1 << 40, None]
     # null x
@@ -74,9 +74,9 @@ def test_forward_validation_before_launch():
     a[5] = fake + 2
     assert lib.mosaic_moe_forward(*a) == C.MOSAIC_ERR_ALIGN
     # misaligned weight bank (TMA needs 32 B)
-    bank.gu_packed = fake + 16
+    bank.gu_tiled = fake + 16
     assert lib.mosaic_moe_forward(*args) == C.MOSAIC_ERR_ALIGN
-    bank.gu_packed = fake
+    bank.gu_tiled = fake
     # workspace too small
     a = list(args)
     a[9] = 16

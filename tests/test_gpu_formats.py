@@ -110,3 +110,12 @@ def test_prepack_scales_layout(ops):
             for kt in range(4):
                 ref[:, rt, kt, b] = a[:, rt * 128 + r_local, kt * 4 + kb]
     assert np.array_equal(out, ref)
+
+
+def test_repack_weights_layout(ops):
+    g = torch.Generator().manual_seed(4)
+    p = torch.randint(0, 256, (2, 256, 192), generator=g, dtype=torch.uint8)  # rows 256, K 384
+    out = ops.repack_weights(p.cuda()).cpu().numpy()
+    a = p.numpy()
+    ref = a.reshape(2, 2, 128, 3, 64).transpose(0, 1, 3, 2, 4)
+    assert np.array_equal(out, ref)
