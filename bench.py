@@ -138,6 +138,15 @@ def timed_graph(graph, steps, warmup, dist_on):
     return ms
 
 
+def check_device_error(layer, t, where):
+    """Fail loudly if a kernel of the timed region recorded an error (e.g. a bounded wait that ran out)."""
+    from mosaic_b200 import ops
+
+    code = ops.read_error(layer.workspace(t, torch.device("cuda")))
+    if code:
+        raise RuntimeError(f"device error {code} recorded during {where}")
+
+
 def capture(layer, x):
     static_x = x.clone()
     for _ in range(3):
@@ -310,6 +319,7 @@ def main():
     with Clocks(gpu_index(local)) as clk:
         ms = timed_graph(g, steps, warmup, dist_on)
     clocks = clk.summary()
+    check_device_error(layer, t, "graph replays")
     stages, idx = stage_times(layer, x, reps=2 if args.profile_small else 20)
     u = int(torch.unique(idx).numel())
     w_last = layer.last_weights
@@ -317,6 +327,7 @@ def main():
     gu_bytes = (u + 1) * GU_BYTES
     achieved = gu_bytes / (stages["gemm_gate_up"] * 1e-3) / 1e9
     e2e_ms, bi, bo = e2e(layer, x, max(steps // 4, 10), dist_on)
+    check_device_error(layer, t, "e2e")
     value = t * world / (ms / 1e3)
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,

@@ -91,10 +91,10 @@ typedef struct mosaic_moe_dims {
  * mosaic_repack_weights into contiguous 8 KB tiles, scales by
  * mosaic_prepack_scales into the 512-byte chunks the MMA reads. */
 typedef struct mosaic_expert_bank {
-  const uint8_t* gu_tiled;  /* [n_bank][2I/128][H/128][128][64] from mosaic_repack_weights, 32-B aligned */
-  const uint8_t* gu_sf;     /* [n_bank][2I/128][H/128][512] from mosaic_prepack_scales */
-  const uint8_t* dn_tiled;  /* [n_bank][H/128][I/128][128][64], 32-B aligned */
-  const uint8_t* dn_sf;     /* [n_bank][H/128][I/128][512] */
+  const uint8_t* gu_tiled;  /* [n_bank][I/128][H/128][2][128][64]: mosaic_repack_weights(halves=2), 32-B aligned */
+  const uint8_t* gu_sf;     /* [n_bank][I/128][H/128][2][512]: mosaic_prepack_scales(halves=2) */
+  const uint8_t* dn_tiled;  /* [n_bank][H/128][I/128][128][64]: mosaic_repack_weights(halves=1), 32-B aligned */
+  const uint8_t* dn_sf;     /* [n_bank][H/128][I/128][512]: mosaic_prepack_scales(halves=1) */
 } mosaic_expert_bank;
 
 MOSAIC_API int mosaic_version(void);
@@ -137,16 +137,19 @@ MOSAIC_API int mosaic_pack_mxfp4(const float* w, int32_t N, int32_t K, uint8_t* 
                       mosaic_stream_t stream);
 
 /* Re-lay packed E2M1 codes [n_mats][rows][K/2] (the reference layout) into
- * [n_mats][rows/128][K/128][128][64]: each 128-row x 128-value tile becomes one
- * contiguous 8 KB block.  rows % 128 == 0, K % 128 == 0, 16-B aligned pointers. */
-MOSAIC_API int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int32_t rows, int32_t K,
+ * 8 KB tiles of 128 rows x 128 values, [n_mats][row block][K/128][halves][128][64].
+ * halves = 2 splits the rows into two halves (gate rows, up rows) and puts the
+ * two tiles of the same row block and K-tile next to each other; halves = 1 is
+ * plain.  rows % (128 * halves) == 0, K % 128 == 0, 16-B aligned pointers. */
+MOSAIC_API int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int32_t rows, int32_t K, int32_t halves,
                                      uint8_t* tiled, mosaic_stream_t stream);
 
 /* Re-lay E8M0 scales [n_mats][rows][K/32] into the chunks the block-scaled MMA
- * consumes: [n_mats][rows/128][K/128][512] with byte (r%32)*16 + ((r%128)/32)*4 + kb
- * of a chunk holding row r, K32 block kb.  rows % 128 == 0, K % 128 == 0. */
-MOSAIC_API int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, uint8_t* sf_chunks,
-                          mosaic_stream_t stream);
+ * consumes, in the same tile order as mosaic_repack_weights:
+ * [n_mats][row block][K/128][halves][512], byte (r%32)*16 + ((r%128)/32)*4 + kb
+ * of a chunk holding row r, K32 block kb.  rows % (128 * halves) == 0, K % 128 == 0. */
+MOSAIC_API int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, int32_t halves,
+                                     uint8_t* sf_chunks, mosaic_stream_t stream);
 
 /* Workspace for mosaic_moe_forward / mosaic_moe_routed (256-B aligned pointer). */
 MOSAIC_API size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims);

@@ -90,8 +90,8 @@ _SIGS = {
     "mosaic_emit_tiles": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_act_quant": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
     "mosaic_pack_mxfp4": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
-    "mosaic_repack_weights": ([_P, _I, _I, _I, _P, _P], ctypes.c_int),
-    "mosaic_prepack_scales": ([_P, _I, _I, _I, _P, _P], ctypes.c_int),
+    "mosaic_repack_weights": ([_P, _I, _I, _I, _I, _P, _P], ctypes.c_int),
+    "mosaic_prepack_scales": ([_P, _I, _I, _I, _I, _P, _P], ctypes.c_int),
     "mosaic_moe_workspace_bytes": ([ctypes.POINTER(MoEDims)], _SZ),
     "mosaic_moe_forward": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _P, _P, _SZ, _P],
                            ctypes.c_int),

@@ -12,15 +12,9 @@
 
 using namespace mosaic;
 
-#ifndef MOSAIC_DECODE_TILE_ROWS
+// Token rows per bf16 (decode) tile; the hi + lo planes of a tile make MMA N = 32.
 #define MOSAIC_DECODE_TILE_ROWS 16
-#endif
-#ifndef MOSAIC_DECODE_CHAINS_GU
-#define MOSAIC_DECODE_CHAINS_GU 2
-#endif
-#ifndef MOSAIC_DECODE_CHAINS_DN
-#define MOSAIC_DECODE_CHAINS_DN 3
-#endif
+
 
 namespace {
 
@@ -53,16 +47,17 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Weights: 3-D map {128 values, 128 rows, tiles} over the tiled E2M1 codes (one
-// box = one contiguous 8 KB tile), unpacked by TMA into the 16-byte-per-16-values
-// smem layout that kind::mxf8f6f4 reads.  Tile index = (expert*RT + rt)*KT + kt.
-int make_weight_map(CUtensorMap* map, const uint8_t* tiled, int n_bank, int rows, int K) {
+// Weights: 3-D map {128 values, 128 rows, tiles} over the tiled E2M1 codes; one
+// box = two consecutive 8 KB tiles (gate + up of one K-tile, or two K-tiles of
+// down), unpacked by TMA into the 16-byte-per-16-values smem layout that
+// kind::mxf8f6f4 reads.
+int make_weight_map(CUtensorMap* map, const uint8_t* tiled, int n_bank, int rows, int K, int box_tiles) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return MOSAIC_ERR_CUDA;
   const cuuint64_t n_tiles = static_cast<cuuint64_t>(n_bank) * (rows / 128) * (K / 128);
   cuuint64_t dims[3] = {128, 128, n_tiles};
   cuuint64_t strides[2] = {64, 8192};
-  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t box[3] = {128, 128, static_cast<cuuint32_t>(box_tiles)};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<uint8_t*>(tiled), dims, strides, box,
                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -70,22 +65,26 @@ int make_weight_map(CUtensorMap* map, const uint8_t* tiled, int n_bank, int rows
   return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
-// Activations: 2-D map {K, rows} over E4M3 bytes, 16-row boxes.
-int make_act_map(CUtensorMap* map, const uint8_t* q, int rows, int K) {
+// Activations: 4-D map {128 bytes, rows, planes, K-tiles} over E4M3 rows stored
+// K-tile-major ([K/128][planes][R_pad][128 B]); one box = brows rows of every
+// plane for ks consecutive K-tiles.
+int make_act_map(CUtensorMap* map, const uint8_t* q, int R_pad, int planes, int K, int brows, int ks) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return MOSAIC_ERR_CUDA;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
-  cuuint32_t box[2] = {128, 16};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, es,
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(R_pad), static_cast<cuuint64_t>(planes),
+                        static_cast<cuuint64_t>(K / 128)};
+  cuuint64_t strides[3] = {128, static_cast<cuuint64_t>(R_pad) * 128, static_cast<cuuint64_t>(planes) * R_pad * 128};
+  cuuint32_t box[4] = {128, static_cast<cuuint32_t>(brows), static_cast<cuuint32_t>(planes),
+                       static_cast<cuuint32_t>(ks)};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(q), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
 struct WsPlan {
-  int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32, max_n, nbuf, chains_gu, chains_dn;
+  int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32, max_n, nbuf, parities;
   size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, row_tile, row_pos, tiles,
       n_tiles;
   size_t xq, x_sft, zq, z_sft, partial, total;
@@ -115,17 +114,14 @@ WsPlan plan_ws(const mosaic_moe_dims* d) {
   w.R_pad = (w.R + 15) & ~15;
   w.planes = hilo ? 2 : 1;
   // Token rows per tile.  bf16 (decode) tiles carry hi + lo planes: MMA N = 2 * rows.
-  // Small-N tiles are latency-bound in the tensor pipe, so they get several
-  // independent accumulation chains and two TMEM buffers; FP8 (prefill) tiles take
-  // 128 rows in one buffer and one chain (512 TMEM columns in all).
   w.tt = hilo ? MOSAIC_DECODE_TILE_ROWS : 128;
   w.max_n = hilo ? 2 * w.tt : w.tt;
-  w.nbuf = hilo ? 2 : 1;
-  w.chains_gu = hilo ? MOSAIC_DECODE_CHAINS_GU : 1;
-  w.chains_dn = hilo ? MOSAIC_DECODE_CHAINS_DN : 1;
-  if (w.chains_gu > H / 128) w.chains_gu = H / 128;  // every chain needs at least one K tile
-  if (w.chains_dn > d->inter / 128) w.chains_dn = d->inter / 128;
+  // sum over experts of ceil(count / tt) <= A / tt + (experts with a partial tile)
   w.max_tiles = (T * k) / w.tt + w.n_bank + T / w.tt + 2;
+  // Decode tiles (small N, 64 TMEM columns per gate+up accumulator): two TMEM
+  // buffers and two stage parities.  Prefill tiles (N = 128): one of each.
+  w.nbuf = hilo ? 2 : 1;
+  w.parities = hilo ? 2 : 1;
   const int sms = sm_count();
   w.splits = router_splits(T, H, E, sms > 0 ? sms : 148);
   w.partial_f32 = hilo ? 1 : 0;
@@ -225,17 +221,19 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   gp.max_tiles = w.max_tiles;
   gp.row_weight = lp.row_weight;
   gp.max_n = w.max_n;
+  gp.brows = w.tt;
   gp.nbuf = w.nbuf;
   gp.swiglu_limit = d->swiglu_limit;
   gp.err = err;
 
   // gate/up
-  int st = make_weight_map(&tw, bank->gu_tiled, w.n_bank, 2 * I, H);
+  int st = make_weight_map(&tw, bank->gu_tiled, w.n_bank, 2 * I, H, 2);
   if (st) return st;
-  st = make_act_map(&tx, xq, w.planes * w.R_pad, H);
+  st = make_act_map(&tx, xq, w.R_pad, w.planes, H, w.tt, 1);
   if (st) return st;
   gp.mode = 0;
-  gp.chains = w.chains_gu;
+  gp.ks = 1;
+  gp.parities = w.parities;
   gp.K = H;
   gp.n_blocks = I / 128;
   gp.x_sft = ws + w.x_sft;
@@ -247,12 +245,14 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
 
   // down
-  st = make_weight_map(&tw, bank->dn_tiled, w.n_bank, H, I);
+  const int ks_dn = ((I / 128) % 2 == 0) ? 2 : 1;
+  st = make_weight_map(&tw, bank->dn_tiled, w.n_bank, H, I, ks_dn);
   if (st) return st;
-  st = make_act_map(&tx, gp.zq, w.planes * w.R_pad, I);
+  st = make_act_map(&tx, gp.zq, w.R_pad, w.planes, I, w.tt, ks_dn);
   if (st) return st;
   gp.mode = 1;
-  gp.chains = w.chains_dn;
+  gp.ks = ks_dn;
+  gp.parities = w.parities;
   gp.K = I;
   gp.n_blocks = H / 128;
   gp.x_sft = ws + w.z_sft;
@@ -354,20 +354,24 @@ int mosaic_pack_mxfp4(const float* w, int32_t N, int32_t K, uint8_t* packed, uin
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
-int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int32_t rows, int32_t K, uint8_t* tiled,
-                          mosaic_stream_t stream) {
+int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int32_t rows, int32_t K, int32_t halves,
+                          uint8_t* tiled, mosaic_stream_t stream) {
   if (!packed || !tiled) return MOSAIC_ERR_SHAPE;
-  if (n_mats < 1 || rows < 128 || rows % 128 || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
+  if (halves != 1 && halves != 2) return MOSAIC_ERR_SHAPE;
+  if (n_mats < 1 || rows < 128 * halves || rows % (128 * halves) || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
   if (!aligned(packed, 16) || !aligned(tiled, 16)) return MOSAIC_ERR_ALIGN;
-  cudaError_t e = launch_repack_weights(packed, n_mats, rows, K, tiled, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e =
+      launch_repack_weights(packed, n_mats, rows, K, halves, tiled, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
-int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, uint8_t* sf_chunks,
-                          mosaic_stream_t stream) {
+int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, int32_t halves,
+                          uint8_t* sf_chunks, mosaic_stream_t stream) {
   if (!scale || !sf_chunks) return MOSAIC_ERR_SHAPE;
-  if (n_mats < 1 || rows < 128 || rows % 128 || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
-  cudaError_t e = launch_prepack_scales(scale, n_mats, rows, K, sf_chunks, reinterpret_cast<cudaStream_t>(stream));
+  if (halves != 1 && halves != 2) return MOSAIC_ERR_SHAPE;
+  if (n_mats < 1 || rows < 128 * halves || rows % (128 * halves) || K < 128 || K % 128) return MOSAIC_ERR_SHAPE;
+  cudaError_t e =
+      launch_prepack_scales(scale, n_mats, rows, K, halves, sf_chunks, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 

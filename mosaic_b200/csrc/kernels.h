@@ -23,9 +23,11 @@ struct GemmParams {
   int max_tiles;
   const uint8_t* x_sft;  // activation scale chunks per token tile: [tile][K/128][512]
   int max_n;             // largest MMA N of the launch (token rows x planes), <= 128
+  int brows;             // token rows per activation box (= rows per tile)
+  int ks;                // K-tiles per pipeline stage (gate/up: 1; down: 2, or 1 when K/128 is odd)
   int nbuf;              // TMEM accumulator buffers
-  int chains;            // independent K accumulation chains per buffer (1..4)
-  const uint8_t* w_sf;   // weight scale chunks [bank][rows/128][K/128][512]
+  int parities;          // 2: stages alternate between two issuer pairs (own chains); 1: one pair
+  const uint8_t* w_sf;   // weight scale chunks [bank][row block][K/128][half][512]
   int w_rowtiles;
   const float* row_weight;  // [R] route weight of each packed row
   float swiglu_limit;
@@ -35,7 +37,7 @@ struct GemmParams {
   int out_f32;
   int* err;
 };
-size_t gemm_smem_bytes(int mode, int max_n);
+size_t gemm_smem_bytes(int mode, int planes, int brows, int ks);
 cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmParams& p, int grid,
                             cudaStream_t stream);
 
@@ -74,16 +76,19 @@ cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max
 // ---- quantisation (quant.cu)
 // x bf16 [T][H] -> packed activation rows: row_of[t][s] (s < k) and, when
 // shared_base >= 0, row shared_base + t.  hilo: hi/lo planes with per-32
-// scales; else act_quant_ref per 128.  Scales go straight into the token
-// tile's MMA scale chunks sft [tile][H/128][128 words].
+// scales; else act_quant_ref per 128.  Rows are stored K-tile-major,
+// xq[H/128][planes][R_pad][128 B]; scales go straight into the token tile's
+// MMA scale chunks sft [tile][H/128][128 words].
 cudaError_t launch_rows_quant(const void* x, int T, int H, int k, const int* row_of, int shared_base, int hilo,
                               int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
                               cudaStream_t stream);
 cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
 cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
-cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, int K, uint8_t* tiled,
+// halves = 2 interleaves the two row halves of each matrix (gate rows, up rows)
+// per (row block, K-tile): tile order [mat][row block][K-tile][half].
+cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, int K, int halves, uint8_t* tiled,
                                   cudaStream_t stream);
-cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, uint8_t* chunks,
+cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, int halves, uint8_t* chunks,
                                   cudaStream_t stream);
 
 // ---- combine (combine.cu)

@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __
     for (int s = 0; s < nrows; ++s) {
       const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
       if (r < 0) continue;
-      *reinterpret_cast<uint2*>(xq + static_cast<size_t>(r) * H + k0) = pq;
+      *reinterpret_cast<uint2*>(xq + (static_cast<size_t>(kt) * R_pad + r) * 128 + (k0 & 127)) = pq;
       if ((lane & 15) == 0) {
         const int n = row_pos[r] & 0xFF;
         sft[(static_cast<size_t>(row_tile[r]) * KT + kt) * 128 + (n & 31) * 4 + (n >> 5)] = word;
@@ -136,8 +136,8 @@ __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __
     for (int s = 0; s < nrows; ++s) {
       const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
       if (r < 0) continue;
-      *reinterpret_cast<uint2*>(xq + static_cast<size_t>(r) * H + k0) = ph;
-      *reinterpret_cast<uint2*>(xq + (static_cast<size_t>(R_pad) + r) * H + k0) = pl;
+      *reinterpret_cast<uint2*>(xq + ((static_cast<size_t>(kt) * 2 + 0) * R_pad + r) * 128 + (k0 & 127)) = ph;
+      *reinterpret_cast<uint2*>(xq + ((static_cast<size_t>(kt) * 2 + 1) * R_pad + r) * 128 + (k0 & 127)) = pl;
       if ((lane & 15) == 0) {
         const int pos = row_pos[r];
         const int n = pos & 0xFF, rp = pos >> 8, n2 = rp + n;
@@ -228,53 +228,62 @@ __global__ void pack_mxfp4_kernel(const float* __restrict__ w, int N, int K, uin
   scale[blk] = static_cast<uint8_t>(sb);
 }
 
-// One thread per output byte of the chunked scale layout.
-__global__ void prepack_scales_kernel(const uint8_t* __restrict__ in, int n_mats, int rows, int K,
+// One thread per output byte of the chunked scale layout
+// [n][row block][K-tile][half][512]; chunk byte (r%32)*16 + ((r%128)/32)*4 + kb
+// holds row r (of the 128-row block), K32 block kb.
+__global__ void prepack_scales_kernel(const uint8_t* __restrict__ in, int n_mats, int rows, int K, int halves,
                                       uint8_t* __restrict__ out) {
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int RT = rows / 128, KT = K / 128, KB = K / 32;
-  const size_t total = static_cast<size_t>(n_mats) * RT * KT * 512;
+  const int NB = rows / 128 / halves, KT = K / 128, KB = K / 32;
+  const size_t total = static_cast<size_t>(n_mats) * (rows / 128) * KT * 512;
   if (i >= total) return;
   const int b = static_cast<int>(i % 512);
   size_t c = i / 512;
+  const int h = static_cast<int>(c % halves);
+  c /= halves;
   const int kt = static_cast<int>(c % KT);
   c /= KT;
-  const int rt = static_cast<int>(c % RT);
-  const int m = static_cast<int>(c / RT);
+  const int nb = static_cast<int>(c % NB);
+  const int m = static_cast<int>(c / NB);
   const int r_local = (b >> 4) + 32 * ((b & 15) >> 2);
   const int kb = b & 3;
-  out[i] = in[(static_cast<size_t>(m) * rows + rt * 128 + r_local) * KB + kt * 4 + kb];
+  const int row = h * (rows / halves) + nb * 128 + r_local;
+  out[i] = in[(static_cast<size_t>(m) * rows + row) * KB + kt * 4 + kb];
 }
 
-// Weight re-layout: packed codes [n][rows][K/2] -> [n][rows/128][K/128][128][64 B],
-// so every 128-row x 128-value MMA tile is one contiguous 8 KB block.
-// One thread per 16-byte piece.
-__global__ void repack_weights_kernel(const uint4* __restrict__ in, int n_mats, int rows, int K,
+// Weight re-layout: packed codes [n][rows][K/2] -> 8 KB tiles of 128 rows x 128
+// values, [n][row block][K-tile][half][128][64 B], where with halves = 2 the
+// matrix rows split into two halves (gate rows, up rows) whose tiles of the
+// same row block and K-tile sit next to each other.  One thread per 16 bytes.
+__global__ void repack_weights_kernel(const uint4* __restrict__ in, int n_mats, int rows, int K, int halves,
                                       uint4* __restrict__ out) {
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int RT = rows / 128, KT = K / 128;
+  const int NB = rows / 128 / halves, KT = K / 128;
   const size_t total = static_cast<size_t>(n_mats) * rows * (K / 32);  // 16-byte pieces
   if (i >= total) return;
   const int c = static_cast<int>(i & 3);             // piece in the 64-byte row segment
   size_t rest = i >> 2;
   const int r = static_cast<int>(rest % 128);
   rest /= 128;
+  const int h = static_cast<int>(rest % halves);
+  rest /= halves;
   const int kt = static_cast<int>(rest % KT);
   rest /= KT;
-  const int rt = static_cast<int>(rest % RT);
-  const int m = static_cast<int>(rest / RT);
-  const size_t src = ((static_cast<size_t>(m) * rows + rt * 128 + r) * (K / 2) + kt * 64 + c * 16) / 16;
+  const int nb = static_cast<int>(rest % NB);
+  const int m = static_cast<int>(rest / NB);
+  const int row = h * (rows / halves) + nb * 128 + r;
+  const size_t src = ((static_cast<size_t>(m) * rows + row) * (K / 2) + kt * 64 + c * 16) / 16;
   out[i] = in[src];
 }
 
 }  // namespace
 
-cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, int K, uint8_t* tiled,
+cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, int K, int halves, uint8_t* tiled,
                                   cudaStream_t stream) {
   const size_t total = static_cast<size_t>(n_mats) * rows * (K / 32);
   const int threads = 256;
   const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
-  repack_weights_kernel<<<grid, threads, 0, stream>>>(reinterpret_cast<const uint4*>(packed), n_mats, rows, K,
+  repack_weights_kernel<<<grid, threads, 0, stream>>>(reinterpret_cast<const uint4*>(packed), n_mats, rows, K, halves,
                                                       reinterpret_cast<uint4*>(tiled));
   return cudaGetLastError();
 }
@@ -302,12 +311,12 @@ cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uin
   return cudaGetLastError();
 }
 
-cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, uint8_t* chunks,
+cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, int halves, uint8_t* chunks,
                                   cudaStream_t stream) {
   const size_t total = static_cast<size_t>(n_mats) * (rows / 128) * (K / 128) * 512;
   const int threads = 256;
   const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
-  prepack_scales_kernel<<<grid, threads, 0, stream>>>(scale, n_mats, rows, K, chunks);
+  prepack_scales_kernel<<<grid, threads, 0, stream>>>(scale, n_mats, rows, K, halves, chunks);
   return cudaGetLastError();
 }
 

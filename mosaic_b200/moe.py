@@ -118,10 +118,10 @@ class ExpertBank:
         if self.dn_scale.shape != (n, self.hidden, self.inter // 32):
             raise ValueError("scale_down must be [E, H, I/32]")
         self.has_shared = bool(has_shared)
-        self.gu_sf = ops.prepack_scales(self.gu_scale)
-        self.dn_sf = ops.prepack_scales(self.dn_scale)
-        self.gu_tiled = ops.repack_weights(self.gu_packed)
-        self.dn_tiled = ops.repack_weights(self.dn_packed)
+        self.gu_sf = ops.prepack_scales(self.gu_scale, halves=2)
+        self.dn_sf = ops.prepack_scales(self.dn_scale, halves=1)
+        self.gu_tiled = ops.repack_weights(self.gu_packed, halves=2)
+        self.dn_tiled = ops.repack_weights(self.dn_packed, halves=1)
         if not keep_packed:
             self.gu_packed = self.dn_packed = None
 

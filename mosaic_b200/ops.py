@@ -131,33 +131,37 @@ def pack_mxfp4_nk(w: torch.Tensor):
     return packed, scale
 
 
-def prepack_scales(scale: torch.Tensor) -> torch.Tensor:
-    """E8M0 [n_mats, rows, K/32] -> MMA scale chunks [n_mats, rows/128, K/128, 512] (uint8)."""
+def prepack_scales(scale: torch.Tensor, halves: int = 1) -> torch.Tensor:
+    """E8M0 [n_mats, rows, K/32] -> MMA scale chunks [n_mats, rows/128/halves, K/128, halves, 512] (uint8).
+
+    halves=2 interleaves the two row halves (gate rows, up rows) per K-tile."""
     scale = _u8(scale).contiguous()
     if scale.dim() == 2:
         scale = scale.unsqueeze(0)
     _need_cuda(scale, what="prepack_scales")
     n, rows, kb = scale.shape
-    if rows % 128 or (kb * 32) % 128:
-        raise ValueError("prepack_scales needs rows % 128 == 0 and K % 128 == 0")
-    out = torch.empty(n, rows // 128, kb // 4, 512, dtype=torch.uint8, device=scale.device)
-    C.check(C.lib().mosaic_prepack_scales(_ptr(scale), n, rows, kb * 32, _ptr(out), _stream()),
+    if rows % (128 * halves) or (kb * 32) % 128:
+        raise ValueError("prepack_scales needs rows % (128 * halves) == 0 and K % 128 == 0")
+    out = torch.empty(n, rows // 128 // halves, kb // 4, halves, 512, dtype=torch.uint8, device=scale.device)
+    C.check(C.lib().mosaic_prepack_scales(_ptr(scale), n, rows, kb * 32, halves, _ptr(out), _stream()),
             "mosaic_prepack_scales")
     return out
 
 
-def repack_weights(packed: torch.Tensor) -> torch.Tensor:
-    """Packed E2M1 codes [n_mats, rows, K/2] -> contiguous 8 KB MMA tiles [n_mats, rows/128, K/128, 128, 64]."""
+def repack_weights(packed: torch.Tensor, halves: int = 1) -> torch.Tensor:
+    """Packed E2M1 codes [n_mats, rows, K/2] -> contiguous 8 KB MMA tiles
+    [n_mats, rows/128/halves, K/128, halves, 128, 64] (halves=2: gate/up interleave)."""
     packed = _u8(packed).contiguous()
     if packed.dim() == 2:
         packed = packed.unsqueeze(0)
     _need_cuda(packed, what="repack_weights")
     n, rows, half_k = packed.shape
     k = half_k * 2
-    if rows % 128 or k % 128:
-        raise ValueError("repack_weights needs rows % 128 == 0 and K % 128 == 0")
-    out = torch.empty(n, rows // 128, k // 128, 128, 64, dtype=torch.uint8, device=packed.device)
-    C.check(C.lib().mosaic_repack_weights(_ptr(packed), n, rows, k, _ptr(out), _stream()), "mosaic_repack_weights")
+    if rows % (128 * halves) or k % 128:
+        raise ValueError("repack_weights needs rows % (128 * halves) == 0 and K % 128 == 0")
+    out = torch.empty(n, rows // 128 // halves, k // 128, halves, 128, 64, dtype=torch.uint8, device=packed.device)
+    C.check(C.lib().mosaic_repack_weights(_ptr(packed), n, rows, k, halves, _ptr(out), _stream()),
+            "mosaic_repack_weights")
     return out
 
 

@@ -97,25 +97,31 @@ def test_act_quant_random(ops, m, k):
     assert np.array_equal(s.cpu().numpy(), sr)
 
 
-def test_prepack_scales_layout(ops):
+@pytest.mark.parametrize("halves", [1, 2])
+def test_prepack_scales_layout(ops, halves):
     g = torch.Generator().manual_seed(3)
-    sc = torch.randint(0, 255, (3, 256, 16), generator=g, dtype=torch.uint8)
-    out = ops.prepack_scales(sc.cuda()).cpu().numpy()
-    ref = np.empty((3, 2, 4, 512), dtype=np.uint8)
+    sc = torch.randint(0, 255, (3, 512, 16), generator=g, dtype=torch.uint8)
+    out = ops.prepack_scales(sc.cuda(), halves=halves).cpu().numpy()
+    nb = 512 // 128 // halves
+    ref = np.empty((3, nb, 4, halves, 512), dtype=np.uint8)
     a = sc.numpy()
     for b in range(512):
         r_local = (b >> 4) + 32 * ((b & 15) >> 2)
         kb = b & 3
-        for rt in range(2):
-            for kt in range(4):
-                ref[:, rt, kt, b] = a[:, rt * 128 + r_local, kt * 4 + kb]
+        for h in range(halves):
+            for n in range(nb):
+                for kt in range(4):
+                    ref[:, n, kt, h, b] = a[:, h * (512 // halves) + n * 128 + r_local, kt * 4 + kb]
     assert np.array_equal(out, ref)
 
 
-def test_repack_weights_layout(ops):
+@pytest.mark.parametrize("halves", [1, 2])
+def test_repack_weights_layout(ops, halves):
     g = torch.Generator().manual_seed(4)
-    p = torch.randint(0, 256, (2, 256, 192), generator=g, dtype=torch.uint8)  # rows 256, K 384
-    out = ops.repack_weights(p.cuda()).cpu().numpy()
+    p = torch.randint(0, 256, (2, 512, 192), generator=g, dtype=torch.uint8)  # rows 512, K 384
+    out = ops.repack_weights(p.cuda(), halves=halves).cpu().numpy()
     a = p.numpy()
-    ref = a.reshape(2, 2, 128, 3, 64).transpose(0, 1, 3, 2, 4)
+    nb = 512 // 128 // halves
+    # rows = (half, row block, r); columns = (K-tile, 64 bytes)
+    ref = a.reshape(2, halves, nb, 128, 3, 64).transpose(0, 2, 4, 1, 3, 5)
     assert np.array_equal(out, ref)
