@@ -115,6 +115,32 @@ MOSAIC_API int mosaic_router(const void* x, const float* weight, const float* bi
                   float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
                   mosaic_stream_t stream);
 
+/* Size of the fixed device scratch of mosaic_router_noalloc (16 MiB). */
+#define MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* mosaic_router without a caller workspace; it has no counterpart in the
+ * reference (whose Router.forward allocates through torch).  The split-K
+ * logit partials live in a file-scope device array of
+ * MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES, so the call allocates and frees no
+ * device memory (no cudaMalloc/cudaFree, no torch allocator); results are
+ * bit-identical to mosaic_router on the same inputs.  Inputs whose partials
+ * need more than the scratch (mosaic_router_workspace_bytes(T, H, E) >
+ * MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES, e.g. T = 16384, E = 256) return
+ * MOSAIC_ERR_WORKSPACE without launching.
+ * - One scratch per device: calls that overlap on a device (two streams, two
+ *   host threads, or two launches in one graph that may run concurrently)
+ *   race on it and give undefined results.  Serialise them.
+ * - The first call on each device looks up the scratch address
+ *   (cudaGetSymbolAddress, which may load the module); make that first call
+ *   outside any stream capture.  Later calls are capture-safe.
+ * - A non-finite score is recorded in the scratch's error word, which this
+ *   entry point does not report; use mosaic_router with mosaic_read_error
+ *   where that check is needed. */
+MOSAIC_API int mosaic_router_noalloc(const void* x, const float* weight, const float* bias, int32_t T, int32_t H,
+                                     int32_t E, int32_t top_k, int32_t n_group, int32_t topk_group,
+                                     float route_scale, int32_t norm_topk_prob, float* weights_out,
+                                     int64_t* idx_out, mosaic_stream_t stream);
+
 /* ids int64 [A] -> sorted_ids int64 [A], perm int64 [A] (stable: ascending
  * flat index inside each expert segment), offsets int32 [E+1], counts int32 [E].
  * Single-CTA histogram / prefix scan / stable scatter; A <= 1<<20. */

@@ -22,6 +22,9 @@ MOSAIC_ERR_TIMEOUT = 6
 MOSAIC_ERR_UNSUPPORTED = 7
 MOSAIC_ERR_WORKSPACE = 8
 
+# include/mosaic_moe.h MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
+MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 16 << 20
+
 MOSAIC_ACT_BF16 = 0
 MOSAIC_ACT_FP8 = 1
 
@@ -32,6 +35,7 @@ EXPORTED = (
     "mosaic_device_sm_count",
     "mosaic_router_workspace_bytes",
     "mosaic_router",
+    "mosaic_router_noalloc",
     "mosaic_layout_assignments",
     "mosaic_emit_tiles",
     "mosaic_act_quant",
@@ -86,6 +90,7 @@ _SIGS = {
     "mosaic_device_sm_count": ([], ctypes.c_int),
     "mosaic_router_workspace_bytes": ([_I, _I, _I], _SZ),
     "mosaic_router": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P], ctypes.c_int),
+    "mosaic_router_noalloc": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P], ctypes.c_int),
     "mosaic_layout_assignments": ([_P, _I, _I, _P, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_emit_tiles": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_act_quant": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),

@@ -271,6 +271,43 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
 
 }  // namespace
 
+// Scratch of mosaic_router_noalloc: the error word at byte 0, the split-K
+// logit partials from byte 256 (the same layout as a mosaic_router workspace).
+// Zero-initialised when the module loads; shared by every call on a device.
+static __device__ __align__(256) uint8_t g_router_scratch[MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Argument checks shared by mosaic_router and mosaic_router_noalloc.
+int router_args_ok(const void* x, const float* weight, int32_t T, int32_t H, int32_t E, int32_t top_k,
+                   int32_t n_group, int32_t topk_group, const float* weights_out, const int64_t* idx_out) {
+  if (!x || !weight || !weights_out || !idx_out) return MOSAIC_ERR_SHAPE;
+  if (T < 1 || H < 32 || H % 32 || E < 1 || E > 256 || top_k < 1 || top_k > 8 || top_k > E) return MOSAIC_ERR_SHAPE;
+  if (n_group < 1 || n_group > 32 || E % n_group || topk_group < 1 || topk_group > n_group) return MOSAIC_ERR_SHAPE;
+  if (topk_group * (E / n_group) < top_k) return MOSAIC_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(weight, 16)) return MOSAIC_ERR_ALIGN;
+  return MOSAIC_OK;
+}
+
+constexpr int kMaxDevices = 64;
+
+// Device address of g_router_scratch, looked up once per device.
+int router_scratch(int dev, uint8_t** out) {
+  static std::mutex mu;
+  static uint8_t* addr[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return MOSAIC_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_router_scratch) != cudaSuccess || !p) return MOSAIC_ERR_CUDA;
+    addr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = addr[dev];
+  return MOSAIC_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int mosaic_version(void) { return kVersion; }
@@ -303,16 +340,37 @@ int mosaic_router(const void* x, const float* weight, const float* bias, int32_t
                   int32_t top_k, int32_t n_group, int32_t topk_group, float route_scale, int32_t norm_topk_prob,
                   float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
                   mosaic_stream_t stream) {
-  if (!x || !weight || !weights_out || !idx_out || !workspace) return MOSAIC_ERR_SHAPE;
-  if (T < 1 || H < 32 || H % 32 || E < 1 || E > 256 || top_k < 1 || top_k > 8 || top_k > E) return MOSAIC_ERR_SHAPE;
-  if (n_group < 1 || n_group > 32 || E % n_group || topk_group < 1 || topk_group > n_group) return MOSAIC_ERR_SHAPE;
-  if (topk_group * (E / n_group) < top_k) return MOSAIC_ERR_SHAPE;
-  if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  if (!workspace) return MOSAIC_ERR_SHAPE;
+  const int st = router_args_ok(x, weight, T, H, E, top_k, n_group, topk_group, weights_out, idx_out);
+  if (st != MOSAIC_OK) return st;
+  if (!aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
   if (workspace_bytes < mosaic_router_workspace_bytes(T, H, E)) return MOSAIC_ERR_WORKSPACE;
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   const int splits = router_splits(T, H, E, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
+                                weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
+                                reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_router_noalloc(const void* x, const float* weight, const float* bias, int32_t T, int32_t H, int32_t E,
+                          int32_t top_k, int32_t n_group, int32_t topk_group, float route_scale,
+                          int32_t norm_topk_prob, float* weights_out, int64_t* idx_out, mosaic_stream_t stream) {
+  const int st = router_args_ok(x, weight, T, H, E, top_k, n_group, topk_group, weights_out, idx_out);
+  if (st != MOSAIC_OK) return st;
+  // Same split count (hence bit-identical results) as mosaic_router; inputs whose
+  // partials do not fit the fixed scratch are rejected, never truncated.
+  if (mosaic_router_workspace_bytes(T, H, E) > MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES) return MOSAIC_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  uint8_t* ws = nullptr;
+  const int sst = router_scratch(dev, &ws);
+  if (sst != MOSAIC_OK) return sst;
+  const int splits = router_splits(T, H, E, sms);
   cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
                                 weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
                                 reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream));

@@ -64,6 +64,35 @@ def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, *, 
     return w, idx
 
 
+def router_noalloc(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, weights_out: torch.Tensor,
+                   idx_out: torch.Tensor, *, top_k: int, n_group: int = 1, topk_group: int = 1,
+                   route_scale: float = 1.0, norm_topk_prob: bool = True) -> None:
+    """:func:`router` into caller-owned outputs through ``mosaic_router_noalloc``.
+
+    Neither this wrapper nor the library allocates device memory: inputs must
+    already be contiguous CUDA tensors of the right dtypes (no conversion), the
+    split-K scratch is the library's fixed per-device array, and calls that
+    overlap on one device race on it.  No counterpart in the reference.
+    """
+    _need_cuda(x, weight, bias, weights_out, idx_out, what="router_noalloc")
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise ValueError("router_noalloc expects bf16 x [T, H]")
+    if weight.dtype != torch.float32 or bias is not None and bias.dtype != torch.float32:
+        raise ValueError("router_noalloc expects fp32 weight [E, H] and bias [E]")
+    t, h = x.shape
+    e = weight.shape[0]
+    if weight.shape != (e, h) or (bias is not None and bias.shape != (e,)):
+        raise ValueError("router weight/bias shape mismatch")
+    if weights_out.dtype != torch.float32 or weights_out.shape != (t, top_k):
+        raise ValueError("weights_out must be fp32 [T, top_k]")
+    if idx_out.dtype != torch.int64 or idx_out.shape != (t, top_k):
+        raise ValueError("idx_out must be int64 [T, top_k]")
+    st = C.lib().mosaic_router_noalloc(_ptr(x), _ptr(weight), _ptr(bias), t, h, e, top_k, n_group, topk_group,
+                                       float(route_scale), int(bool(norm_topk_prob)), _ptr(weights_out),
+                                       _ptr(idx_out), _stream())
+    C.check(st, "mosaic_router_noalloc")
+
+
 def layout_assignments(expert_ids: torch.Tensor, n_experts: int):
     """ids [A] -> (sorted_ids int64 [A], perm int64 [A], offsets int32 [E+1], counts int32 [E]).
 

@@ -127,3 +127,23 @@ def test_ops_reject_cpu_tensors():
         ops.layout_assignments(torch.tensor([0, 1, 2]), 4)
     with pytest.raises(ValueError):
         ops.act_quant(torch.zeros(2, 100))
+
+
+def test_router_noalloc_constant_matches_header():
+    m = re.search(r"#define MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES \((\d+)u << (\d+)\)", HEADER.read_text())
+    assert m and int(m.group(1)) << int(m.group(2)) == C.MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
+
+
+def test_router_noalloc_validation_before_launch():
+    """Bad shapes, misalignment and inputs larger than the fixed scratch are
+    rejected on the host, before any device call."""
+    lib = C.lib()
+    fake = 1 << 20
+    st = lib.mosaic_router_noalloc(fake, fake, None, 4, 512, 32, 9, 1, 1, 1.0, 1, fake, fake, None)
+    assert st == C.MOSAIC_ERR_SHAPE
+    st = lib.mosaic_router_noalloc(fake + 4, fake, None, 4, 512, 32, 4, 1, 1, 1.0, 1, fake, fake, None)
+    assert st == C.MOSAIC_ERR_ALIGN
+    # T = 16384 tokens over 256 experts needs 16 MiB of partials + the error word
+    assert lib.mosaic_router_workspace_bytes(16384, 7168, 256) > C.MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
+    st = lib.mosaic_router_noalloc(fake, fake, None, 16384, 7168, 256, 8, 8, 4, 2.5, 1, fake, fake, None)
+    assert st == C.MOSAIC_ERR_WORKSPACE
