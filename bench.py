@@ -35,6 +35,11 @@ EXPERT_BYTES = 23_396_352          # MXFP4 codes + E8M0 scales of one V3 expert 
 GU_BYTES = 2 * 2048 * 3584 + 2 * 2048 * 224
 DN_BYTES = 7168 * 1024 + 7168 * 64
 ROUTER_BYTES = 256 * 7168 * 4
+# DRAM traffic / algorithmic bytes of the gate/up launch: dram__bytes_read.sum +
+# dram__bytes_write.sum of one ncu capture of `bench.py --experts 64 --profile-small`
+# (65 experts streamed).  Traffic grows with the number of experts streamed, so the
+# full launch's traffic is this ratio times its algorithmic bytes.
+GU_TRAFFIC_RATIO = 1.0719e9 / 1_013_841_920
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; % of HBM / FP4 tensor roofline"
 
 
@@ -48,6 +53,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true", help="skip the T sweep and the prefill line")
     p.add_argument("--experts", type=int, default=256, help="routed experts in the bank (V3: 256)")
+    p.add_argument("--act", choices=["bf16", "fp8"], default="bf16",
+                   help="activation mode of the main layer (bf16: decode configs; fp8: prefill configs)")
     p.add_argument("--profile-small", action="store_true",
                    help="small case for ncu captures: no extras, no CPU baseline, 2 profiled stage runs")
     return p.parse_args()
@@ -312,7 +319,7 @@ def main():
     hbm, bf16_tf, peak_src = peaks()
     n_exp = args.experts
     t = args.tokens
-    layer, x = synthetic.make_layer(tokens=t, seed=1234 + rank, act_mode="bf16", n_experts=n_exp)
+    layer, x = synthetic.make_layer(tokens=t, seed=1234 + rank, act_mode=args.act, n_experts=n_exp)
 
     g, sx, sy = capture(layer, x)
     steps, warmup = args.steps, max(args.warmup, 3)
@@ -332,8 +339,11 @@ def main():
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "mxfp4*bf16 (bf16 as hi+lo e4m3, fp32 accumulate)", "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)",
-        "config": {"workload": "V3 MoE layer decode (BASELINE config 2), T=128", "tokens_per_gpu": t, "hidden": 7168,
+        "dtype": ("mxfp4*bf16 (bf16 as hi+lo e4m3, fp32 accumulate)" if args.act == "bf16"
+                  else "mxfp4*fp8 (e4m3, per-128 pow2 scales, fp32 accumulate)"), "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)",
+        "config": {"workload": (f"V3 MoE layer decode (BASELINE config 2), T={t}" if args.act == "bf16"
+                                else f"V3 MoE layer, FP8 activations, T={t}, uniform routing"),
+                   "tokens_per_gpu": t, "hidden": 7168,
                    "inter": 2048, "experts": n_exp, "shared": 1, "top_k": 8, "groups": "8/4",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "no flush: ~5.9 GB of touched expert weights per step >> 126 MB L2",
@@ -341,7 +351,8 @@ def main():
         "clocks": clocks,
         "gpu_launches": 7 * steps,
         "roofline": {"kernel": "moe_gemm_kernel (gate/up, tcgen05 mxf8f6f4)", "bound": "hbm",
-                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": GU_TRAFFIC_RATIO * gu_bytes,
+                     "traffic_source": "ncu dram bytes of a 65-expert launch scaled by experts streamed",
                      "algorithmic_bytes": gu_bytes, "peak_source": peak_src,
                      "note": "algorithmic bytes = (distinct experts + shared) x gate/up MXFP4 codes + scales"},
         "layer_roofline": {"bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms * 1e-3) / 1e9,
