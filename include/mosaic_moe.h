@@ -206,6 +206,58 @@ MOSAIC_API int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, con
                       const float* expert_weights, const mosaic_expert_bank* bank, void* y, void* workspace,
                       size_t workspace_bytes, mosaic_stream_t stream);
 
+/* ---- Expert parallelism -------------------------------------------------
+ * Rank d of `world` owns the contiguous experts [d*E/world, (d+1)*E/world)
+ * (.mosaicvm/source/inference_model.py:620-627) plus a replica of the shared
+ * expert.  One layer step on a rank:
+ *   mosaic_router -> mosaic_ep_dispatch -> exchange send rows (all-to-all,
+ *   split by dest_counts) -> mosaic_moe_expert_rows on the received rows ->
+ *   return the partials (reverse all-to-all) -> mosaic_moe_expert_rows for the
+ *   shared expert on the local tokens -> mosaic_ep_combine.
+ * The exchange is the caller's (NCCL all_to_all in mosaic_b200/ep.py).
+ * Because send rows are sorted by expert id and come back in the order they
+ * were sent, the combine sums each token's partials in ascending expert id,
+ * exactly as mosaic_moe_forward does: the layer output is bit-identical to
+ * the single-GPU layer on the same tokens.
+ *
+ * Send row (MOSAIC_EP_ROW_BYTES(H) bytes, 16-B aligned): H bf16 token values,
+ * then int32 {local expert id, route weight (fp32 bits), source token, dest}. */
+#define MOSAIC_EP_ROW_BYTES(H) ((size_t)(H) * 2u + 16u)
+
+/* Layout + gather of one rank's assignments.  dims: the layer (tokens = this
+ * rank's T, n_experts = global E, E % world == 0).  idx int64 [T, top_k],
+ * weights fp32 [T, top_k] (NULL = 1.0); send_rows [T*top_k] rows in expert
+ * order (rank-major); dest_counts int32 [world] = rows for each rank.
+ * workspace: mosaic_moe_workspace_bytes(dims); keep it for mosaic_ep_combine.
+ * Replaces the dispatch half of MoE.forward (inference_model.py:634-650). */
+MOSAIC_API int mosaic_ep_dispatch(const mosaic_moe_dims* dims, int32_t world, const void* x, const int64_t* idx,
+                                  const float* weights, void* send_rows, int32_t* dest_counts, void* workspace,
+                                  size_t workspace_bytes, mosaic_stream_t stream);
+
+/* Per-row expert pass: row r of x_rows (bf16, row stride ldx elements, first
+ * H used) goes through expert ids[r * meta_stride] of the bank with route
+ * weight weights[r * meta_stride] (weight before down, as in the layer);
+ * ids NULL = every row uses default_id, weights NULL = 1.0.  dims: n_experts =
+ * routed experts in this bank (<= 256), has_shared = 1 when the bank's last
+ * expert (id n_experts) is the shared one; tokens, top_k and the router
+ * fields are ignored.  partials [rows, H] in input row order: fp32 in
+ * MOSAIC_ACT_BF16 mode, bf16 in MOSAIC_ACT_FP8 mode (what the layer's combine
+ * consumes).  rows == 0 is a no-op.  Ids out of range are recorded as
+ * MOSAIC_ERR_RANGE in the workspace error word. */
+MOSAIC_API size_t mosaic_moe_expert_rows_workspace_bytes(const mosaic_moe_dims* dims, int32_t max_rows);
+MOSAIC_API int mosaic_moe_expert_rows(const mosaic_moe_dims* dims, int32_t rows, const void* x_rows, int32_t ldx,
+                                      const int32_t* ids, const float* weights, int32_t meta_stride,
+                                      int32_t default_id, const mosaic_expert_bank* bank, void* partials,
+                                      void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
+
+/* Ordered combine of one rank's returned partials: partials [T*top_k (+ T
+ * when dims->has_shared), H] — rows [0, T*top_k) in send-row order, rows
+ * [T*top_k, T*top_k + T) the shared expert's partials of the local tokens —
+ * same dtype as mosaic_moe_expert_rows writes.  workspace / dims: those of the
+ * matching mosaic_ep_dispatch.  y bf16 [T, H]. */
+MOSAIC_API int mosaic_ep_combine(const mosaic_moe_dims* dims, const void* partials, const void* workspace, void* y,
+                                 mosaic_stream_t stream);
+
 /* Device error word of a workspace used by mosaic_moe_* (0 = none).
  * Synchronises the stream.  reset != 0 clears it afterwards. */
 MOSAIC_API int mosaic_read_error(const void* workspace, int32_t reset, int32_t* code_out, mosaic_stream_t stream);

@@ -3,8 +3,8 @@
 Router (sigmoid, group-limited top-k, selection-only bias), histogram / scan
 permutation, MXFP4 x E4M3 block-scaled tcgen05 expert GEMMs with a fused
 SwiGLU epilogue, shared expert and ordered combine, behind the reference's
-MoE module / operator API.  The CUDA library is loaded lazily; building it is
-``python -m mosaic_b200.build``.
+MoE module / operator API; expert parallelism across GPUs in ``ep``.  The
+CUDA library is loaded lazily; building it is ``python -m mosaic_b200.build``.
 """
 from .moe import (  # noqa: F401
     ExactContractError,
@@ -16,14 +16,18 @@ from .moe import (  # noqa: F401
     exact_target,
     grouped_expert_forward,
 )
+from .ep import ExpertParallelMoELayer, expert_range, shard_bank  # noqa: F401
 
 __all__ = [
     "ExactContractError",
     "ExpertBank",
+    "ExpertParallelMoELayer",
     "MoEConfig",
     "MoELayer",
     "Router",
     "exact_moe",
     "exact_target",
+    "expert_range",
     "grouped_expert_forward",
+    "shard_bank",
 ]

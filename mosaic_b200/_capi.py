@@ -22,6 +22,11 @@ MOSAIC_ERR_TIMEOUT = 6
 MOSAIC_ERR_UNSUPPORTED = 7
 MOSAIC_ERR_WORKSPACE = 8
 
+def ep_row_bytes(hidden: int) -> int:
+    """include/mosaic_moe.h MOSAIC_EP_ROW_BYTES: H bf16 values + a 16-byte tail."""
+    return 2 * hidden + 16
+
+
 # include/mosaic_moe.h MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
 MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -46,6 +51,10 @@ EXPORTED = (
     "mosaic_moe_forward",
     "mosaic_moe_forward_profiled",
     "mosaic_moe_routed",
+    "mosaic_ep_dispatch",
+    "mosaic_moe_expert_rows_workspace_bytes",
+    "mosaic_moe_expert_rows",
+    "mosaic_ep_combine",
     "mosaic_read_error",
 )
 
@@ -104,6 +113,11 @@ _SIGS = {
                                      _SZ, _P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "mosaic_moe_routed": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _SZ, _P],
                           ctypes.c_int),
+    "mosaic_ep_dispatch": ([ctypes.POINTER(MoEDims), _I, _P, _P, _P, _P, _P, _P, _SZ, _P], ctypes.c_int),
+    "mosaic_moe_expert_rows_workspace_bytes": ([ctypes.POINTER(MoEDims), _I], _SZ),
+    "mosaic_moe_expert_rows": ([ctypes.POINTER(MoEDims), _I, _P, _I, _P, _P, _I, _I, ctypes.POINTER(ExpertBankC), _P,
+                                _P, _SZ, _P], ctypes.c_int),
+    "mosaic_ep_combine": ([ctypes.POINTER(MoEDims), _P, _P, _P, _P], ctypes.c_int),
     "mosaic_read_error": ([_P, _I, ctypes.POINTER(ctypes.c_int32), _P], ctypes.c_int),
 }
 

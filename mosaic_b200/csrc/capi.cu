@@ -87,7 +87,7 @@ struct WsPlan {
   int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32, max_n, nbuf, parities;
   size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, row_tile, row_pos, tiles,
       n_tiles;
-  size_t xq, x_sft, zq, z_sft, partial, total;
+  size_t xq, x_sft, zq, z_sft, partial, row_idx, row_w, total;
 };
 
 int check_dims(const mosaic_moe_dims* d) {
@@ -104,7 +104,10 @@ int check_dims(const mosaic_moe_dims* d) {
   return MOSAIC_OK;
 }
 
-WsPlan plan_ws(const mosaic_moe_dims* d) {
+// rows_mode: the per-row expert pass (mosaic_moe_expert_rows) — no router
+// partials and no partial buffer (the caller owns the output), plus the
+// per-row expert ids / weights it unpacks.
+WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   WsPlan w{};
   const int T = d->tokens, H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
@@ -132,7 +135,7 @@ WsPlan plan_ws(const mosaic_moe_dims* d) {
     return at;
   };
   w.err = take(16);
-  w.router_part = take(sizeof(float) * static_cast<size_t>(w.splits) * T * E);
+  w.router_part = take(rows_mode ? 0 : sizeof(float) * static_cast<size_t>(w.splits) * T * E);
   w.counts = take(sizeof(int) * (E + 1));
   w.offsets = take(sizeof(int) * (E + 2));
   w.row_of = take(sizeof(int) * static_cast<size_t>(T) * k);
@@ -147,7 +150,9 @@ WsPlan plan_ws(const mosaic_moe_dims* d) {
   w.x_sft = take(static_cast<size_t>(w.max_tiles) * (H / 128) * 512);
   w.zq = take(static_cast<size_t>(w.planes) * w.R_pad * I);
   w.z_sft = take(static_cast<size_t>(w.max_tiles) * (I / 128) * 512);
-  w.partial = take(static_cast<size_t>(w.R) * H * (w.partial_f32 ? 4 : 2));
+  w.partial = take(rows_mode ? 0 : static_cast<size_t>(w.R) * H * (w.partial_f32 ? 4 : 2));
+  w.row_idx = take(rows_mode ? sizeof(int64_t) * static_cast<size_t>(T) : 0);
+  w.row_w = take(rows_mode ? sizeof(float) * static_cast<size_t>(T) : 0);
   w.total = o;
   return w;
 }
@@ -167,21 +172,7 @@ inline bool rec(void* const* ev, int i, cudaStream_t s) {
   return !ev || !ev[i] || cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s) == cudaSuccess;
 }
 
-int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const void* x, const int64_t* idx,
-                const float* weights, const mosaic_expert_bank* bank, void* y, cudaStream_t stream,
-                void* const* ev = nullptr) {
-  const int T = d->tokens, H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
-  const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
-  int* err = reinterpret_cast<int*>(ws + w.err);
-  const int shared_base = d->has_shared ? T * k : -1;
-
-  LayoutParams lp{};
-  lp.idx = idx;
-  lp.weights = weights;
-  lp.T = T;
-  lp.k = k;
-  lp.E = E;
-  lp.with_shared = d->has_shared ? 1 : 0;
+void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
   lp.tt_routed = w.tt;
   lp.tt_shared = w.tt;
   lp.max_tiles = w.max_tiles;
@@ -195,16 +186,17 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   lp.row_pos = reinterpret_cast<int*>(ws + w.row_pos);
   lp.tiles = reinterpret_cast<int*>(ws + w.tiles);
   lp.n_tiles = reinterpret_cast<int*>(ws + w.n_tiles);
-  lp.err = err;
-  if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
-  if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
+  lp.err = reinterpret_cast<int*>(ws + w.err);
+}
 
-  uint8_t* xq = ws + w.xq;
-  if (launch_rows_quant(x, T, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos, xq,
-                        reinterpret_cast<uint32_t*>(ws + w.x_sft), stream) != cudaSuccess)
-    return MOSAIC_ERR_CUDA;
-  if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
-
+// Gate/up (+ SwiGLU, route weight, re-quantisation) then down over the packed
+// rows the layout and rows_quant left in the workspace.  Down partials go to
+// partial_out, row r at out_row[r] (out_row null: row r).
+int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const LayoutParams& lp,
+              const mosaic_expert_bank* bank, int shared_expert, const int* out_row, void* partial_out,
+              cudaStream_t stream, void* const* ev) {
+  const int H = d->hidden, I = d->inter;
+  const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   CUtensorMap tw, tx;
@@ -215,7 +207,7 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   gp.H = H;
   gp.R = w.R;
   gp.R_pad = w.R_pad;
-  gp.shared_expert = d->has_shared ? E : -1;
+  gp.shared_expert = shared_expert;
   gp.tiles = lp.tiles;
   gp.n_tiles = lp.n_tiles;
   gp.max_tiles = w.max_tiles;
@@ -224,12 +216,12 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   gp.brows = w.tt;
   gp.nbuf = w.nbuf;
   gp.swiglu_limit = d->swiglu_limit;
-  gp.err = err;
+  gp.err = lp.err;
 
   // gate/up
   int st = make_weight_map(&tw, bank->gu_tiled, w.n_bank, 2 * I, H, 2);
   if (st) return st;
-  st = make_act_map(&tx, xq, w.R_pad, w.planes, H, w.tt, 1);
+  st = make_act_map(&tx, ws + w.xq, w.R_pad, w.planes, H, w.tt, 1);
   if (st) return st;
   gp.mode = 0;
   gp.ks = 1;
@@ -258,15 +250,67 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   gp.x_sft = ws + w.z_sft;
   gp.w_sf = bank->dn_sf;
   gp.w_rowtiles = H / 128;
-  gp.out = ws + w.partial;
+  gp.out = partial_out;
   gp.out_f32 = w.partial_f32;
+  gp.out_row = out_row;
   if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(ev, 5, stream)) return MOSAIC_ERR_CUDA;
+  return MOSAIC_OK;
+}
+
+int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const void* x, const int64_t* idx,
+                const float* weights, const mosaic_expert_bank* bank, void* y, cudaStream_t stream,
+                void* const* ev = nullptr) {
+  const int T = d->tokens, H = d->hidden, E = d->n_experts, k = d->top_k;
+  const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
+  const int shared_base = d->has_shared ? T * k : -1;
+
+  LayoutParams lp{};
+  lp.idx = idx;
+  lp.weights = weights;
+  lp.T = T;
+  lp.k = k;
+  lp.E = E;
+  lp.with_shared = d->has_shared ? 1 : 0;
+  fill_layout(lp, w, ws);
+  if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
+
+  if (launch_rows_quant(x, T, H, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos,
+                        ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), stream) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
+
+  const int st = run_gemms(d, w, ws, lp, bank, d->has_shared ? E : -1, nullptr, ws + w.partial, stream, ev);
+  if (st) return st;
 
   if (launch_combine(ws + w.partial, w.partial_f32, lp.row_sorted, T, k, H, shared_base, y, stream) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
   if (!rec(ev, 6, stream)) return MOSAIC_ERR_CUDA;
   return MOSAIC_OK;
+}
+
+// Dims of the per-row expert pass: every row is one assignment (k = 1) to one
+// of the bank's experts, the shared one included as an ordinary id; no router.
+// The per-row pass accepts up to 256 routed experts plus the shared one.
+int check_rows_dims(const mosaic_moe_dims* r) {
+  if (r->tokens < 1 || r->tokens > (1 << 20)) return MOSAIC_ERR_SHAPE;
+  if (r->hidden < 128 || r->hidden % 128 || r->inter < 128 || r->inter % 128) return MOSAIC_ERR_SHAPE;
+  if (r->n_experts < 1 || r->n_experts > 257) return MOSAIC_ERR_UNSUPPORTED;
+  if (r->act_mode != MOSAIC_ACT_BF16 && r->act_mode != MOSAIC_ACT_FP8) return MOSAIC_ERR_DTYPE;
+  if (!(r->swiglu_limit >= 0.f)) return MOSAIC_ERR_RANGE;
+  return MOSAIC_OK;
+}
+
+mosaic_moe_dims rows_dims(const mosaic_moe_dims* d, int rows) {
+  mosaic_moe_dims r = *d;
+  r.tokens = rows;
+  r.n_experts = d->n_experts + (d->has_shared ? 1 : 0);
+  r.top_k = 1;
+  r.n_group = 1;
+  r.topk_group = 1;
+  r.has_shared = 0;
+  return r;
 }
 
 }  // namespace
@@ -487,6 +531,109 @@ int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, const int64_t*
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   return run_experts(dims, w, ws, x, expert_ids, expert_weights, bank, y, s);
+}
+
+int mosaic_ep_dispatch(const mosaic_moe_dims* dims, int32_t world, const void* x, const int64_t* idx,
+                       const float* weights, void* send_rows, int32_t* dest_counts, void* workspace,
+                       size_t workspace_bytes, mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!x || !idx || !send_rows || !dest_counts || !workspace) return MOSAIC_ERR_SHAPE;
+  if (world < 1 || dims->n_experts % world) return MOSAIC_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(send_rows, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  const int T = dims->tokens, k = dims->top_k, E = dims->n_experts;
+  LayoutParams lp{};
+  lp.idx = idx;
+  lp.weights = weights;
+  lp.T = T;
+  lp.k = k;
+  lp.E = E;
+  lp.with_shared = 0;
+  fill_layout(lp, w, ws);
+  lp.row_tile = nullptr;  // no GEMM tiles on the sending side
+  lp.row_pos = nullptr;
+  lp.tiles = nullptr;
+  if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (launch_ep_pack(x, dims->hidden, T * k, E, E / world, world, lp.offsets, lp.row_token, lp.row_weight,
+                     send_rows, dest_counts, s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  return MOSAIC_OK;
+}
+
+size_t mosaic_moe_expert_rows_workspace_bytes(const mosaic_moe_dims* dims, int32_t max_rows) {
+  if (!dims || max_rows < 1) return 0;
+  if (dims->n_experts > 256) return 0;
+  const mosaic_moe_dims r = rows_dims(dims, max_rows);
+  if (check_rows_dims(&r) != MOSAIC_OK) return 0;
+  return plan_ws(&r, true).total;
+}
+
+int mosaic_moe_expert_rows(const mosaic_moe_dims* dims, int32_t rows, const void* x_rows, int32_t ldx,
+                           const int32_t* ids, const float* weights, int32_t meta_stride, int32_t default_id,
+                           const mosaic_expert_bank* bank, void* partials, void* workspace, size_t workspace_bytes,
+                           mosaic_stream_t stream) {
+  if (!dims) return MOSAIC_ERR_SHAPE;
+  if (rows < 0) return MOSAIC_ERR_SHAPE;
+  if (rows == 0) return MOSAIC_OK;
+  if (dims->n_experts > 256) return MOSAIC_ERR_UNSUPPORTED;
+  const mosaic_moe_dims r = rows_dims(dims, rows);
+  int st = check_rows_dims(&r);
+  if (st) return st;
+  if (!x_rows || !partials || !workspace) return MOSAIC_ERR_SHAPE;
+  if (ldx < dims->hidden || ldx % 8 || ((ids || weights) && meta_stride < 1)) return MOSAIC_ERR_SHAPE;
+  if (!ids && (default_id < 0 || default_id >= r.n_experts)) return MOSAIC_ERR_RANGE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(x_rows, 16) || !aligned(partials, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  if ((ids && !aligned(ids, 4)) || (weights && !aligned(weights, 4))) return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(&r, true);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  int64_t* idx = reinterpret_cast<int64_t*>(ws + w.row_idx);
+  float* wt = reinterpret_cast<float*>(ws + w.row_w);
+  if (launch_rows_meta(ids, weights, meta_stride, rows, r.n_experts, default_id, idx, wt,
+                       reinterpret_cast<int*>(ws + w.err), s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  LayoutParams lp{};
+  lp.idx = idx;
+  lp.weights = wt;
+  lp.T = rows;
+  lp.k = 1;
+  lp.E = r.n_experts;
+  lp.with_shared = 0;
+  fill_layout(lp, w, ws);
+  lp.row_sorted = nullptr;
+  if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  const bool hilo = r.act_mode == MOSAIC_ACT_BF16;
+  if (launch_rows_quant(x_rows, rows, r.hidden, ldx, 1, lp.row_of, -1, hilo ? 1 : 0, w.R_pad, lp.row_tile,
+                        lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  // with k = 1 the packed row of input row t is sorted row row_of[t], and
+  // row_token[sorted row] = t: partials land in input row order
+  return run_gemms(&r, w, ws, lp, bank, dims->has_shared ? dims->n_experts : -1, lp.row_token, partials, s,
+                   nullptr);
+}
+
+int mosaic_ep_combine(const mosaic_moe_dims* dims, const void* partials, const void* workspace, void* y,
+                      mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!partials || !workspace || !y) return MOSAIC_ERR_SHAPE;
+  if (!aligned(partials, 16) || !aligned(y, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  const int T = dims->tokens, k = dims->top_k;
+  if (launch_combine(partials, w.partial_f32, reinterpret_cast<const int*>(ws + w.row_sorted), T, k, dims->hidden,
+                     dims->has_shared ? T * k : -1, y, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  return MOSAIC_OK;
 }
 
 int mosaic_read_error(const void* workspace, int32_t reset, int32_t* code_out, mosaic_stream_t stream) {

@@ -424,7 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (col < m.rows) {
               float v = ds[j];
               if (round_mid) v = bf16r(v);
-              const size_t o = static_cast<size_t>(m.row0 + col) * p.H + nn;
+              const int orow = p.out_row ? p.out_row[m.row0 + col] : m.row0 + col;
+              const size_t o = static_cast<size_t>(orow) * p.H + nn;
               if (p.out_f32)
                 reinterpret_cast<float*>(p.out)[o] = v;
               else

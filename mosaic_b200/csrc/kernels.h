@@ -35,6 +35,7 @@ struct GemmParams {
   uint32_t* z_sft;    // their scale chunks per token tile [tile][I/128][128 words]
   void* out;          // down partials [R][H]
   int out_f32;
+  const int* out_row; // null: partial of packed row r goes to out row r; else to out row out_row[r]
   int* err;
 };
 size_t gemm_smem_bytes(int mode, int planes, int brows, int ks);
@@ -74,14 +75,14 @@ cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max
                               int32_t* m_start, int32_t* n_tiles, int32_t* tile_rows, cudaStream_t stream);
 
 // ---- quantisation (quant.cu)
-// x bf16 [T][H] -> packed activation rows: row_of[t][s] (s < k) and, when
-// shared_base >= 0, row shared_base + t.  hilo: hi/lo planes with per-32
-// scales; else act_quant_ref per 128.  Rows are stored K-tile-major,
-// xq[H/128][planes][R_pad][128 B]; scales go straight into the token tile's
-// MMA scale chunks sft [tile][H/128][128 words].
-cudaError_t launch_rows_quant(const void* x, int T, int H, int k, const int* row_of, int shared_base, int hilo,
-                              int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
-                              cudaStream_t stream);
+// x bf16 [T][ldx] (first H values of each row used) -> packed activation rows:
+// row_of[t][s] (s < k) and, when shared_base >= 0, row shared_base + t.
+// hilo: hi/lo planes with per-32 scales; else act_quant_ref per 128.  Rows are
+// stored K-tile-major, xq[H/128][planes][R_pad][128 B]; scales go straight into
+// the token tile's MMA scale chunks sft [tile][H/128][128 words].
+cudaError_t launch_rows_quant(const void* x, int T, int H, int ldx, int k, const int* row_of, int shared_base,
+                              int hilo, int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq,
+                              uint32_t* sft, cudaStream_t stream);
 cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
 cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
 // halves = 2 interleaves the two row halves of each matrix (gate rows, up rows)
@@ -90,6 +91,20 @@ cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, i
                                   cudaStream_t stream);
 cudaError_t launch_prepack_scales(const uint8_t* scale, int n_mats, int rows, int K, int halves, uint8_t* chunks,
                                   cudaStream_t stream);
+
+// ---- expert parallelism (ep.cu)
+// Send rows of one rank, in the layout's expert-sorted row order: row r holds
+// x[row_token[r]] (H bf16) then a 16-byte tail {local expert id, route weight
+// bits, source token, destination rank} (int32 each).  dest_counts[d] = rows
+// for rank d = experts [d*E_local, (d+1)*E_local).
+cudaError_t launch_ep_pack(const void* x, int H, int A, int E, int E_local, int world, const int* offsets,
+                           const int* row_token, const float* row_weight, void* send, int* dest_counts,
+                           cudaStream_t stream);
+// Per-row expert ids / weights with an element stride (ids null: every row
+// uses default_id; weights null: 1.0) -> int64 idx [R], fp32 w [R]; ids outside
+// [0, E) are recorded as MOSAIC_ERR_RANGE and replaced by 0 with weight 0.
+cudaError_t launch_rows_meta(const int32_t* ids, const float* weights, int stride, int R, int E, int default_id,
+                             int64_t* idx, float* w, int* err, cudaStream_t stream);
 
 // ---- combine (combine.cu)
 cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,

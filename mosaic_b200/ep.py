@@ -1,0 +1,217 @@
+"""Expert-parallel MoE layer: one process per GPU, experts sharded by rank.
+
+Rank d of W owns the contiguous routed experts [d*E/W, (d+1)*E/W) and a
+replica of the shared expert (the expert-sharded ``MoE`` of
+``.mosaicvm/source/inference_model.py:614-650``, whose cross-rank
+``all_reduce`` becomes a dispatch / combine all-to-all here).  Every rank
+routes its own tokens with the replicated router.  One layer step:
+
+1. ``mosaic_router`` on the local tokens;
+2. ``mosaic_ep_dispatch``: assignments sorted by expert id (hence grouped by
+   destination rank) and gathered into send rows (token values + local expert
+   id + route weight), with per-destination row counts;
+3. all-to-all of the counts, then of the send rows (NCCL over NVLink);
+4. the shared expert on the local tokens, overlapping the exchange;
+5. ``mosaic_moe_expert_rows`` on the received rows: one partial per row;
+6. all-to-all of the partials back to their source ranks, in send order;
+7. ``mosaic_ep_combine``: each token's partials summed in ascending expert id.
+
+Because the order of every fp32 sum is the single-GPU layer's, the output is
+bit-identical to ``MoELayer`` on the same tokens.  The exchange sizes are read
+on the host after the count exchange (one synchronisation per layer).
+
+The kernels are reached through a ``kernels`` object; the default is the CUDA
+library and there is no CPU path in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import _capi as C
+from . import ops
+from .moe import ExpertBank, MoEConfig, Router
+
+
+def expert_range(n_experts: int, world: int, rank: int) -> tuple[int, int]:
+    """Routed experts [lo, hi) owned by ``rank``."""
+    if world < 1 or n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split evenly over {world} ranks")
+    per = n_experts // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_bank(gu_packed, gu_scale, dn_packed, dn_scale, *, rank: int, world: int, n_experts: int,
+               has_shared: bool, keep_packed: bool = False) -> ExpertBank:
+    """Local bank of ``rank`` from a reference-layout bank of E routed experts
+    (+ the shared expert as expert E): its expert range, then the shared expert."""
+    lo, hi = expert_range(n_experts, world, rank)
+    sel = list(range(lo, hi)) + ([n_experts] if has_shared else [])
+    sel_t = torch.tensor(sel, device=gu_packed.device)
+    pick = [t.index_select(0, sel_t) for t in (gu_packed, gu_scale, dn_packed, dn_scale)]
+    return ExpertBank(*pick, has_shared=has_shared, keep_packed=keep_packed)
+
+
+class _Buffer:
+    """Device byte buffer that grows to the largest size asked for."""
+
+    def __init__(self):
+        self.t = None
+
+    def get(self, nbytes: int, device) -> torch.Tensor:
+        nbytes = max(int(nbytes), 256)
+        if self.t is None or self.t.numel() < nbytes or self.t.device != torch.device(device):
+            self.t = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        return self.t
+
+
+class CudaEPKernels:
+    """The CUDA kernels of one expert-parallel rank, through the C ABI."""
+
+    def __init__(self):
+        self._ws_dispatch = _Buffer()
+        self._ws_rows = _Buffer()
+        self._ws_shared = _Buffer()
+
+    def route(self, router: Router, x: torch.Tensor):
+        return router(x)
+
+    def dispatch(self, dims: C.MoEDims, world: int, x, idx, w):
+        lib = C.lib()
+        ws = self._ws_dispatch.get(lib.mosaic_moe_workspace_bytes(ctypes.byref(dims)), x.device)
+        a = dims.tokens * dims.top_k
+        send = torch.empty(a, C.ep_row_bytes(dims.hidden), dtype=torch.uint8, device=x.device)
+        counts = torch.empty(world, dtype=torch.int32, device=x.device)
+        C.check(lib.mosaic_ep_dispatch(ctypes.byref(dims), world, ops._ptr(x), ops._ptr(idx), ops._ptr(w),
+                                       ops._ptr(send), ops._ptr(counts), ops._ptr(ws), ws.numel(), ops._stream()),
+                "mosaic_ep_dispatch")
+        return send, counts, ws
+
+    def _rows(self, dims_local: C.MoEDims, bank: ExpertBank, rows: int, x_ptr: int, ldx: int, ids_ptr, w_ptr,
+              stride: int, default_id: int, out: torch.Tensor, buf: _Buffer, device):
+        lib = C.lib()
+        if rows == 0:
+            return
+        ws = buf.get(lib.mosaic_moe_expert_rows_workspace_bytes(ctypes.byref(dims_local), rows), device)
+        b = bank.c_struct()
+        C.check(lib.mosaic_moe_expert_rows(ctypes.byref(dims_local), rows, ctypes.c_void_p(x_ptr), ldx,
+                                           ctypes.c_void_p(ids_ptr), ctypes.c_void_p(w_ptr), stride, default_id,
+                                           ctypes.byref(b), ops._ptr(out), ops._ptr(ws), ws.numel(), ops._stream()),
+                "mosaic_moe_expert_rows")
+
+    def expert_rows(self, dims_local: C.MoEDims, bank: ExpertBank, recv: torch.Tensor, out: torch.Tensor):
+        """Partials of received send rows (uint8 [R, row bytes]) into out [R, H]."""
+        h = dims_local.hidden
+        rb = C.ep_row_bytes(h)
+        base = recv.data_ptr()
+        self._rows(dims_local, bank, recv.shape[0], base, rb // 2, base + 2 * h, base + 2 * h + 4, rb // 4, 0, out,
+                   self._ws_rows, recv.device)
+
+    def shared_rows(self, dims_local: C.MoEDims, bank: ExpertBank, x: torch.Tensor, out: torch.Tensor):
+        """Shared-expert partials of the local tokens x [T, H] into out [T, H]."""
+        self._rows(dims_local, bank, x.shape[0], x.data_ptr(), x.shape[1], None, None, 1, dims_local.n_experts, out,
+                   self._ws_shared, x.device)
+
+    def combine(self, dims: C.MoEDims, partials: torch.Tensor, ws: torch.Tensor, y: torch.Tensor):
+        C.check(C.lib().mosaic_ep_combine(ctypes.byref(dims), ops._ptr(partials), ops._ptr(ws), ops._ptr(y),
+                                          ops._stream()), "mosaic_ep_combine")
+
+    def read_error(self, ws: torch.Tensor) -> int:
+        return ops.read_error(ws)
+
+
+class ExpertParallelMoELayer(nn.Module):
+    """``MoELayer`` with its routed experts sharded over the ranks of ``group``.
+
+    ``local_bank`` holds this rank's experts (``expert_range``) followed by the
+    shared expert when ``cfg.n_shared_experts``; ``shard_bank`` builds it from
+    the full reference-layout bank.  ``forward`` takes this rank's tokens and
+    returns their layer output; every rank of the group must call it.
+    """
+
+    def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None):
+        super().__init__()
+        cfg.validate()
+        self.cfg = cfg
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.e_lo, self.e_hi = expert_range(cfg.n_routed_experts, self.world, self.rank)
+        self.bank = local_bank
+        self.has_shared = cfg.n_shared_experts > 0
+        self.router = Router(cfg)
+        self.kernels = kernels if kernels is not None else CudaEPKernels()
+        self.last_weights = None
+        self.last_idx = None
+        self.last_counts = None
+
+    @classmethod
+    def from_layer(cls, layer, *, group=None, kernels=None):
+        """EP layer of this rank from a full single-GPU ``MoELayer`` (same config,
+        router weights and experts; the bank keeps its reference-layout copies)."""
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        b = layer.bank
+        local = shard_bank(b.gu_packed, b.gu_scale, b.dn_packed, b.dn_scale, rank=rank, world=world,
+                           n_experts=layer.cfg.n_routed_experts, has_shared=b.has_shared)
+        ep = cls(layer.cfg, local, group=group, kernels=kernels)
+        ep.router.weight.data = layer.router.weight.data
+        ep.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
+        return ep
+
+    def _local_dims(self, tokens: int) -> C.MoEDims:
+        d = self.cfg.dims(tokens, self.has_shared)
+        d.n_experts = self.e_hi - self.e_lo
+        return d
+
+    def _a2a(self, out, inp, out_splits, in_splits, async_op=False):
+        if self.world == 1:  # no process group needed: the exchange is a copy
+            out.copy_(inp)
+            return None
+        return dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                                      group=self.group, async_op=async_op)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        t, h = xf.shape
+        k = self.cfg.num_experts_per_tok
+        kern = self.kernels
+        dims = self.cfg.dims(t, self.has_shared)
+        if t > 0:
+            w, idx = kern.route(self.router, xf)
+            send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
+        else:  # no tokens here, but this rank still serves its experts in every exchange
+            w = torch.empty(0, k, dtype=torch.float32, device=xf.device)
+            idx = torch.empty(0, k, dtype=torch.int64, device=xf.device)
+            send = torch.empty(0, C.ep_row_bytes(h), dtype=torch.uint8, device=xf.device)
+            counts = torch.zeros(self.world, dtype=torch.int32, device=xf.device)
+            ws = None
+        # row counts: rows this rank sends to each rank, rows it receives from each
+        recv_counts = torch.empty_like(counts)
+        self._a2a(recv_counts, counts, None, None)
+        sc = counts.tolist()
+        rc = recv_counts.tolist()
+        n_send, n_recv = sum(sc), sum(rc)
+        recv = torch.empty(n_recv, send.shape[1], dtype=torch.uint8, device=xf.device)
+        work = self._a2a(recv, send[:n_send], rc, sc, async_op=True)
+        pdt = torch.float32 if self.cfg.act_mode == "bf16" else torch.bfloat16
+        # rows [0, n_send) come back from the owners, [t*k, t*k + t) are the shared
+        # expert's; rows of assignments with invalid ids are never read
+        partials = torch.empty(t * k + (t if self.has_shared else 0), h, dtype=pdt, device=xf.device)
+        dl = self._local_dims(t)
+        if self.has_shared and t > 0:  # overlaps the exchange
+            kern.shared_rows(dl, self.bank, xf, partials[t * k:])
+        if work is not None:
+            work.wait()
+        recv_part = torch.empty(n_recv, h, dtype=pdt, device=xf.device)
+        kern.expert_rows(dl, self.bank, recv, recv_part)
+        self._a2a(partials[:n_send], recv_part, sc, rc)
+        y = torch.empty_like(xf)
+        if t > 0:
+            kern.combine(dims, partials, ws, y)
+        self.last_weights, self.last_idx, self.last_counts = w, idx, (sc, rc)
+        return y.to(x.dtype).view(shape)
