@@ -69,7 +69,7 @@ enum mosaic_act_mode { MOSAIC_ACT_BF16 = 0, MOSAIC_ACT_FP8 = 1 };
 
 typedef struct mosaic_moe_dims {
   int32_t tokens;         /* T: rows of x */
-  int32_t hidden;         /* H: multiple of 128 */
+  int32_t hidden;         /* H: multiple of 256 */
   int32_t inter;          /* I: moe_intermediate_size, multiple of 128 */
   int32_t n_experts;      /* E routed experts, 1..256 */
   int32_t top_k;          /* 1..8, <= E */
@@ -93,8 +93,8 @@ typedef struct mosaic_moe_dims {
 typedef struct mosaic_expert_bank {
   const uint8_t* gu_tiled;  /* [n_bank][I/128][H/128][2][128][64]: mosaic_repack_weights(halves=2), 32-B aligned */
   const uint8_t* gu_sf;     /* [n_bank][I/128][H/128][2][512]: mosaic_prepack_scales(halves=2) */
-  const uint8_t* dn_tiled;  /* [n_bank][H/128][I/128][128][64]: mosaic_repack_weights(halves=1), 32-B aligned */
-  const uint8_t* dn_sf;     /* [n_bank][H/128][I/128][512]: mosaic_prepack_scales(halves=1) */
+  const uint8_t* dn_tiled;  /* [n_bank][H/256][I/128][2][128][64]: mosaic_repack_weights(halves=2), 32-B aligned */
+  const uint8_t* dn_sf;     /* [n_bank][H/256][I/128][2][512]: mosaic_prepack_scales(halves=2) */
 } mosaic_expert_bank;
 
 MOSAIC_API int mosaic_version(void);

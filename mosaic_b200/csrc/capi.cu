@@ -93,7 +93,8 @@ struct WsPlan {
 int check_dims(const mosaic_moe_dims* d) {
   if (!d) return MOSAIC_ERR_SHAPE;
   if (d->tokens < 1 || d->tokens > (1 << 20)) return MOSAIC_ERR_SHAPE;
-  if (d->hidden < 128 || d->hidden % 128 || d->inter < 128 || d->inter % 128) return MOSAIC_ERR_SHAPE;
+  // H: whole pairs of 128-row down blocks; I: whole 128-row gate/up blocks
+  if (d->hidden < 256 || d->hidden % 256 || d->inter < 128 || d->inter % 128) return MOSAIC_ERR_SHAPE;
   if (d->n_experts < 1 || d->n_experts > 256) return MOSAIC_ERR_UNSUPPORTED;
   if (d->top_k < 1 || d->top_k > 8 || d->top_k > d->n_experts) return MOSAIC_ERR_SHAPE;
   if (d->n_group < 1 || d->n_group > 32 || d->n_experts % d->n_group) return MOSAIC_ERR_SHAPE;
@@ -117,13 +118,16 @@ WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   w.R_pad = (w.R + 15) & ~15;
   w.planes = hilo ? 2 : 1;
   // Token rows per tile.  bf16 (decode) tiles carry hi + lo planes: MMA N = 2 * rows.
-  w.tt = hilo ? MOSAIC_DECODE_TILE_ROWS : 128;
+  // E4M3 (prefill) tiles hold 112 rows so that two accumulator buffers fit TMEM
+  // (2 x 2 x 112 columns + 32 scale columns <= 512): the epilogue of one work
+  // item then overlaps the MMAs of the next instead of stalling them.
+  w.tt = hilo ? MOSAIC_DECODE_TILE_ROWS : 112;
   w.max_n = hilo ? 2 * w.tt : w.tt;
   // sum over experts of ceil(count / tt) <= A / tt + (experts with a partial tile)
   w.max_tiles = (T * k) / w.tt + w.n_bank + T / w.tt + 2;
-  // Decode tiles (small N, 64 TMEM columns per gate+up accumulator): two TMEM
-  // buffers and two stage parities.  Prefill tiles (N = 128): one of each.
-  w.nbuf = hilo ? 2 : 1;
+  // Two TMEM accumulator buffers in both modes; decode tiles (small N) also use
+  // two stage parities (four MMA issuers), prefill tiles one.
+  w.nbuf = 2;
   w.parities = hilo ? 2 : 1;
   const int sms = sm_count();
   w.splits = router_splits(T, H, E, sms > 0 ? sms : 148);
@@ -224,32 +228,27 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   st = make_act_map(&tx, ws + w.xq, w.R_pad, w.planes, H, w.tt, 1);
   if (st) return st;
   gp.mode = 0;
-  gp.ks = 1;
   gp.parities = w.parities;
   gp.K = H;
   gp.n_blocks = I / 128;
   gp.x_sft = ws + w.x_sft;
   gp.w_sf = bank->gu_sf;
-  gp.w_rowtiles = 2 * I / 128;
   gp.zq = ws + w.zq;
   gp.z_sft = reinterpret_cast<uint32_t*>(ws + w.z_sft);
   if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
 
-  // down
-  const int ks_dn = ((I / 128) % 2 == 0) ? 2 : 1;
-  st = make_weight_map(&tw, bank->dn_tiled, w.n_bank, H, I, ks_dn);
+  // down: pairs of hidden blocks (nb, nb + H/256), adjacent in the bank
+  st = make_weight_map(&tw, bank->dn_tiled, w.n_bank, H, I, 2);
   if (st) return st;
-  st = make_act_map(&tx, gp.zq, w.R_pad, w.planes, I, w.tt, ks_dn);
+  st = make_act_map(&tx, gp.zq, w.R_pad, w.planes, I, w.tt, 1);
   if (st) return st;
   gp.mode = 1;
-  gp.ks = ks_dn;
   gp.parities = w.parities;
   gp.K = I;
-  gp.n_blocks = H / 128;
+  gp.n_blocks = H / 256;
   gp.x_sft = ws + w.z_sft;
   gp.w_sf = bank->dn_sf;
-  gp.w_rowtiles = H / 128;
   gp.out = partial_out;
   gp.out_f32 = w.partial_f32;
   gp.out_row = out_row;
@@ -295,7 +294,7 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
 // The per-row pass accepts up to 256 routed experts plus the shared one.
 int check_rows_dims(const mosaic_moe_dims* r) {
   if (r->tokens < 1 || r->tokens > (1 << 20)) return MOSAIC_ERR_SHAPE;
-  if (r->hidden < 128 || r->hidden % 128 || r->inter < 128 || r->inter % 128) return MOSAIC_ERR_SHAPE;
+  if (r->hidden < 256 || r->hidden % 256 || r->inter < 128 || r->inter % 128) return MOSAIC_ERR_SHAPE;
   if (r->n_experts < 1 || r->n_experts > 257) return MOSAIC_ERR_UNSUPPORTED;
   if (r->act_mode != MOSAIC_ACT_BF16 && r->act_mode != MOSAIC_ACT_FP8) return MOSAIC_ERR_DTYPE;
   if (!(r->swiglu_limit >= 0.f)) return MOSAIC_ERR_RANGE;

@@ -1,38 +1,40 @@
 // Grouped block-scaled expert GEMM for the MoE layer (tcgen05, sm_100a).
 //
-// One persistent kernel serves both expert projections:
-//   mode 0 (gate/up): D_gate = W_gate . X^T and D_up = W_up . X^T for a 128-row
-//     block of the intermediate dimension, then the epilogue computes
-//     z = SiLU(clamp(gate)) * clamp(up) * route_weight, rounds z to bf16 and
-//     re-quantises it (FP8 mode: the reference act_quant per 128; bf16 mode:
-//     hi + lo E4M3 with per-32 scales) straight into the down GEMM's input
-//     rows and scale-factor chunks;
-//   mode 1 (down): D = W_down . Z^T for a 128-row block of the hidden
-//     dimension, written as per-assignment partials (fp32 or bf16).
+// One persistent kernel serves both expert projections.  A work item is one
+// token tile of one expert times a PAIR of 128-row weight blocks, which share
+// the item's activation tile:
+//   mode 0 (gate/up): the gate block and the up block of 128 intermediate
+//     rows; the epilogue computes z = SiLU(clamp(gate)) * clamp(up) *
+//     route_weight, rounds z to bf16 and re-quantises it (FP8 mode: the
+//     reference act_quant per 128; bf16 mode: hi + lo E4M3 with per-32
+//     scales) straight into the down GEMM's input rows and scale chunks;
+//   mode 1 (down): hidden rows [nb*128, +128) and [H/2 + nb*128, +128); the
+//     epilogue writes per-assignment partials (fp32 or bf16).
+// The bank keeps the two tiles of a pair adjacent for every K-tile (the
+// "halves" re-layout), so one tensor load moves both.
 //
 // Swap-AB orientation: A = expert weights (E2M1 codes, E8M0 per-32 scales;
 // MMA M = 128 weight rows), B = the activation rows of one token tile of one
 // expert (E4M3, per-32 scales; MMA N = token rows padded to 16, doubled in
 // bf16 mode for the lo plane).
 //
-// Data movement is shaped for the TMA unit, whose per-operation cost dominates
-// at decode sizes: every stage moves its 16 KB of packed weights with ONE
-// tensor load (gate + up tiles of one K-tile are adjacent in the bank, and the
-// down GEMM takes two consecutive K-tiles per stage), unpacked by the
-// 16U4_ALIGN16B type into the smem layout kind::mxf8f6f4 reads.  A dedicated
-// warp issues only those loads; a second producer warp issues the activation
-// rows (one 4-D box: K-tiles x planes x rows) and the scale-factor chunks.
-// Scale factors go smem -> TMEM with tcgen05.cp; accumulators live in TMEM,
-// double-buffered with independent K chains at decode sizes.
+// Data movement: every stage moves its 16 KB of packed weights with ONE
+// tensor load, unpacked by the 16U4_ALIGN16B type into the smem layout
+// kind::mxf8f6f4 reads, from a warp that issues nothing else; a second
+// producer warp issues the activation K-tile (one 4-D box: planes x rows) and
+// the scale-factor chunks.  Scale factors go smem -> TMEM with tcgen05.cp;
+// accumulators live in TMEM, double-buffered, so the epilogue of one item
+// overlaps the MMAs of the next.  The epilogue stages its output in shared
+// memory and writes whole token rows with 16-byte stores.
 //
 // Warp roles (320 threads): warp 0 = weight producer, warp 6 = activation /
 // scale producer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31),
 // warps 1, 7, 8, 9 = MMA issuers (warp 1 also owns TMEM).  A tcgen05.mma costs
-// its issuing thread ~150-200 cycles whatever its size, so a single issuer
-// caps small-N decode tiles far below HBM speed; four issuers split every
-// stage into two units (gate / up, or the two K-tiles of a down stage) and
-// alternate stages by parity, each accumulating into its own TMEM chain with
-// its own scale-factor columns.  The epilogue sums the chains in a fixed order.
+// its issuing thread ~150-200 cycles whatever its size, so each stage is split
+// into two units (the two blocks of the pair), and at decode sizes two issuer
+// pairs alternate stages by parity, each accumulating into its own TMEM chain
+// with its own scale-factor columns.  The epilogue sums the chains in a fixed
+// order.
 // Reference behaviour: mosaicvm/kernels/qpa_mma.py:337-486 (grouped ordered
 // gate/up and down kernels), mosaicvm/kernels/mxint.py:1301-1346 (fused
 // SwiGLU / route weight / bf16 / act_quant epilogue).
@@ -47,6 +49,7 @@ constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 225 * 1024;
+constexpr int kEpiBytes = 16 * 256 * 4;  // epilogue staging: 16 token columns x 256 values (fp32)
 
 struct Ctrl {
   uint64_t full[kMaxStages];
@@ -59,23 +62,22 @@ struct Ctrl {
   float red[4][16];
 };
 
-// Per stage: two 16 KB weight tiles (gate+up of one K-tile, or two K-tiles of
-// down), KS activation sub-tiles of planes x brows rows, two weight scale
-// chunks and KS activation scale chunks.
+// Per stage: the two 16 KB (unpacked) weight tiles of the pair for one
+// K-tile, the activation K-tile (planes x brows rows of 128 B), the pair's two
+// weight scale chunks and the token tile's scale chunk.
 struct Plan {
-  int stage_bytes, off_b, b_sub, off_sfa, off_sfb, stages, ks;
+  int stage_bytes, off_b, off_sfa, off_sfb, stages, epi;
 };
 
-__host__ __device__ inline Plan make_plan(int mode, int planes, int brows, int ks) {
+__host__ __device__ inline Plan make_plan(int planes, int brows) {
   Plan pl;
-  pl.ks = (mode == 0) ? 1 : ks;
-  pl.b_sub = planes * brows * 128;
   pl.off_b = 32768;
-  pl.off_sfa = pl.off_b + ((pl.ks * pl.b_sub + 1023) / 1024) * 1024;
+  pl.off_sfa = pl.off_b + ((planes * brows * 128 + 1023) / 1024) * 1024;
   pl.off_sfb = pl.off_sfa + 1024;
-  pl.stage_bytes = ((pl.off_sfb + 512 * pl.ks + 1023) / 1024) * 1024;
-  int s = (kSmemBudget - static_cast<int>(sizeof(Ctrl)) - 1024) / pl.stage_bytes;
+  pl.stage_bytes = ((pl.off_sfb + 512 + 1023) / 1024) * 1024;
+  int s = (kSmemBudget - static_cast<int>(sizeof(Ctrl)) - kEpiBytes - 1024) / pl.stage_bytes;
   pl.stages = s > kMaxStages ? kMaxStages : s;
+  pl.epi = pl.stages * pl.stage_bytes;  // epilogue staging right after the ring (1 KB aligned)
   return pl;
 }
 
@@ -136,22 +138,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int planes = p.hilo ? 2 : 1;
-  const Plan pl = make_plan(p.mode, planes, p.brows, p.ks);
+  const Plan pl = make_plan(planes, p.brows);
   const int S = pl.stages;
-  const int KS = pl.ks;
-  Ctrl* ctrl = reinterpret_cast<Ctrl*>(smem + S * pl.stage_bytes);
+  uint8_t* epi = smem + pl.epi;
+  Ctrl* ctrl = reinterpret_cast<Ctrl*>(epi + kEpiBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const bool gu = (p.mode == 0);
   const int nbuf = p.nbuf;
   const int P = p.parities;  // stage parities split across issuer pairs (1 or 2)
-  // TMEM: accumulator of (buffer b, chain c) at column (b*CH + c) * acc_w with
-  // CH = P chains (gate/up: the up half at +max_n) or P*KS chains (down: chain
-  // p*KS + u).  Issuer i's scale factors: weight chunk at sf_base + 8i, token
-  // chunk at +4.
-  const uint32_t acc_w = static_cast<uint32_t>((gu ? 2 : 1) * p.max_n);
-  const uint32_t up_off = static_cast<uint32_t>(p.max_n);
-  const int CH = gu ? P : P * KS;
+  // TMEM: accumulator pair of (buffer b, chain c) at column (b*P + c) * acc_w,
+  // the second block of the pair at +max_n.  Issuer i's scale factors: weight
+  // chunk at sf_base + 8i, token chunk at +4.
+  const uint32_t acc_w = static_cast<uint32_t>(2 * p.max_n);
+  const uint32_t half_off = static_cast<uint32_t>(p.max_n);
   const uint32_t sf_base = kTmemCols - 32u;
 
   if (threadIdx.x == 0) {
@@ -183,26 +183,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (n_tiles > p.max_tiles) n_tiles = p.max_tiles;
   const int n_items = n_tiles * p.n_blocks;
   const int KT = p.K / 128;
-  const int n_stages_item = KT / KS;
 
   if (warp == 0 || warp == 6) {
     // ----------------------------------------------------------- producers
     const bool wprod = (warp == 0);
+    const uint32_t tx = wprod ? 2u * 8192u  // packed global bytes of the two weight tiles
+                              : 2u * 512u + static_cast<uint32_t>(planes * p.brows) * 128u + 512u;
     int it = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
       const Item m = get_item(p, item);
-      // weight tile index of (expert, row block, K-tile 0); the tiles of one K-tile
-      // are [gate, up] in mode 0, and consecutive K-tiles follow each other
-      const int wtile = ((m.e * p.n_blocks + m.nb) * KT) * (gu ? 2 : 1);
-      // The weight warp issues exactly one TMA per stage (the TMA unit's per-op
-      // cost, not bytes, limits a single issuing thread); everything small -
-      // activation rows and all scale-factor chunks - comes from warp 6.
-      const uint32_t wtiles = gu ? 2u : static_cast<uint32_t>(KS);  // 8 KB tiles per weight box
-      const uint32_t tx = wprod ? wtiles * 8192u
-                                : wtiles * 512u +
-                                      static_cast<uint32_t>(KS) * (static_cast<uint32_t>(planes * p.brows) * 128u + 512u);
-      for (int ks = 0; ks < n_stages_item; ++ks, ++it) {
+      // tile index of (expert, block pair, K-tile 0, first of the pair); the two
+      // tiles of the pair are adjacent for every K-tile
+      const int wtile = ((m.e * p.n_blocks + m.nb) * KT) * 2;
+      for (int kt = 0; kt < KT; ++kt, ++it) {
         const int s = it % S;
         const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
         if (!mbar_wait(&ctrl->empty[s], ph ^ 1u, abort)) {
@@ -212,16 +206,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           uint8_t* st = smem + s * pl.stage_bytes;
           uint64_t* fb = &ctrl->full[s];
-          const int kt = ks * KS;
-          // gate+up of K-tile kt (mode 0) or K-tiles kt.. kt+KS-1 (mode 1)
-          const int t0 = wtile + kt * (gu ? 2 : 1);
+          const int t0 = wtile + kt * 2;
           mbar_arrive_expect_tx(fb, tx);
           if (wprod) {
             tma_load_3d(st, &tmap_w, fb, 0, 0, t0);
           } else {
             tma_load_4d(st + pl.off_b, &tmap_x, fb, 0, m.row0, 0, kt);
-            bulk_load(st + pl.off_sfa, p.w_sf + static_cast<size_t>(t0) * 512, 512u * wtiles, fb);
-            bulk_load(st + pl.off_sfb, p.x_sft + (static_cast<size_t>(m.tile) * KT + kt) * 512, 512 * KS, fb);
+            bulk_load(st + pl.off_sfa, p.w_sf + static_cast<size_t>(t0) * 512, 1024u, fb);
+            bulk_load(st + pl.off_sfb, p.x_sft + (static_cast<size_t>(m.tile) * KT + kt) * 512, 512u, fb);
           }
         }
         __syncwarp();
@@ -242,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------------- MMA
     const int issuer = (warp == 1) ? 0 : warp - 6;  // 0..3
     const int ip = issuer >> 1;                     // stage parity this issuer takes
-    const int iu = issuer & 1;                      // unit: gate/up half, or down K sub-tile
+    const int iu = issuer & 1;                      // unit: block of the pair
     const uint32_t col_sfw = tmem + sf_base + 8u * issuer;  // weight scale chunk
     const uint32_t col_sfx = col_sfw + 4u;                  // token scale chunk
     int it = 0, li = 0;
@@ -256,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      for (int ks = 0; ks < n_stages_item; ++ks, ++it) {
+      for (int kt = 0; kt < KT; ++kt, ++it) {
         const int s = it % S;
         const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
         // Every issuer observes every phase of every full barrier and arrives on
@@ -268,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (ks % P != ip) {
+        if (kt % P != ip) {
           if (lane == 0) mbar_arrive(&ctrl->empty[s]);
           __syncwarp();
           continue;
@@ -276,29 +268,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (lane == 0) {
           const uint32_t sw = smem_u32(smem + s * pl.stage_bytes);
-          const bool first = (ks < P);  // first stage of this issuer's chain in the item
-          if (gu) {
-            const uint32_t d = tmem + static_cast<uint32_t>(b * CH + ip) * acc_w + (iu ? up_off : 0u);
-            tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
-            tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
-            const uint32_t a = sw + 16384 * iu, bb = sw + pl.off_b;
+          const bool first = (kt < P);  // first stage of this issuer's chain in the item
+          const uint32_t d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
+          tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
+          tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
+          const uint32_t a = sw + 16384 * iu, bb = sw + pl.off_b;
 #pragma unroll
-            for (uint32_t kb = 0; kb < 4; ++kb) {
-              tc_mma_mxf8f6f4(d, desc_sw128(a + kb * 32), desc_sw128(bb + kb * 32), idesc_mxf8f6f4(m.n, kb),
-                              (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
-            }
-          } else if (iu < KS) {
-            const uint32_t d = tmem + static_cast<uint32_t>(b * CH + ip * KS + iu) * acc_w;
-            tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
-            tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb + 512 * iu));
-            const uint32_t a = sw + 16384 * iu, bb = sw + pl.off_b + pl.b_sub * iu;
-#pragma unroll
-            for (uint32_t kb = 0; kb < 4; ++kb) {
-              tc_mma_mxf8f6f4(d, desc_sw128(a + kb * 32), desc_sw128(bb + kb * 32), idesc_mxf8f6f4(m.n, kb),
-                              (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
-            }
+          for (uint32_t kb = 0; kb < 4; ++kb) {
+            tc_mma_mxf8f6f4(d, desc_sw128(a + kb * 32), desc_sw128(bb + kb * 32), idesc_mxf8f6f4(m.n, kb),
+                            (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
           }
-          tc_commit(&ctrl->empty[s]);  // a unit without work still arrives
+          tc_commit(&ctrl->empty[s]);
           issued = true;
         }
         __syncwarp();
@@ -325,9 +305,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int lrow = q * 32 + lane;
+    const int et = threadIdx.x - 64;  // 0..127: this thread's index among the epilogue warps
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const size_t z_plane = static_cast<size_t>(p.R_pad) * 128;    // bytes per (K-tile, plane) of z rows
     const size_t z_ktile = static_cast<size_t>(planes) * z_plane;  // bytes per K-tile of z rows
+    float* stage_f = reinterpret_cast<float*>(epi);                // [16 tokens][256 values]
+    uint8_t* stage_b = epi;                                        // [planes][16 tokens][128 B]
+    const int P_used = KT < P ? KT : P;                            // chains that received MMAs
     int li = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
       const Item m = get_item(p, item);
@@ -340,20 +324,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t c_buf = static_cast<uint32_t>(b * CH) * acc_w;
-      const int P_used = n_stages_item < P ? n_stages_item : P;  // chains that received MMAs
-      const int C = gu ? P_used : P_used * KS;
+      const uint32_t c_buf = static_cast<uint32_t>(b * P) * acc_w;
+      const int lo = p.hilo ? m.rpad : 0;
       for (int c0 = 0; c0 < m.rpad; c0 += 16) {
+        float s0[16], s1[16];
+        tmem_sum16(tq + c_buf + c0, P_used, acc_w, lo, s0);
+        tmem_sum16(tq + c_buf + half_off + c0, P_used, acc_w, lo, s1);
+        const int ncol = min(16, m.rows - c0);  // token columns of this block that exist
         if (gu) {
-          float gs[16], us[16];
-          tmem_sum16(tq + c_buf + c0, C, acc_w, p.hilo ? m.rpad : 0, gs);
-          tmem_sum16(tq + c_buf + up_off + c0, C, acc_w, p.hilo ? m.rpad : 0, us);
           float zd[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int col = c0 + j;
-            float gv = gs[j];
-            float uv = us[j];
+            float gv = s0[j];
+            float uv = s1[j];
             if (round_mid) {
               gv = bf16r(gv);
               uv = bf16r(uv);
@@ -362,13 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               gv = fminf(gv, p.swiglu_limit);
               uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
             }
-            const float w = (col < m.rows) ? p.row_weight[m.row0 + col] : 0.f;
+            const float w = (j < ncol) ? p.row_weight[m.row0 + col] : 0.f;
             float z = gv / (1.0f + expf(-gv)) * uv;
             z = z * w;
-            zd[j] = (col < m.rows) ? bf16r(z) : 0.f;
+            zd[j] = (j < ncol) ? bf16r(z) : 0.f;
           }
-          // z rows: [K-tile = nb][plane][row][128 B]; this thread owns byte lrow of the K-tile
-          uint8_t* zq = p.zq + static_cast<size_t>(m.nb) * z_ktile + lrow;
+          // quantised bytes staged as [plane][token][128 B] (this thread: byte lrow)
           uint32_t* zsf = p.z_sft + (static_cast<size_t>(m.tile) * (p.I / 128) + m.nb) * 128;
           if (p.fp8) {
 #pragma unroll
@@ -379,21 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             epi_bar();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const int col = c0 + j;
               const float amax =
                   fmaxf(fmaxf(ctrl->red[0][j], ctrl->red[1][j]), fmaxf(ctrl->red[2][j], ctrl->red[3][j]));
               const int ex = pow2_scale_exp(amax, 1e-4f);
               const float y = fminf(fmaxf(zd[j] * exp2i(-ex), -448.f), 448.f);
-              if (col < m.rows) {
-                zq[static_cast<size_t>(m.row0 + col) * 128] = f32_to_e4m3(y);
-                if (lrow == 0) zsf[sf_word(col)] = (static_cast<uint32_t>(ex + 127) & 0xFFu) * 0x01010101u;
-              }
+              stage_b[j * 128 + lrow] = f32_to_e4m3(y);
+              if (lrow == 0 && j < ncol) zsf[sf_word(c0 + j)] = (static_cast<uint32_t>(ex + 127) & 0xFFu) * 0x01010101u;
             }
-            epi_bar();
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const int col = c0 + j;
               const float mx = warp_max(fabsf(zd[j]));
               int eh = pow2_scale_exp(mx, 1e-30f);
               eh = max(-126, min(127, eh));
@@ -403,35 +381,66 @@ __global__ void __launch_bounds__(kThreads, 1)
               int el = pow2_scale_exp(m2, fmaxf(mx * 1e-7f, 1e-30f));
               el = max(-126, min(127, el));
               const uint8_t lb = f32_to_e4m3(res * exp2i(-el));
-              if (col < m.rows) {
-                const size_t r = static_cast<size_t>(m.row0 + col) * 128;
-                zq[r] = hb;
-                zq[z_plane + r] = lb;
-                if (lane == 0) {
-                  reinterpret_cast<uint8_t*>(zsf + sf_word(col))[q] = static_cast<uint8_t>(eh + 127);
-                  reinterpret_cast<uint8_t*>(zsf + sf_word(m.rpad + col))[q] = static_cast<uint8_t>(el + 127);
-                }
+              stage_b[j * 128 + lrow] = hb;
+              stage_b[2048 + j * 128 + lrow] = lb;
+              if (lane == 0 && j < ncol) {
+                reinterpret_cast<uint8_t*>(zsf + sf_word(c0 + j))[q] = static_cast<uint8_t>(eh + 127);
+                reinterpret_cast<uint8_t*>(zsf + sf_word(m.rpad + c0 + j))[q] = static_cast<uint8_t>(el + 127);
               }
             }
           }
+          epi_bar();
+          // 16-byte stores of whole 128-byte z rows: planes x 16 tokens x 8 vectors
+          uint8_t* zq = p.zq + static_cast<size_t>(m.nb) * z_ktile;
+          for (int v = et; v < planes * 128; v += 128) {
+            const int pl_ = v >> 7, j = (v >> 3) & 15, off = (v & 7) * 16;
+            if (j < ncol)
+              *reinterpret_cast<uint4*>(zq + pl_ * z_plane + static_cast<size_t>(m.row0 + c0 + j) * 128 + off) =
+                  *reinterpret_cast<const uint4*>(stage_b + pl_ * 2048 + j * 128 + off);
+          }
+          epi_bar();  // the staging buffer is rewritten by the next column block
         } else {
-          float ds[16];
-          tmem_sum16(tq + c_buf + c0, C, acc_w, p.hilo ? m.rpad : 0, ds);
-          const int nn = m.nb * 128 + lrow;
+          // partials of the two hidden blocks, staged as [token][256 values]
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int col = c0 + j;
-            if (col < m.rows) {
-              float v = ds[j];
-              if (round_mid) v = bf16r(v);
-              const int orow = p.out_row ? p.out_row[m.row0 + col] : m.row0 + col;
-              const size_t o = static_cast<size_t>(orow) * p.H + nn;
-              if (p.out_f32)
-                reinterpret_cast<float*>(p.out)[o] = v;
-              else
-                reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+            float v0 = s0[j], v1 = s1[j];
+            if (round_mid) {
+              v0 = bf16r(v0);
+              v1 = bf16r(v1);
+            }
+            stage_f[j * 256 + lrow] = v0;
+            stage_f[j * 256 + 128 + lrow] = v1;
+          }
+          epi_bar();
+          // 16-byte stores: per token, two runs of 128 values (block nb of each half)
+          const int hb = p.H / 2;
+          if (p.out_f32) {
+            for (int v = et; v < 16 * 64; v += 128) {  // 16 tokens x 2 halves x 32 float4
+              const int j = v >> 6, h = (v >> 5) & 1, w4 = v & 31;
+              if (j < ncol) {
+                const int orow = p.out_row ? p.out_row[m.row0 + c0 + j] : m.row0 + c0 + j;
+                float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(orow) * p.H + h * hb + m.nb * 128;
+                reinterpret_cast<float4*>(dst)[w4] =
+                    *reinterpret_cast<const float4*>(stage_f + j * 256 + h * 128 + w4 * 4);
+              }
+            }
+          } else {
+            for (int v = et; v < 16 * 32; v += 128) {  // 16 tokens x 2 halves x 16 vectors of 8 bf16
+              const int j = v >> 5, h = (v >> 4) & 1, w8 = v & 15;
+              if (j < ncol) {
+                const int orow = p.out_row ? p.out_row[m.row0 + c0 + j] : m.row0 + c0 + j;
+                const float* src = stage_f + j * 256 + h * 128 + w8 * 8;
+                uint4 pk;
+                __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(src[2 * i], src[2 * i + 1]);
+                __nv_bfloat16* dst =
+                    reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(orow) * p.H + h * hb + m.nb * 128;
+                reinterpret_cast<uint4*>(dst)[w8] = pk;
+              }
             }
           }
+          epi_bar();
         }
       }
       tc_fence_before();
@@ -447,9 +456,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-size_t gemm_smem_bytes(int mode, int planes, int brows, int ks) {
-  const Plan pl = make_plan(mode, planes, brows, ks);
-  return static_cast<size_t>(pl.stages) * pl.stage_bytes + sizeof(Ctrl) + 1024;
+size_t gemm_smem_bytes(int planes, int brows) {
+  const Plan pl = make_plan(planes, brows);
+  return static_cast<size_t>(pl.stages) * pl.stage_bytes + kEpiBytes + sizeof(Ctrl) + 1024;
 }
 
 cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmParams& p, int grid,
@@ -457,16 +466,13 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   if (p.max_n < 16 || p.max_n > 128 || p.nbuf < 1 || p.nbuf > 2 || p.parities < 1 || p.parities > 2)
     return cudaErrorInvalidValue;
   const int planes = p.hilo ? 2 : 1;
-  if (p.brows * planes != p.max_n || p.brows % 16) return cudaErrorInvalidValue;
-  const int acc_w = (p.mode == 0 ? 2 : 1) * p.max_n;
-  const int ch = (p.mode == 0) ? p.parities : p.parities * p.ks;
-  if (p.nbuf * ch * acc_w > static_cast<int>(kTmemCols) - 32) return cudaErrorInvalidValue;
-  const int KT = p.K / 128;
-  if (p.ks < 1 || p.ks > 2 || (p.mode == 0 && p.ks != 1)) return cudaErrorInvalidValue;
-  if (KT % p.ks) return cudaErrorInvalidValue;
-  const Plan pl = make_plan(p.mode, planes, p.brows, p.ks);
+  if (p.brows * planes != p.max_n || p.brows % 16 || p.brows > 128) return cudaErrorInvalidValue;
+  if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols) - 32) return cudaErrorInvalidValue;
+  if (p.K % 128 || p.K < 128) return cudaErrorInvalidValue;
+  if (p.mode == 1 && p.H % 256) return cudaErrorInvalidValue;
+  const Plan pl = make_plan(planes, p.brows);
   if (pl.stages < 2) return cudaErrorInvalidValue;
-  const size_t smem = gemm_smem_bytes(p.mode, planes, p.brows, p.ks);
+  const size_t smem = gemm_smem_bytes(planes, p.brows);
   cudaError_t err = cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;

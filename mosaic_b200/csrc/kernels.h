@@ -11,10 +11,11 @@ namespace mosaic {
 // ---- grouped block-scaled expert GEMM (gemm_bs.cu)
 struct GemmParams {
   int mode;           // 0 = gate/up (+SwiGLU, re-quantise), 1 = down (partials)
+                      // a work item is a token tile x a pair of 128-row weight blocks
   int hilo;           // 1: activation rows come as hi and lo E4M3 planes
   int fp8;            // 1: reference FP8 semantics (act_quant per 128, bf16-rounded linears)
   int K;              // reduction length (H for gate/up, I for down)
-  int n_blocks;       // 128-row output blocks (I/128 for gate/up, H/128 for down)
+  int n_blocks;       // block pairs per expert (I/128 gate/up pairs; H/256 down pairs)
   int I, H;
   int R, R_pad;       // packed activation rows (routed + shared) and padded row count
   int shared_expert;  // bank index of the shared expert, or -1
@@ -24,11 +25,9 @@ struct GemmParams {
   const uint8_t* x_sft;  // activation scale chunks per token tile: [tile][K/128][512]
   int max_n;             // largest MMA N of the launch (token rows x planes), <= 128
   int brows;             // token rows per activation box (= rows per tile)
-  int ks;                // K-tiles per pipeline stage (gate/up: 1; down: 2, or 1 when K/128 is odd)
   int nbuf;              // TMEM accumulator buffers
   int parities;          // 2: stages alternate between two issuer pairs (own chains); 1: one pair
-  const uint8_t* w_sf;   // weight scale chunks [bank][row block][K/128][half][512]
-  int w_rowtiles;
+  const uint8_t* w_sf;   // weight scale chunks [bank][block pair][K/128][half][512]
   const float* row_weight;  // [R] route weight of each packed row
   float swiglu_limit;
   uint8_t* zq;        // gate/up output rows [plane][R_pad][I] (E4M3)
@@ -38,7 +37,7 @@ struct GemmParams {
   const int* out_row; // null: partial of packed row r goes to out row r; else to out row out_row[r]
   int* err;
 };
-size_t gemm_smem_bytes(int mode, int planes, int brows, int ks);
+size_t gemm_smem_bytes(int planes, int brows);
 cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmParams& p, int grid,
                             cudaStream_t stream);
 

@@ -21,11 +21,43 @@ constexpr int kTileT = 64;
 constexpr int kTileE = 64;
 constexpr int kTileK = 32;
 
+// Loads this thread's share of one K-slice: 8 consecutive k of one token row
+// and of one expert row (zeros past T / E).
+__device__ __forceinline__ void load_slice(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w, int T,
+                                           int H, int E, int t, int e, int k, float (&xv)[8], float (&wv)[8]) {
+  if (t < T) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H + k);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h2[i]);
+      xv[2 * i] = f.x;
+      xv[2 * i + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = 0.f;
+  }
+  if (e < E) {
+    const float4 a = *reinterpret_cast<const float4*>(w + static_cast<size_t>(e) * H + k);
+    const float4 b = *reinterpret_cast<const float4*>(w + static_cast<size_t>(e) * H + k + 4);
+    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+    wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wv[i] = 0.f;
+  }
+}
+
+// 64 tokens x 64 experts x one K range per CTA, 4 x 4 outputs per thread.  The
+// next K-slice is loaded into registers while the current one is multiplied
+// out of a double-buffered shared tile, so global latency overlaps the FMAs.
+// Each output sums its K range in ascending k with FMAs (deterministic).
 __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16* __restrict__ x,
                                                             const float* __restrict__ w, int T, int H, int E,
                                                             int kchunk, float* __restrict__ partial) {
-  __shared__ float xs[kTileK][kTileT + 4];
-  __shared__ float ws[kTileK][kTileE + 4];
+  __shared__ float xs[2][kTileK][kTileT + 4];
+  __shared__ float ws[2][kTileK][kTileE + 4];
   const int t0 = blockIdx.x * kTileT;
   const int e0 = blockIdx.y * kTileE;
   const int split = blockIdx.z;
@@ -42,55 +74,29 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
+  float xv[8], wv[8];
+  load_slice(x, w, T, H, E, t0 + lrow, e0 + lrow, kbeg + lk, xv, wv);
+  int buf = 0;
   for (int k0 = kbeg; k0 < kend; k0 += kTileK) {
-    {
-      const int t = t0 + lrow;
-      float v[8];
-      if (t < T) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H + k0 + lk);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h2[i]);
-          v[2 * i] = f.x;
-          v[2 * i + 1] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) xs[lk + i][lrow] = v[i];
-    }
-    {
-      const int e = e0 + lrow;
-      float v[8];
-      if (e < E) {
-        const float4 a = *reinterpret_cast<const float4*>(w + static_cast<size_t>(e) * H + k0 + lk);
-        const float4 b = *reinterpret_cast<const float4*>(w + static_cast<size_t>(e) * H + k0 + lk + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ws[lk + i][lrow] = v[i];
+    for (int i = 0; i < 8; ++i) {
+      xs[buf][lk + i][lrow] = xv[i];
+      ws[buf][lk + i][lrow] = wv[i];
     }
     __syncthreads();
+    if (k0 + kTileK < kend) load_slice(x, w, T, H, E, t0 + lrow, e0 + lrow, k0 + kTileK + lk, xv, wv);
 #pragma unroll 8
     for (int kk = 0; kk < kTileK; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx * 4 + j];
+      const float4 a = *reinterpret_cast<const float4*>(&xs[buf][kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&ws[buf][kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
-    __syncthreads();
+    buf ^= 1;  // the next slice goes to the other buffer: one barrier per slice suffices
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -116,16 +122,56 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
                                                           int norm, float* __restrict__ w_out,
                                                           int64_t* __restrict__ idx_out, int* err) {
   const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // one warp per token
   if (t >= T) return;
   float s[PER], sel[PER];
+  // logits: partials added in split order; a lane's PER experts are contiguous,
+  // so each split is PER/4 16-byte loads, and four splits are in flight at once
+  float logit[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) logit[i] = 0.f;
+  // vector path: this lane's experts in range and every row start 16-byte aligned
+  const bool full = (lane + 1) * PER <= E && (PER % 4 == 0) && (E % 4 == 0);
+  const float* pp = partial + static_cast<size_t>(t) * E + lane * PER;
+  const size_t stride = static_cast<size_t>(T) * E;
+  if (full) {
+    int sp = 0;
+    for (; sp + 4 <= splits; sp += 4) {
+      float4 v[4][PER / 4 > 0 ? PER / 4 : 1];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int q = 0; q < PER / 4; ++q) v[u][q] = *reinterpret_cast<const float4*>(pp + (sp + u) * stride + 4 * q);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int q = 0; q < PER / 4; ++q) {
+          logit[4 * q + 0] += v[u][q].x;
+          logit[4 * q + 1] += v[u][q].y;
+          logit[4 * q + 2] += v[u][q].z;
+          logit[4 * q + 3] += v[u][q].w;
+        }
+    }
+    for (; sp < splits; ++sp)
+#pragma unroll
+      for (int q = 0; q < PER / 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(pp + sp * stride + 4 * q);
+        logit[4 * q + 0] += v.x;
+        logit[4 * q + 1] += v.y;
+        logit[4 * q + 2] += v.z;
+        logit[4 * q + 3] += v.w;
+      }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane * PER + i < E)
+        for (int sp = 0; sp < splits; ++sp) logit[i] += pp[sp * stride + i];
+  }
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane * PER + i;
     if (e < E) {
-      float logit = 0.f;
-      for (int sp = 0; sp < splits; ++sp) logit += partial[(static_cast<size_t>(sp) * T + t) * E + e];
-      s[i] = 1.0f / (1.0f + expf(-logit));
+      s[i] = 1.0f / (1.0f + expf(-logit[i]));
       sel[i] = s[i] + (bias ? bias[e] : 0.f);
     } else {
       s[i] = 0.f;
@@ -252,10 +298,12 @@ cudaError_t launch_router(const void* x, const float* w, const float* bias, int 
   const int used = (H + kchunk - 1) / kchunk;
   dim3 g1((T + kTileT - 1) / kTileT, (E + kTileE - 1) / kTileE, used);
   router_logits_kernel<<<g1, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), w, T, H, E, kchunk, partial);
-  dim3 g2((T + 7) / 8);
+  // warps per block: spread small batches over the SMs, pack large ones
+  const int wpb = T >= 8 * 148 ? 8 : (T >= 4 * 148 ? 4 : (T >= 2 * 148 ? 2 : 1));
+  dim3 g2((T + wpb - 1) / wpb);
   const int per = (E + 31) / 32;
 #define MOSAIC_TOPK(P)                                                                                      \
-  router_topk_kernel<P><<<g2, 256, 0, stream>>>(partial, used, bias, T, E, top_k, n_group, topk_group,     \
+  router_topk_kernel<P><<<g2, 32 * wpb, 0, stream>>>(partial, used, bias, T, E, top_k, n_group, topk_group,     \
                                                 route_scale, norm, weights_out, idx_out, err)
   if (per <= 1)
     MOSAIC_TOPK(1);

@@ -118,10 +118,14 @@ class ExpertBank:
         if self.dn_scale.shape != (n, self.hidden, self.inter // 32):
             raise ValueError("scale_down must be [E, H, I/32]")
         self.has_shared = bool(has_shared)
+        if self.hidden % 256:
+            raise ValueError("hidden size must be a multiple of 256 (pairs of 128-row down blocks)")
+        # gate rows / up rows, and the two hidden halves of down, interleaved per
+        # (128-row block, K-tile): each GEMM stage loads a pair of adjacent tiles
         self.gu_sf = ops.prepack_scales(self.gu_scale, halves=2)
-        self.dn_sf = ops.prepack_scales(self.dn_scale, halves=1)
+        self.dn_sf = ops.prepack_scales(self.dn_scale, halves=2)
         self.gu_tiled = ops.repack_weights(self.gu_packed, halves=2)
-        self.dn_tiled = ops.repack_weights(self.dn_packed, halves=1)
+        self.dn_tiled = ops.repack_weights(self.dn_packed, halves=2)
         if not keep_packed:
             self.gu_packed = self.dn_packed = None
 

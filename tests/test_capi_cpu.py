@@ -44,7 +44,7 @@ def _dims(**kw):
     return d
 
 
-@pytest.mark.parametrize("bad", [dict(hidden=500), dict(inter=100), dict(n_experts=300), dict(top_k=9),
+@pytest.mark.parametrize("bad", [dict(hidden=500), dict(hidden=384), dict(inter=100), dict(n_experts=300), dict(top_k=9),
                                  dict(n_group=3), dict(topk_group=5), dict(n_group=8, topk_group=1, top_k=8),
                                  dict(act_mode=7), dict(tokens=0)])
 def test_workspace_bytes_rejects_bad_dims(bad):

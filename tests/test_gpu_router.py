@@ -96,3 +96,11 @@ def test_router_rejects_bad_shapes(ops):
         ops.router(x, wt, None, top_k=4, n_group=3, topk_group=1)  # 32 % 3 != 0
     with pytest.raises(ValueError):
         ops.router(x, wt, None, top_k=9)
+
+
+@pytest.mark.parametrize("e", [250, 100, 36, 33, 256])
+def test_router_ragged_expert_counts(ops, e):
+    """Expert counts that are not a multiple of 4 or of the per-lane width take
+    the scalar partial-sum path; all must match the oracle."""
+    x, wt, bias = make_gate_case(24, 1024, e, seed=300 + e)
+    _check(ops, x, wt, bias, 4, 1, 1, 1.0, max_ties=1)
