@@ -110,6 +110,71 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16*
   }
 }
 
+// Large batches: 128 tokens x 128 experts per CTA over all of K, 8 x 8 outputs
+// per thread (FMA-bound; every output still sums K in ascending order).
+constexpr int kBigT = 128;
+constexpr int kBigE = 128;
+constexpr int kBigK = 16;
+
+bool use_big_tiles(int T, int E, int num_sms) {
+  // one wave of 128 x 128 tiles on at least half the SMs beats split-K partials
+  return E % kBigE == 0 && 2 * ((T + kBigT - 1) / kBigT) * (E / kBigE) >= num_sms;
+}
+
+__global__ void __launch_bounds__(256) router_logits_big_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                const float* __restrict__ w, int T, int H, int E,
+                                                                float* __restrict__ logits) {
+  __shared__ __align__(16) float xs[2][kBigK][kBigT];
+  __shared__ __align__(16) float ws[2][kBigK][kBigE];
+  const int t0 = blockIdx.x * kBigT;
+  const int e0 = blockIdx.y * kBigE;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15;   // expert group: experts e0 + tx*4 + {0..3} and + 64
+  const int ty = tid >> 4;   // token group: tokens t0 + ty*4 + {0..3} and + 64
+  // loaders: 128 rows x 16 k per operand; thread loads row (tid >> 1), k half (tid & 1) * 8
+  const int lrow = tid >> 1;
+  const int lk = (tid & 1) * 8;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  float xv[8], wv[8];
+  load_slice(x, w, T, H, E, t0 + lrow, e0 + lrow, lk, xv, wv);
+  int buf = 0;
+  for (int k0 = 0; k0 < H; k0 += kBigK) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xs[buf][lk + i][lrow] = xv[i];
+      ws[buf][lk + i][lrow] = wv[i];
+    }
+    __syncthreads();
+    if (k0 + kBigK < H) load_slice(x, w, T, H, E, t0 + lrow, e0 + lrow, k0 + kBigK + lk, xv, wv);
+#pragma unroll
+    for (int kk = 0; kk < kBigK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&xs[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&xs[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&ws[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&ws[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    buf ^= 1;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (t >= T) continue;
+    float* row = logits + static_cast<size_t>(t) * E + e0;
+    *reinterpret_cast<float4*>(row + tx * 4) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    *reinterpret_cast<float4*>(row + 64 + tx * 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+  }
+}
+
 // Better candidate: larger value, ties to the lower expert id.
 __device__ __forceinline__ bool better(float v, int e, float v2, int e2) {
   return v > v2 || (v == v2 && e < e2);
@@ -126,7 +191,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   if (t >= T) return;
   float s[PER], sel[PER];
   // logits: partials added in split order; a lane's PER experts are contiguous,
-  // so each split is PER/4 16-byte loads, and four splits are in flight at once
+  // so each split is PER/4 16-byte loads, and eight splits are in flight at once
   float logit[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) logit[i] = 0.f;
@@ -136,14 +201,14 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   const size_t stride = static_cast<size_t>(T) * E;
   if (full) {
     int sp = 0;
-    for (; sp + 4 <= splits; sp += 4) {
-      float4 v[4][PER / 4 > 0 ? PER / 4 : 1];
+    for (; sp + 8 <= splits; sp += 8) {
+      float4 v[8][PER / 4 > 0 ? PER / 4 : 1];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u)
 #pragma unroll
         for (int q = 0; q < PER / 4; ++q) v[u][q] = *reinterpret_cast<const float4*>(pp + (sp + u) * stride + 4 * q);
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u)
 #pragma unroll
         for (int q = 0; q < PER / 4; ++q) {
           logit[4 * q + 0] += v[u][q].x;
@@ -181,6 +246,32 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   if (n_group > 1 && topk_group < n_group) {
     const int gsz = E / n_group;
     float my_gscore = -INFINITY;
+    const int lpg = gsz / PER;  // lanes per group when a lane's experts lie in one group
+    if (gsz % PER == 0 && lpg >= 1 && lpg <= 32 && (lpg & (lpg - 1)) == 0) {
+      // top-2 of this lane's experts, then a butterfly over the group's lanes
+      float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const float v = sel[i];
+        if (v > m1) {
+          m2 = m1;
+          m1 = v;
+        } else if (v > m2) {
+          m2 = v;
+        }
+      }
+      for (int o = 1; o < lpg; o <<= 1) {
+        const float o1 = __shfl_xor_sync(0xFFFFFFFFu, m1, o);
+        const float o2 = __shfl_xor_sync(0xFFFFFFFFu, m2, o);
+        const float n1 = fmaxf(m1, o1);
+        const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+        m1 = n1;
+        m2 = n2;
+      }
+      // lane g takes group g's score from the group's first lane
+      const float gs = __shfl_sync(0xFFFFFFFFu, m1 + m2, (lane * lpg) & 31);
+      if (lane < n_group) my_gscore = gs;
+    } else
     for (int g = 0; g < n_group; ++g) {
       float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
@@ -281,7 +372,10 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 
 }  // namespace
 
+// Split-K factor of the logits kernel for small batches: ~2 CTAs per SM with
+// K ranges of at least 256 (more splits only add partials for the top-k pass).
 int router_splits(int T, int H, int E, int num_sms) {
+  if (use_big_tiles(T, E, num_sms)) return 1;
   const int tiles = ((T + kTileT - 1) / kTileT) * ((E + kTileE - 1) / kTileE);
   int s = (2 * num_sms + tiles - 1) / tiles;
   const int smax = H / 256 > 0 ? H / 256 : 1;
@@ -296,8 +390,13 @@ cudaError_t launch_router(const void* x, const float* w, const float* bias, int 
   int kchunk = (H + splits - 1) / splits;
   kchunk = (kchunk + kTileK - 1) / kTileK * kTileK;
   const int used = (H + kchunk - 1) / kchunk;
-  dim3 g1((T + kTileT - 1) / kTileT, (E + kTileE - 1) / kTileE, used);
-  router_logits_kernel<<<g1, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), w, T, H, E, kchunk, partial);
+  if (splits == 1 && use_big_tiles(T, E, 148)) {
+    dim3 gb((T + kBigT - 1) / kBigT, E / kBigE);
+    router_logits_big_kernel<<<gb, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), w, T, H, E, partial);
+  } else {
+    dim3 g1((T + kTileT - 1) / kTileT, (E + kTileE - 1) / kTileE, used);
+    router_logits_kernel<<<g1, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), w, T, H, E, kchunk, partial);
+  }
   // warps per block: spread small batches over the SMs, pack large ones
   const int wpb = T >= 8 * 148 ? 8 : (T >= 4 * 148 ? 4 : (T >= 2 * 148 ? 2 : 1));
   dim3 g2((T + wpb - 1) / wpb);
