@@ -5,7 +5,9 @@
  * unless stated otherwise; every call is asynchronous on the given stream,
  * performs no host synchronisation and allocates nothing (the caller passes
  * outputs and a workspace sized by the matching *_workspace_bytes call), so
- * a whole layer can be captured in a CUDA graph.  Shapes, alignment and
+ * a whole layer can be captured in a CUDA graph.  The exceptions are the
+ * one-time set-up calls of the peer-memory exchange (mosaic_ep_region_alloc /
+ * _open / _close / _free), which allocate, map and synchronise.  Shapes, alignment and
  * ranges are checked on the host before anything is launched; a failed check
  * returns a MOSAIC_ERR_* code and launches nothing.  Errors found on the
  * device (an expert id out of range, a pipeline wait that timed out) are
@@ -257,6 +259,64 @@ MOSAIC_API int mosaic_moe_expert_rows(const mosaic_moe_dims* dims, int32_t rows,
  * matching mosaic_ep_dispatch.  y bf16 [T, H]. */
 MOSAIC_API int mosaic_ep_combine(const mosaic_moe_dims* dims, const void* partials, const void* workspace, void* y,
                                  mosaic_stream_t stream);
+
+/* ---- Device-driven exchange over NVLink peer memory ----------------------
+ * The same dispatch / return steps without host synchronisation, so a whole
+ * EP layer step can be captured in a CUDA graph.  Every rank owns one exchange
+ * region (mosaic_ep_region_bytes), allocated with mosaic_ep_region_alloc; the
+ * 64-byte IPC handles are shared between the ranks over any host channel and
+ * opened with mosaic_ep_region_open (plain CUDA IPC mappings of ordinary
+ * device memory; no multicast objects).  A region holds: the error word
+ * (first 4 bytes, read with mosaic_read_error), per-source flags stamped with
+ * a per-step epoch, the world x world row-count matrix, the receive rows and
+ * the return partials.  Flags use release / acquire at system scope; every
+ * wait is bounded (~2 s) and records MOSAIC_ERR_TIMEOUT in the region.
+ * Steps:
+ *   mosaic_ep_exchange_rows: publish dest_counts to every rank, wait for all
+ *     counts, write this rank's send rows into the owners' receive buffers
+ *     (rows from source s after those of sources < s), wait until every
+ *     source's rows have landed here.  The received row count is left in the
+ *     region (mosaic_ep_region_view) for mosaic_moe_expert_rows' rows_dev.
+ *   mosaic_ep_return_partials: write the partial of every received row back
+ *     into its source's return buffer at the row's send position, wait for
+ *     every owner's partials to land here.  The return buffer then holds the
+ *     rows mosaic_ep_combine reads (the caller puts the shared expert's
+ *     partials at rows [T*top_k, T*top_k + T)).
+ * All ranks must run the same steps in the same order. */
+#define MOSAIC_EP_MAX_WORLD 8
+
+typedef struct mosaic_ep_peers {
+  int32_t world;          /* ranks, 1..MOSAIC_EP_MAX_WORLD */
+  int32_t rank;           /* this rank */
+  int32_t max_recv_rows;  /* receive capacity: world * T_max * min(top_k, E / world) covers any routing */
+  int32_t max_send_rows;  /* T_max * top_k */
+  int32_t max_tokens;     /* T_max (shared-expert rows of the return buffer) */
+  int32_t hidden;         /* H */
+  int32_t partial_f32;    /* 1: fp32 partials (MOSAIC_ACT_BF16), 0: bf16 (MOSAIC_ACT_FP8) */
+  int32_t reserved;
+  void* regions[MOSAIC_EP_MAX_WORLD];  /* rank r's region as mapped in this process (own at [rank]) */
+} mosaic_ep_peers;
+
+MOSAIC_API size_t mosaic_ep_region_bytes(const mosaic_ep_peers* peers);
+MOSAIC_API int mosaic_ep_region_alloc(size_t bytes, void** region, uint8_t* ipc_handle64);
+MOSAIC_API int mosaic_ep_region_open(const uint8_t* ipc_handle64, void** peer_region);
+MOSAIC_API int mosaic_ep_region_close(void* peer_region);
+MOSAIC_API int mosaic_ep_region_free(void* region);
+/* Pointers into this rank's own region: receive rows [max_recv_rows][MOSAIC_EP_ROW_BYTES(H)],
+ * the device int32 received-row count, and the return buffer
+ * [max_send_rows + max_tokens][H] (fp32 or bf16). */
+MOSAIC_API int mosaic_ep_region_view(const mosaic_ep_peers* peers, void** recv_rows, int32_t** recv_count,
+                                     void** ret_partials);
+MOSAIC_API int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void* send_rows, const int32_t* dest_counts,
+                                       mosaic_stream_t stream);
+MOSAIC_API int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials, mosaic_stream_t stream);
+/* mosaic_moe_expert_rows with the row count read on the device from rows_dev
+ * (at most max_rows; the workspace is sized for max_rows). */
+MOSAIC_API int mosaic_moe_expert_rows_dev(const mosaic_moe_dims* dims, int32_t max_rows, const int32_t* rows_dev,
+                                          const void* x_rows, int32_t ldx, const int32_t* ids, const float* weights,
+                                          int32_t meta_stride, int32_t default_id, const mosaic_expert_bank* bank,
+                                          void* partials, void* workspace, size_t workspace_bytes,
+                                          mosaic_stream_t stream);
 
 /* Device error word of a workspace used by mosaic_moe_* (0 = none).
  * Synchronises the stream.  reset != 0 clears it afterwards. */

@@ -55,6 +55,15 @@ EXPORTED = (
     "mosaic_moe_expert_rows_workspace_bytes",
     "mosaic_moe_expert_rows",
     "mosaic_ep_combine",
+    "mosaic_ep_region_bytes",
+    "mosaic_ep_region_alloc",
+    "mosaic_ep_region_open",
+    "mosaic_ep_region_close",
+    "mosaic_ep_region_free",
+    "mosaic_ep_region_view",
+    "mosaic_ep_exchange_rows",
+    "mosaic_ep_return_partials",
+    "mosaic_moe_expert_rows_dev",
     "mosaic_read_error",
 )
 
@@ -82,6 +91,23 @@ class ExpertBankC(ctypes.Structure):
         ("gu_sf", ctypes.c_void_p),
         ("dn_tiled", ctypes.c_void_p),
         ("dn_sf", ctypes.c_void_p),
+    ]
+
+
+EP_MAX_WORLD = 8  # include/mosaic_moe.h MOSAIC_EP_MAX_WORLD
+
+
+class EpPeersC(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("max_recv_rows", ctypes.c_int32),
+        ("max_send_rows", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("partial_f32", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("regions", ctypes.c_void_p * EP_MAX_WORLD),
     ]
 
 
@@ -118,6 +144,17 @@ _SIGS = {
     "mosaic_moe_expert_rows": ([ctypes.POINTER(MoEDims), _I, _P, _I, _P, _P, _I, _I, ctypes.POINTER(ExpertBankC), _P,
                                 _P, _SZ, _P], ctypes.c_int),
     "mosaic_ep_combine": ([ctypes.POINTER(MoEDims), _P, _P, _P, _P], ctypes.c_int),
+    "mosaic_ep_region_bytes": ([ctypes.POINTER(EpPeersC)], _SZ),
+    "mosaic_ep_region_alloc": ([_SZ, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_uint8)], ctypes.c_int),
+    "mosaic_ep_region_open": ([ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mosaic_ep_region_close": ([_P], ctypes.c_int),
+    "mosaic_ep_region_free": ([_P], ctypes.c_int),
+    "mosaic_ep_region_view": ([ctypes.POINTER(EpPeersC), ctypes.POINTER(ctypes.c_void_p),
+                               ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mosaic_ep_exchange_rows": ([ctypes.POINTER(EpPeersC), _P, _P, _P], ctypes.c_int),
+    "mosaic_ep_return_partials": ([ctypes.POINTER(EpPeersC), _P, _P], ctypes.c_int),
+    "mosaic_moe_expert_rows_dev": ([ctypes.POINTER(MoEDims), _I, _P, _P, _I, _P, _P, _I, _I,
+                                    ctypes.POINTER(ExpertBankC), _P, _P, _SZ, _P], ctypes.c_int),
     "mosaic_read_error": ([_P, _I, ctypes.POINTER(ctypes.c_int32), _P], ctypes.c_int),
 }
 

@@ -5,6 +5,7 @@
 // synchronises a stream (except mosaic_read_error, which exists to do so).
 // cuTensorMapEncodeTiled is resolved through cudaGetDriverEntryPoint so the
 // library does not link libcuda and loads on hosts without a GPU.
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -275,7 +276,7 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
 
-  if (launch_rows_quant(x, T, H, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos,
+  if (launch_rows_quant(x, T, nullptr, H, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos,
                         ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), stream) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
   if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
@@ -320,6 +321,58 @@ mosaic_moe_dims rows_dims(const mosaic_moe_dims* d, int rows) {
 static __device__ __align__(256) uint8_t g_router_scratch[MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES];
 
 namespace {
+
+// Per-row expert pass; rows_dev (optional) holds the row count on the device
+// (at most `rows`, which sizes the workspace and the launches).
+int expert_rows_impl(const mosaic_moe_dims* dims, int32_t rows, const int32_t* rows_dev, const void* x_rows,
+                     int32_t ldx, const int32_t* ids, const float* weights, int32_t meta_stride, int32_t default_id,
+                     const mosaic_expert_bank* bank, void* partials, void* workspace, size_t workspace_bytes,
+                     mosaic_stream_t stream) {
+  if (!dims) return MOSAIC_ERR_SHAPE;
+  if (rows < 0) return MOSAIC_ERR_SHAPE;
+  if (rows == 0) return MOSAIC_OK;
+  if (dims->n_experts > 256) return MOSAIC_ERR_UNSUPPORTED;
+  const mosaic_moe_dims r = rows_dims(dims, rows);
+  int st = check_rows_dims(&r);
+  if (st) return st;
+  if (!x_rows || !partials || !workspace) return MOSAIC_ERR_SHAPE;
+  if (ldx < dims->hidden || ldx % 8 || ((ids || weights) && meta_stride < 1)) return MOSAIC_ERR_SHAPE;
+  if (!ids && (default_id < 0 || default_id >= r.n_experts)) return MOSAIC_ERR_RANGE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(x_rows, 16) || !aligned(partials, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  if ((ids && !aligned(ids, 4)) || (weights && !aligned(weights, 4)) || (rows_dev && !aligned(rows_dev, 4)))
+    return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(&r, true);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  int64_t* idx = reinterpret_cast<int64_t*>(ws + w.row_idx);
+  float* wt = reinterpret_cast<float*>(ws + w.row_w);
+  if (launch_rows_meta(ids, weights, meta_stride, rows, rows_dev, r.n_experts, default_id, idx, wt,
+                       reinterpret_cast<int*>(ws + w.err), s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  LayoutParams lp{};
+  lp.idx = idx;
+  lp.weights = wt;
+  lp.T = rows;
+  lp.k = 1;
+  lp.E = r.n_experts;
+  lp.with_shared = 0;
+  fill_layout(lp, w, ws);
+  lp.T_dev = rows_dev;
+  lp.row_sorted = nullptr;
+  if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  const bool hilo = r.act_mode == MOSAIC_ACT_BF16;
+  if (launch_rows_quant(x_rows, rows, rows_dev, r.hidden, ldx, 1, lp.row_of, -1, hilo ? 1 : 0, w.R_pad, lp.row_tile,
+                        lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  // with k = 1 the packed row of input row t is sorted row row_of[t], and
+  // row_token[sorted row] = t: partials land in input row order
+  return run_gemms(&r, w, ws, lp, bank, dims->has_shared ? dims->n_experts : -1, lp.row_token, partials, s,
+                   nullptr);
+}
 
 // Argument checks shared by mosaic_router and mosaic_router_noalloc.
 int router_args_ok(const void* x, const float* weight, int32_t T, int32_t H, int32_t E, int32_t top_k,
@@ -576,48 +629,145 @@ int mosaic_moe_expert_rows(const mosaic_moe_dims* dims, int32_t rows, const void
                            const int32_t* ids, const float* weights, int32_t meta_stride, int32_t default_id,
                            const mosaic_expert_bank* bank, void* partials, void* workspace, size_t workspace_bytes,
                            mosaic_stream_t stream) {
-  if (!dims) return MOSAIC_ERR_SHAPE;
-  if (rows < 0) return MOSAIC_ERR_SHAPE;
-  if (rows == 0) return MOSAIC_OK;
-  if (dims->n_experts > 256) return MOSAIC_ERR_UNSUPPORTED;
-  const mosaic_moe_dims r = rows_dims(dims, rows);
-  int st = check_rows_dims(&r);
-  if (st) return st;
-  if (!x_rows || !partials || !workspace) return MOSAIC_ERR_SHAPE;
-  if (ldx < dims->hidden || ldx % 8 || ((ids || weights) && meta_stride < 1)) return MOSAIC_ERR_SHAPE;
-  if (!ids && (default_id < 0 || default_id >= r.n_experts)) return MOSAIC_ERR_RANGE;
-  st = check_bank(bank);
-  if (st) return st;
-  if (!aligned(x_rows, 16) || !aligned(partials, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
-  if ((ids && !aligned(ids, 4)) || (weights && !aligned(weights, 4))) return MOSAIC_ERR_ALIGN;
-  const WsPlan w = plan_ws(&r, true);
-  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
-  int64_t* idx = reinterpret_cast<int64_t*>(ws + w.row_idx);
-  float* wt = reinterpret_cast<float*>(ws + w.row_w);
-  if (launch_rows_meta(ids, weights, meta_stride, rows, r.n_experts, default_id, idx, wt,
-                       reinterpret_cast<int*>(ws + w.err), s) != cudaSuccess)
+  return expert_rows_impl(dims, rows, nullptr, x_rows, ldx, ids, weights, meta_stride, default_id, bank, partials,
+                          workspace, workspace_bytes, stream);
+}
+
+int mosaic_moe_expert_rows_dev(const mosaic_moe_dims* dims, int32_t max_rows, const int32_t* rows_dev,
+                               const void* x_rows, int32_t ldx, const int32_t* ids, const float* weights,
+                               int32_t meta_stride, int32_t default_id, const mosaic_expert_bank* bank,
+                               void* partials, void* workspace, size_t workspace_bytes, mosaic_stream_t stream) {
+  if (!rows_dev) return MOSAIC_ERR_SHAPE;
+  return expert_rows_impl(dims, max_rows, rows_dev, x_rows, ldx, ids, weights, meta_stride, default_id, bank,
+                          partials, workspace, workspace_bytes, stream);
+}
+
+// ------------------------------------------------- peer-memory exchange ---
+
+namespace {
+
+int check_peers(const mosaic_ep_peers* p) {
+  if (!p || p->world < 1 || p->world > MOSAIC_EP_MAX_WORLD || p->rank < 0 || p->rank >= p->world)
+    return MOSAIC_ERR_SHAPE;
+  if (p->max_recv_rows < 1 || p->max_send_rows < 1 || p->max_tokens < 1) return MOSAIC_ERR_SHAPE;
+  if (p->hidden < 256 || p->hidden % 256) return MOSAIC_ERR_SHAPE;
+  return MOSAIC_OK;
+}
+
+size_t ep_recv_bytes(const mosaic_ep_peers* p) {
+  return static_cast<size_t>(p->max_recv_rows) * MOSAIC_EP_ROW_BYTES(p->hidden);
+}
+
+int ep_ret_row_bytes(const mosaic_ep_peers* p) { return p->hidden * (p->partial_f32 ? 4 : 2); }
+
+EpPeersDev ep_dev(const mosaic_ep_peers* p) {
+  EpPeersDev d{};
+  d.world = p->world;
+  d.rank = p->rank;
+  d.max_recv_rows = p->max_recv_rows;
+  d.row_bytes = static_cast<int>(MOSAIC_EP_ROW_BYTES(p->hidden));
+  d.ret_row_bytes = ep_ret_row_bytes(p);
+  d.recv_off = kEpHeaderBytes;
+  d.ret_off = up256(kEpHeaderBytes + ep_recv_bytes(p));
+  for (int r = 0; r < p->world; ++r) d.regions[r] = static_cast<uint8_t*>(p->regions[r]);
+  return d;
+}
+
+int check_regions(const mosaic_ep_peers* p) {
+  for (int r = 0; r < p->world; ++r)
+    if (!p->regions[r] || !aligned(p->regions[r], 256)) return MOSAIC_ERR_SHAPE;
+  return MOSAIC_OK;
+}
+
+}  // namespace
+
+size_t mosaic_ep_region_bytes(const mosaic_ep_peers* peers) {
+  if (check_peers(peers) != MOSAIC_OK) return 0;
+  const size_t ret_rows = static_cast<size_t>(peers->max_send_rows) + peers->max_tokens;
+  return up256(kEpHeaderBytes + ep_recv_bytes(peers)) + ret_rows * ep_ret_row_bytes(peers);
+}
+
+int mosaic_ep_region_alloc(size_t bytes, void** region, uint8_t* ipc_handle64) {
+  if (!region || !ipc_handle64 || bytes < kEpHeaderBytes) return MOSAIC_ERR_SHAPE;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  // zeroed: epochs and flags start at 0 on every rank
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
     return MOSAIC_ERR_CUDA;
-  LayoutParams lp{};
-  lp.idx = idx;
-  lp.weights = wt;
-  lp.T = rows;
-  lp.k = 1;
-  lp.E = r.n_experts;
-  lp.with_shared = 0;
-  fill_layout(lp, w, ws);
-  lp.row_sorted = nullptr;
-  if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
-  const bool hilo = r.act_mode == MOSAIC_ACT_BF16;
-  if (launch_rows_quant(x_rows, rows, r.hidden, ldx, 1, lp.row_of, -1, hilo ? 1 : 0, w.R_pad, lp.row_tile,
-                        lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), s) != cudaSuccess)
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
     return MOSAIC_ERR_CUDA;
-  // with k = 1 the packed row of input row t is sorted row row_of[t], and
-  // row_token[sorted row] = t: partials land in input row order
-  return run_gemms(&r, w, ws, lp, bank, dims->has_shared ? dims->n_experts : -1, lp.row_token, partials, s,
-                   nullptr);
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  memcpy(ipc_handle64, &h, 64);
+  *region = p;
+  return MOSAIC_OK;
+}
+
+int mosaic_ep_region_open(const uint8_t* ipc_handle64, void** peer_region) {
+  if (!ipc_handle64 || !peer_region) return MOSAIC_ERR_SHAPE;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle64, 64);
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  *peer_region = p;
+  return MOSAIC_OK;
+}
+
+int mosaic_ep_region_close(void* peer_region) {
+  if (!peer_region) return MOSAIC_ERR_SHAPE;
+  return cudaIpcCloseMemHandle(peer_region) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_ep_region_free(void* region) {
+  if (!region) return MOSAIC_ERR_SHAPE;
+  return cudaFree(region) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_ep_region_view(const mosaic_ep_peers* peers, void** recv_rows, int32_t** recv_count, void** ret_partials) {
+  int st = check_peers(peers);
+  if (st) return st;
+  uint8_t* own = static_cast<uint8_t*>(peers->regions[peers->rank]);
+  if (!own) return MOSAIC_ERR_SHAPE;
+  const EpPeersDev d = ep_dev(peers);
+  if (recv_rows) *recv_rows = own + d.recv_off;
+  if (recv_count) *recv_count = &reinterpret_cast<EpRegionHeader*>(own)->recv_count;
+  if (ret_partials) *ret_partials = own + d.ret_off;
+  return MOSAIC_OK;
+}
+
+int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void* send_rows, const int32_t* dest_counts,
+                            mosaic_stream_t stream) {
+  int st = check_peers(peers);
+  if (st) return st;
+  st = check_regions(peers);
+  if (st) return st;
+  if (!send_rows || !dest_counts) return MOSAIC_ERR_SHAPE;
+  if (!aligned(send_rows, 16) || !aligned(dest_counts, 4)) return MOSAIC_ERR_ALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  return launch_ep_exchange_rows(ep_dev(peers), send_rows, dest_counts, sms, reinterpret_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? MOSAIC_OK
+             : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials, mosaic_stream_t stream) {
+  int st = check_peers(peers);
+  if (st) return st;
+  st = check_regions(peers);
+  if (st) return st;
+  if (!partials) return MOSAIC_ERR_SHAPE;
+  if (!aligned(partials, 16)) return MOSAIC_ERR_ALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  return launch_ep_return_partials(ep_dev(peers), partials, sms, reinterpret_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? MOSAIC_OK
+             : MOSAIC_ERR_CUDA;
 }
 
 int mosaic_ep_combine(const mosaic_moe_dims* dims, const void* partials, const void* workspace, void* y,

@@ -64,9 +64,10 @@ __global__ void ep_dest_counts_kernel(const int* __restrict__ offsets, int E_loc
 }
 
 __global__ void rows_meta_kernel(const int32_t* __restrict__ ids, const float* __restrict__ weights, int stride, int R,
-                                 int E, int default_id, int64_t* __restrict__ idx, float* __restrict__ w, int* err) {
+                                 const int* __restrict__ rows_dev, int E, int default_id, int64_t* __restrict__ idx,
+                                 float* __restrict__ w, int* err) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= R) return;
+  if (r >= R || (rows_dev && r >= *rows_dev)) return;
   int e = ids ? ids[static_cast<size_t>(r) * stride] : default_id;
   float wt = weights ? weights[static_cast<size_t>(r) * stride] : 1.0f;
   if (e < 0 || e >= E) {
@@ -76,6 +77,169 @@ __global__ void rows_meta_kernel(const int32_t* __restrict__ ids, const float* _
   }
   idx[r] = e;
   w[r] = wt;
+}
+
+// ------------------------------------------------- peer-memory exchange ---
+// Rank r's region holds rows and partials that other ranks write with plain
+// stores through their CUDA IPC mapping of it (NVLink peer memory).  A writer
+// makes its stores visible (fence at system scope) before it stamps the
+// reader's flag with the step's epoch (release); the reader waits on its own
+// flags (acquire).  Waits are bounded; a timeout records MOSAIC_ERR_TIMEOUT in
+// the waiting rank's region and the kernel returns.
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// true once *flag has reached epoch (epochs only grow; the signed difference
+// handles wrap-around)
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch) {
+  if (static_cast<int>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const long long t0 = clock64();
+  while (static_cast<int>(ld_acquire_sys(flag) - epoch) < 0) {
+    if (clock64() - t0 > MOSAIC_WAIT_CYCLES) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+__device__ __forceinline__ EpRegionHeader* hdr_of(const EpPeersDev& P, int r) {
+  return reinterpret_cast<EpRegionHeader*>(P.regions[r]);
+}
+
+// One CTA: start a step (epoch + 1), publish this rank's row counts to every
+// rank, wait for every rank's counts, record the rows this rank receives.
+__global__ void ep_counts_kernel(const EpPeersDev P, const int* __restrict__ dest_counts) {
+  __shared__ uint32_t epoch;
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  if (threadIdx.x == 0) {
+    epoch = own->epoch + 1;
+    own->epoch = epoch;
+  }
+  __syncthreads();
+  const int p = threadIdx.x;
+  if (p < P.world) {
+    EpRegionHeader* ph = hdr_of(P, p);
+    for (int d = 0; d < P.world; ++d) ph->counts[P.rank][d] = dest_counts[d];
+    __threadfence_system();
+    st_release_sys(&ph->count_flag[P.rank], epoch);
+  }
+  __syncthreads();
+  if (p < P.world && !wait_epoch(&own->count_flag[p], epoch)) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    int total = 0;
+    for (int s = 0; s < P.world; ++s) total += own->counts[s][P.rank];
+    if (total > P.max_recv_rows) set_error(&own->err, MOSAIC_ERR_WORKSPACE);
+    own->recv_count = min(total, P.max_recv_rows);
+  }
+}
+
+// Count-matrix geometry of a step, from this rank's copy of the matrix.
+struct EpGeom {
+  int send_start[MOSAIC_EP_MAX_WORLD + 1];  // this rank's send rows for destination d start here
+  int dest_off[MOSAIC_EP_MAX_WORLD];        // ... and land at this receive row of d
+  int recv_start[MOSAIC_EP_MAX_WORLD + 1];  // rows received from source s start here
+  int src_pos[MOSAIC_EP_MAX_WORLD];         // ... and sit at this send row of s
+  bool fits[MOSAIC_EP_MAX_WORLD];           // destination d's receive buffer holds its rows
+};
+
+__device__ __forceinline__ void ep_geometry(const EpPeersDev& P, const EpRegionHeader* own, EpGeom& g) {
+  const int W = P.world, me = P.rank;
+  g.send_start[0] = 0;
+  g.recv_start[0] = 0;
+  for (int d = 0; d < W; ++d) {
+    g.send_start[d + 1] = g.send_start[d] + own->counts[me][d];
+    g.recv_start[d + 1] = g.recv_start[d] + own->counts[d][me];
+    int off = 0, tot = 0;
+    for (int s = 0; s < W; ++s) {
+      if (s < me) off += own->counts[s][d];
+      tot += own->counts[s][d];
+    }
+    g.dest_off[d] = off;
+    g.fits[d] = tot <= P.max_recv_rows;
+    int pos = 0;
+    for (int dd = 0; dd < me; ++dd) pos += own->counts[d][dd];
+    g.src_pos[d] = pos;  // for d as a source: its send rows for this rank start here
+  }
+}
+
+// Grid-stride copy of this rank's send rows into the owners' receive buffers;
+// the last CTA to finish stamps every owner's data flag.
+__global__ void __launch_bounds__(256) ep_send_kernel(const EpPeersDev P, const uint4* __restrict__ send) {
+  __shared__ EpGeom g;
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  if (threadIdx.x == 0) ep_geometry(P, own, g);
+  __syncthreads();
+  const uint32_t epoch = own->epoch;
+  const int cpr = P.row_bytes / 16;
+  const long long total = static_cast<long long>(g.send_start[P.world]) * cpr;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cpr), c = static_cast<int>(i - static_cast<long long>(r) * cpr);
+    int d = 0;
+    while (r >= g.send_start[d + 1]) ++d;
+    if (!g.fits[d]) continue;
+    uint4* dst = reinterpret_cast<uint4*>(P.regions[d] + P.recv_off) +
+                 static_cast<size_t>(g.dest_off[d] + r - g.send_start[d]) * cpr + c;
+    *dst = send[static_cast<size_t>(r) * cpr + c];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(&own->send_done, 1u) == gridDim.x - 1) {
+      own->send_done = 0;
+      __threadfence_system();
+      for (int d = 0; d < P.world; ++d) st_release_sys(&hdr_of(P, d)->data_flag[P.rank], epoch);
+    }
+  }
+}
+
+// Grid-stride copy of the partial of every received row back to its source's
+// return buffer; the last CTA stamps every source's return flag.
+__global__ void __launch_bounds__(256) ep_return_kernel(const EpPeersDev P, const uint4* __restrict__ partials) {
+  __shared__ EpGeom g;
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  if (threadIdx.x == 0) ep_geometry(P, own, g);
+  __syncthreads();
+  const uint32_t epoch = own->epoch;
+  const int cpr = P.ret_row_bytes / 16;
+  const int rows = own->recv_count;
+  const long long total = static_cast<long long>(rows) * cpr;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cpr), c = static_cast<int>(i - static_cast<long long>(r) * cpr);
+    int s = 0;
+    while (r >= g.recv_start[s + 1]) ++s;
+    uint4* dst = reinterpret_cast<uint4*>(P.regions[s] + P.ret_off) +
+                 static_cast<size_t>(g.src_pos[s] + r - g.recv_start[s]) * cpr + c;
+    *dst = partials[static_cast<size_t>(r) * cpr + c];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(&own->ret_done, 1u) == gridDim.x - 1) {
+      own->ret_done = 0;
+      __threadfence_system();
+      for (int s = 0; s < P.world; ++s) st_release_sys(&hdr_of(P, s)->ret_flag[P.rank], epoch);
+    }
+  }
+}
+
+// One CTA: wait until every rank stamped this rank's flags (data or return) with the step's epoch.
+__global__ void ep_wait_kernel(const EpPeersDev P, int which) {
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  const uint32_t epoch = own->epoch;
+  const int p = threadIdx.x;
+  if (p < P.world) {
+    const uint32_t* f = (which == 0) ? &own->data_flag[p] : &own->ret_flag[p];
+    if (!wait_epoch(f, epoch)) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
+  }
 }
 
 }  // namespace
@@ -93,10 +257,24 @@ cudaError_t launch_ep_pack(const void* x, int H, int A, int E, int E_local, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_rows_meta(const int32_t* ids, const float* weights, int stride, int R, int E, int default_id,
-                             int64_t* idx, float* w, int* err, cudaStream_t stream) {
+cudaError_t launch_rows_meta(const int32_t* ids, const float* weights, int stride, int R, const int* rows_dev, int E,
+                             int default_id, int64_t* idx, float* w, int* err, cudaStream_t stream) {
   if (R <= 0) return cudaSuccess;
-  rows_meta_kernel<<<(R + 255) / 256, 256, 0, stream>>>(ids, weights, stride, R, E, default_id, idx, w, err);
+  rows_meta_kernel<<<(R + 255) / 256, 256, 0, stream>>>(ids, weights, stride, R, rows_dev, E, default_id, idx, w, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_exchange_rows(const EpPeersDev& P, const void* send_rows, const int* dest_counts, int sms,
+                                    cudaStream_t stream) {
+  ep_counts_kernel<<<1, 32, 0, stream>>>(P, dest_counts);
+  ep_send_kernel<<<2 * sms, 256, 0, stream>>>(P, static_cast<const uint4*>(send_rows));
+  ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return_partials(const EpPeersDev& P, const void* partials, int sms, cudaStream_t stream) {
+  ep_return_kernel<<<2 * sms, 256, 0, stream>>>(P, static_cast<const uint4*>(partials));
+  ep_wait_kernel<<<1, 32, 0, stream>>>(P, 1);
   return cudaGetLastError();
 }
 

@@ -53,6 +53,7 @@ struct LayoutParams {
   const float* weights;   // [T][k] or null (1.0)
   int T, k, E;
   int with_shared;
+  const int* T_dev;          // optional: token count read on the device (<= T)
   int tt_routed, tt_shared;  // token rows per GEMM tile
   int max_tiles;
   int* counts;            // [E+1]
@@ -79,9 +80,9 @@ cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max
 // hilo: hi/lo planes with per-32 scales; else act_quant_ref per 128.  Rows are
 // stored K-tile-major, xq[H/128][planes][R_pad][128 B]; scales go straight into
 // the token tile's MMA scale chunks sft [tile][H/128][128 words].
-cudaError_t launch_rows_quant(const void* x, int T, int H, int ldx, int k, const int* row_of, int shared_base,
-                              int hilo, int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq,
-                              uint32_t* sft, cudaStream_t stream);
+cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int ldx, int k, const int* row_of,
+                              int shared_base, int hilo, int R_pad, const int* row_tile, const int* row_pos,
+                              uint8_t* xq, uint32_t* sft, cudaStream_t stream);
 cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
 cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
 // halves = 2 interleaves the two row halves of each matrix (gate rows, up rows)
@@ -102,8 +103,36 @@ cudaError_t launch_ep_pack(const void* x, int H, int A, int E, int E_local, int 
 // Per-row expert ids / weights with an element stride (ids null: every row
 // uses default_id; weights null: 1.0) -> int64 idx [R], fp32 w [R]; ids outside
 // [0, E) are recorded as MOSAIC_ERR_RANGE and replaced by 0 with weight 0.
-cudaError_t launch_rows_meta(const int32_t* ids, const float* weights, int stride, int R, int E, int default_id,
-                             int64_t* idx, float* w, int* err, cudaStream_t stream);
+// rows_dev (optional): only the first *rows_dev rows are read.
+cudaError_t launch_rows_meta(const int32_t* ids, const float* weights, int stride, int R, const int* rows_dev, int E,
+                             int default_id, int64_t* idx, float* w, int* err, cudaStream_t stream);
+
+// Exchange region of one rank (peer-memory EP): this header, then the receive
+// rows, then the return partials.
+struct EpRegionHeader {
+  int err;                   // device error word (first: mosaic_read_error reads it)
+  int err_pad[3];            // mosaic_read_error's reset clears 16 bytes: nothing else lives here
+  uint32_t epoch;            // step counter, advanced by the count exchange
+  uint32_t send_done;        // CTAs of the row copy that finished (last one signals)
+  uint32_t ret_done;         // same for the partial copy
+  int recv_count;            // rows received in the current step
+  int pad[3];
+  uint32_t count_flag[MOSAIC_EP_MAX_WORLD];  // [source]: its counts of this epoch are here
+  uint32_t data_flag[MOSAIC_EP_MAX_WORLD];   // [source]: its rows of this epoch are here
+  uint32_t ret_flag[MOSAIC_EP_MAX_WORLD];    // [owner]: its partials of this epoch are here
+  int counts[MOSAIC_EP_MAX_WORLD][MOSAIC_EP_MAX_WORLD];  // [source][destination] rows
+};
+constexpr size_t kEpHeaderBytes = 1024;
+static_assert(sizeof(EpRegionHeader) <= kEpHeaderBytes, "EP region header");
+
+struct EpPeersDev {
+  int world, rank, max_recv_rows, row_bytes, ret_row_bytes;
+  size_t recv_off, ret_off;  // byte offsets of the receive rows / return partials in a region
+  uint8_t* regions[MOSAIC_EP_MAX_WORLD];
+};
+cudaError_t launch_ep_exchange_rows(const EpPeersDev& P, const void* send_rows, const int* dest_counts,
+                                    int sms, cudaStream_t stream);
+cudaError_t launch_ep_return_partials(const EpPeersDev& P, const void* partials, int sms, cudaStream_t stream);
 
 // ---- combine (combine.cu)
 cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,

@@ -45,7 +45,8 @@ struct LayoutExtra {
 
 __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtra x) {
   extern __shared__ int sm[];
-  const int E = p.E, T = p.T, k = p.k;
+  const int E = p.E, k = p.k;
+  const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;  // device-side count (EP receive side)
   const int NE = E + (p.with_shared ? 1 : 0);
   int* hist = sm;                      // NE
   int* offs = hist + NE;               // NE + 1

@@ -91,13 +91,14 @@ __device__ __forceinline__ uint32_t gather_word(int e) {
 // and writes them to every packed row of the token; the scale words go into the
 // row's token-tile chunk (word (n%32)*4 + n/32 of chunk [tile][kt]; the lo plane
 // of a bf16 tile sits at rows rpad + n of the same chunk).
-__global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
-                                                         int ldx, int k,
+__global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T,
+                                                         const int* __restrict__ T_dev, int H, int ldx, int k,
                                                          const int* __restrict__ row_of, int shared_base, int hilo,
                                                          int R_pad, const int* __restrict__ row_tile,
                                                          const int* __restrict__ row_pos, uint8_t* __restrict__ xq,
                                                          uint32_t* __restrict__ sft) {
   const int t = blockIdx.x;
+  if (T_dev && t >= *T_dev) return;  // rows beyond the device-side count (uniform per block)
   const int lane = threadIdx.x & 31;
   const int k0 = blockIdx.y * 1024 + (threadIdx.x >> 5) * 256 + lane * 8;
   const bool valid = k0 < H;
@@ -289,11 +290,12 @@ cudaError_t launch_repack_weights(const uint8_t* packed, int n_mats, int rows, i
   return cudaGetLastError();
 }
 
-cudaError_t launch_rows_quant(const void* x, int T, int H, int ldx, int k, const int* row_of, int shared_base,
+cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int ldx, int k, const int* row_of,
+                              int shared_base,
                               int hilo, int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq,
                               uint32_t* sft, cudaStream_t stream) {
   dim3 grid(T, (H + 1023) / 1024);
-  rows_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, ldx, k, row_of,
+  rows_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k, row_of,
                                                shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
   return cudaGetLastError();
 }

@@ -68,6 +68,16 @@ class _Buffer:
         return self.t
 
 
+class _RawOut:
+    """A raw device address passed where a tensor output is expected."""
+
+    def __init__(self, ptr: int):
+        self._ptr = ptr
+
+    def data_ptr(self) -> int:
+        return self._ptr
+
+
 class CudaEPKernels:
     """The CUDA kernels of one expert-parallel rank, through the C ABI."""
 
@@ -75,6 +85,13 @@ class CudaEPKernels:
         self._ws_dispatch = _Buffer()
         self._ws_rows = _Buffer()
         self._ws_shared = _Buffer()
+        self._part = None
+
+    def p2p_partials(self, rows: int, h: int, dtype, device) -> torch.Tensor:
+        """Partials of the received rows (peer exchange), kept across steps."""
+        if self._part is None or self._part.shape != (rows, h) or self._part.dtype != dtype:
+            self._part = torch.empty(rows, h, dtype=dtype, device=device)
+        return self._part
 
     def route(self, router: Router, x: torch.Tensor):
         return router(x)
@@ -123,6 +140,86 @@ class CudaEPKernels:
         return ops.read_error(ws)
 
 
+class PeerExchange:
+    """Exchange regions of every rank of a group, mapped into this process.
+
+    Each rank allocates one region (``mosaic_ep_region_alloc``), the 64-byte
+    CUDA IPC handles are shared with ``all_gather_object`` and the peers'
+    regions are opened (plain IPC mappings, no multicast).  The regions hold
+    the flags, the count matrix, the receive rows and the return partials of
+    the device-driven exchange (``mosaic_ep_exchange_rows`` /
+    ``mosaic_ep_return_partials``).  Capacity: ``max_tokens`` tokens per rank;
+    the receive side is sized for any routing.
+    """
+
+    def __init__(self, *, group=None, max_tokens: int, top_k: int, n_experts: int, hidden: int,
+                 partial_f32: bool):
+        lib = C.lib()
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > C.EP_MAX_WORLD:
+            raise ValueError(f"peer exchange supports at most {C.EP_MAX_WORLD} ranks")
+        e_local = n_experts // self.world
+        self.max_tokens = max_tokens
+        self.hidden = hidden
+        pe = C.EpPeersC()
+        pe.world, pe.rank = self.world, self.rank
+        pe.max_recv_rows = self.world * max_tokens * min(top_k, e_local)
+        pe.max_send_rows = max_tokens * top_k
+        pe.max_tokens = max_tokens
+        pe.hidden = hidden
+        pe.partial_f32 = int(bool(partial_f32))
+        nbytes = lib.mosaic_ep_region_bytes(ctypes.byref(pe))
+        if nbytes == 0:
+            raise ValueError("invalid peer-exchange geometry")
+        region = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        C.check(lib.mosaic_ep_region_alloc(nbytes, ctypes.byref(region), handle), "mosaic_ep_region_alloc")
+        self._own = region.value
+        self._opened = []
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        for r in range(self.world):
+            if r == self.rank:
+                pe.regions[r] = self._own
+                continue
+            h = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+            ptr = ctypes.c_void_p()
+            C.check(lib.mosaic_ep_region_open(h, ctypes.byref(ptr)), "mosaic_ep_region_open")
+            pe.regions[r] = ptr.value
+            self._opened.append(ptr.value)
+        if self.world > 1:
+            dist.barrier(group=group)
+        self.peers = pe
+        recv, cnt, ret = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        C.check(lib.mosaic_ep_region_view(ctypes.byref(pe), ctypes.byref(recv), ctypes.byref(cnt), ctypes.byref(ret)),
+                "mosaic_ep_region_view")
+        self.recv_rows, self.recv_count, self.ret_partials = recv.value, cnt.value, ret.value
+        self.max_recv_rows = pe.max_recv_rows
+
+    def error(self) -> int:
+        """Device error word of this rank's region (synchronises the stream)."""
+        code = ctypes.c_int32(0)
+        C.check(C.lib().mosaic_read_error(ctypes.c_void_p(self._own), 1, ctypes.byref(code), ops._stream()),
+                "mosaic_read_error")
+        return int(code.value)
+
+    def close(self) -> None:
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no rank may still write into a region being released
+        lib = C.lib()
+        for ptr in self._opened:
+            lib.mosaic_ep_region_close(ctypes.c_void_p(ptr))
+        lib.mosaic_ep_region_free(ctypes.c_void_p(self._own))
+        self._own, self._opened = None, []
+
+
 class ExpertParallelMoELayer(nn.Module):
     """``MoELayer`` with its routed experts sharded over the ranks of ``group``.
 
@@ -132,8 +229,14 @@ class ExpertParallelMoELayer(nn.Module):
     returns their layer output; every rank of the group must call it.
     """
 
-    def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None):
+    def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None, exchange: str = "nccl",
+                 max_tokens: int | None = None):
         super().__init__()
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.exchange = exchange
+        self.max_tokens = max_tokens
+        self._px = None
         cfg.validate()
         self.cfg = cfg
         self.group = group
@@ -148,8 +251,24 @@ class ExpertParallelMoELayer(nn.Module):
         self.last_idx = None
         self.last_counts = None
 
+    def peer_exchange(self) -> PeerExchange:
+        """The peer-memory exchange of this layer (created on first use; every
+        rank of the group must reach this point together)."""
+        if self._px is None:
+            if self.max_tokens is None:
+                raise ValueError("exchange='p2p' needs max_tokens")
+            self._px = PeerExchange(group=self.group, max_tokens=self.max_tokens,
+                                    top_k=self.cfg.num_experts_per_tok, n_experts=self.cfg.n_routed_experts,
+                                    hidden=self.cfg.hidden_size, partial_f32=self.cfg.act_mode == "bf16")
+        return self._px
+
+    def close(self) -> None:
+        if self._px is not None:
+            self._px.close()
+            self._px = None
+
     @classmethod
-    def from_layer(cls, layer, *, group=None, kernels=None):
+    def from_layer(cls, layer, *, group=None, kernels=None, exchange: str = "nccl", max_tokens: int | None = None):
         """EP layer of this rank from a full single-GPU ``MoELayer`` (same config,
         router weights and experts; the bank keeps its reference-layout copies)."""
         world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -157,7 +276,7 @@ class ExpertParallelMoELayer(nn.Module):
         b = layer.bank
         local = shard_bank(b.gu_packed, b.gu_scale, b.dn_packed, b.dn_scale, rank=rank, world=world,
                            n_experts=layer.cfg.n_routed_experts, has_shared=b.has_shared)
-        ep = cls(layer.cfg, local, group=group, kernels=kernels)
+        ep = cls(layer.cfg, local, group=group, kernels=kernels, exchange=exchange, max_tokens=max_tokens)
         ep.router.weight.data = layer.router.weight.data
         ep.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
         return ep
@@ -174,8 +293,53 @@ class ExpertParallelMoELayer(nn.Module):
         return dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
                                       group=self.group, async_op=async_op)
 
+    def _forward_p2p(self, xf: torch.Tensor) -> torch.Tensor:
+        """One step with the device-driven peer-memory exchange: no host
+        synchronisation, so the step can be captured in a CUDA graph."""
+        t, h = xf.shape
+        k = self.cfg.num_experts_per_tok
+        px = self.peer_exchange()
+        if t > px.max_tokens:
+            raise ValueError(f"{t} tokens exceed the exchange capacity {px.max_tokens}")
+        if t == 0:
+            raise ValueError("exchange='p2p' needs at least one token per rank")
+        lib = C.lib()
+        kern = self.kernels
+        w, idx = kern.route(self.router, xf)
+        dims = self.cfg.dims(t, self.has_shared)
+        send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
+        pe = ctypes.byref(px.peers)
+        C.check(lib.mosaic_ep_exchange_rows(pe, ops._ptr(send), ops._ptr(counts), ops._stream()),
+                "mosaic_ep_exchange_rows")
+        dl = self._local_dims(t)
+        elem = 4 if self.cfg.act_mode == "bf16" else 2
+        if self.has_shared:  # straight into this rank's return buffer, rows [t*k, t*k + t)
+            out = px.ret_partials + t * k * h * elem
+            kern._rows(dl, self.bank, t, xf.data_ptr(), h, None, None, 1, dl.n_experts, _RawOut(out),
+                       kern._ws_shared, xf.device)
+        rb = C.ep_row_bytes(h)
+        pdt = torch.float32 if elem == 4 else torch.bfloat16
+        part = kern.p2p_partials(px.max_recv_rows, h, pdt, xf.device)
+        ws_rows = kern._ws_rows.get(lib.mosaic_moe_expert_rows_workspace_bytes(ctypes.byref(dl), px.max_recv_rows),
+                                    xf.device)
+        b = self.bank.c_struct()
+        C.check(lib.mosaic_moe_expert_rows_dev(
+            ctypes.byref(dl), px.max_recv_rows, ctypes.c_void_p(px.recv_count), ctypes.c_void_p(px.recv_rows),
+            rb // 2, ctypes.c_void_p(px.recv_rows + 2 * h), ctypes.c_void_p(px.recv_rows + 2 * h + 4), rb // 4, 0,
+            ctypes.byref(b), ops._ptr(part), ops._ptr(ws_rows), ws_rows.numel(), ops._stream()),
+            "mosaic_moe_expert_rows_dev")
+        C.check(lib.mosaic_ep_return_partials(pe, ops._ptr(part), ops._stream()), "mosaic_ep_return_partials")
+        y = torch.empty_like(xf)
+        C.check(lib.mosaic_ep_combine(ctypes.byref(dims), ctypes.c_void_p(px.ret_partials), ops._ptr(ws), ops._ptr(y),
+                                      ops._stream()), "mosaic_ep_combine")
+        self.last_weights, self.last_idx, self.last_counts = w, idx, None
+        return y
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
+        if self.exchange == "p2p":
+            xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+            return self._forward_p2p(xf).to(x.dtype).view(shape)
         xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
         t, h = xf.shape
         k = self.cfg.num_experts_per_tok

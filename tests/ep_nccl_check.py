@@ -13,6 +13,47 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
+def check_p2p(rank) -> bool:
+    """Device-driven peer-memory exchange: eager and CUDA-graph steps equal the
+    single-GPU layer on every rank, with no device error."""
+    from mosaic_b200 import synthetic
+    from mosaic_b200.ep import ExpertParallelMoELayer
+
+    ok = True
+    for act_mode, t in (("bf16", 128), ("fp8", 256)):
+        layer, _ = synthetic.make_layer(tokens=1, seed=78, act_mode=act_mode, n_experts=64)
+        x = synthetic.make_tokens(t, 7168, 2000 + rank)
+        ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=t)
+        ref = layer(x)
+        for _ in range(3):
+            y = ep(x)
+        torch.cuda.synchronize()
+        if not torch.equal(y, ref):
+            ok = False
+            print(f"rank {rank} p2p {act_mode}: eager mismatch", flush=True)
+        xs = x.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ys = ep(xs)
+        x2 = synthetic.make_tokens(t, 7168, 3000 + rank)
+        xs.copy_(x2)
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize()
+        if not torch.equal(ys, layer(x2)):
+            ok = False
+            print(f"rank {rank} p2p {act_mode}: graph mismatch", flush=True)
+        err = ep.peer_exchange().error()
+        if err:
+            ok = False
+            print(f"rank {rank} p2p {act_mode}: device error {err}", flush=True)
+        del g
+        ep.close()
+        del layer, ep
+        torch.cuda.empty_cache()
+    return ok
+
+
 def main():
     rank = int(os.environ["RANK"])
     local = int(os.environ["LOCAL_RANK"])
@@ -22,6 +63,7 @@ def main():
     from mosaic_b200.ep import ExpertParallelMoELayer
 
     ok = True
+    ok &= check_p2p(rank)
     for act_mode, t, e in (("bf16", 128, 64), ("fp8", 512, 64), ("bf16", 1, 64)):
         layer, _ = synthetic.make_layer(tokens=1, seed=77, act_mode=act_mode, n_experts=e)  # same bank everywhere
         x = synthetic.make_tokens(t, 7168, 1000 + rank)  # each rank its own tokens
