@@ -327,8 +327,10 @@ def timed_eager(fn, steps, warmup):
 
 def run_ep(args, rank, world, local, hbm, peak_src):
     """N > 1: expert parallelism (BASELINE configs 4/5 layout).  Every rank holds
-    E/N routed experts + the shared expert and its own decode tokens; dispatch
-    and combine are NCCL all-to-alls; time is the max over ranks."""
+    E/N routed experts + the shared expert and its own decode tokens.  The
+    headline step uses the device-driven peer-memory exchange and runs as one
+    CUDA graph; the NCCL all-to-all path (host-synchronised split sizes) is
+    timed beside it.  Times are the max over ranks."""
     from mosaic_b200 import synthetic
     from mosaic_b200.ep import ExpertParallelMoELayer
 
@@ -336,18 +338,31 @@ def run_ep(args, rank, world, local, hbm, peak_src):
     n_exp, t, h = args.experts, args.tokens, 7168
     # the same bank on every rank (same seed), each rank keeps its own shard
     layer, _ = synthetic.make_layer(tokens=1, seed=1234, act_mode="bf16", n_experts=n_exp)
-    ep = ExpertParallelMoELayer.from_layer(layer)
+    ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=t)
+    ep_nccl = ExpertParallelMoELayer(layer.cfg, ep.bank)
+    ep_nccl.router = ep.router
     layer.bank = None  # drop the full bank: only the local shard stays resident
     torch.cuda.empty_cache()
     x = synthetic.make_tokens(t, h, 1234 + rank)
     steps, warmup = args.steps, max(args.warmup, 3)
+
+    # one CUDA graph per layer step (peer exchange: no host synchronisation)
+    xs = x.clone()
+    for _ in range(3):
+        ep(xs)
+    torch.cuda.synchronize()
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ys = ep(xs)
     with Clocks(gpu_index(local)) as clk:
-        ms = timed_eager(lambda: ep(x), steps, warmup)
+        ms = timed_graph(g, steps, warmup, True)
     clocks = clk.summary()
-    idx = ep.last_idx
-    sc, rc = ep.last_counts
+    if ep.peer_exchange().error():
+        raise RuntimeError("device error recorded in the peer exchange")
+    idx = ep.last_idx.clone()
     lo, hi = ep.e_lo, ep.e_hi
-    # distinct local experts this rank streamed in the last step, from every rank's routing
+    # distinct local experts this rank streamed in a step, from every rank's routing
     all_idx = [torch.empty_like(idx) for _ in range(world)]
     dist.all_gather(all_idx, idx)
     ids = torch.unique(torch.cat(all_idx))
@@ -356,21 +371,22 @@ def run_ep(args, rank, world, local, hbm, peak_src):
     frac = torch.tensor([rank_bytes / (ms * 1e-3) / 1e9 / hbm], device="cuda")
     dist.all_reduce(frac, op=dist.ReduceOp.MIN)
 
-    # e2e through the public API with host buffers
+    # e2e through the public API with host buffers: pinned H2D, the graph-replayed
+    # step, D2H of the result, every step
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(x)
 
     def step_e2e():
-        xd.copy_(xh, non_blocking=True)
-        yh.copy_(ep(xd), non_blocking=True)
+        xs.copy_(xh, non_blocking=True)
+        g.replay()
+        yh.copy_(ys, non_blocking=True)
 
     e2e_ms = timed_eager(step_e2e, max(steps // 4, 10), 3)
-    from mosaic_b200 import ops
-
-    for ws in (ep.kernels._ws_dispatch.t, ep.kernels._ws_rows.t, ep.kernels._ws_shared.t):
-        if ws is not None and ops.read_error(ws):
-            raise RuntimeError("device error recorded during the EP steps")
+    # the NCCL all-to-all path, eager (split sizes read on the host every step)
+    nccl_ms = timed_eager(lambda: ep_nccl(x), max(steps // 4, 10), 3)
+    sc, rc = ep_nccl.last_counts
+    if ep.peer_exchange().error():
+        raise RuntimeError("device error recorded in the peer exchange")
     out = {
         "metric": METRIC, "value": t * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -379,23 +395,26 @@ def run_ep(args, rank, world, local, hbm, peak_src):
         "config": {"workload": f"V3 MoE layer decode, expert parallel over {world} GPUs, T={t} per rank",
                    "tokens_per_gpu": t, "hidden": h, "inter": 2048, "experts": n_exp,
                    "experts_per_gpu": n_exp // world, "shared": "replicated", "top_k": 8, "groups": "8/4",
-                   "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single (dispatch rows, fp32 partials)",
+                   "parallelism": f"ep{world}",
+                   "exchange": "NVLink peer-memory stores with device-side counts and flags (CUDA IPC)",
                    "l2": "no flush: every rank streams its touched experts (>> 126 MB L2) each step",
-                   "graph": "eager (split sizes read on the host once per step)"},
+                   "graph": "one CUDA graph per layer step"},
         "clocks": clocks,
-        # router 2, dispatch 3 (layout, pack, counts), received rows 5 and shared
-        # expert 5 (meta, layout, quantise, gate/up, down), combine 1
-        "gpu_launches": 16 * steps,
+        # router 2, dispatch 3, exchange 3, shared expert 5, received rows 5, return 2, combine 1
+        "gpu_launches": 21 * steps,
         "roofline": {"kernel": "whole EP layer step per rank (HBM: local experts streamed)", "bound": "hbm",
                      "achieved": rank_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                      "frac": float(frac.item()), "traffic": None, "peak_source": peak_src,
                      "distinct_local_experts": u_local},
         "exchange_bytes_per_rank": {"dispatch": sum(sc) * (2 * h + 16), "return": sum(sc) * h * 4},
+        "nccl_path": {"ms_per_step": nccl_ms, "tokens_per_s": t * world / (nccl_ms / 1e3),
+                      "exchange": "NCCL all_to_all_single, eager"},
         "e2e": {"value": t * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": xh.numel() * 2,
                 "d2h_bytes_per_step": yh.numel() * 2, "ms_per_step": e2e_ms},
     }
+    del g
     if not args.no_extras:
-        # 4096 FP8 tokens per rank, uniform routing
+        # 4096 FP8 tokens per rank, uniform routing (NCCL exchange)
         from mosaic_b200 import MoEConfig
 
         cfgp = MoEConfig(act_mode="fp8", **{k: v for k, v in synthetic.V3.items()})
@@ -408,11 +427,13 @@ def run_ep(args, rank, world, local, hbm, peak_src):
         flops = tp * world * 9 * 88_080_384
         out["ep_prefill"] = {"tokens_per_gpu": tp, "ms": msp, "tokens_per_s": tp * world / (msp / 1e3),
                              "expert_tflops_per_gpu": flops / world / (msp * 1e-3) / 1e12,
-                             "act": "fp8 (e4m3, per-128 pow2 scales)", "routing": "uniform"}
+                             "act": "fp8 (e4m3, per-128 pow2 scales)", "routing": "uniform",
+                             "exchange": "NCCL all_to_all_single"}
         del epp, xp
     if rank == 0:
         print(json.dumps(out), flush=True)
-    del ep
+    ep.close()
+    del ep, ep_nccl
     dist.barrier()
     dist.destroy_process_group()
 
