@@ -451,6 +451,9 @@ def main():
     torch.cuda.set_device(local)
     dist_on = world > 1
     if dist_on:
+        # NCCL's own messages (its version banner included) go to stderr: stdout
+        # carries exactly one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, bf16_tf, peak_src = peaks()
     if dist_on:

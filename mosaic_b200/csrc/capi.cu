@@ -119,16 +119,21 @@ WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   w.R_pad = (w.R + 15) & ~15;
   w.planes = hilo ? 2 : 1;
   // Token rows per tile.  bf16 (decode) tiles carry hi + lo planes: MMA N = 2 * rows.
+  // When the batch averages 16 or more rows per expert (e.g. the receive side
+  // of expert parallelism), 32-row tiles stop a second tile from streaming the
+  // same expert's weights again; they use one TMEM accumulator buffer
+  // (2 parities x 2 x 64 columns + 32 scale columns) instead of two.
   // E4M3 (prefill) tiles hold 112 rows so that two accumulator buffers fit TMEM
   // (2 x 2 x 112 columns + 32 scale columns <= 512): the epilogue of one work
   // item then overlaps the MMAs of the next instead of stalling them.
-  w.tt = hilo ? MOSAIC_DECODE_TILE_ROWS : 112;
+  const bool wide = hilo && w.R >= 16 * w.n_bank;
+  w.tt = hilo ? (wide ? 2 * MOSAIC_DECODE_TILE_ROWS : MOSAIC_DECODE_TILE_ROWS) : 112;
   w.max_n = hilo ? 2 * w.tt : w.tt;
   // sum over experts of ceil(count / tt) <= A / tt + (experts with a partial tile)
   w.max_tiles = (T * k) / w.tt + w.n_bank + T / w.tt + 2;
   // Two TMEM accumulator buffers in both modes; decode tiles (small N) also use
   // two stage parities (four MMA issuers), prefill tiles one.
-  w.nbuf = 2;
+  w.nbuf = wide ? 1 : 2;
   w.parities = hilo ? 2 : 1;
   const int sms = sm_count();
   w.splits = router_splits(T, H, E, sms > 0 ? sms : 148);
@@ -180,6 +185,7 @@ inline bool rec(void* const* ev, int i, cudaStream_t s) {
 void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
   lp.tt_routed = w.tt;
   lp.tt_shared = w.tt;
+  lp.rpad_to_tile = w.planes == 2 ? 1 : 0;
   lp.max_tiles = w.max_tiles;
   lp.counts = reinterpret_cast<int*>(ws + w.counts);
   lp.offsets = reinterpret_cast<int*>(ws + w.offsets);

@@ -127,7 +127,9 @@ __device__ __forceinline__ Item get_item(const GemmParams& p, int item) {
   it.e = p.tiles[3 * it.tile + 0];
   it.row0 = p.tiles[3 * it.tile + 1];
   it.rows = p.tiles[3 * it.tile + 2];
-  it.rpad = (it.rows + 15) & ~15;
+  // two-plane (bf16) tiles are padded to the box rows, so the lo plane sits at
+  // MMA column brows + n as the activation box lays it out; E4M3 tiles to 16
+  it.rpad = p.hilo ? p.brows : (it.rows + 15) & ~15;
   it.n = p.hilo ? 2 * it.rpad : it.rpad;
   return it;
 }

@@ -55,6 +55,7 @@ struct LayoutParams {
   int with_shared;
   const int* T_dev;          // optional: token count read on the device (<= T)
   int tt_routed, tt_shared;  // token rows per GEMM tile
+  int rpad_to_tile;          // 1: every tile's rows are padded to the tile size (two-plane tiles), else to 16
   int max_tiles;
   int* counts;            // [E+1]
   int* offsets;           // [E+2]

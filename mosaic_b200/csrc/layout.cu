@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
             const int ti = rank / tt;
             const int rows_t = min(tt, hist[e] - ti * tt);
             p.row_tile[row] = toff[e] + ti;
-            p.row_pos[row] = (((rows_t + 15) & ~15) << 8) | (rank - ti * tt);
+            p.row_pos[row] = ((p.rpad_to_tile ? tt : (rows_t + 15) & ~15) << 8) | (rank - ti * tt);
           }
           if (p.row_weight) p.row_weight[row] = p.weights ? p.weights[static_cast<size_t>(t) * k + s] : 1.0f;
           if (x.perm) x.perm[row] = static_cast<int64_t>(t) * k + s;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
         const int ti = t / tt;
         const int rows_t = min(tt, T - ti * tt);
         p.row_tile[row] = toff[E] + ti;
-        p.row_pos[row] = (((rows_t + 15) & ~15) << 8) | (t - ti * tt);
+        p.row_pos[row] = ((p.rpad_to_tile ? tt : (rows_t + 15) & ~15) << 8) | (t - ti * tt);
       }
     }
   }

@@ -91,14 +91,10 @@ __device__ __forceinline__ uint32_t gather_word(int e) {
 // and writes them to every packed row of the token; the scale words go into the
 // row's token-tile chunk (word (n%32)*4 + n/32 of chunk [tile][kt]; the lo plane
 // of a bf16 tile sits at rows rpad + n of the same chunk).
-__global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T,
-                                                         const int* __restrict__ T_dev, int H, int ldx, int k,
-                                                         const int* __restrict__ row_of, int shared_base, int hilo,
-                                                         int R_pad, const int* __restrict__ row_tile,
-                                                         const int* __restrict__ row_pos, uint8_t* __restrict__ xq,
-                                                         uint32_t* __restrict__ sft) {
-  const int t = blockIdx.x;
-  if (T_dev && t >= *T_dev) return;  // rows beyond the device-side count (uniform per block)
+__device__ __forceinline__ void quant_token_row(const __nv_bfloat16* __restrict__ x, int t, int H, int ldx, int k,
+                                                const int* __restrict__ row_of, int shared_base, int hilo, int R_pad,
+                                                const int* __restrict__ row_tile, const int* __restrict__ row_pos,
+                                                uint8_t* __restrict__ xq, uint32_t* __restrict__ sft) {
   const int lane = threadIdx.x & 31;
   const int k0 = blockIdx.y * 1024 + (threadIdx.x >> 5) * 256 + lane * 8;
   const bool valid = k0 < H;
@@ -149,6 +145,19 @@ __global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __
       }
     }
   }
+}
+
+// grid-stride over token rows: blockIdx.y picks the 1024-value slab of H; with
+// T_dev only the first *T_dev rows exist (the grid is sized for T)
+__global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T,
+                                                         const int* __restrict__ T_dev, int H, int ldx, int k,
+                                                         const int* __restrict__ row_of, int shared_base, int hilo,
+                                                         int R_pad, const int* __restrict__ row_tile,
+                                                         const int* __restrict__ row_pos, uint8_t* __restrict__ xq,
+                                                         uint32_t* __restrict__ sft) {
+  const int rows = T_dev ? min(*T_dev, T) : T;
+  for (int t = blockIdx.x; t < rows; t += gridDim.x)
+    quant_token_row(x, t, H, ldx, k, row_of, shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
 }
 
 // act_quant_ref: grid (M, ceil(K / 1024)), 128 threads.
@@ -294,7 +303,8 @@ cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int
                               int shared_base,
                               int hilo, int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq,
                               uint32_t* sft, cudaStream_t stream) {
-  dim3 grid(T, (H + 1023) / 1024);
+  // a block per token row, or a bounded grid looping over a device-side count
+  dim3 grid(T_dev ? (T < 1184 ? T : 1184) : T, (H + 1023) / 1024);
   rows_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k, row_of,
                                                shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
   return cudaGetLastError();

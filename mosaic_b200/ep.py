@@ -237,6 +237,7 @@ class ExpertParallelMoELayer(nn.Module):
         self.exchange = exchange
         self.max_tokens = max_tokens
         self._px = None
+        self._side = None
         cfg.validate()
         self.cfg = cfg
         self.group = group
@@ -305,18 +306,26 @@ class ExpertParallelMoELayer(nn.Module):
             raise ValueError("exchange='p2p' needs at least one token per rank")
         lib = C.lib()
         kern = self.kernels
+        main = torch.cuda.current_stream()
+        if self._side is None:
+            self._side = torch.cuda.Stream()
+        side = self._side
+        # fork: the shared expert needs only this step's tokens, and the previous
+        # step's combine (which read the same return rows) is before this point
+        side.wait_stream(main)
+        dl = self._local_dims(t)
+        elem = 4 if self.cfg.act_mode == "bf16" else 2
+        if self.has_shared:  # overlaps the exchange; writes return rows [t*k, t*k + t)
+            with torch.cuda.stream(side):
+                out = px.ret_partials + t * k * h * elem
+                kern._rows(dl, self.bank, t, xf.data_ptr(), h, None, None, 1, dl.n_experts, _RawOut(out),
+                           kern._ws_shared, xf.device)
         w, idx = kern.route(self.router, xf)
         dims = self.cfg.dims(t, self.has_shared)
         send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
         pe = ctypes.byref(px.peers)
         C.check(lib.mosaic_ep_exchange_rows(pe, ops._ptr(send), ops._ptr(counts), ops._stream()),
                 "mosaic_ep_exchange_rows")
-        dl = self._local_dims(t)
-        elem = 4 if self.cfg.act_mode == "bf16" else 2
-        if self.has_shared:  # straight into this rank's return buffer, rows [t*k, t*k + t)
-            out = px.ret_partials + t * k * h * elem
-            kern._rows(dl, self.bank, t, xf.data_ptr(), h, None, None, 1, dl.n_experts, _RawOut(out),
-                       kern._ws_shared, xf.device)
         rb = C.ep_row_bytes(h)
         pdt = torch.float32 if elem == 4 else torch.bfloat16
         part = kern.p2p_partials(px.max_recv_rows, h, pdt, xf.device)
@@ -329,6 +338,7 @@ class ExpertParallelMoELayer(nn.Module):
             ctypes.byref(b), ops._ptr(part), ops._ptr(ws_rows), ws_rows.numel(), ops._stream()),
             "mosaic_moe_expert_rows_dev")
         C.check(lib.mosaic_ep_return_partials(pe, ops._ptr(part), ops._stream()), "mosaic_ep_return_partials")
+        main.wait_stream(side)  # join: the shared expert's rows are in the return buffer
         y = torch.empty_like(xf)
         C.check(lib.mosaic_ep_combine(ctypes.byref(dims), ctypes.c_void_p(px.ret_partials), ops._ptr(ws), ops._ptr(y),
                                       ops._stream()), "mosaic_ep_combine")

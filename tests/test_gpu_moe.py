@@ -202,3 +202,18 @@ def test_v3_repeated_launches_stable(t, mode):
     assert ops.read_error(ws) == 0
     for y in outs[::10] + [outs[-1]]:
         assert torch.equal(y, y0)
+
+
+def test_wide_decode_tiles_match_oracle():
+    """bf16 batches averaging >= 16 rows per expert use 32-row tiles (one TMEM
+    buffer); a 4-expert layer with 128 tokens exercises them against the oracle."""
+    from mosaic_b200 import MoEConfig, MoELayer
+    from tests.golden.recipes import make_moe_case
+
+    case = make_moe_case(T=128, H=512, I=256, E=4, k=2, n_group=1, topk_group=1, scale=1.0, swiglu_limit=0.0,
+                         seed=21)
+    obank, full = pack_case(case)
+    layer = layer_for(case, gpu_bank(full), "bf16")
+    y = layer(case["x"].cuda()).float().cpu().numpy()
+    ref = moe_layer(case["x"], case["weights"], case["idx"], obank, mode="bf16")
+    assert rel_l2(y, ref) <= TOL["bf16"]
