@@ -301,7 +301,7 @@ def run_reference(args):
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["cores"], "kind": r["kind"],
                             "sample": sample_desc, "cpu": r["cpu"]},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(out), flush=True)
+    emit(out)
 
 
 def timed_eager(fn, steps, warmup):
@@ -431,14 +431,29 @@ def run_ep(args, rank, world, local, hbm, peak_src):
                              "exchange": "NCCL all_to_all_single"}
         del epp, xp
     if rank == 0:
-        print(json.dumps(out), flush=True)
+        emit(out)
     ep.close()
     del ep, ep_nccl
     dist.barrier()
     dist.destroy_process_group()
 
 
+_RESULT_FD = None
+
+
+def emit(out: dict) -> None:
+    """Write the result line to the real stdout (see main)."""
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(out) + "\n").encode())
+
+
 def main():
+    global _RESULT_FD
+    # Libraries write to stdout from C (NCCL's version banner, for one); the
+    # result must be the only line there, so stdout points at stderr while
+    # the bench runs and emit() writes to a saved copy of the real stdout.
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse()
     if args.impl == "reference":
         run_reference(args)
@@ -451,9 +466,6 @@ def main():
     torch.cuda.set_device(local)
     dist_on = world > 1
     if dist_on:
-        # NCCL's own messages (its version banner included) go to stderr: stdout
-        # carries exactly one JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, bf16_tf, peak_src = peaks()
     if dist_on:
@@ -550,7 +562,7 @@ def main():
         del gp
     del g
     if rank == 0:
-        print(json.dumps(out), flush=True)
+        emit(out)
     if dist_on:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
