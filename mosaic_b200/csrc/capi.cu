@@ -122,7 +122,7 @@ WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   // When the batch averages 16 or more rows per expert (e.g. the receive side
   // of expert parallelism), 32-row tiles stop a second tile from streaming the
   // same expert's weights again; they use one TMEM accumulator buffer
-  // (2 parities x 2 x 64 columns + 32 scale columns) instead of two.
+  // (3 parities x 2 x 64 columns + 48 scale columns) instead of two.
   // E4M3 (prefill) tiles hold 112 rows so that two accumulator buffers fit TMEM
   // (2 x 2 x 112 columns + 32 scale columns <= 512): the epilogue of one work
   // item then overlaps the MMAs of the next instead of stalling them.
@@ -131,10 +131,11 @@ WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   w.max_n = hilo ? 2 * w.tt : w.tt;
   // sum over experts of ceil(count / tt) <= A / tt + (experts with a partial tile)
   w.max_tiles = (T * k) / w.tt + w.n_bank + T / w.tt + 2;
-  // Two TMEM accumulator buffers in both modes; decode tiles (small N) also use
-  // two stage parities (four MMA issuers), prefill tiles one.
+  // Two TMEM accumulator buffers (one for wide decode tiles); decode tiles
+  // (small N, issue-bound) use three stage parities (six MMA issuers),
+  // prefill tiles one.
   w.nbuf = wide ? 1 : 2;
-  w.parities = hilo ? 2 : 1;
+  w.parities = hilo ? 3 : 1;
   const int sms = sm_count();
   w.splits = router_splits(T, H, E, sms > 0 ? sms : 148);
   w.partial_f32 = hilo ? 1 : 0;

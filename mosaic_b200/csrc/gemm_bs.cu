@@ -27,14 +27,14 @@
 // overlaps the MMAs of the next.  The epilogue stages its output in shared
 // memory and writes whole token rows with 16-byte stores.
 //
-// Warp roles (320 threads): warp 0 = weight producer, warp 6 = activation /
+// Warp roles (384 threads): warp 0 = weight producer, warp 6 = activation /
 // scale producer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31),
-// warps 1, 7, 8, 9 = MMA issuers (warp 1 also owns TMEM).  A tcgen05.mma costs
-// its issuing thread ~150-200 cycles whatever its size, so each stage is split
-// into two units (the two blocks of the pair), and at decode sizes two issuer
-// pairs alternate stages by parity, each accumulating into its own TMEM chain
-// with its own scale-factor columns.  The epilogue sums the chains in a fixed
-// order.
+// warps 1, 7..11 = up to three pairs of MMA issuers (warp 1 also owns TMEM).  A
+// tcgen05.mma costs its issuing thread ~150-200 cycles whatever its size, so
+// each stage is split into two units (the two blocks of the pair), and at
+// decode sizes three issuer pairs take the stages in turn (stage parity modulo
+// 3), each accumulating into its own TMEM chain with its own scale-factor
+// columns.  The epilogue sums the chains in a fixed order.
 // Reference behaviour: mosaicvm/kernels/qpa_mma.py:337-486 (grouped ordered
 // gate/up and down kernels), mosaicvm/kernels/mxint.py:1301-1346 (fused
 // SwiGLU / route weight / bf16 / act_quant epilogue).
@@ -45,18 +45,20 @@ namespace mosaic {
 
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 225 * 1024;
 constexpr int kEpiBytes = 16 * 256 * 4;  // epilogue staging: 16 token columns x 256 values (fp32)
+constexpr int kMaxParities = 3;          // issuer pairs (two MMA warps each)
+constexpr uint32_t kSfCols = 8u * 2 * kMaxParities;  // TMEM scale columns: 8 per issuer
 
 struct Ctrl {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
-  uint64_t drain[4];
+  uint64_t drain[6];
   uint32_t tmem_base;
   int abort;
   float red[4][16];
@@ -154,18 +156,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // chunk at sf_base + 8i, token chunk at +4.
   const uint32_t acc_w = static_cast<uint32_t>(2 * p.max_n);
   const uint32_t half_off = static_cast<uint32_t>(p.max_n);
-  const uint32_t sf_base = kTmemCols - 32u;
+  const uint32_t sf_base = kTmemCols - kSfCols;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&ctrl->full[s], 2);   // one arrival from each producer warp
-      mbar_init(&ctrl->empty[s], 4);  // every issuer: a commit (consumer) or an arrive (observer)
+      mbar_init(&ctrl->empty[s], 2 * P);  // every issuer: a commit (consumer) or an arrive (observer)
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&ctrl->acc_full[b], 4);  // one commit from each issuer
+      mbar_init(&ctrl->acc_full[b], 2 * P);  // one commit from each issuer
       mbar_init(&ctrl->acc_empty[b], 128);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&ctrl->drain[i], 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&ctrl->drain[i], 1);
     ctrl->abort = 0;
     fence_mbar_init();
   }
@@ -232,9 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&ctrl->full[s], static_cast<uint32_t>((it - 1) / S) & 1u, &never);
     }
     __syncwarp();
-  } else if (warp == 1 || warp >= 7) {
+  } else if ((warp == 1 || warp >= 7) && (warp == 1 ? 0 : warp - 6) < 2 * P) {
     // ----------------------------------------------------------------- MMA
-    const int issuer = (warp == 1) ? 0 : warp - 6;  // 0..3
+    const int issuer = (warp == 1) ? 0 : warp - 6;  // 0 .. 2P-1
     const int ip = issuer >> 1;                     // stage parity this issuer takes
     const int iu = issuer & 1;                      // unit: block of the pair
     const uint32_t col_sfw = tmem + sf_base + 8u * issuer;  // weight scale chunk
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&ctrl->drain[issuer], 0, &never);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int lrow = q * 32 + lane;
@@ -465,11 +467,11 @@ size_t gemm_smem_bytes(int planes, int brows) {
 
 cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x, const GemmParams& p, int grid,
                             cudaStream_t stream) {
-  if (p.max_n < 16 || p.max_n > 128 || p.nbuf < 1 || p.nbuf > 2 || p.parities < 1 || p.parities > 2)
+  if (p.max_n < 16 || p.max_n > 128 || p.nbuf < 1 || p.nbuf > 2 || p.parities < 1 || p.parities > kMaxParities)
     return cudaErrorInvalidValue;
   const int planes = p.hilo ? 2 : 1;
   if (p.brows * planes != p.max_n || p.brows % 16 || p.brows > 128) return cudaErrorInvalidValue;
-  if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols) - 32) return cudaErrorInvalidValue;
+  if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols - kSfCols)) return cudaErrorInvalidValue;
   if (p.K % 128 || p.K < 128) return cudaErrorInvalidValue;
   if (p.mode == 1 && p.H % 256) return cudaErrorInvalidValue;
   const Plan pl = make_plan(planes, p.brows);
