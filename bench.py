@@ -41,7 +41,7 @@ ROUTER_BYTES = 256 * 7168 * 4
 # dram__bytes_write.sum of one ncu capture of `bench.py --experts 64 --profile-small`
 # (65 experts streamed).  Traffic grows with the number of experts streamed, so the
 # full launch's traffic is this ratio times its algorithmic bytes.
-GU_TRAFFIC_RATIO = 1.0719e9 / 1_013_841_920
+GU_TRAFFIC_RATIO = (1.0408e9 + 7.37e6) / 1_013_841_920
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; % of HBM / FP4 tensor roofline"
 
 
