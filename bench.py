@@ -430,12 +430,78 @@ def run_ep(args, rank, world, local, hbm, peak_src):
                              "act": "fp8 (e4m3, per-128 pow2 scales)", "routing": "uniform",
                              "exchange": "NCCL all_to_all_single"}
         del epp, xp
+    if not args.no_extras and world >= 4:
+        # the 58-layer decode stack, expert parallel, one CUDA graph
+        del ep_nccl
+        ep.close()
+        del ep
+        torch.cuda.empty_cache()
+        out["stack"] = run_stack(58, t, world, rank)
+        if rank == 0:
+            emit(out)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     if rank == 0:
         emit(out)
     ep.close()
     del ep, ep_nccl
     dist.barrier()
     dist.destroy_process_group()
+
+
+def run_stack(n_layers, t, world, rank):
+    """Decode step through n_layers independent V3 MoE layers (fresh uniform
+    router each, every layer reading the step's hidden states), expert parallel
+    over the group, the whole step captured in one CUDA graph.  One peer
+    exchange serves every layer (they run one after the other)."""
+    from mosaic_b200 import MoEConfig, synthetic
+    from mosaic_b200.ep import CudaEPKernels, ExpertParallelMoELayer, PeerExchange, expert_range
+
+    dist = torch.distributed
+    h, n_exp = 7168, 256
+    kern = CudaEPKernels()  # workspaces shared: the layers run one after the other
+    cfg = MoEConfig(act_mode="bf16", **synthetic.V3)
+    lo, hi = expert_range(n_exp, world, rank)
+    px = PeerExchange(max_tokens=t, top_k=8, n_experts=n_exp, hidden=h, partial_f32=True)
+    layers = []
+    for layer_id in range(n_layers):
+        bank = synthetic.make_local_bank(h, 2048, n_exp, seed=5000 + layer_id, lo=lo, hi=hi)
+        ep = ExpertParallelMoELayer(cfg, bank, exchange="p2p", peer_exchange=px, kernels=kern)
+        w, b = synthetic.make_router_weights(h, n_exp, seed=7000 + layer_id)
+        ep.router.weight.data = w
+        ep.router.e_score_correction_bias.data = b
+        layers.append(ep)
+    x = synthetic.make_tokens(t, h, 99 + rank)
+    outs = [None] * n_layers
+
+    def step(xin):
+        for i, ep in enumerate(layers):
+            outs[i] = ep(xin)
+        return outs[-1]
+
+    for _ in range(2):
+        step(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step(x)
+    ms = timed_graph(g, 20, 3, True)
+    if px.error():
+        raise RuntimeError("device error recorded in the peer exchange (stack)")
+    res = {"layers": n_layers, "tokens_per_gpu": t, "ms_per_step": ms, "ms_per_layer": ms / n_layers,
+           "tokens_per_s": t * world / (ms / 1e3), "experts_per_gpu": hi - lo,
+           "expert_weights_per_gpu_gb": n_layers * (hi - lo + 1) * EXPERT_BYTES / 1e9,
+           "graph": f"one CUDA graph, {n_layers} layers x 21 kernels",
+           "note": "layers are independent (each reads the step's hidden states); no norm / attention between them"}
+    del g
+    for ep in layers:
+        ep.close()
+    px.close()
+    del layers, outs
+    torch.cuda.empty_cache()
+    return res
 
 
 _RESULT_FD = None

@@ -230,13 +230,15 @@ class ExpertParallelMoELayer(nn.Module):
     """
 
     def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None, exchange: str = "nccl",
-                 max_tokens: int | None = None):
+                 max_tokens: int | None = None, peer_exchange: "PeerExchange | None" = None):
         super().__init__()
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.exchange = exchange
-        self.max_tokens = max_tokens
-        self._px = None
+        self.max_tokens = max_tokens if peer_exchange is None else peer_exchange.max_tokens
+        # layers that run one after the other on a stream may share one exchange
+        self._px = peer_exchange
+        self._owns_px = peer_exchange is None
         self._side = None
         cfg.validate()
         self.cfg = cfg
@@ -264,9 +266,9 @@ class ExpertParallelMoELayer(nn.Module):
         return self._px
 
     def close(self) -> None:
-        if self._px is not None:
+        if self._px is not None and self._owns_px:
             self._px.close()
-            self._px = None
+        self._px = None
 
     @classmethod
     def from_layer(cls, layer, *, group=None, kernels=None, exchange: str = "nccl", max_tokens: int | None = None):

@@ -48,6 +48,37 @@ def make_bank(hidden: int, inter: int, n_experts: int, seed: int, *, has_shared:
     return ExpertBank(gu_p, gu_s, dn_p, dn_s, has_shared=has_shared)
 
 
+def make_local_bank(hidden: int, inter: int, n_experts: int, seed: int, *, lo: int, hi: int, std: float = 0.02,
+                    device="cuda") -> ExpertBank:
+    """Experts [lo, hi) of an n_experts bank plus its shared expert (last), each
+    drawn from a generator seeded by (seed, expert id): every rank of an
+    expert-parallel group gets the same weights for an expert without
+    generating the whole bank."""
+    ids = list(range(lo, hi)) + [n_experts]
+    n = len(ids)
+    gu_p = torch.empty(n, 2 * inter, hidden // 2, dtype=torch.uint8, device=device)
+    gu_s = torch.empty(n, 2 * inter, hidden // 32, dtype=torch.uint8, device=device)
+    dn_p = torch.empty(n, hidden, inter // 2, dtype=torch.uint8, device=device)
+    dn_s = torch.empty(n, hidden, inter // 32, dtype=torch.uint8, device=device)
+    for i, e in enumerate(ids):
+        g = _gen(seed * 1009 + e, device)
+        w = torch.randn(2 * inter, hidden, generator=g, device=device) * std
+        gu_p[i], gu_s[i] = ops.pack_mxfp4_nk(w)
+        w = torch.randn(hidden, inter, generator=g, device=device) * std
+        dn_p[i], dn_s[i] = ops.pack_mxfp4_nk(w)
+        del w
+    return ExpertBank(gu_p, gu_s, dn_p, dn_s, has_shared=True, keep_packed=False)
+
+
+def make_router_weights(hidden: int, n_experts: int, seed: int, device="cuda"):
+    """Router weight U(-1/sqrt(H), 1/sqrt(H)) and bias N(0, 0.01), seeded."""
+    g = _gen(seed + 1, device)
+    bound = 1.0 / math.sqrt(hidden)
+    w = (torch.rand(n_experts, hidden, generator=g, device=device) * 2 - 1) * bound
+    b = torch.randn(n_experts, generator=g, device=device) * 0.01
+    return w, b
+
+
 def make_router(layer: MoELayer, seed: int, device="cuda") -> None:
     cfg = layer.cfg
     g = _gen(seed + 1, device)
