@@ -310,6 +310,16 @@ MOSAIC_API int mosaic_ep_region_view(const mosaic_ep_peers* peers, void** recv_r
 MOSAIC_API int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void* send_rows, const int32_t* dest_counts,
                                        mosaic_stream_t stream);
 MOSAIC_API int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials, mosaic_stream_t stream);
+/* The expert pass on this rank's received rows with the return fused in: the
+ * down GEMM's epilogue stores every partial straight into its source rank's
+ * return buffer (NVLink stores overlapping the GEMM), then every source's
+ * return flag is stamped and this rank waits for its own.  Replaces
+ * mosaic_moe_expert_rows_dev + mosaic_ep_return_partials.  dims as for
+ * mosaic_moe_expert_rows (n_experts = this rank's routed experts); workspace:
+ * mosaic_moe_expert_rows_workspace_bytes(dims, peers->max_recv_rows). */
+MOSAIC_API int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers,
+                                            const mosaic_expert_bank* bank, void* workspace, size_t workspace_bytes,
+                                            mosaic_stream_t stream);
 /* mosaic_moe_expert_rows with the row count read on the device from rows_dev
  * (at most max_rows; the workspace is sized for max_rows). */
 MOSAIC_API int mosaic_moe_expert_rows_dev(const mosaic_moe_dims* dims, int32_t max_rows, const int32_t* rows_dev,

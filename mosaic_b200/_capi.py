@@ -63,6 +63,7 @@ EXPORTED = (
     "mosaic_ep_region_view",
     "mosaic_ep_exchange_rows",
     "mosaic_ep_return_partials",
+    "mosaic_ep_expert_rows_return",
     "mosaic_moe_expert_rows_dev",
     "mosaic_read_error",
 )
@@ -153,6 +154,8 @@ _SIGS = {
                                ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "mosaic_ep_exchange_rows": ([ctypes.POINTER(EpPeersC), _P, _P, _P], ctypes.c_int),
     "mosaic_ep_return_partials": ([ctypes.POINTER(EpPeersC), _P, _P], ctypes.c_int),
+    "mosaic_ep_expert_rows_return": ([ctypes.POINTER(MoEDims), ctypes.POINTER(EpPeersC), ctypes.POINTER(ExpertBankC),
+                                      _P, _SZ, _P], ctypes.c_int),
     "mosaic_moe_expert_rows_dev": ([ctypes.POINTER(MoEDims), _I, _P, _P, _I, _P, _P, _I, _I,
                                     ctypes.POINTER(ExpertBankC), _P, _P, _SZ, _P], ctypes.c_int),
     "mosaic_read_error": ([_P, _I, ctypes.POINTER(ctypes.c_int32), _P], ctypes.c_int),

@@ -206,7 +206,7 @@ void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
 // partial_out, row r at out_row[r] (out_row null: row r).
 int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const LayoutParams& lp,
               const mosaic_expert_bank* bank, int shared_expert, const int* out_row, void* partial_out,
-              cudaStream_t stream, void* const* ev) {
+              cudaStream_t stream, void* const* ev, const EpPeersDev* ep = nullptr) {
   const int H = d->hidden, I = d->inter;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
   const int sms = sm_count();
@@ -260,6 +260,14 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   gp.out = partial_out;
   gp.out_f32 = w.partial_f32;
   gp.out_row = out_row;
+  if (ep) {  // partials go straight into the source ranks' return buffers
+    const EpRegionHeader* own = reinterpret_cast<const EpRegionHeader*>(ep->regions[ep->rank]);
+    gp.ep_world = ep->world;
+    gp.ep_recv_start = own->recv_start;
+    gp.ep_src_pos = own->src_pos;
+    gp.ep_ret_off = ep->ret_off;
+    for (int r = 0; r < ep->world; ++r) gp.ep_regions[r] = ep->regions[r];
+  }
   if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(ev, 5, stream)) return MOSAIC_ERR_CUDA;
   return MOSAIC_OK;
@@ -334,7 +342,7 @@ namespace {
 int expert_rows_impl(const mosaic_moe_dims* dims, int32_t rows, const int32_t* rows_dev, const void* x_rows,
                      int32_t ldx, const int32_t* ids, const float* weights, int32_t meta_stride, int32_t default_id,
                      const mosaic_expert_bank* bank, void* partials, void* workspace, size_t workspace_bytes,
-                     mosaic_stream_t stream) {
+                     mosaic_stream_t stream, const EpPeersDev* ep = nullptr) {
   if (!dims) return MOSAIC_ERR_SHAPE;
   if (rows < 0) return MOSAIC_ERR_SHAPE;
   if (rows == 0) return MOSAIC_OK;
@@ -342,7 +350,7 @@ int expert_rows_impl(const mosaic_moe_dims* dims, int32_t rows, const int32_t* r
   const mosaic_moe_dims r = rows_dims(dims, rows);
   int st = check_rows_dims(&r);
   if (st) return st;
-  if (!x_rows || !partials || !workspace) return MOSAIC_ERR_SHAPE;
+  if (!x_rows || (!partials && !ep) || !workspace) return MOSAIC_ERR_SHAPE;
   if (ldx < dims->hidden || ldx % 8 || ((ids || weights) && meta_stride < 1)) return MOSAIC_ERR_SHAPE;
   if (!ids && (default_id < 0 || default_id >= r.n_experts)) return MOSAIC_ERR_RANGE;
   st = check_bank(bank);
@@ -378,7 +386,7 @@ int expert_rows_impl(const mosaic_moe_dims* dims, int32_t rows, const int32_t* r
   // with k = 1 the packed row of input row t is sorted row row_of[t], and
   // row_token[sorted row] = t: partials land in input row order
   return run_gemms(&r, w, ws, lp, bank, dims->has_shared ? dims->n_experts : -1, lp.row_token, partials, s,
-                   nullptr);
+                   nullptr, ep);
 }
 
 // Argument checks shared by mosaic_router and mosaic_router_noalloc.
@@ -760,6 +768,30 @@ int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void* send_rows,
                  cudaSuccess
              ? MOSAIC_OK
              : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers,
+                                 const mosaic_expert_bank* bank, void* workspace, size_t workspace_bytes,
+                                 mosaic_stream_t stream) {
+  int st = check_peers(peers);
+  if (st) return st;
+  st = check_regions(peers);
+  if (st) return st;
+  if (!dims) return MOSAIC_ERR_SHAPE;
+  if (dims->hidden != peers->hidden || (dims->act_mode == MOSAIC_ACT_BF16) != (peers->partial_f32 != 0))
+    return MOSAIC_ERR_SHAPE;
+  const EpPeersDev ep = ep_dev(peers);
+  uint8_t* own = static_cast<uint8_t*>(peers->regions[peers->rank]);
+  uint8_t* recv = own + ep.recv_off;
+  const int32_t* count = &reinterpret_cast<EpRegionHeader*>(own)->recv_count;
+  const int rb = ep.row_bytes;
+  const int h = peers->hidden;
+  st = expert_rows_impl(dims, peers->max_recv_rows, count, recv, rb / 2, reinterpret_cast<const int32_t*>(recv + 2 * h),
+                        reinterpret_cast<const float*>(recv + 2 * h + 4), rb / 4, 0, bank, nullptr, workspace,
+                        workspace_bytes, stream, &ep);
+  if (st) return st;
+  return launch_ep_signal_return(ep, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? MOSAIC_OK
+                                                                                          : MOSAIC_ERR_CUDA;
 }
 
 int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials, mosaic_stream_t stream) {

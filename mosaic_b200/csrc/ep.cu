@@ -134,7 +134,14 @@ __global__ void ep_counts_kernel(const EpPeersDev P, const int* __restrict__ des
   if (threadIdx.x == 0) {
     __threadfence_system();
     int total = 0;
-    for (int s = 0; s < P.world; ++s) total += own->counts[s][P.rank];
+    for (int s = 0; s < P.world; ++s) {
+      own->recv_start[s] = total;
+      int pos = 0;
+      for (int d = 0; d < P.rank; ++d) pos += own->counts[s][d];
+      own->src_pos[s] = pos;
+      total += own->counts[s][P.rank];
+    }
+    own->recv_start[P.world] = total;
     if (total > P.max_recv_rows) set_error(&own->err, MOSAIC_ERR_WORKSPACE);
     own->recv_count = min(total, P.max_recv_rows);
   }
@@ -231,6 +238,17 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpPeersDev P, cons
   }
 }
 
+// One CTA, after the down GEMM wrote this rank's partials into the sources'
+// return buffers (its threads fenced them at system scope before exiting):
+// stamp every source's return flag.
+__global__ void ep_signal_return_kernel(const EpPeersDev P) {
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  const uint32_t epoch = own->epoch;
+  const int s = threadIdx.x;
+  __threadfence_system();
+  if (s < P.world) st_release_sys(&hdr_of(P, s)->ret_flag[P.rank], epoch);
+}
+
 // One CTA: wait until every rank stamped this rank's flags (data or return) with the step's epoch.
 __global__ void ep_wait_kernel(const EpPeersDev P, int which) {
   EpRegionHeader* own = hdr_of(P, P.rank);
@@ -269,6 +287,12 @@ cudaError_t launch_ep_exchange_rows(const EpPeersDev& P, const void* send_rows, 
   ep_counts_kernel<<<1, 32, 0, stream>>>(P, dest_counts);
   ep_send_kernel<<<2 * sms, 256, 0, stream>>>(P, static_cast<const uint4*>(send_rows));
   ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_signal_return(const EpPeersDev& P, cudaStream_t stream) {
+  ep_signal_return_kernel<<<1, 32, 0, stream>>>(P);
+  ep_wait_kernel<<<1, 32, 0, stream>>>(P, 1);
   return cudaGetLastError();
 }
 

@@ -418,30 +418,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_bar();
           // 16-byte stores: per token, two runs of 128 values (block nb of each half)
           const int hb = p.H / 2;
-          if (p.out_f32) {
-            for (int v = et; v < 16 * 64; v += 128) {  // 16 tokens x 2 halves x 32 float4
-              const int j = v >> 6, h = (v >> 5) & 1, w4 = v & 31;
-              if (j < ncol) {
-                const int orow = p.out_row ? p.out_row[m.row0 + c0 + j] : m.row0 + c0 + j;
-                float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(orow) * p.H + h * hb + m.nb * 128;
-                reinterpret_cast<float4*>(dst)[w4] =
-                    *reinterpret_cast<const float4*>(stage_f + j * 256 + h * 128 + w4 * 4);
-              }
+          const int esz = p.out_f32 ? 4 : 2;
+          for (int v = et; v < (p.out_f32 ? 16 * 64 : 16 * 32); v += 128) {
+            // fp32: 16 tokens x 2 halves x 32 float4; bf16: 16 x 2 x 16 vectors of 8
+            const int per = p.out_f32 ? 32 : 16;
+            const int j = v / (2 * per), h = (v / per) & 1, w16 = v % per;
+            if (j >= ncol) continue;
+            const int orow = p.out_row ? p.out_row[m.row0 + c0 + j] : m.row0 + c0 + j;
+            uint8_t* row_base;
+            if (p.ep_world) {
+              // receive row orow of source s goes to s's send position of it
+              int sr = 0;
+              while (sr + 1 < p.ep_world && orow >= p.ep_recv_start[sr + 1]) ++sr;
+              row_base = p.ep_regions[sr] + p.ep_ret_off +
+                         static_cast<size_t>(p.ep_src_pos[sr] + orow - p.ep_recv_start[sr]) * p.H * esz;
+            } else {
+              row_base = static_cast<uint8_t*>(p.out) + static_cast<size_t>(orow) * p.H * esz;
             }
-          } else {
-            for (int v = et; v < 16 * 32; v += 128) {  // 16 tokens x 2 halves x 16 vectors of 8 bf16
-              const int j = v >> 5, h = (v >> 4) & 1, w8 = v & 15;
-              if (j < ncol) {
-                const int orow = p.out_row ? p.out_row[m.row0 + c0 + j] : m.row0 + c0 + j;
-                const float* src = stage_f + j * 256 + h * 128 + w8 * 8;
-                uint4 pk;
-                __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+            uint4* dst = reinterpret_cast<uint4*>(row_base + static_cast<size_t>(h * hb + m.nb * 128) * esz) + w16;
+            const float* src = stage_f + j * 256 + h * 128;
+            if (p.out_f32) {
+              *dst = *reinterpret_cast<const uint4*>(src + w16 * 4);
+            } else {
+              uint4 pk;
+              __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(src[2 * i], src[2 * i + 1]);
-                __nv_bfloat16* dst =
-                    reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(orow) * p.H + h * hb + m.nb * 128;
-                reinterpret_cast<uint4*>(dst)[w8] = pk;
-              }
+              for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(src[w16 * 8 + 2 * i], src[w16 * 8 + 2 * i + 1]);
+              *dst = pk;
             }
           }
           epi_bar();
@@ -450,6 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&ctrl->acc_empty[b]);
     }
+    // partials stored into other ranks' memory are made visible at system
+    // scope before the kernel ends (the next kernel stamps their flags)
+    if (p.ep_world) __threadfence_system();
   }
 
   tc_fence_before();

@@ -35,6 +35,14 @@ struct GemmParams {
   void* out;          // down partials [R][H]
   int out_f32;
   const int* out_row; // null: partial of packed row r goes to out row r; else to out row out_row[r]
+  // EP return fused into the down epilogue: output row r (after out_row) is a
+  // receive row and goes to its source rank's return buffer, found from the
+  // geometry in this rank's exchange region header
+  int ep_world;       // 0: plain output
+  const int* ep_recv_start;
+  const int* ep_src_pos;
+  size_t ep_ret_off;
+  uint8_t* ep_regions[MOSAIC_EP_MAX_WORLD];
   int* err;
 };
 size_t gemm_smem_bytes(int planes, int brows);
@@ -122,6 +130,11 @@ struct EpRegionHeader {
   uint32_t data_flag[MOSAIC_EP_MAX_WORLD];   // [source]: its rows of this epoch are here
   uint32_t ret_flag[MOSAIC_EP_MAX_WORLD];    // [owner]: its partials of this epoch are here
   int counts[MOSAIC_EP_MAX_WORLD][MOSAIC_EP_MAX_WORLD];  // [source][destination] rows
+  // geometry of the step's received rows, written with the counts: rows from
+  // source s are receive rows [recv_start[s], recv_start[s+1]) and go back to
+  // s's send rows from src_pos[s]
+  int recv_start[MOSAIC_EP_MAX_WORLD + 1];
+  int src_pos[MOSAIC_EP_MAX_WORLD];
 };
 constexpr size_t kEpHeaderBytes = 1024;
 static_assert(sizeof(EpRegionHeader) <= kEpHeaderBytes, "EP region header");
@@ -134,6 +147,9 @@ struct EpPeersDev {
 cudaError_t launch_ep_exchange_rows(const EpPeersDev& P, const void* send_rows, const int* dest_counts,
                                     int sms, cudaStream_t stream);
 cudaError_t launch_ep_return_partials(const EpPeersDev& P, const void* partials, int sms, cudaStream_t stream);
+// After a down GEMM that wrote the partials straight into the sources' return
+// buffers: stamp every source's return flag, then wait for this rank's.
+cudaError_t launch_ep_signal_return(const EpPeersDev& P, cudaStream_t stream);
 
 // ---- combine (combine.cu)
 cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,

@@ -85,13 +85,6 @@ class CudaEPKernels:
         self._ws_dispatch = _Buffer()
         self._ws_rows = _Buffer()
         self._ws_shared = _Buffer()
-        self._part = None
-
-    def p2p_partials(self, rows: int, h: int, dtype, device) -> torch.Tensor:
-        """Partials of the received rows (peer exchange), kept across steps."""
-        if self._part is None or self._part.shape != (rows, h) or self._part.dtype != dtype:
-            self._part = torch.empty(rows, h, dtype=dtype, device=device)
-        return self._part
 
     def route(self, router: Router, x: torch.Tensor):
         return router(x)
@@ -328,18 +321,13 @@ class ExpertParallelMoELayer(nn.Module):
         pe = ctypes.byref(px.peers)
         C.check(lib.mosaic_ep_exchange_rows(pe, ops._ptr(send), ops._ptr(counts), ops._stream()),
                 "mosaic_ep_exchange_rows")
-        rb = C.ep_row_bytes(h)
-        pdt = torch.float32 if elem == 4 else torch.bfloat16
-        part = kern.p2p_partials(px.max_recv_rows, h, pdt, xf.device)
+        # expert pass on the received rows; the down epilogue stores every partial
+        # straight into its source's return buffer
         ws_rows = kern._ws_rows.get(lib.mosaic_moe_expert_rows_workspace_bytes(ctypes.byref(dl), px.max_recv_rows),
                                     xf.device)
         b = self.bank.c_struct()
-        C.check(lib.mosaic_moe_expert_rows_dev(
-            ctypes.byref(dl), px.max_recv_rows, ctypes.c_void_p(px.recv_count), ctypes.c_void_p(px.recv_rows),
-            rb // 2, ctypes.c_void_p(px.recv_rows + 2 * h), ctypes.c_void_p(px.recv_rows + 2 * h + 4), rb // 4, 0,
-            ctypes.byref(b), ops._ptr(part), ops._ptr(ws_rows), ws_rows.numel(), ops._stream()),
-            "mosaic_moe_expert_rows_dev")
-        C.check(lib.mosaic_ep_return_partials(pe, ops._ptr(part), ops._stream()), "mosaic_ep_return_partials")
+        C.check(lib.mosaic_ep_expert_rows_return(ctypes.byref(dl), pe, ctypes.byref(b), ops._ptr(ws_rows),
+                                                 ws_rows.numel(), ops._stream()), "mosaic_ep_expert_rows_return")
         main.wait_stream(side)  # join: the shared expert's rows are in the return buffer
         y = torch.empty_like(xf)
         C.check(lib.mosaic_ep_combine(ctypes.byref(dims), ctypes.c_void_p(px.ret_partials), ops._ptr(ws), ops._ptr(y),
