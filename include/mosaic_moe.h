@@ -17,6 +17,10 @@
  * Reference interfaces replaced (paths inside fazin-ahamed/Mosaic):
  *   mosaic_router            <- mosaicvm/model/layers.py:118-150 (Router.forward) with the
  *                               sigmoid score of .mosaicvm/source/inference_model.py:569-589 (Gate)
+ *   mosaic_router_ext        <- the same plus the other score functions
+ *                               (layers.py:110-115 _router_scores: sqrt(softplus); Gate: softmax)
+ *                               and hash routing (layers.py:153-197 HashRouter.forward; Gate's
+ *                               tid2eid branch, inference_model.py:581-582)
  *   mosaic_layout_assignments<- mosaicvm/kernels/moe_layout.py:8-27 (layout_assignments)
  *   mosaic_emit_tiles        <- mosaicvm/kernels/w4a16_grouped.py:151-169 (emit_tiles)
  *   mosaic_act_quant         <- mosaicvm/kernels/fp4_source.py:110-129 (act_quant_ref)
@@ -26,6 +30,8 @@
  *   mosaic_moe_routed        <- mosaicvm/kernels/exact_moe.py:12-19 (exact_moe) /
  *                               mosaicvm/kernels/qpa_mma.py:681-784 (fused_moe_qpa)
  *   mosaic_moe_forward       <- mosaicvm/model/layers.py:284-303 (MoELayer.forward)
+ *   mosaic_moe_forward_ext   <- the same with mosaic_router_ext's routing, which with hash
+ *                               routing is layers.py:394-405 (HashMoELayer.forward)
  *   mosaic_ep_*              <- .mosaicvm/source/inference_model.py:614-650 (MoE.forward,
  *                               expert-sharded; all_reduce replaced by all-to-all)
  */
@@ -117,6 +123,45 @@ MOSAIC_API int mosaic_router(const void* x, const float* weight, const float* bi
                   float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
                   mosaic_stream_t stream);
 
+/* Score functions of the router (the reference's scoring_func / score_func). */
+enum mosaic_score_func {
+  MOSAIC_SCORE_SIGMOID = 0,      /* 1 / (1 + exp(-l))          inference_model.py:573-574 */
+  MOSAIC_SCORE_SQRTSOFTPLUS = 1, /* sqrt(softplus(l)), softplus threshold 20   layers.py:110-115 */
+  MOSAIC_SCORE_SOFTMAX = 2       /* exp(l - max) / sum over the E experts  inference_model.py:571-572 */
+};
+
+/* Router variant: score function and hash routing.  NULL = sigmoid top-k. */
+typedef struct mosaic_route_ext {
+  int32_t score_func;       /* enum mosaic_score_func */
+  int32_t hash;             /* 1: expert ids by token id, not by score (HashRouter) */
+  int32_t layer_idx;        /* hash without a table: the salt's layer index, >= 0 */
+  int32_t reserved;         /* 0 */
+  int64_t table_rows;       /* rows of tid2eid (the vocabulary size), >= 1 */
+  const int32_t* tid2eid;   /* hash table int32 [table_rows, top_k] (device), row token % table_rows
+                               (floor modulo); NULL with hash = 1: the salted hash, top_k 1 */
+  const int64_t* token_ids; /* int64 [T] (device); NULL = 0..T-1 */
+} mosaic_route_ext;
+
+/* mosaic_router with a variant (ext NULL: identical to mosaic_router).
+ * Score s = score_func(logits); without hash the selection is as in
+ * mosaic_router on s + bias.  With hash the ids of token t are row
+ * token_ids[t] mod table_rows of tid2eid in table order (an id outside
+ * [0, E) sets MOSAIC_ERR_RANGE in the error word and reads as 0), the group
+ * limit and bias play no part, and the weights are s gathered at those ids,
+ * normalised when norm_topk_prob and times route_scale (the reference
+ * normalises unless the score is softmax: pass norm_topk_prob accordingly).
+ * Without a table (tid2eid NULL) top_k must be 1, no logits are computed,
+ * weight = route_scale and id = hashed mod E with
+ * salt = layer_idx * 2654435761 mod 2^31 and
+ * hashed = ((int32(token) + salt) * 2654435761) mod 2^31 in int32 tensor
+ * arithmetic (layers.py:180-184 as torch evaluates it: wrapping sum and
+ * product, the literal 2^31 read as -2^31, floor modulo).  x and weight may
+ * be NULL in that case. */
+MOSAIC_API int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, const float* weight, const float* bias,
+                                 int32_t T, int32_t H, int32_t E, int32_t top_k, int32_t n_group,
+                                 int32_t topk_group, float route_scale, int32_t norm_topk_prob, float* weights_out,
+                                 int64_t* idx_out, void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
+
 /* Size of the fixed device scratch of mosaic_router_noalloc (16 MiB). */
 #define MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES (16u << 20)
 
@@ -188,6 +233,15 @@ MOSAIC_API size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims);
 MOSAIC_API int mosaic_moe_forward(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
                        const float* router_bias, const mosaic_expert_bank* bank, void* y, float* weights_out,
                        int64_t* idx_out, void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
+
+/* mosaic_moe_forward with the routing of mosaic_router_ext (ext NULL:
+ * identical to mosaic_moe_forward).  With hash routing and a table this is
+ * HashMoELayer.forward (layers.py:394-405): ids from tid2eid, weights from the
+ * router scores; router_bias is ignored. */
+MOSAIC_API int mosaic_moe_forward_ext(const mosaic_moe_dims* dims, const mosaic_route_ext* ext, const void* x,
+                                      const float* router_weight, const float* router_bias,
+                                      const mosaic_expert_bank* bank, void* y, float* weights_out, int64_t* idx_out,
+                                      void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
 
 /* mosaic_moe_forward that also records caller-created CUDA events
  * (cudaEvent_t handles, any slot may be NULL) on the stream at the stage

@@ -1,6 +1,7 @@
 """mosaic_b200 — B200-native (sm_100a) MoE-layer hot path of Mosaic.
 
-Router (sigmoid, group-limited top-k, selection-only bias), histogram / scan
+Router (sigmoid / sqrt-softplus / softmax scores, group-limited top-k,
+selection-only bias; hash routing by token id), histogram / scan
 permutation, MXFP4 x E4M3 block-scaled tcgen05 expert GEMMs with a fused
 SwiGLU epilogue, shared expert and ordered combine, behind the reference's
 MoE module / operator API; expert parallelism across GPUs in ``ep``.  The
@@ -9,6 +10,8 @@ CUDA library is loaded lazily; building it is ``python -m mosaic_b200.build``.
 from .moe import (  # noqa: F401
     ExactContractError,
     ExpertBank,
+    HashMoELayer,
+    HashRouter,
     MoEConfig,
     MoELayer,
     Router,
@@ -22,6 +25,8 @@ __all__ = [
     "ExactContractError",
     "ExpertBank",
     "ExpertParallelMoELayer",
+    "HashMoELayer",
+    "HashRouter",
     "MoEConfig",
     "MoELayer",
     "Router",

@@ -33,6 +33,13 @@ MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 16 << 20
 MOSAIC_ACT_BF16 = 0
 MOSAIC_ACT_FP8 = 1
 
+# enum mosaic_score_func
+MOSAIC_SCORE_SIGMOID = 0
+MOSAIC_SCORE_SQRTSOFTPLUS = 1
+MOSAIC_SCORE_SOFTMAX = 2
+SCORE_FUNCS = {"sigmoid": MOSAIC_SCORE_SIGMOID, "sqrtsoftplus": MOSAIC_SCORE_SQRTSOFTPLUS,
+               "softmax": MOSAIC_SCORE_SOFTMAX}
+
 # Every symbol the header declares; tests check the library exports all of them.
 EXPORTED = (
     "mosaic_version",
@@ -41,6 +48,7 @@ EXPORTED = (
     "mosaic_router_workspace_bytes",
     "mosaic_router",
     "mosaic_router_noalloc",
+    "mosaic_router_ext",
     "mosaic_layout_assignments",
     "mosaic_emit_tiles",
     "mosaic_act_quant",
@@ -50,6 +58,7 @@ EXPORTED = (
     "mosaic_moe_workspace_bytes",
     "mosaic_moe_forward",
     "mosaic_moe_forward_profiled",
+    "mosaic_moe_forward_ext",
     "mosaic_moe_routed",
     "mosaic_ep_dispatch",
     "mosaic_moe_expert_rows_workspace_bytes",
@@ -95,6 +104,18 @@ class ExpertBankC(ctypes.Structure):
     ]
 
 
+class RouteExtC(ctypes.Structure):
+    _fields_ = [
+        ("score_func", ctypes.c_int32),
+        ("hash", ctypes.c_int32),
+        ("layer_idx", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("table_rows", ctypes.c_int64),
+        ("tid2eid", ctypes.c_void_p),
+        ("token_ids", ctypes.c_void_p),
+    ]
+
+
 EP_MAX_WORLD = 8  # include/mosaic_moe.h MOSAIC_EP_MAX_WORLD
 
 
@@ -127,6 +148,8 @@ _SIGS = {
     "mosaic_router_workspace_bytes": ([_I, _I, _I], _SZ),
     "mosaic_router": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P, _SZ, _P], ctypes.c_int),
     "mosaic_router_noalloc": ([_P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P, _P], ctypes.c_int),
+    "mosaic_router_ext": ([ctypes.POINTER(RouteExtC), _P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _P, _P,
+                           _P, _SZ, _P], ctypes.c_int),
     "mosaic_layout_assignments": ([_P, _I, _I, _P, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_emit_tiles": ([_P, _I, _I, _I, _P, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_act_quant": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
@@ -138,6 +161,8 @@ _SIGS = {
                            ctypes.c_int),
     "mosaic_moe_forward_profiled": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _P, _P,
                                      _SZ, _P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mosaic_moe_forward_ext": ([ctypes.POINTER(MoEDims), ctypes.POINTER(RouteExtC), _P, _P, _P,
+                                ctypes.POINTER(ExpertBankC), _P, _P, _P, _P, _SZ, _P], ctypes.c_int),
     "mosaic_moe_routed": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _SZ, _P],
                           ctypes.c_int),
     "mosaic_ep_dispatch": ([ctypes.POINTER(MoEDims), _I, _P, _P, _P, _P, _P, _P, _SZ, _P], ctypes.c_int),

@@ -400,6 +400,32 @@ int router_args_ok(const void* x, const float* weight, int32_t T, int32_t H, int
   return MOSAIC_OK;
 }
 
+// Host-side check of a router variant; fills the launch-side description.
+int route_variant(const mosaic_route_ext* ext, int32_t top_k, RouteVariant* rv) {
+  *rv = RouteVariant{};
+  if (!ext) return MOSAIC_OK;
+  if (ext->score_func < MOSAIC_SCORE_SIGMOID || ext->score_func > MOSAIC_SCORE_SOFTMAX) return MOSAIC_ERR_UNSUPPORTED;
+  if ((ext->hash != 0 && ext->hash != 1) || ext->reserved != 0) return MOSAIC_ERR_SHAPE;
+  rv->score_func = ext->score_func;
+  rv->hash = ext->hash;
+  if (!ext->hash) return MOSAIC_OK;
+  if (ext->token_ids && !aligned(ext->token_ids, 8)) return MOSAIC_ERR_ALIGN;
+  rv->token_ids = ext->token_ids;
+  if (ext->tid2eid) {
+    if (ext->table_rows < 1) return MOSAIC_ERR_SHAPE;
+    if (!aligned(ext->tid2eid, 4)) return MOSAIC_ERR_ALIGN;
+    rv->tid2eid = ext->tid2eid;
+    rv->table_rows = ext->table_rows;
+    return MOSAIC_OK;
+  }
+  if (ext->layer_idx < 0 || top_k != 1) return MOSAIC_ERR_SHAPE;
+  rv->salt = static_cast<int32_t>((static_cast<int64_t>(ext->layer_idx) * 2654435761LL) % 2147483648LL);
+  return MOSAIC_OK;
+}
+
+// True when the variant needs no logits (table-less hash routing).
+bool salted_hash(const RouteVariant& rv) { return rv.hash && !rv.tid2eid; }
+
 constexpr int kMaxDevices = 64;
 
 // Device address of g_router_scratch, looked up once per device.
@@ -463,6 +489,36 @@ int mosaic_router(const void* x, const float* weight, const float* bias, int32_t
   cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
                                 weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
                                 reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, const float* weight, const float* bias, int32_t T,
+                      int32_t H, int32_t E, int32_t top_k, int32_t n_group, int32_t topk_group, float route_scale,
+                      int32_t norm_topk_prob, float* weights_out, int64_t* idx_out, void* workspace,
+                      size_t workspace_bytes, mosaic_stream_t stream) {
+  RouteVariant rv;
+  int st = route_variant(ext, top_k, &rv);
+  if (st != MOSAIC_OK) return st;
+  if (salted_hash(rv)) {  // no logits: x and weight are not read
+    if (!weights_out || !idx_out) return MOSAIC_ERR_SHAPE;
+    if (T < 1 || E < 1 || E > 256) return MOSAIC_ERR_SHAPE;
+    cudaError_t e = launch_router(nullptr, nullptr, nullptr, T, H, E, top_k, 1, 1, route_scale, norm_topk_prob,
+                                  weights_out, idx_out, nullptr, 1, nullptr, reinterpret_cast<cudaStream_t>(stream),
+                                  &rv);
+    return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  }
+  if (!workspace) return MOSAIC_ERR_SHAPE;
+  st = router_args_ok(x, weight, T, H, E, top_k, n_group, topk_group, weights_out, idx_out);
+  if (st != MOSAIC_OK) return st;
+  if (!aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  if (workspace_bytes < mosaic_router_workspace_bytes(T, H, E)) return MOSAIC_ERR_WORKSPACE;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  const int splits = router_splits(T, H, E, sms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
+                                weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
+                                reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream), &rv);
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
@@ -549,16 +605,24 @@ size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims) {
   return plan_ws(dims).total;
 }
 
-int mosaic_moe_forward_profiled(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
-                                const float* router_bias, const mosaic_expert_bank* bank, void* y,
-                                float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
-                                mosaic_stream_t stream, void* const* stage_events) {
+}  // extern "C"
+
+namespace {
+
+int moe_forward_impl(const mosaic_moe_dims* dims, const mosaic_route_ext* ext, const void* x,
+                     const float* router_weight, const float* router_bias, const mosaic_expert_bank* bank, void* y,
+                     float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
+                     mosaic_stream_t stream, void* const* stage_events) {
   int st = check_dims(dims);
   if (st) return st;
-  if (!x || !router_weight || !y || !weights_out || !idx_out || !workspace) return MOSAIC_ERR_SHAPE;
+  RouteVariant rv;
+  st = route_variant(ext, dims->top_k, &rv);
+  if (st) return st;
+  const bool need_logits = !salted_hash(rv);
+  if (!x || (need_logits && !router_weight) || !y || !weights_out || !idx_out || !workspace) return MOSAIC_ERR_SHAPE;
   st = check_bank(bank);
   if (st) return st;
-  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(router_weight, 16) || !aligned(workspace, 256))
+  if (!aligned(x, 16) || !aligned(y, 16) || (need_logits && !aligned(router_weight, 16)) || !aligned(workspace, 256))
     return MOSAIC_ERR_ALIGN;
   const WsPlan w = plan_ws(dims);
   if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
@@ -566,21 +630,41 @@ int mosaic_moe_forward_profiled(const mosaic_moe_dims* dims, const void* x, cons
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(stage_events, 0, s)) return MOSAIC_ERR_CUDA;
-  cudaError_t e = launch_router(x, router_weight, router_bias, dims->tokens, dims->hidden, dims->n_experts,
-                                dims->top_k, dims->n_group, dims->topk_group, dims->route_scale,
+  cudaError_t e = launch_router(x, router_weight, rv.hash ? nullptr : router_bias, dims->tokens, dims->hidden,
+                                dims->n_experts, dims->top_k, dims->n_group, dims->topk_group, dims->route_scale,
                                 dims->norm_topk_prob, weights_out, idx_out,
                                 reinterpret_cast<float*>(ws + w.router_part), w.splits,
-                                reinterpret_cast<int*>(ws + w.err), s);
+                                reinterpret_cast<int*>(ws + w.err), s, &rv);
   if (e != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(stage_events, 1, s)) return MOSAIC_ERR_CUDA;
   return run_experts(dims, w, ws, x, idx_out, weights_out, bank, y, s, stage_events);
 }
 
+}  // namespace
+
+extern "C" {
+
+int mosaic_moe_forward_profiled(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
+                                const float* router_bias, const mosaic_expert_bank* bank, void* y,
+                                float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
+                                mosaic_stream_t stream, void* const* stage_events) {
+  return moe_forward_impl(dims, nullptr, x, router_weight, router_bias, bank, y, weights_out, idx_out, workspace,
+                          workspace_bytes, stream, stage_events);
+}
+
 int mosaic_moe_forward(const mosaic_moe_dims* dims, const void* x, const float* router_weight,
                        const float* router_bias, const mosaic_expert_bank* bank, void* y, float* weights_out,
                        int64_t* idx_out, void* workspace, size_t workspace_bytes, mosaic_stream_t stream) {
-  return mosaic_moe_forward_profiled(dims, x, router_weight, router_bias, bank, y, weights_out, idx_out, workspace,
-                                     workspace_bytes, stream, nullptr);
+  return moe_forward_impl(dims, nullptr, x, router_weight, router_bias, bank, y, weights_out, idx_out, workspace,
+                          workspace_bytes, stream, nullptr);
+}
+
+int mosaic_moe_forward_ext(const mosaic_moe_dims* dims, const mosaic_route_ext* ext, const void* x,
+                           const float* router_weight, const float* router_bias, const mosaic_expert_bank* bank,
+                           void* y, float* weights_out, int64_t* idx_out, void* workspace, size_t workspace_bytes,
+                           mosaic_stream_t stream) {
+  return moe_forward_impl(dims, ext, x, router_weight, router_bias, bank, y, weights_out, idx_out, workspace,
+                          workspace_bytes, stream, nullptr);
 }
 
 int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,

@@ -50,10 +50,20 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
                             cudaStream_t stream);
 
 // ---- router (router.cu)
+// Score function and hash routing of one router call (defaults: sigmoid top-k).
+struct RouteVariant {
+  int score_func = MOSAIC_SCORE_SIGMOID;
+  int hash = 0;                        // ids by token id instead of by score
+  int32_t salt = 0;                    // table-less hash: layer_idx * 2654435761 mod 2^31
+  const int32_t* tid2eid = nullptr;    // [table_rows][top_k]; null with hash = salted hash
+  long long table_rows = 0;
+  const int64_t* token_ids = nullptr;  // [T]; null = 0..T-1
+};
 int router_splits(int T, int H, int E, int num_sms);
 cudaError_t launch_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
                           int n_group, int topk_group, float route_scale, int norm, float* weights_out,
-                          int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream);
+                          int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream,
+                          const RouteVariant* variant = nullptr);
 
 // ---- layout (layout.cu)
 struct LayoutParams {

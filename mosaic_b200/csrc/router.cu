@@ -1,15 +1,21 @@
-// Sigmoid group-limited top-k router (fp32 CUDA cores).
+// Group-limited top-k router and hash router (fp32 CUDA cores).
 //
-// Reference behaviour: mosaicvm/model/layers.py:127-150 (Router.forward) with
-// the sigmoid score of .mosaicvm/source/inference_model.py:573-574 (Gate);
-// the group limit follows the published DeepSeek-V3 rule (group score = sum
-// of the two largest biased scores, keep topk_group groups, mask the rest).
+// Reference behaviour: mosaicvm/model/layers.py:127-150 (Router.forward) and
+// the vendored Gate, .mosaicvm/source/inference_model.py:569-589, whose three
+// score functions are kept: sigmoid (:573-574), softmax (:571-572) and
+// sqrt(softplus) (:575-576, = layers.py:110-115 _router_scores).  The group
+// limit follows the published DeepSeek-V3 rule (group score = sum of the two
+// largest biased scores, keep topk_group groups, mask the rest).  Hash routing
+// (layers.py:171-197 HashRouter.forward, Gate's tid2eid branch :581-582) takes
+// the ids from a token-id table instead of the top-k, and without a table uses
+// the salted multiplicative hash of layers.py:180-184.
 //
 // Kernel 1 computes fp32 logits x . W^T with a deterministic split-K: every
 // split sums its K range sequentially with FMAs and writes its own partial;
 // kernel 2 (one warp per token) adds the partials in split order, so a
-// logit never depends on scheduling.  Kernel 2 then applies sigmoid + bias,
-// the group limit and the top-k, and normalises the unbiased weights.
+// logit never depends on scheduling.  Kernel 2 then applies the score function
+// + bias, the group limit and the top-k (or the table lookup), and normalises
+// the unbiased weights.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -180,12 +186,27 @@ __device__ __forceinline__ bool better(float v, int e, float v2, int e2) {
   return v > v2 || (v == v2 && e < e2);
 }
 
+// Warp-wide reductions (every lane gets the result).
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// sqrt(softplus(l)) with torch's softplus (beta 1, threshold 20: l itself above 20).
+__device__ __forceinline__ float sqrt_softplus(float l) { return sqrtf(l > 20.f ? l : log1pf(expf(l))); }
+
 template <int PER>
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits,
                                                           const float* __restrict__ bias, int T, int E, int top_k,
                                                           int n_group, int topk_group, float route_scale,
                                                           int norm, float* __restrict__ w_out,
-                                                          int64_t* __restrict__ idx_out, int* err) {
+                                                          int64_t* __restrict__ idx_out, int* err, RouteVariant rv) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // one warp per token
   if (t >= T) return;
@@ -232,18 +253,46 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
       if (lane * PER + i < E)
         for (int sp = 0; sp < splits; ++sp) logit[i] += pp[sp * stride + i];
   }
+  if (rv.score_func == MOSAIC_SCORE_SOFTMAX) {
+    // max-shifted exponentials times the reciprocal of their sum
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane * PER + i < E) m = fmaxf(m, logit[i]);
+    m = warp_max(m);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      s[i] = lane * PER + i < E ? expf(logit[i] - m) : 0.f;
+      sum += s[i];
+    }
+    const float inv = 1.0f / warp_sum(sum);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) s[i] *= inv;
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      s[i] = rv.score_func == MOSAIC_SCORE_SQRTSOFTPLUS ? sqrt_softplus(logit[i]) : 1.0f / (1.0f + expf(-logit[i]));
+  }
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane * PER + i;
     if (e < E) {
-      s[i] = 1.0f / (1.0f + expf(-logit[i]));
       sel[i] = s[i] + (bias ? bias[e] : 0.f);
     } else {
       s[i] = 0.f;
       sel[i] = -INFINITY;
     }
   }
-  if (n_group > 1 && topk_group < n_group) {
+  // hash routing: the ids come from the token's table row, in table order
+  const int32_t* trow = nullptr;
+  if (rv.tid2eid) {
+    const long long tk = rv.token_ids ? static_cast<long long>(rv.token_ids[t]) : static_cast<long long>(t);
+    long long r = tk % rv.table_rows;
+    if (r < 0) r += rv.table_rows;  // floor modulo, as torch's % on int64
+    trow = rv.tid2eid + r * top_k;
+  }
+  if (!trow && n_group > 1 && topk_group < n_group) {
     const int gsz = E / n_group;
     float my_gscore = -INFINITY;
     const int lpg = gsz / PER;  // lanes per group when a lane's experts lie in one group
@@ -315,28 +364,37 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   int iv[8];
   float sum = 0.f;
   for (int j = 0; j < top_k; ++j) {
-    float bv = -INFINITY;
-    int be = 0x7FFFFFFF;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = lane * PER + i;
-      if (e < E && better(sel[i], e, bv, be)) {
-        bv = sel[i];
-        be = e;
+    int be;
+    if (trow) {
+      be = trow[j];  // warp-uniform
+      if (be < 0 || be >= E) {
+        if (lane == 0) set_error(err, MOSAIC_ERR_RANGE);
+        be = 0;
       }
-    }
+    } else {
+      float bv = -INFINITY;
+      be = 0x7FFFFFFF;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-      if (better(ov, oe, bv, be)) {
-        bv = ov;
-        be = oe;
+      for (int i = 0; i < PER; ++i) {
+        const int e = lane * PER + i;
+        if (e < E && better(sel[i], e, bv, be)) {
+          bv = sel[i];
+          be = e;
+        }
       }
-    }
-    if (be >= E || bv == -INFINITY) {
-      if (lane == 0) set_error(err, MOSAIC_ERR_RANGE);
-      be = 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
+        if (better(ov, oe, bv, be)) {
+          bv = ov;
+          be = oe;
+        }
+      }
+      if (be >= E || bv == -INFINITY) {
+        if (lane == 0) set_error(err, MOSAIC_ERR_RANGE);
+        be = 0;
+      }
     }
     const int owner = be / PER;
     float my_s = 0.f;
@@ -344,7 +402,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     for (int i = 0; i < PER; ++i) {
       if (lane == owner && lane * PER + i == be) {
         my_s = s[i];
-        sel[i] = -INFINITY;
+        if (!trow) sel[i] = -INFINITY;  // a table may name an expert twice
       }
     }
     const float sv = __shfl_sync(0xFFFFFFFFu, my_s, owner);
@@ -370,6 +428,29 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   }
 }
 
+// Table-less hash routing (layers.py:180-184): one expert per token,
+//   salt   = layer_idx * 2654435761 mod 2^31          (Python integers)
+//   hashed = ((int32(token) + salt) * 2654435761) mod 2^31
+//   id     = hashed mod E,  weight = route_scale
+// evaluated as torch evaluates it on int32 tensors: the sum and the product
+// wrap modulo 2^32, the literal 2^31 wraps to -2^31, and % is the floor
+// modulo, so the first remainder lies in (-2^31, 0] and the second in [0, E).
+__global__ void router_hash_salted_kernel(const int64_t* __restrict__ token_ids, int T, int E, int32_t salt,
+                                          float route_scale, float* __restrict__ w_out,
+                                          int64_t* __restrict__ idx_out) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const uint32_t tok = static_cast<uint32_t>(token_ids ? token_ids[t] : static_cast<int64_t>(t));
+  const uint32_t h = (tok + static_cast<uint32_t>(salt)) * 2654435761u;
+  const int32_t hs = static_cast<int32_t>(h);
+  // floor(hs / -2^31) is -1 for hs > 0 and 0 otherwise (hs > -2^31 or == -2^31 -> 0 remainder)
+  int64_t r = hs > 0 ? static_cast<int64_t>(hs) - 2147483648LL : (hs == INT32_MIN ? 0 : static_cast<int64_t>(hs));
+  int64_t id = r % E;
+  if (id < 0) id += E;
+  w_out[t] = route_scale;
+  idx_out[t] = id;
+}
+
 }  // namespace
 
 // Split-K factor of the logits kernel for small batches: ~2 CTAs per SM with
@@ -386,7 +467,14 @@ int router_splits(int T, int H, int E, int num_sms) {
 
 cudaError_t launch_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
                           int n_group, int topk_group, float route_scale, int norm, float* weights_out,
-                          int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream) {
+                          int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream,
+                          const RouteVariant* variant) {
+  const RouteVariant rv = variant ? *variant : RouteVariant{};
+  if (rv.hash && !rv.tid2eid) {
+    router_hash_salted_kernel<<<(T + 255) / 256, 256, 0, stream>>>(rv.token_ids, T, E, rv.salt, route_scale,
+                                                                   weights_out, idx_out);
+    return cudaGetLastError();
+  }
   int kchunk = (H + splits - 1) / splits;
   kchunk = (kchunk + kTileK - 1) / kTileK * kTileK;
   const int used = (H + kchunk - 1) / kchunk;
@@ -403,7 +491,7 @@ cudaError_t launch_router(const void* x, const float* w, const float* bias, int 
   const int per = (E + 31) / 32;
 #define MOSAIC_TOPK(P)                                                                                      \
   router_topk_kernel<P><<<g2, 32 * wpb, 0, stream>>>(partial, used, bias, T, E, top_k, n_group, topk_group,     \
-                                                route_scale, norm, weights_out, idx_out, err)
+                                                route_scale, norm, weights_out, idx_out, err, rv)
   if (per <= 1)
     MOSAIC_TOPK(1);
   else if (per <= 2)

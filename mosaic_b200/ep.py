@@ -33,7 +33,7 @@ from torch import nn
 
 from . import _capi as C
 from . import ops
-from .moe import ExpertBank, MoEConfig, Router
+from .moe import ExpertBank, HashRouter, MoEConfig, Router
 
 
 def expert_range(n_experts: int, world: int, rank: int) -> tuple[int, int]:
@@ -88,6 +88,9 @@ class CudaEPKernels:
 
     def route(self, router: Router, x: torch.Tensor):
         return router(x)
+
+    def route_hash(self, router: HashRouter, x: torch.Tensor, token_ids):
+        return router(x, token_ids)
 
     def dispatch(self, dims: C.MoEDims, world: int, x, idx, w):
         lib = C.lib()
@@ -219,11 +222,15 @@ class ExpertParallelMoELayer(nn.Module):
     ``local_bank`` holds this rank's experts (``expert_range``) followed by the
     shared expert when ``cfg.n_shared_experts``; ``shard_bank`` builds it from
     the full reference-layout bank.  ``forward`` takes this rank's tokens and
-    returns their layer output; every rank of the group must call it.
+    returns their layer output; every rank of the group must call it.  With
+    ``layer_idx`` the layer is hash-routed (``HashMoELayer``,
+    mosaicvm/model/layers.py:376-405): ``.hash_router`` replaces ``.router``
+    and ``forward(x, token_ids)`` routes by token id.
     """
 
     def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None, exchange: str = "nccl",
-                 max_tokens: int | None = None, peer_exchange: "PeerExchange | None" = None):
+                 max_tokens: int | None = None, peer_exchange: "PeerExchange | None" = None,
+                 layer_idx: int | None = None):
         super().__init__()
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
@@ -241,7 +248,8 @@ class ExpertParallelMoELayer(nn.Module):
         self.e_lo, self.e_hi = expert_range(cfg.n_routed_experts, self.world, self.rank)
         self.bank = local_bank
         self.has_shared = cfg.n_shared_experts > 0
-        self.router = Router(cfg)
+        self.router = Router(cfg) if layer_idx is None else None
+        self.hash_router = HashRouter(cfg, layer_idx) if layer_idx is not None else None
         self.kernels = kernels if kernels is not None else CudaEPKernels()
         self.last_weights = None
         self.last_idx = None
@@ -254,7 +262,8 @@ class ExpertParallelMoELayer(nn.Module):
             if self.max_tokens is None:
                 raise ValueError("exchange='p2p' needs max_tokens")
             self._px = PeerExchange(group=self.group, max_tokens=self.max_tokens,
-                                    top_k=self.cfg.num_experts_per_tok, n_experts=self.cfg.n_routed_experts,
+                                    top_k=max(self.cfg.num_experts_per_tok, self._k()),
+                                    n_experts=self.cfg.n_routed_experts,
                                     hidden=self.cfg.hidden_size, partial_f32=self.cfg.act_mode == "bf16")
         return self._px
 
@@ -272,13 +281,38 @@ class ExpertParallelMoELayer(nn.Module):
         b = layer.bank
         local = shard_bank(b.gu_packed, b.gu_scale, b.dn_packed, b.dn_scale, rank=rank, world=world,
                            n_experts=layer.cfg.n_routed_experts, has_shared=b.has_shared)
-        ep = cls(layer.cfg, local, group=group, kernels=kernels, exchange=exchange, max_tokens=max_tokens)
-        ep.router.weight.data = layer.router.weight.data
-        ep.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
+        hr = getattr(layer, "hash_router", None)
+        ep = cls(layer.cfg, local, group=group, kernels=kernels, exchange=exchange, max_tokens=max_tokens,
+                 layer_idx=None if hr is None else hr.layer_idx)
+        if hr is not None:
+            ep.hash_router.weight.data = hr.weight.data
+            ep.hash_router.tid2eid = hr.tid2eid
+        else:
+            ep.router.weight.data = layer.router.weight.data
+            ep.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
         return ep
 
-    def _local_dims(self, tokens: int) -> C.MoEDims:
+    def _k(self) -> int:
+        """Experts per token: the config's, or a hash table's width (1 without a table)."""
+        hr = self.hash_router
+        if hr is None:
+            return self.cfg.num_experts_per_tok
+        if hr.tid2eid is None:
+            return 1
+        return 1 if hr.tid2eid.dim() == 1 else int(hr.tid2eid.shape[1])
+
+    def _route(self, xf, token_ids):
+        if self.hash_router is not None:
+            return self.kernels.route_hash(self.hash_router, xf, token_ids)
+        return self.kernels.route(self.router, xf)
+
+    def _dims(self, tokens: int) -> C.MoEDims:
         d = self.cfg.dims(tokens, self.has_shared)
+        d.top_k = self._k()
+        return d
+
+    def _local_dims(self, tokens: int) -> C.MoEDims:
+        d = self._dims(tokens)
         d.n_experts = self.e_hi - self.e_lo
         return d
 
@@ -289,11 +323,11 @@ class ExpertParallelMoELayer(nn.Module):
         return dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
                                       group=self.group, async_op=async_op)
 
-    def _forward_p2p(self, xf: torch.Tensor) -> torch.Tensor:
+    def _forward_p2p(self, xf: torch.Tensor, token_ids=None) -> torch.Tensor:
         """One step with the device-driven peer-memory exchange: no host
         synchronisation, so the step can be captured in a CUDA graph."""
         t, h = xf.shape
-        k = self.cfg.num_experts_per_tok
+        k = self._k()
         px = self.peer_exchange()
         if t > px.max_tokens:
             raise ValueError(f"{t} tokens exceed the exchange capacity {px.max_tokens}")
@@ -315,8 +349,8 @@ class ExpertParallelMoELayer(nn.Module):
                 out = px.ret_partials + t * k * h * elem
                 kern._rows(dl, self.bank, t, xf.data_ptr(), h, None, None, 1, dl.n_experts, _RawOut(out),
                            kern._ws_shared, xf.device)
-        w, idx = kern.route(self.router, xf)
-        dims = self.cfg.dims(t, self.has_shared)
+        w, idx = self._route(xf, token_ids)
+        dims = self._dims(t)
         send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
         pe = ctypes.byref(px.peers)
         C.check(lib.mosaic_ep_exchange_rows(pe, ops._ptr(send), ops._ptr(counts), ops._stream()),
@@ -335,18 +369,20 @@ class ExpertParallelMoELayer(nn.Module):
         self.last_weights, self.last_idx, self.last_counts = w, idx, None
         return y
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, token_ids: torch.Tensor | None = None) -> torch.Tensor:
         shape = x.shape
+        if token_ids is not None and self.hash_router is None:
+            raise ValueError("token_ids are only used by a hash-routed layer")
         if self.exchange == "p2p":
             xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
-            return self._forward_p2p(xf).to(x.dtype).view(shape)
+            return self._forward_p2p(xf, token_ids).to(x.dtype).view(shape)
         xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
         t, h = xf.shape
-        k = self.cfg.num_experts_per_tok
+        k = self._k()
         kern = self.kernels
-        dims = self.cfg.dims(t, self.has_shared)
+        dims = self._dims(t)
         if t > 0:
-            w, idx = kern.route(self.router, xf)
+            w, idx = self._route(xf, token_ids)
             send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
         else:  # no tokens here, but this rank still serves its experts in every exchange
             w = torch.empty(0, k, dtype=torch.float32, device=xf.device)

@@ -4,9 +4,15 @@ Reference API mirrored (paths inside fazin-ahamed/Mosaic):
 
 * ``Router`` <- ``mosaicvm/model/layers.py:118-150``: parameters ``weight`` [E, H]
   and ``e_score_correction_bias`` [E]; ``forward(x) -> (weights fp32 [bt, k],
-  idx int64 [bt, k])``.  Sigmoid scores (vendored ``Gate``,
-  ``.mosaicvm/source/inference_model.py:573-574``) plus the DeepSeek-V3 group
-  limit (``n_group`` / ``topk_group``).
+  idx int64 [bt, k])``.  ``scoring_func`` "sigmoid" (vendored ``Gate``,
+  ``.mosaicvm/source/inference_model.py:573-574``), "sqrtsoftplus"
+  (``layers.py:110-115``) or "softmax" (``Gate``, ``:571-572``), plus the
+  DeepSeek-V3 group limit (``n_group`` / ``topk_group``).
+* ``HashRouter`` <- ``mosaicvm/model/layers.py:153-197``: ``weight``,
+  ``tid2eid`` (None = salted fallback, an ``ExactContractError`` under the
+  exact target), ``forward(x, token_ids=None)``.
+* ``HashMoELayer`` <- ``mosaicvm/model/layers.py:376-405``:
+  ``.hash_router``, ``forward(x, token_ids=None)``.
 * ``MoELayer`` <- ``mosaicvm/model/layers.py:274-306``: ``.router``,
   ``.shared_expert`` (here the bank's last expert), ``.experts_gate_up()``,
   ``.experts_down()``, ``forward(x [b, t, H]) -> [b, t, H]`` in x's dtype.
@@ -64,7 +70,7 @@ class MoEConfig:
     act_mode: str = "bf16"  # "bf16" (decode) or "fp8" (reference act_quant semantics)
 
     def validate(self) -> None:
-        if self.scoring_func != "sigmoid":
+        if self.scoring_func not in C.SCORE_FUNCS:
             raise ValueError(f"unknown scoring_func {self.scoring_func}")
         if self.n_shared_experts not in (0, 1):
             raise ExactContractError("n_shared_experts must be 0 or 1")
@@ -169,7 +175,7 @@ class _Workspace:
 
 
 class Router(nn.Module):
-    """Linear + sigmoid scores + bias-corrected (group-limited) top-k (layers.py:118-150)."""
+    """Linear + scores + bias-corrected (group-limited) top-k (layers.py:118-150)."""
 
     def __init__(self, cfg: MoEConfig):
         super().__init__()
@@ -182,7 +188,65 @@ class Router(nn.Module):
         return ops.router(x.to(torch.bfloat16).contiguous(), self.weight.float().contiguous(),
                           self.e_score_correction_bias.float().contiguous(), top_k=c.num_experts_per_tok,
                           n_group=c.n_group, topk_group=c.topk_group, route_scale=c.routed_scaling_factor,
-                          norm_topk_prob=c.norm_topk_prob)
+                          norm_topk_prob=c.norm_topk_prob, score_func=c.scoring_func)
+
+
+class HashRouter(nn.Module):
+    """Hash-routed layers (layers.py:153-197): ids from ``tid2eid``, weights the
+    router scores gathered there, normalised unless the score is softmax, times
+    ``routed_scaling_factor``.  Without a table: ``ExactContractError`` under the
+    exact target, else the salted hash (one expert per token, weight
+    ``routed_scaling_factor``)."""
+
+    def __init__(self, cfg: MoEConfig, layer_idx: int):
+        super().__init__()
+        cfg.validate()
+        self.cfg = cfg
+        self.layer_idx = layer_idx
+        self.weight = nn.Parameter(torch.zeros(cfg.n_routed_experts, cfg.hidden_size), requires_grad=False)
+        self.tid2eid = None
+        self._table = (None, None)  # (source tensor, checked device int32 table)
+
+    def table(self, device):
+        """The int32 [V, k] device table, range-checked once per ``tid2eid`` tensor.
+
+        An id outside [0, E) raises ``IndexError``, as the reference's gather would."""
+        src, tab = self._table
+        if src is not self.tid2eid or tab is None or tab.device != torch.device(device):
+            tab = ops.hash_table(self.tid2eid, device)
+            if int(tab.min()) < 0 or int(tab.max()) >= self.cfg.n_routed_experts:
+                raise IndexError(f"HashRouter layer {self.layer_idx}: tid2eid holds an id outside "
+                                 f"[0, {self.cfg.n_routed_experts})")
+            self._table = (self.tid2eid, tab)
+        return tab
+
+    def route_ext(self, x, token_ids):
+        """(mosaic_route_ext, tensors it points at, top_k) of one call."""
+        c = self.cfg
+        n = x.shape[0]
+        tok = None
+        if token_ids is not None:
+            tok = token_ids.reshape(-1)
+            if tok.numel() != n:
+                raise ValueError(f"token_ids has {tok.numel()} entries for {n} tokens")
+            tok = tok.to(device=x.device, dtype=torch.int64).contiguous()
+        if self.tid2eid is None:
+            if exact_target():
+                raise ExactContractError(f"HashRouter layer {self.layer_idx}: tid2eid required under exact target")
+            ext = ops.route_ext(c.scoring_func, token_ids=tok, hash_routing=True, layer_idx=self.layer_idx)
+            return ext, (tok,), 1
+        tab = self.table(x.device)
+        ext = ops.route_ext(c.scoring_func, tid2eid=tab, token_ids=tok, hash_routing=True, layer_idx=self.layer_idx)
+        return ext, (tok, tab), tab.shape[1]
+
+    def forward(self, x, token_ids=None):
+        c = self.cfg
+        if self.tid2eid is None and exact_target():
+            raise ExactContractError(f"HashRouter layer {self.layer_idx}: tid2eid required under exact target")
+        tab = None if self.tid2eid is None else self.table(x.device)
+        return ops.hash_router(x.to(torch.bfloat16).contiguous(), self.weight.float().contiguous(), tab, token_ids,
+                               n_experts=c.n_routed_experts, layer_idx=self.layer_idx, score_func=c.scoring_func,
+                               route_scale=c.routed_scaling_factor)
 
 
 class MoELayer(nn.Module):
@@ -223,21 +287,59 @@ class MoELayer(nn.Module):
             raise NotImplementedError("MoELayer has no expert bank")
         shape = x.shape
         xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
-        t = xf.shape[0]
         if xf.device.type != "cuda":
             raise ValueError("MoELayer.forward requires a CUDA input (no CPU path)")
+        ext = None if self.cfg.scoring_func == "sigmoid" else ops.route_ext(self.cfg.scoring_func)
+        y = self._forward(xf, ext, self.cfg.num_experts_per_tok, self.cfg.norm_topk_prob,
+                          self.router.weight.data, self.router.e_score_correction_bias.data)
+        return y.to(x.dtype).view(shape)
+
+    def _forward(self, xf, ext, top_k, norm, router_weight, router_bias):
+        """One mosaic_moe_forward(_ext) call on bf16 rows ``xf`` [T, H]."""
+        t = xf.shape[0]
         dims = self.cfg.dims(t, self.bank.has_shared)
+        dims.top_k = top_k
+        dims.norm_topk_prob = int(bool(norm))
         ws = self._ws.get(dims, xf.device)
         y = torch.empty_like(xf)
-        w = torch.empty(t, self.cfg.num_experts_per_tok, dtype=torch.float32, device=xf.device)
-        idx = torch.empty(t, self.cfg.num_experts_per_tok, dtype=torch.int64, device=xf.device)
+        w = torch.empty(t, top_k, dtype=torch.float32, device=xf.device)
+        idx = torch.empty(t, top_k, dtype=torch.int64, device=xf.device)
         bank = self.bank.c_struct()
-        st = C.lib().mosaic_moe_forward(ctypes.byref(dims), ops._ptr(xf), ops._ptr(self.router.weight.data),
-                                        ops._ptr(self.router.e_score_correction_bias.data), ctypes.byref(bank),
-                                        ops._ptr(y), ops._ptr(w), ops._ptr(idx), ops._ptr(ws), ws.numel(),
-                                        ops._stream())
-        C.check(st, "mosaic_moe_forward")
+        rw = None if router_weight is None else router_weight.float().contiguous()
+        rb = None if router_bias is None else router_bias.float().contiguous()
+        if ext is None:
+            st = C.lib().mosaic_moe_forward(ctypes.byref(dims), ops._ptr(xf), ops._ptr(rw), ops._ptr(rb),
+                                            ctypes.byref(bank), ops._ptr(y), ops._ptr(w), ops._ptr(idx), ops._ptr(ws),
+                                            ws.numel(), ops._stream())
+            C.check(st, "mosaic_moe_forward")
+        else:
+            st = C.lib().mosaic_moe_forward_ext(ctypes.byref(dims), ctypes.byref(ext), ops._ptr(xf), ops._ptr(rw),
+                                                ops._ptr(rb), ctypes.byref(bank), ops._ptr(y), ops._ptr(w),
+                                                ops._ptr(idx), ops._ptr(ws), ws.numel(), ops._stream())
+            C.check(st, "mosaic_moe_forward_ext")
         self.last_weights, self.last_idx = w, idx
+        return y
+
+
+class HashMoELayer(MoELayer):
+    """MoE layer with hash routing (layers.py:376-405) on an MXFP4 bank:
+    ``.hash_router`` (a :class:`HashRouter`), ``forward(x, token_ids=None)``."""
+
+    def __init__(self, cfg: MoEConfig, layer_idx: int, bank: ExpertBank | None = None):
+        super().__init__(cfg, bank)
+        self.router = None
+        self.hash_router = HashRouter(cfg, layer_idx)
+
+    def forward(self, x, token_ids=None):
+        if self.bank is None:
+            raise NotImplementedError("MoELayer has no expert bank")
+        shape = x.shape
+        xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        if xf.device.type != "cuda":
+            raise ValueError("HashMoELayer.forward requires a CUDA input (no CPU path)")
+        ext, keep, k = self.hash_router.route_ext(xf, token_ids)
+        y = self._forward(xf, ext, k, self.cfg.scoring_func != "softmax", self.hash_router.weight.data, None)
+        del keep
         return y.to(x.dtype).view(shape)
 
 

@@ -40,9 +40,36 @@ def _u8(t: torch.Tensor) -> torch.Tensor:
     raise TypeError(f"expected uint8-compatible tensor, got {t.dtype}")
 
 
+def score_func_code(score_func: str) -> int:
+    """``scoring_func`` name (V4Config / ModelArgs.score_func) -> enum mosaic_score_func."""
+    try:
+        return C.SCORE_FUNCS[score_func]
+    except KeyError:
+        raise ValueError(f"unknown scoring_func {score_func}") from None
+
+
+def route_ext(score_func: str = "sigmoid", *, tid2eid: torch.Tensor | None = None,
+              token_ids: torch.Tensor | None = None, hash_routing: bool = False,
+              layer_idx: int = 0) -> C.RouteExtC:
+    """The ``mosaic_route_ext`` of a router call (the tensors must outlive the call)."""
+    ext = C.RouteExtC()
+    ext.score_func = score_func_code(score_func)
+    ext.hash = int(bool(hash_routing))
+    ext.layer_idx = int(layer_idx)
+    ext.table_rows = 0 if tid2eid is None else int(tid2eid.shape[0])
+    ext.tid2eid = None if tid2eid is None else tid2eid.data_ptr()
+    ext.token_ids = None if token_ids is None else token_ids.data_ptr()
+    return ext
+
+
 def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, *, top_k: int, n_group: int = 1,
-           topk_group: int = 1, route_scale: float = 1.0, norm_topk_prob: bool = True):
-    """Sigmoid (group-limited) top-k router -> (weights fp32 [T, k], idx int64 [T, k])."""
+           topk_group: int = 1, route_scale: float = 1.0, norm_topk_prob: bool = True,
+           score_func: str = "sigmoid"):
+    """(Group-limited) top-k router -> (weights fp32 [T, k], idx int64 [T, k]).
+
+    ``score_func``: "sigmoid" (mosaic_router), "sqrtsoftplus" or "softmax"
+    (mosaic_router_ext).
+    """
     _need_cuda(x, weight, bias, what="router")
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise ValueError("router expects bf16 x [T, H]")
@@ -57,10 +84,88 @@ def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, *, 
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=x.device)
     w = torch.empty(t, top_k, dtype=torch.float32, device=x.device)
     idx = torch.empty(t, top_k, dtype=torch.int64, device=x.device)
-    st = lib.mosaic_router(_ptr(x), _ptr(weight), _ptr(bias), t, h, e, top_k, n_group, topk_group,
-                           float(route_scale), int(bool(norm_topk_prob)), _ptr(w), _ptr(idx), _ptr(ws), ws.numel(),
-                           _stream())
-    C.check(st, "mosaic_router")
+    if score_func == "sigmoid":
+        st = lib.mosaic_router(_ptr(x), _ptr(weight), _ptr(bias), t, h, e, top_k, n_group, topk_group,
+                               float(route_scale), int(bool(norm_topk_prob)), _ptr(w), _ptr(idx), _ptr(ws),
+                               ws.numel(), _stream())
+        C.check(st, "mosaic_router")
+    else:
+        ext = route_ext(score_func)
+        st = lib.mosaic_router_ext(ctypes.byref(ext), _ptr(x), _ptr(weight), _ptr(bias), t, h, e, top_k, n_group,
+                                   topk_group, float(route_scale), int(bool(norm_topk_prob)), _ptr(w), _ptr(idx),
+                                   _ptr(ws), ws.numel(), _stream())
+        C.check(st, "mosaic_router_ext")
+    return w, idx
+
+
+def hash_table(tid2eid: torch.Tensor, device) -> torch.Tensor:
+    """tid2eid [V] or [V, k] (any integer dtype) -> contiguous int32 [V, k] on ``device``."""
+    if tid2eid.dtype.is_floating_point or tid2eid.dtype == torch.bool:
+        raise ValueError("tid2eid must be an integer tensor")
+    table = tid2eid.reshape(tid2eid.shape[0], -1) if tid2eid.dim() != 1 else tid2eid.reshape(-1, 1)
+    if table.dim() != 2 or table.shape[0] < 1:
+        raise ValueError("tid2eid must be [V] or [V, k] with V >= 1")
+    if table.dtype != torch.int32:
+        lo, hi = int(table.min()), int(table.max())
+        if lo < -2 ** 31 or hi >= 2 ** 31:
+            raise ValueError("tid2eid entries do not fit int32")
+        table = table.to(torch.int32)
+    return table.to(device).contiguous()
+
+
+def hash_router(x: torch.Tensor, weight: torch.Tensor | None, tid2eid: torch.Tensor | None,
+                token_ids: torch.Tensor | None = None, *, n_experts: int, layer_idx: int = 0,
+                score_func: str = "sqrtsoftplus", route_scale: float = 1.0, norm_topk_prob: bool | None = None):
+    """Hash routing (mosaicvm/model/layers.py:171-197) -> (weights fp32 [T, k], idx int64 [T, k]).
+
+    With ``tid2eid`` ([V] or [V, k]): ids = tid2eid[token_ids mod V], weights
+    the scores gathered there, normalised unless ``score_func`` is softmax
+    (``norm_topk_prob`` overrides), times ``route_scale``.  Without it: the
+    salted hash of ``layer_idx``, one expert per token, weight ``route_scale``
+    (the caller enforces the exact-target contract).
+    """
+    _need_cuda(x, what="hash_router")
+    if x.dim() != 2:
+        raise ValueError("hash_router expects x [T, H]")
+    t, h = x.shape
+    if token_ids is None:
+        tok = None
+    else:
+        tok = token_ids.reshape(-1)
+        if tok.numel() != t:
+            raise ValueError(f"token_ids has {tok.numel()} entries for {t} tokens")
+        if tok.dtype.is_floating_point or tok.dtype == torch.bool:
+            raise ValueError("token_ids must be an integer tensor")
+        tok = tok.to(device=x.device, dtype=torch.int64).contiguous()
+    if norm_topk_prob is None:
+        norm_topk_prob = score_func != "softmax"
+    lib = C.lib()
+    if tid2eid is None:
+        if layer_idx < 0:
+            raise ValueError("layer_idx must be >= 0")
+        ext = route_ext(score_func, token_ids=tok, hash_routing=True, layer_idx=layer_idx)
+        w = torch.empty(t, 1, dtype=torch.float32, device=x.device)
+        idx = torch.empty(t, 1, dtype=torch.int64, device=x.device)
+        st = lib.mosaic_router_ext(ctypes.byref(ext), None, None, None, t, h, n_experts, 1, 1, 1, float(route_scale),
+                                   int(bool(norm_topk_prob)), _ptr(w), _ptr(idx), None, 0, _stream())
+        C.check(st, "mosaic_router_ext")
+        return w, idx
+    if x.dtype != torch.bfloat16:
+        raise ValueError("hash_router expects bf16 x [T, H]")
+    _need_cuda(weight, what="hash_router")
+    if weight is None or weight.dtype != torch.float32 or weight.shape != (n_experts, h):
+        raise ValueError("hash_router expects fp32 weight [E, H]")
+    table = hash_table(tid2eid, x.device)
+    k = table.shape[1]
+    ext = route_ext(score_func, tid2eid=table, token_ids=tok, hash_routing=True, layer_idx=layer_idx)
+    ws = torch.empty(max(lib.mosaic_router_workspace_bytes(t, h, n_experts), 256), dtype=torch.uint8,
+                     device=x.device)
+    w = torch.empty(t, k, dtype=torch.float32, device=x.device)
+    idx = torch.empty(t, k, dtype=torch.int64, device=x.device)
+    st = lib.mosaic_router_ext(ctypes.byref(ext), _ptr(x), _ptr(weight), None, t, h, n_experts, k, 1, 1,
+                               float(route_scale), int(bool(norm_topk_prob)), _ptr(w), _ptr(idx), _ptr(ws),
+                               ws.numel(), _stream())
+    C.check(st, "mosaic_router_ext")
     return w, idx
 
 

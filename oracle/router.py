@@ -1,4 +1,7 @@
-"""Sigmoid group-limited top-k router with a selection-only bias (test oracle).
+"""Group-limited top-k router with a selection-only bias, and hash routing (test oracle).
+
+Test infrastructure only: the tests, ``__graft_entry__.smoke()`` and
+``bench.py``'s CPU baseline use it as the checker; the product never calls it.
 
 Reference behaviour followed:
 
@@ -7,8 +10,13 @@ Reference behaviour followed:
   for selection only; ``torch.topk``; weights gathered from the UNBIASED
   scores; normalised by ``sum.clamp_min(1e-9)``; times
   ``routed_scaling_factor``.
-* ``.mosaicvm/source/inference_model.py:569-589`` (vendored ``Gate``):
-  the ``score_func == "sigmoid"`` branch (``scores.sigmoid()``).
+* Score functions: ``sigmoid`` and ``softmax`` from the vendored ``Gate``
+  (``.mosaicvm/source/inference_model.py:571-574``), ``sqrtsoftplus`` from
+  ``layers.py:110-115`` (``_router_scores``: ``F.softplus(l).sqrt()``).
+* ``hash_route`` follows ``layers.py:171-197`` (``HashRouter.forward``): ids
+  ``tid2eid[token_ids % V]``, weights the scores gathered there, normalised
+  unless softmax, times the scale; without a table the salted hash of
+  ``layers.py:180-184`` evaluated in torch's int32 tensor arithmetic.
 * The group limit (n_group / topk_group) is absent from the reference.  It is
   restated from the published DeepSeek-V3 rule: each group's score is the sum
   of its two largest biased scores; the ``topk_group`` best groups survive;
@@ -36,16 +44,29 @@ import torch
 import torch.nn.functional as F
 
 
+SCORE_FUNCS = ("sigmoid", "sqrtsoftplus", "softmax")
+
+
+def router_scores(logits: torch.Tensor, score_func: str) -> torch.Tensor:
+    """fp32 scores of fp32 logits [T, E] (inference_model.py:571-576, layers.py:110-115)."""
+    if score_func == "sigmoid":
+        return logits.sigmoid()
+    if score_func == "sqrtsoftplus":
+        return F.softplus(logits.float()).sqrt()
+    if score_func == "softmax":
+        return logits.softmax(dim=-1)
+    raise ValueError(f"unknown scoring_func {score_func}")
+
+
 def route(x, weight, bias, *, top_k: int, n_group: int = 1, topk_group: int = 1,
-          route_scale: float = 1.0, norm_topk_prob: bool = True):
-    """x [T, H] (bf16 or fp32 tensor), weight [E, H] fp32, bias [E] fp32
+          route_scale: float = 1.0, norm_topk_prob: bool = True, score_func: str = "sigmoid"):
+    """x [T, H] (bf16 or fp32 tensor), weight [E, H] fp32, bias [E] fp32 (or None)
     -> (weights fp32 [T, k], idx int64 [T, k]) in torch.topk (descending) order."""
     x = torch.as_tensor(x)
     weight = torch.as_tensor(weight, dtype=torch.float32)
-    bias = torch.as_tensor(bias, dtype=torch.float32)
     logits = F.linear(x.float(), weight.float())
-    scores = logits.sigmoid()
-    sel = scores + bias
+    scores = router_scores(logits, score_func)
+    sel = scores if bias is None else scores + torch.as_tensor(bias, dtype=torch.float32)
     t, e = sel.shape
     if n_group > 1 and topk_group < n_group:
         g = sel.view(t, n_group, e // n_group)
@@ -61,8 +82,27 @@ def route(x, weight, bias, *, top_k: int, n_group: int = 1, topk_group: int = 1,
     return w.float(), idx
 
 
+def _scores_and_error(logits, err, score_func):
+    """float64 scores and a first-order bound on their change for logit errors ``err``."""
+    if score_func == "sigmoid":
+        s = 1.0 / (1.0 + np.exp(-logits))
+        return s, err * s * (1.0 - s)
+    if score_func == "sqrtsoftplus":
+        sp = np.where(logits > 20.0, logits, np.log1p(np.exp(np.minimum(logits, 20.0))))
+        s = np.sqrt(sp)
+        sig = 1.0 / (1.0 + np.exp(-logits))
+        ds = np.where(logits > 20.0, 0.5 / np.maximum(s, 1e-300), sig / (2.0 * np.maximum(s, 1e-300)))
+        return s, err * ds
+    if score_func == "softmax":
+        z = np.exp(logits - logits.max(axis=-1, keepdims=True))
+        s = z / z.sum(axis=-1, keepdims=True)
+        # d s_i = s_i (d l_i - sum_j s_j d l_j)
+        return s, s * (err + (s * err).sum(axis=-1, keepdims=True))
+    raise ValueError(f"unknown scoring_func {score_func}")
+
+
 def route_ties(x, weight, bias, *, top_k: int, n_group: int = 1, topk_group: int = 1,
-               eval_ulps: float = 8.0, lam: float = 10.0):
+               eval_ulps: float = 8.0, lam: float = 10.0, score_func: str = "sigmoid"):
     """Return (sel_tie [T] bool, order_tie [T] bool).
 
     sel_tie: the SET of selected experts is not decidable in fp32.
@@ -71,14 +111,14 @@ def route_ties(x, weight, bias, *, top_k: int, n_group: int = 1, topk_group: int
     """
     xd = torch.as_tensor(x).to(torch.float64).numpy()
     wd = torch.as_tensor(weight).to(torch.float64).numpy()
-    b = torch.as_tensor(bias).to(torch.float64).numpy()
+    b = 0.0 if bias is None else torch.as_tensor(bias).to(torch.float64).numpy()
     k_dim = xd.shape[1]
     u = 2.0 ** -24
     logits = xd @ wd.T
     err = lam * u * np.sqrt(k_dim / 2.0) * np.sqrt((xd * xd) @ (wd * wd).T)
-    s = 1.0 / (1.0 + np.exp(-logits))
+    s, ds = _scores_and_error(logits, err, score_func)
     sel = s + b
-    dsel = err / 4.0 + eval_ulps * np.spacing(np.abs(sel).astype(np.float32)).astype(np.float64)
+    dsel = ds + eval_ulps * np.spacing(np.abs(sel).astype(np.float32)).astype(np.float64)
     t, e = sel.shape
     sel_tie = np.zeros(t, dtype=bool)
     order_tie = np.zeros(t, dtype=bool)
@@ -113,3 +153,47 @@ def route_ties(x, weight, bias, *, top_k: int, n_group: int = 1, topk_group: int
                 order_tie[ti] = True
                 break
     return sel_tie, order_tie
+
+
+def salted_hash_ids(token_ids, layer_idx: int, n_experts: int) -> np.ndarray:
+    """Table-less hash routing ids (layers.py:180-184) as torch evaluates them.
+
+    ``token_ids.int()`` truncates to int32; ``+ salt`` and ``* 2654435761``
+    wrap modulo 2^32 on the int32 tensor; the literal ``2**31`` becomes the
+    int32 scalar -2^31, and ``%`` is the floor modulo (sign of the divisor).
+    Pinned against the reference's own outputs in tests/golden/routing.npz.
+    """
+    salt = layer_idx * 2654435761 % (2 ** 31)  # Python integers, as in the reference
+    out = []
+    for tid in np.asarray(token_ids, dtype=np.int64).reshape(-1).tolist():
+        t32 = ((tid + 2 ** 31) % 2 ** 32) - 2 ** 31          # .int()
+        a = ((t32 + salt + 2 ** 31) % 2 ** 32) - 2 ** 31      # int32 add
+        h = ((a * 2654435761 + 2 ** 31) % 2 ** 32) - 2 ** 31  # int32 multiply
+        r = h - (h // -(2 ** 31)) * -(2 ** 31)                # h % (-2^31), floor modulo
+        out.append(r % n_experts)                              # floor modulo, E > 0
+    return np.array(out, dtype=np.int64).reshape(-1, 1)
+
+
+def hash_route(x, weight, tid2eid, token_ids=None, *, n_experts: int, layer_idx: int = 0,
+               score_func: str = "sqrtsoftplus", route_scale: float = 1.0, norm_topk_prob=None):
+    """HashRouter.forward (layers.py:171-197) -> (weights fp32 [T, k], idx int64 [T, k]).
+
+    ``tid2eid`` None: the salted hash (k = 1, weight = route_scale).  Otherwise
+    ``[V]`` or ``[V, k]``: ids ``tid2eid[token_ids mod V]``; weights the scores
+    gathered at the ids, normalised (``clamp_min(1e-9)``) unless the score is
+    softmax (``norm_topk_prob`` overrides), times ``route_scale``.
+    """
+    n = int(torch.as_tensor(x).shape[0])
+    tok = np.arange(n, dtype=np.int64) if token_ids is None else np.asarray(token_ids, dtype=np.int64).reshape(-1)
+    if tid2eid is None:
+        idx = torch.from_numpy(salted_hash_ids(tok, layer_idx, n_experts))
+        return torch.full((n, 1), float(route_scale), dtype=torch.float32), idx
+    table = torch.as_tensor(np.asarray(tid2eid)).long()
+    idx = table[torch.from_numpy(tok) % table.shape[0]].reshape(n, -1)
+    logits = F.linear(torch.as_tensor(x).float(), torch.as_tensor(weight, dtype=torch.float32))
+    s = router_scores(logits, score_func)
+    w = s.gather(-1, idx)
+    norm = score_func != "softmax" if norm_topk_prob is None else norm_topk_prob
+    if norm:
+        w = w / w.sum(-1, keepdim=True).clamp_min(1e-9)
+    return (w * route_scale).float(), idx

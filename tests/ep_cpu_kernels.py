@@ -14,7 +14,7 @@ import torch
 
 from oracle.formats import act_quant_ref
 from oracle.moe import expert_bf16, expert_fp8
-from oracle.router import route
+from oracle.router import hash_route, route
 
 
 class CpuEPKernels:
@@ -31,6 +31,12 @@ class CpuEPKernels:
         c = self.cfg
         return route(x, self.router_w, self.bias, top_k=c.num_experts_per_tok, n_group=c.n_group,
                      topk_group=c.topk_group, route_scale=c.routed_scaling_factor, norm_topk_prob=c.norm_topk_prob)
+
+    def route_hash(self, router, x, token_ids):
+        c = self.cfg
+        tok = None if token_ids is None else token_ids.reshape(-1).numpy()
+        return hash_route(x, self.router_w, router.tid2eid, tok, n_experts=c.n_routed_experts,
+                          layer_idx=router.layer_idx, score_func=c.scoring_func, route_scale=c.routed_scaling_factor)
 
     def dispatch(self, dims, world, x, idx, w):
         t, k = idx.shape

@@ -11,7 +11,10 @@ seeded inputs:
 * ``mosaicvm/kernels/fp4_source.py``: ``pack_mxfp4_nk``, ``act_quant_ref``,
   ``reference_fp4_linear_source_semantics``;
 * ``mosaicvm/runtime/fp8.py``: ``dequant_fp4``;
-* ``.mosaicvm/source/inference_model.py``: ``Gate`` with ``score_func="sigmoid"``;
+* ``.mosaicvm/source/inference_model.py``: ``Gate`` with ``score_func``
+  "sigmoid", "softmax" and "sqrtsoftplus", score-based and on hash layers;
+* ``mosaicvm/model/layers.py``: ``Router`` (sqrtsoftplus) and ``HashRouter``
+  (with a table, and the salted fallback with ``MOSAICVM_EXACT_TARGET=0``);
 * ``mosaicvm/model/layers.py``: ``grouped_expert_forward`` and
   ``SharedExpertMLP`` on dequantised MXFP4 weights (the bf16 MoE path).
 
@@ -41,15 +44,20 @@ from mosaicvm.kernels.fp4_source import (  # noqa: E402
     pack_mxfp4_nk,
     reference_fp4_linear_source_semantics,
 )
-from mosaicvm.model.layers import SharedExpertMLP, grouped_expert_forward  # noqa: E402
+from mosaicvm.model.config import V4Config  # noqa: E402
+from mosaicvm.model.layers import HashRouter, Router, SharedExpertMLP, grouped_expert_forward  # noqa: E402
 from mosaicvm.runtime.fp8 import dequant_fp4  # noqa: E402
 
 from tests.golden.recipes import (  # noqa: E402
     GATE_CASES,
     MOE_CASES,
-    make_gate_case,
+    ROUTING_CASES,
+    SALTED_CASES,
     edge_weight_matrix,
+    make_gate_case,
+    make_hash_case,
     make_moe_case,
+    salted_token_ids,
 )
 
 
@@ -138,6 +146,66 @@ def gen_router():
     np.savez_compressed(HERE / "router.npz", **out)
 
 
+def gen_routing():
+    m = _vendored_gate_module()
+    out = {}
+    for name, c in ROUTING_CASES.items():
+        t, h, e, k = c["T"], c["H"], c["E"], c["k"]
+        src = c["src"]
+        with torch.no_grad():
+            if src in ("router", "gate"):
+                x, wt, bias = make_gate_case(t, h, e, seed=c["seed"])
+                if src == "router":
+                    cfg = V4Config(hidden_size=h, n_routed_experts=e, num_experts_per_tok=k,
+                                   scoring_func=c["score"], routed_scaling_factor=c["scale"])
+                    mod = Router(cfg)
+                    mod.weight.copy_(wt)
+                    mod.e_score_correction_bias.copy_(bias)
+                    w, idx = mod(x)
+                else:
+                    args = m.ModelArgs(dim=h, n_routed_experts=e, n_activated_experts=k, score_func=c["score"],
+                                       route_scale=c["scale"], n_hash_layers=0)
+                    gate = m.Gate(0, args)
+                    gate.weight.copy_(wt)
+                    gate.bias.copy_(bias)
+                    w, idx = gate(x, None)
+                inputs = (x.float().numpy(), wt.numpy(), bias.numpy())
+            else:
+                x, wt, table, tok = make_hash_case(t, h, e, None if src == "hash1d" else k, c["vocab"], c["seed"],
+                                                   in_table=src == "gate_hash")
+                if src == "gate_hash":
+                    args = m.ModelArgs(dim=h, n_routed_experts=e, n_activated_experts=k, score_func=c["score"],
+                                       route_scale=c["scale"], n_hash_layers=1, vocab_size=c["vocab"])
+                    gate = m.Gate(0, args)
+                    gate.weight.copy_(wt)
+                    gate.tid2eid.copy_(table)
+                    w, idx = gate(x, tok)
+                else:
+                    cfg = V4Config(hidden_size=h, n_routed_experts=e, num_experts_per_tok=k,
+                                   scoring_func=c["score"], routed_scaling_factor=c["scale"])
+                    hr = HashRouter(cfg, 3)
+                    hr.weight.copy_(wt)
+                    hr.tid2eid = table
+                    w, idx = hr(x, tok)
+                inputs = (x.float().numpy(), wt.numpy(), table.numpy(), tok.numpy())
+        out[name + "_sha"] = np.frombuffer(_sha(*inputs).encode(), dtype=np.uint8)
+        out[name + "_weights"] = w.float().numpy()
+        out[name + "_idx"] = idx.numpy().astype(np.int64)
+    # table-less salted hash (the reference raises under the exact target)
+    tok = salted_token_ids()
+    os.environ["MOSAICVM_EXACT_TARGET"] = "0"
+    try:
+        for e, layer_idx in SALTED_CASES:
+            cfg = V4Config(hidden_size=64, n_routed_experts=e, num_experts_per_tok=1)
+            w, idx = HashRouter(cfg, layer_idx)(torch.zeros(tok.numel(), 64), tok)
+            out[f"salted_{e}_{layer_idx}_idx"] = idx.numpy().astype(np.int64)
+            out[f"salted_{e}_{layer_idx}_weights"] = w.float().numpy()
+    finally:
+        del os.environ["MOSAICVM_EXACT_TARGET"]
+    out["salted_tokens"] = tok.numpy()
+    np.savez_compressed(HERE / "routing.npz", **out)
+
+
 def gen_moe():
     out = {}
     for name, spec in MOE_CASES.items():
@@ -189,6 +257,7 @@ def gen_moe():
 if __name__ == "__main__":
     gen_formats()
     gen_router()
+    gen_routing()
     gen_moe()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

@@ -76,3 +76,53 @@ def make_moe_case(T, H, I, E, k, n_group, topk_group, scale, swiglu_limit, seed,
                swiglu_limit=swiglu_limit)
     return dict(cfg=cfg, x=x, router_w=router_w, bias=bias, w_gu=w_gu, w_dn=w_dn,
                 weights=weights, idx=idx)
+
+
+# Router variants recorded from the reference into routing.npz:
+#   src "router": mosaicvm/model/layers.py Router (scoring_func, norm_topk_prob, no groups)
+#   src "gate":   vendored .mosaicvm/source/inference_model.py Gate (score-based)
+#   src "gate_hash": the same Gate on a hash layer (tid2eid[input_ids], ids inside the table)
+#   src "hash" / "hash1d": layers.py HashRouter with a [V, k] / [V] table, any token ids
+ROUTING_CASES = {
+    "router_v4_s": dict(src="router", T=64, H=512, E=32, k=6, score="sqrtsoftplus", scale=1.5, seed=21),
+    "router_v4": dict(src="router", T=16, H=4096, E=256, k=6, score="sqrtsoftplus", scale=1.5, seed=22),
+    "gate_softmax": dict(src="gate", T=48, H=512, E=64, k=6, score="softmax", scale=1.0, seed=23),
+    "gate_sqrtsoftplus": dict(src="gate", T=48, H=512, E=64, k=6, score="sqrtsoftplus", scale=2.5, seed=24),
+    "gate_hash_sqrtsoftplus": dict(src="gate_hash", T=40, H=512, E=32, k=6, score="sqrtsoftplus", scale=1.5,
+                                   seed=25, vocab=97),
+    "gate_hash_softmax": dict(src="gate_hash", T=40, H=512, E=32, k=4, score="softmax", scale=1.0, seed=26,
+                              vocab=97),
+    "hash_table": dict(src="hash", T=40, H=512, E=32, k=6, score="sqrtsoftplus", scale=1.5, seed=27, vocab=50),
+    "hash_table_1d": dict(src="hash1d", T=40, H=512, E=32, k=1, score="sqrtsoftplus", scale=1.5, seed=28,
+                          vocab=37),
+    "hash_v4": dict(src="hash", T=16, H=4096, E=256, k=6, score="sqrtsoftplus", scale=1.5, seed=29, vocab=129280),
+}
+
+# Table-less hash routing (layers.py:180-184): (n_experts, layer_idx) pairs, one token-id vector.
+SALTED_CASES = [(1, 0), (3, 1), (16, 2), (24, 7), (100, 42), (255, 1000), (256, 2), (256, 2 ** 31 - 1)]
+
+
+def make_hash_case(T, H, E, k, vocab, seed, in_table: bool = False):
+    """Router inputs of make_gate_case plus an int32 table [vocab, k] of ids in [0, E)
+    (1-D when k is None) and int64 token ids [T]: inside [0, vocab) when
+    ``in_table``, else spanning negatives, multiples of vocab and 2^40."""
+    x, wt, _ = make_gate_case(T, H, E, seed)
+    g = torch.Generator().manual_seed(seed + 500)
+    shape = (vocab,) if k is None else (vocab, k)
+    table = torch.randint(0, E, shape, generator=g, dtype=torch.int64).to(torch.int32)
+    if in_table:
+        tok = torch.randint(0, vocab, (T,), generator=g, dtype=torch.int64)
+    else:
+        tok = torch.randint(-3 * vocab, 3 * vocab, (T,), generator=g, dtype=torch.int64)
+        edge = torch.tensor([0, vocab - 1, vocab, -1, -vocab, 2 ** 40 + 3, -(2 ** 40) - 5], dtype=torch.int64)
+        tok[:edge.numel()] = edge
+    return x, wt, table, tok
+
+
+def salted_token_ids() -> torch.Tensor:
+    """int64 token ids for the table-less hash: random 62-bit values plus int32 / int64 edges."""
+    g = torch.Generator().manual_seed(31)
+    rnd = torch.randint(-2 ** 62, 2 ** 62, (120,), generator=g, dtype=torch.int64)
+    edge = torch.tensor([0, 1, -1, 2 ** 31 - 1, -2 ** 31, 2 ** 31, 2 ** 32 - 1, 2 ** 32, 2 ** 63 - 1, -2 ** 63],
+                        dtype=torch.int64)
+    return torch.cat([edge, rnd, torch.arange(64, dtype=torch.int64)])

@@ -29,7 +29,7 @@ def _local_bank(obank: dict, lo: int, hi: int) -> dict:
             ("gu_packed", "gu_scale", "dn_packed", "dn_scale")}
 
 
-def _worker(rank, world, port, case_name, mode, tokens_split, err_q):
+def _worker(rank, world, port, case_name, mode, tokens_split, err_q, hash_k=None):
     try:
         import sys
 
@@ -40,9 +40,9 @@ def _worker(rank, world, port, case_name, mode, tokens_split, err_q):
         from mosaic_b200 import MoEConfig
         from mosaic_b200.ep import ExpertParallelMoELayer, expert_range
         from oracle.moe import moe_layer
-        from oracle.router import route
+        from oracle.router import hash_route, route
         from tests.ep_cpu_kernels import CpuEPKernels
-        from tests.golden.recipes import MOE_CASES, make_moe_case
+        from tests.golden.recipes import MOE_CASES, make_hash_case, make_moe_case
         from tests.helpers import pack_case
 
         case = make_moe_case(**MOE_CASES[case_name])
@@ -50,16 +50,24 @@ def _worker(rank, world, port, case_name, mode, tokens_split, err_q):
         obank, _ = pack_case(case)
         cfg = MoEConfig(hidden_size=c["H"], moe_intermediate_size=c["I"], n_routed_experts=c["E"],
                         num_experts_per_tok=c["k"], n_group=c["n_group"], topk_group=c["topk_group"],
-                        routed_scaling_factor=c["scale"], swiglu_limit=c["swiglu_limit"], act_mode=mode)
+                        routed_scaling_factor=c["scale"], swiglu_limit=c["swiglu_limit"], act_mode=mode,
+                        scoring_func="sigmoid" if hash_k is None else "sqrtsoftplus")
         bounds = np.cumsum([0] + tokens_split)
         x_local = case["x"][bounds[rank]:bounds[rank + 1]]
         lo, hi = expert_range(c["E"], world, rank)
         kern = CpuEPKernels(case["router_w"], case["bias"], cfg, _local_bank(obank, lo, hi))
-        layer = ExpertParallelMoELayer(cfg, None, kernels=kern)
-        y = layer(x_local).float().numpy()
-
-        w, idx = route(case["x"], case["router_w"], case["bias"], top_k=c["k"], n_group=c["n_group"],
-                       topk_group=c["topk_group"], route_scale=c["scale"])
+        if hash_k is None:
+            layer = ExpertParallelMoELayer(cfg, None, kernels=kern)
+            y = layer(x_local).float().numpy()
+            w, idx = route(case["x"], case["router_w"], case["bias"], top_k=c["k"], n_group=c["n_group"],
+                           topk_group=c["topk_group"], route_scale=c["scale"])
+        else:  # hash-routed layer: ids by token id from a [V, hash_k] table
+            _, _, table, tok = make_hash_case(int(bounds[-1]), c["H"], c["E"], hash_k, 211, seed=17)
+            layer = ExpertParallelMoELayer(cfg, None, kernels=kern, layer_idx=4)
+            layer.hash_router.tid2eid = table
+            y = layer(x_local, tok[bounds[rank]:bounds[rank + 1]]).float().numpy()
+            w, idx = hash_route(case["x"], case["router_w"], table, tok.numpy(), n_experts=c["E"],
+                                score_func="sqrtsoftplus", route_scale=c["scale"])
         ref = moe_layer(case["x"], w, idx, obank, mode=mode, swiglu_limit=c["swiglu_limit"])
         ref = ref[bounds[rank]:bounds[rank + 1]]
         assert y.shape == ref.shape
@@ -79,11 +87,11 @@ def _worker(rank, world, port, case_name, mode, tokens_split, err_q):
         raise
 
 
-def _run(world, case_name, mode, tokens_split):
+def _run(world, case_name, mode, tokens_split, hash_k=None):
     ctx = mp.get_context("spawn")
     err_q = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case_name, mode, tokens_split, err_q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case_name, mode, tokens_split, err_q, hash_k))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -107,3 +115,9 @@ def test_ep_world2_matches_single_process(mode):
 
 def test_ep_world4_uneven_and_empty_rank():
     _run(4, "S", "bf16", [30, 0, 20, 14])  # one rank has no tokens of its own
+
+
+def test_ep_world2_hash_routed():
+    """HashMoELayer semantics across ranks: a [V, 3] table (3 experts per token, not
+    the config's 4) routes by token id; each rank passes its own tokens' ids."""
+    _run(2, "S", "bf16", [40, 24], hash_k=3)

@@ -201,3 +201,30 @@ def test_ep_p2p_world1_bit_identical_and_graph_capturable(act_mode):
         del g
     finally:
         ep.close()
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_ep_world1_hash_routed_bit_identical(exchange):
+    """A hash-routed EP layer (table of 3 columns, token ids given) equals the
+    single-GPU HashMoELayer bit for bit, on both exchanges."""
+    from mosaic_b200 import HashMoELayer, MoEConfig
+    from mosaic_b200 import synthetic
+    from mosaic_b200.ep import ExpertParallelMoELayer
+
+    cfg = MoEConfig(hidden_size=512, moe_intermediate_size=256, n_routed_experts=32, num_experts_per_tok=4,
+                    n_group=1, topk_group=1, routed_scaling_factor=1.5, act_mode="bf16", scoring_func="sqrtsoftplus")
+    layer = HashMoELayer(cfg, 5, synthetic.make_bank(512, 256, 32, 7))
+    g = torch.Generator().manual_seed(7)
+    layer.hash_router.weight.data = (torch.randn(32, 512, generator=g) / 512 ** 0.5).cuda()
+    layer.hash_router.tid2eid = torch.randint(0, 32, (1000, 3), generator=g, dtype=torch.int32)
+    x = synthetic.make_tokens(48, 512, 7)
+    tok = torch.randint(0, 5000, (48,), generator=g).cuda()
+    ep = ExpertParallelMoELayer.from_layer(layer, exchange=exchange, max_tokens=48)
+    try:
+        y_ref = layer(x, tok)
+        y = ep(x, tok)
+        torch.cuda.synchronize()
+        assert torch.equal(ep.last_idx, layer.last_idx) and ep.last_idx.shape == (48, 3)
+        assert torch.equal(y, y_ref)
+    finally:
+        ep.close()
