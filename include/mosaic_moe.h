@@ -32,6 +32,10 @@
  *   mosaic_moe_forward       <- mosaicvm/model/layers.py:284-303 (MoELayer.forward)
  *   mosaic_moe_forward_ext   <- the same with mosaic_router_ext's routing, which with hash
  *                               routing is layers.py:394-405 (HashMoELayer.forward)
+ *   mosaic_hc_pre_norm       <- mosaicvm/model/layers.py:258-267 (HyperConnections.pre, with
+ *                               hc_split_sinkhorn :222-234) + :19-29 (RMSNorm, the block's
+ *                               ffn_norm, :431-433) + fp4_source.py:110-129 (act_quant_ref)
+ *   mosaic_hc_post           <- mosaicvm/model/layers.py:269-271 (HyperConnections.post)
  *   mosaic_ep_*              <- .mosaicvm/source/inference_model.py:614-650 (MoE.forward,
  *                               expert-sharded; all_reduce replaced by all-to-all)
  */
@@ -223,6 +227,29 @@ MOSAIC_API int mosaic_repack_weights(const uint8_t* packed, int32_t n_mats, int3
  * of a chunk holding row r, K32 block kb.  rows % (128 * halves) == 0, K % 128 == 0. */
 MOSAIC_API int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, int32_t K, int32_t halves,
                                      uint8_t* sf_chunks, mosaic_stream_t stream);
+
+/* The step in front of the MoE in a V4 block (layers.py:428-433): the
+ * hyper-connection pre-mix of the hc residual copies, then the ffn RMSNorm,
+ * fused; optionally also act_quant_ref of the result (the FP8 MoE input).
+ *   x           bf16 [T, hc, D] (the block's residual stream)
+ *   fn          fp32 [(2+hc)*hc, hc*D]; base fp32 [(2+hc)*hc]; scale fp32 [3]
+ *   norm_weight fp32 [D] (RMSNorm weight), or NULL for the pre-mix alone
+ *               (HyperConnections.pre); norm_eps both for the rsqrt of the
+ *               pre-mix and for the RMSNorm (both use rms_norm_eps); hc_eps the
+ *               Sinkhorn epsilon; sinkhorn_iters >= 1
+ *   y           bf16 [T, D] = RMSNorm(sum_m pre_m * x_m), the MoE input
+ *   post        fp32 [T, hc], comb fp32 [T, hc, hc]: for mosaic_hc_post
+ *   q, q_scale  E4M3 [T, D] and fp32 [T, D/128] = act_quant_ref(y), or both NULL
+ * hc 1..4; D a multiple of 128 (x, y, q 16-byte aligned; fn, norm_weight too). */
+MOSAIC_API int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const float* scale,
+                                  const float* norm_weight, int32_t T, int32_t D, int32_t hc, int32_t sinkhorn_iters,
+                                  float hc_eps, float norm_eps, void* y, float* post, float* comb, uint8_t* q,
+                                  float* q_scale, mosaic_stream_t stream);
+
+/* The step behind the MoE: out[t, m] = post[t, m] * y[t] + sum_n comb[t, m, n] * residual[t, n]
+ * (fp32, rounded to bf16); y bf16 [T, D] (the MoE output), residual and out bf16 [T, hc, D]. */
+MOSAIC_API int mosaic_hc_post(const void* y, const void* residual, const float* post, const float* comb, int32_t T,
+                              int32_t D, int32_t hc, void* out, mosaic_stream_t stream);
 
 /* Workspace for mosaic_moe_forward / mosaic_moe_routed (256-B aligned pointer). */
 MOSAIC_API size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims);

@@ -600,6 +600,51 @@ int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, in
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
+int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const float* scale,
+                       const float* norm_weight, int32_t T, int32_t D, int32_t hc, int32_t sinkhorn_iters,
+                       float hc_eps, float norm_eps, void* y, float* post, float* comb, uint8_t* q, float* q_scale,
+                       mosaic_stream_t stream) {
+  if (!x || !fn || !base || !scale || !y || !post || !comb) return MOSAIC_ERR_SHAPE;
+  if ((q == nullptr) != (q_scale == nullptr)) return MOSAIC_ERR_SHAPE;
+  if (T < 1 || D < 128 || D % 128 || hc < 1 || hc > 4 || sinkhorn_iters < 1) return MOSAIC_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(fn, 16) || (norm_weight && !aligned(norm_weight, 16)) || !aligned(y, 16) ||
+      (q && !aligned(q, 16)))
+    return MOSAIC_ERR_ALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  if (hc_pre_norm_smem_bytes(hc_tokens_per_cta(T, sms), D) > 227u * 1024u) return MOSAIC_ERR_UNSUPPORTED;
+  HcParams p{};
+  p.x = x;
+  p.fn = fn;
+  p.base = base;
+  p.scale = scale;
+  p.norm_w = norm_weight;
+  p.T = T;
+  p.D = D;
+  p.hc = hc;
+  p.iters = sinkhorn_iters;
+  p.hc_eps = hc_eps;
+  p.norm_eps = norm_eps;
+  p.y = y;
+  p.post = post;
+  p.comb = comb;
+  p.q = q;
+  p.q_scale = q_scale;
+  cudaError_t e = launch_hc_pre_norm(p, sms, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_hc_post(const void* y, const void* residual, const float* post, const float* comb, int32_t T, int32_t D,
+                   int32_t hc, void* out, mosaic_stream_t stream) {
+  if (!y || !residual || !post || !comb || !out) return MOSAIC_ERR_SHAPE;
+  if (T < 1 || D < 8 || D % 8 || hc < 1 || hc > 4) return MOSAIC_ERR_SHAPE;
+  if (!aligned(y, 16) || !aligned(residual, 16) || !aligned(out, 16)) return MOSAIC_ERR_ALIGN;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  cudaError_t e = launch_hc_post(y, residual, post, comb, T, D, hc, out, sms, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
 size_t mosaic_moe_workspace_bytes(const mosaic_moe_dims* dims) {
   if (check_dims(dims) != MOSAIC_OK) return 0;
   return plan_ws(dims).total;

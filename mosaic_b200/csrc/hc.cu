@@ -1,0 +1,337 @@
+// Hyper-connection pre-mix + RMSNorm (+ act_quant) in front of the MoE, and
+// the hyper-connection post-mix behind it (fp32 CUDA cores, HBM-bound).
+//
+// Reference behaviour:
+//   HyperConnections.pre    mosaicvm/model/layers.py:258-267, with the Sinkhorn
+//                           split of hc_split_sinkhorn :222-234
+//   RMSNorm.forward         mosaicvm/model/layers.py:19-29
+//   act_quant_ref           mosaicvm/kernels/fp4_source.py:110-129
+//   HyperConnections.post   mosaicvm/model/layers.py:269-271
+//
+// hc_pre_norm: a CTA takes TT tokens at a time.  Pass A streams the tokens'
+// hc residual copies (x_flat, hc*D bf16) once and accumulates the sum of
+// squares and the (2+hc)*hc mixing dot products against fn (fp32, read from
+// L2, shared by the TT tokens).  One thread per token then runs the Sinkhorn
+// normalisation of the 4x4 combination.  Pass B forms y = sum_m pre_m x_m
+// (bf16) into shared memory with its sum of squares, pass C applies the
+// RMSNorm (skipped without a norm weight) and writes the MoE input (and its
+// E4M3 act_quant).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mosaic {
+
+namespace {
+
+constexpr int kHcThreads = 256;
+constexpr int kHcWarps = kHcThreads / 32;
+constexpr int kHcChunk = kHcThreads * 8;  // x_flat columns per step: 8 per thread
+constexpr int kMaxMix = 24;               // (2 + hc) * hc at hc = 4
+constexpr int kRed = kMaxMix + 1;         // mixes + sum of squares per token
+
+__device__ __forceinline__ float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+template <int TT>
+__global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* ybuf = reinterpret_cast<__nv_bfloat16*>(smem);                   // [TT][D]
+  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(TT) * p.D * 2);  // [warps][TT][kRed]
+  float* tot = red + kHcWarps * TT * kRed;                                          // [TT][kRed]
+  float* pre_s = tot + TT * kRed;                                                   // [TT][4]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hc = p.hc, D = p.D, KD = hc * D, nmix = (2 + hc) * hc;
+  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
+  __nv_bfloat16* yout = static_cast<__nv_bfloat16*>(p.y);
+  for (int t0 = blockIdx.x * TT; t0 < p.T; t0 += gridDim.x * TT) {
+    // ---- pass A: mixing dot products and sum of squares of x_flat
+    float acc[TT][kMaxMix];
+    float ss[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      ss[t] = 0.f;
+#pragma unroll
+      for (int r = 0; r < kMaxMix; ++r) acc[t][r] = 0.f;
+    }
+    for (int c0 = 0; c0 < KD; c0 += kHcChunk) {
+      const int col = c0 + tid * 8;
+      if (col >= KD) continue;
+      float xv[TT][8];
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        if (t0 + t < p.T) {
+          load8_bf16(x + static_cast<size_t>(t0 + t) * KD + col, xv[t]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xv[t][i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss[t] = fmaf(xv[t][i], xv[t][i], ss[t]);
+      }
+#pragma unroll
+      for (int r = 0; r < kMaxMix; ++r) {
+        if (r < nmix) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(p.fn + static_cast<size_t>(r) * KD + col));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(p.fn + static_cast<size_t>(r) * KD + col + 4));
+          const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[t][r] = fmaf(xv[t][i], f[i], acc[t][r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+#pragma unroll
+      for (int r = 0; r < kMaxMix; ++r) {
+        if (r < nmix) {
+          const float v = warp_sum(acc[t][r]);
+          if (lane == 0) red[(warp * TT + t) * kRed + r] = v;
+        }
+      }
+      const float v = warp_sum(ss[t]);
+      if (lane == 0) red[(warp * TT + t) * kRed + kMaxMix] = v;
+    }
+    __syncthreads();
+    for (int i = tid; i < TT * kRed; i += kHcThreads) {
+      float s = 0.f;
+      for (int w = 0; w < kHcWarps; ++w) s += red[w * TT * kRed + i];
+      tot[i] = s;
+    }
+    __syncthreads();
+    // ---- Sinkhorn split, one thread per token
+    if (tid < TT && t0 + tid < p.T) {
+      const int t = t0 + tid;
+      const float* mt = tot + tid * kRed;
+      const float rs = 1.0f / sqrtf(mt[kMaxMix] / static_cast<float>(KD) + p.norm_eps);
+      float mix[kMaxMix];
+#pragma unroll
+      for (int r = 0; r < kMaxMix; ++r) mix[r] = r < nmix ? mt[r] * rs : 0.f;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        if (m < hc) {
+          pre_s[tid * 4 + m] = sigmoidf(mix[m] * p.scale[0] + p.base[m]) + p.hc_eps;
+          p.post[static_cast<size_t>(t) * hc + m] = 2.0f * sigmoidf(mix[hc + m] * p.scale[1] + p.base[hc + m]);
+        }
+      }
+      // comb rows: softmax + eps, then iters - 1 rounds of row / column normalisation
+      float c[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          c[i][j] = (i < hc && j < hc) ? mix[2 * hc + i * hc + j] * p.scale[2] + p.base[2 * hc + i * hc + j] : 0.f;
+          if (i < hc && j < hc) mx = fmaxf(mx, c[i][j]);
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          c[i][j] = (i < hc && j < hc) ? expf(c[i][j] - mx) : 0.f;
+          sum += c[i][j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[i][j] = (i < hc && j < hc) ? c[i][j] / sum + p.hc_eps : 0.f;
+      }
+      for (int it = 1; it < p.iters; ++it) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) s += c[i][j];
+          s += p.hc_eps;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) c[i][j] /= s;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s += c[i][j];
+          s += p.hc_eps;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) c[i][j] /= s;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (i < hc && j < hc) p.comb[(static_cast<size_t>(t) * hc + i) * hc + j] = c[i][j];
+    }
+    __syncthreads();
+    // ---- pass B: y = sum_m pre_m x_m (products rounded, summed in m order), bf16
+    float ss2[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      ss2[t] = 0.f;
+      if (t0 + t >= p.T) continue;
+      const __nv_bfloat16* xt = x + static_cast<size_t>(t0 + t) * KD;
+      for (int d = tid * 8; d < D; d += kHcChunk) {
+        float y[8], xv[8];
+        load8_bf16(xt + d, xv);
+        const float p0 = pre_s[t * 4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(p0, xv[i]);
+        for (int m = 1; m < hc; ++m) {
+          load8_bf16(xt + static_cast<size_t>(m) * D + d, xv);
+          const float pm = pre_s[t * 4 + m];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(y[i], __fmul_rn(pm, xv[i]));
+        }
+        __align__(16) __nv_bfloat16 yb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          yb[i] = __float2bfloat16_rn(y[i]);
+          const float f = __bfloat162float(yb[i]);
+          ss2[t] = fmaf(f, f, ss2[t]);
+        }
+        *reinterpret_cast<uint4*>(ybuf + static_cast<size_t>(t) * D + d) = *reinterpret_cast<const uint4*>(yb);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      const float v = warp_sum(ss2[t]);
+      if (lane == 0) red[warp * TT + t] = v;
+    }
+    __syncthreads();
+    if (tid < TT) {
+      float s = 0.f;
+      for (int w = 0; w < kHcWarps; ++w) s += red[w * TT + tid];
+      tot[tid] = 1.0f / sqrtf(s / static_cast<float>(D) + p.norm_eps);
+    }
+    __syncthreads();
+    // ---- pass C: RMSNorm (x * rsqrt, then * weight), bf16, optional act_quant.
+    // Every lane runs the same iterations: quant_block128 shuffles across 16 lanes.
+    const int steps = (D + kHcChunk - 1) / kHcChunk;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      if (t0 + t >= p.T) continue;
+      const float r = tot[t];
+      for (int s = 0; s < steps; ++s) {
+        const int d = s * kHcChunk + tid * 8;
+        const bool valid = d < D;
+        float v[8];
+        if (valid) {
+          float yv[8];
+          load8_bf16(ybuf + static_cast<size_t>(t) * D + d, yv);
+          __align__(16) __nv_bfloat16 ob[8];
+          if (p.norm_w) {
+            const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d));
+            const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d + 4));
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(yv[i], r), w[i]));
+          } else {  // the pre-mix alone (HyperConnections.pre)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(yv[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(ob[i]);
+          *reinterpret_cast<uint4*>(yout + static_cast<size_t>(t0 + t) * D + d) =
+              *reinterpret_cast<const uint4*>(ob);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        }
+        if (p.q) {
+          uint8_t b[8];
+          const int e = quant_block128(v, b);
+          if (valid) {
+            *reinterpret_cast<uint2*>(p.q + static_cast<size_t>(t0 + t) * D + d) = pack8(b);
+            if ((lane & 15) == 0) p.q_scale[static_cast<size_t>(t0 + t) * (D / 128) + d / 128] = exp2i(e);
+          }
+        }
+      }
+    }
+    __syncthreads();  // ybuf / red / tot are reused by the next token group
+  }
+}
+
+// out[t, m] = post[t, m] * y[t] + sum_n comb[t, m, n] * residual[t, n]; 8 values per thread.
+__global__ void __launch_bounds__(256) hc_post_kernel(const __nv_bfloat16* __restrict__ y,
+                                                      const __nv_bfloat16* __restrict__ res,
+                                                      const float* __restrict__ post, const float* __restrict__ comb,
+                                                      int T, int D, int hc, __nv_bfloat16* __restrict__ out) {
+  const int per_token = D / 8;
+  const long long units = static_cast<long long>(T) * per_token;
+  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < units;
+       u += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(u / per_token);
+    const int d = static_cast<int>(u % per_token) * 8;
+    float yv[8], rv[4][8];
+    load8_bf16(y + static_cast<size_t>(t) * D + d, yv);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      if (n < hc) {
+        load8_bf16(res + (static_cast<size_t>(t) * hc + n) * D + d, rv[n]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rv[n][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      if (m >= hc) break;
+      const float pm = post[static_cast<size_t>(t) * hc + m];
+      const float* cm = comb + (static_cast<size_t>(t) * hc + m) * hc;
+      float cv[4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) cv[n] = n < hc ? cm[n] : 0.f;
+      __align__(16) __nv_bfloat16 ob[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float e = 0.f;
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+          if (n < hc) e = fmaf(cv[n], rv[n][i], e);
+        ob[i] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(pm, yv[i]), e));
+      }
+      *reinterpret_cast<uint4*>(out + (static_cast<size_t>(t) * hc + m) * D + d) = *reinterpret_cast<const uint4*>(ob);
+    }
+  }
+}
+
+}  // namespace
+
+size_t hc_pre_norm_smem_bytes(int tt, int D) {
+  return static_cast<size_t>(tt) * D * 2 + sizeof(float) * (kHcWarps * tt * kRed + tt * kRed + tt * 4);
+}
+
+int hc_tokens_per_cta(int T, int num_sms) { return T >= 4 * num_sms ? 4 : (T >= 2 * num_sms ? 2 : 1); }
+
+cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream) {
+  const int tt = hc_tokens_per_cta(p.T, num_sms);
+  const int groups = (p.T + tt - 1) / tt;
+  const int grid = groups < num_sms ? groups : num_sms;
+  const size_t smem = hc_pre_norm_smem_bytes(tt, p.D);
+#define MOSAIC_HC(TT)                                                                                     \
+  do {                                                                                                    \
+    cudaError_t e = cudaFuncSetAttribute(hc_pre_norm_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                         static_cast<int>(smem));                                         \
+    if (e != cudaSuccess) return e;                                                                       \
+    hc_pre_norm_kernel<TT><<<grid, kHcThreads, smem, stream>>>(p);                                        \
+  } while (0)
+  if (tt == 4)
+    MOSAIC_HC(4);
+  else if (tt == 2)
+    MOSAIC_HC(2);
+  else
+    MOSAIC_HC(1);
+#undef MOSAIC_HC
+  return cudaGetLastError();
+}
+
+cudaError_t launch_hc_post(const void* y, const void* residual, const float* post, const float* comb, int T, int D,
+                           int hc, void* out, int num_sms, cudaStream_t stream) {
+  const long long units = static_cast<long long>(T) * (D / 8);
+  long long blocks = (units + 255) / 256;
+  const long long cap = static_cast<long long>(num_sms) * 8;
+  if (blocks > cap) blocks = cap;
+  hc_post_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(residual), post, comb, T, D, hc,
+      static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+}  // namespace mosaic

@@ -65,6 +65,27 @@ cudaError_t launch_router(const void* x, const float* w, const float* bias, int 
                           int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream,
                           const RouteVariant* variant = nullptr);
 
+// ---- hyper-connection pre-mix + RMSNorm, post-mix (hc.cu)
+struct HcParams {
+  const void* x;         // bf16 [T][hc][D]
+  const float* fn;       // [(2+hc)*hc][hc*D]
+  const float* base;     // [(2+hc)*hc]
+  const float* scale;    // [3]
+  const float* norm_w;   // [D] RMSNorm weight
+  int T, D, hc, iters;
+  float hc_eps, norm_eps;
+  void* y;               // bf16 [T][D]
+  float* post;           // [T][hc]
+  float* comb;           // [T][hc][hc]
+  uint8_t* q;            // E4M3 [T][D] or null
+  float* q_scale;        // [T][D/128]
+};
+size_t hc_pre_norm_smem_bytes(int tt, int D);
+int hc_tokens_per_cta(int T, int num_sms);
+cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream);
+cudaError_t launch_hc_post(const void* y, const void* residual, const float* post, const float* comb, int T, int D,
+                           int hc, void* out, int num_sms, cudaStream_t stream);
+
 // ---- layout (layout.cu)
 struct LayoutParams {
   const int64_t* idx;     // [T][k]

@@ -14,39 +14,6 @@ namespace mosaic {
 
 namespace {
 
-__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h2[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-
-__device__ __forceinline__ uint2 pack8(const uint8_t (&b)[8]) {
-  uint2 r;
-  r.x = b[0] | (b[1] << 8) | (b[2] << 16) | (static_cast<uint32_t>(b[3]) << 24);
-  r.y = b[4] | (b[5] << 8) | (b[6] << 16) | (static_cast<uint32_t>(b[7]) << 24);
-  return r;
-}
-
-// act_quant_ref on 8 values held by this lane; the 128-block spans 16 lanes.
-// Returns the scale exponent and fills q.
-__device__ __forceinline__ int quant_block128(const float (&v)[8], uint8_t (&q)[8]) {
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-  const int e = pow2_scale_exp(m, 1e-4f);
-  const float inv = exp2i(-e);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) q[i] = f32_to_e4m3(fminf(fmaxf(v[i] * inv, -448.f), 448.f));
-  return e;
-}
-
 // hi + lo split on 8 values; the 32-block spans 4 lanes.
 __device__ __forceinline__ void split_block32(const float (&v)[8], uint8_t (&hi)[8], uint8_t (&lo)[8], int& eh,
                                               int& el) {

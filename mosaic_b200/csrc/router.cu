@@ -186,18 +186,6 @@ __device__ __forceinline__ bool better(float v, int e, float v2, int e2) {
   return v > v2 || (v == v2 && e < e2);
 }
 
-// Warp-wide reductions (every lane gets the result).
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-  return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-  return v;
-}
-
 // sqrt(softplus(l)) with torch's softplus (beta 1, threshold 20: l itself above 20).
 __device__ __forceinline__ float sqrt_softplus(float l) { return sqrtf(l > 20.f ? l : log1pf(expf(l))); }
 

@@ -13,6 +13,7 @@ seeded inputs:
 * ``mosaicvm/runtime/fp8.py``: ``dequant_fp4``;
 * ``.mosaicvm/source/inference_model.py``: ``Gate`` with ``score_func``
   "sigmoid", "softmax" and "sqrtsoftplus", score-based and on hash layers;
+* ``mosaicvm/model/layers.py``: ``HyperConnections`` (pre / post) and ``RMSNorm``;
 * ``mosaicvm/model/layers.py``: ``Router`` (sqrtsoftplus) and ``HashRouter``
   (with a table, and the salted fallback with ``MOSAICVM_EXACT_TARGET=0``);
 * ``mosaicvm/model/layers.py``: ``grouped_expert_forward`` and
@@ -45,17 +46,26 @@ from mosaicvm.kernels.fp4_source import (  # noqa: E402
     reference_fp4_linear_source_semantics,
 )
 from mosaicvm.model.config import V4Config  # noqa: E402
-from mosaicvm.model.layers import HashRouter, Router, SharedExpertMLP, grouped_expert_forward  # noqa: E402
+from mosaicvm.model.layers import (  # noqa: E402
+    HashRouter,
+    HyperConnections,
+    RMSNorm,
+    Router,
+    SharedExpertMLP,
+    grouped_expert_forward,
+)
 from mosaicvm.runtime.fp8 import dequant_fp4  # noqa: E402
 
 from tests.golden.recipes import (  # noqa: E402
     GATE_CASES,
+    HC_CASES,
     MOE_CASES,
     ROUTING_CASES,
     SALTED_CASES,
     edge_weight_matrix,
     make_gate_case,
     make_hash_case,
+    make_hc_case,
     make_moe_case,
     salted_token_ids,
 )
@@ -206,6 +216,32 @@ def gen_routing():
     np.savez_compressed(HERE / "routing.npz", **out)
 
 
+def gen_hc():
+    out = {}
+    for name, (b, s_, hc, d, iters, seed) in HC_CASES.items():
+        x, fn, base, scale, norm_w, y = make_hc_case(b, s_, hc, d, seed)
+        cfg = V4Config(hidden_size=d, hc_mult=hc, hc_sinkhorn_iters=iters)
+        mod = HyperConnections(cfg, "ffn")
+        norm = RMSNorm(d, cfg.rms_norm_eps)
+        with torch.no_grad():
+            mod.fn.copy_(fn)
+            mod.base.copy_(base)
+            mod.scale.copy_(scale)
+            norm.weight.copy_(norm_w)
+            y_pre, post, comb = mod.pre(x)
+            y_norm = norm(y_pre)
+            q, qs = act_quant_ref(y_norm.reshape(-1, d))
+            out_post = mod.post(y, x, post, comb)
+        out[name + "_y_pre"] = y_pre.float().numpy()
+        out[name + "_post"] = post.numpy()
+        out[name + "_comb"] = comb.numpy()
+        out[name + "_y_norm"] = y_norm.float().numpy()
+        out[name + "_q"] = q.view(torch.uint8).numpy()
+        out[name + "_qs"] = qs.numpy()
+        out[name + "_out_post"] = out_post.float().numpy()
+    np.savez_compressed(HERE / "hc.npz", **out)
+
+
 def gen_moe():
     out = {}
     for name, spec in MOE_CASES.items():
@@ -258,6 +294,7 @@ if __name__ == "__main__":
     gen_formats()
     gen_router()
     gen_routing()
+    gen_hc()
     gen_moe()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

@@ -126,3 +126,28 @@ def salted_token_ids() -> torch.Tensor:
     edge = torch.tensor([0, 1, -1, 2 ** 31 - 1, -2 ** 31, 2 ** 31, 2 ** 32 - 1, 2 ** 32, 2 ** 63 - 1, -2 ** 63],
                         dtype=torch.int64)
     return torch.cat([edge, rnd, torch.arange(64, dtype=torch.int64)])
+
+
+# Hyper-connection + RMSNorm cases recorded from the reference into hc.npz:
+# name: (batch, seq, hc_mult, D, sinkhorn iters, seed)
+HC_CASES = {
+    "hc_s": (2, 3, 4, 256, 20, 51),
+    "hc_v4": (1, 4, 4, 4096, 20, 52),
+    "hc_mult2": (1, 5, 2, 512, 7, 53),
+}
+
+
+def make_hc_case(b, s, hc, d, seed):
+    """Seeded hyper-connection inputs: x bf16 [b, s, hc, d] (~N(0,1)), fn fp32
+    [(2+hc)*hc, hc*d] (~N(0, 0.01), the reference init), base ~N(0, 0.5), scale
+    ~U(0.5, 1.5) [3], RMSNorm weight 1 + N(0, 0.1) [d], and a sub-layer output y
+    bf16 [b, s, d] for the post-mix."""
+    g = torch.Generator().manual_seed(seed)
+    mix = (2 + hc) * hc
+    x = torch.randn(b, s, hc, d, generator=g).to(torch.bfloat16)
+    fn = torch.randn(mix, hc * d, generator=g) * 0.01
+    base = torch.randn(mix, generator=g) * 0.5
+    scale = torch.rand(3, generator=g) + 0.5
+    norm_w = 1.0 + torch.randn(d, generator=g) * 0.1
+    y = torch.randn(b, s, d, generator=g).to(torch.bfloat16)
+    return x, fn, base, scale, norm_w, y

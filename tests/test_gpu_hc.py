@@ -1,0 +1,101 @@
+"""Hyper-connection pre-mix + RMSNorm (+ act_quant) and post-mix on the GPU.
+
+Bars: post / comb within rtol 1e-4, atol 1e-6 (the mixing dot products run over
+hc*D products in another order than torch's CPU GEMM); bf16 outputs within one
+bf16 ulp of the reference everywhere and bit-equal on at least 98 % of the
+elements; the fused E4M3 act_quant bit-equal to act_quant_ref applied to the
+kernel's own bf16 output.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.formats import act_quant_ref
+from oracle.hc import hc_post, hc_pre, rms_norm
+from tests.golden.recipes import HC_CASES, make_hc_case
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).parent / "golden"
+
+
+def _bf16_close(got, ref, what):
+    got = np.asarray(got, dtype=np.float32)
+    ref = np.asarray(ref, dtype=np.float32)
+    ulp = np.maximum(np.abs(ref), np.abs(got)) * 2.0 ** -7 + 1e-30
+    assert np.all(np.abs(got - ref) <= ulp), (what, float(np.max(np.abs(got - ref) / ulp)))
+    assert np.mean(got == ref) >= 0.98, (what, float(np.mean(got == ref)))
+
+
+def _modules(hc_mult, d, iters, fn, base, scale, norm_w):
+    from mosaic_b200.hc import HyperConnections, RMSNorm
+
+    hc = HyperConnections(d, hc_mult=hc_mult, sinkhorn_iters=iters)
+    hc.fn.data, hc.base.data, hc.scale.data = fn.cuda(), base.cuda(), scale.cuda()
+    norm = RMSNorm(d)
+    norm.weight.data = norm_w.cuda()
+    return hc, norm
+
+
+@pytest.mark.parametrize("name", list(HC_CASES))
+def test_hc_matches_reference_golden(name):
+    from mosaic_b200.hc import ffn_pre_norm
+
+    gold = np.load(GOLD / "hc.npz")
+    b, s, hcm, d, iters, seed = HC_CASES[name]
+    x, fn, base, scale, norm_w, y = make_hc_case(b, s, hcm, d, seed)
+    hc, norm = _modules(hcm, d, iters, fn, base, scale, norm_w)
+    xg = x.cuda()
+    y_pre, post, comb = hc.pre(xg)
+    torch.cuda.synchronize()
+    _bf16_close(y_pre.float().cpu(), gold[name + "_y_pre"], "y_pre")
+    np.testing.assert_allclose(post.cpu().numpy(), gold[name + "_post"], rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(comb.cpu().numpy(), gold[name + "_comb"], rtol=1e-4, atol=1e-6)
+    yn, post2, comb2, q, qs = ffn_pre_norm(xg, hc, norm, quant=True)
+    torch.cuda.synchronize()
+    assert torch.equal(post2, post) and torch.equal(comb2, comb)
+    _bf16_close(yn.float().cpu(), gold[name + "_y_norm"], "y_norm")
+    q_ref, s_ref = act_quant_ref(yn.float().cpu().numpy().reshape(-1, d))
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy().reshape(-1, d), q_ref)
+    assert np.array_equal(qs.cpu().numpy().reshape(-1, d // 128), s_ref)
+    out = hc.post(y.cuda(), xg, torch.from_numpy(gold[name + "_post"]).cuda(),
+                  torch.from_numpy(gold[name + "_comb"]).cuda())
+    torch.cuda.synchronize()
+    _bf16_close(out.float().cpu(), gold[name + "_out_post"], "post-mix")
+
+
+@pytest.mark.parametrize("t", [1, 37, 300, 1001])
+def test_hc_pre_norm_v3_dims(t):
+    """D 7168 (the MoE hidden size of the BASELINE configs), 1..1001 tokens: every
+    tokens-per-CTA variant (1, 2, 4) and a partial last group."""
+    from mosaic_b200.hc import ffn_pre_norm
+
+    d, hcm = 7168, 4
+    x, fn, base, scale, norm_w, _ = make_hc_case(1, t, hcm, d, seed=60 + t)
+    hc, norm = _modules(hcm, d, 20, fn, base, scale, norm_w)
+    yn, post, comb = ffn_pre_norm(x.cuda(), hc, norm)
+    torch.cuda.synchronize()
+    y_pre, post_r, comb_r = hc_pre(x, fn, base, scale, iters=20, eps=1e-6, norm_eps=1e-6)
+    ref = rms_norm(y_pre, norm_w, 1e-6)
+    np.testing.assert_allclose(post.cpu().numpy(), post_r.numpy(), rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(comb.cpu().numpy(), comb_r.numpy(), rtol=1e-4, atol=1e-6)
+    _bf16_close(yn.float().cpu(), ref.float(), "y_norm")
+
+
+def test_hc_pre_norm_feeds_the_moe_layer():
+    """The fused output drives a MoE layer exactly like the same bf16 tensor built on the host."""
+    from mosaic_b200 import synthetic
+    from mosaic_b200.hc import ffn_pre_norm
+
+    layer, _ = synthetic.make_layer(tokens=8, seed=3, act_mode="bf16", n_experts=32)
+    d = layer.cfg.hidden_size
+    x, fn, base, scale, norm_w, _ = make_hc_case(1, 8, 4, d, seed=70)
+    hc, norm = _modules(4, d, 20, fn, base, scale, norm_w)
+    yn, _, _ = ffn_pre_norm(x.cuda(), hc, norm)
+    y1 = layer(yn)
+    y2 = layer(yn.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2) and torch.isfinite(y1.float()).all()
