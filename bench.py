@@ -507,6 +507,47 @@ def run_stack(n_layers, t, world, rank):
 _RESULT_FD = None
 
 
+def offload_bench(layer, n_layers=4, steps=10, warmup=3):
+    """Experts streamed from pinned host memory through an LRU expert cache that
+    holds about one layer's selection: every layer of a step misses, so the step
+    time is the host-to-device copy of the selected experts plus the expert path."""
+    from mosaic_b200.offload import ExpertCache, HostBank, OffloadedMoELayer
+
+    host = HostBank.from_bank(layer.bank)
+    res = {}
+    for t in (1, 8):
+        probe = synthetic.make_tokens(t, 7168, 700 + t)
+        _, idx = layer.router(probe)
+        cap = int(torch.unique(idx).numel()) + 8
+        cache = ExpertCache(7168, 2048, capacity=cap)
+        offs = []
+        for key in range(n_layers):
+            o = OffloadedMoELayer(layer.cfg, host, cache, layer_key=key)
+            o.router.weight.data = layer.router.weight.data
+            o.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
+            offs.append(o)
+        xs = [synthetic.make_tokens(t, 7168, 800 + i) for i in range(steps + warmup)]
+        for i in range(warmup):
+            for o in offs:
+                o(xs[i])
+        torch.cuda.synchronize()
+        b0, m0 = cache.bytes_copied, cache.misses
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(warmup, warmup + steps):
+            for o in offs:
+                o(xs[i])
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        copied = (cache.bytes_copied - b0) / steps
+        res[str(t)] = {"ms_per_layer": ms / n_layers, "cache_experts": cap, "layers": n_layers,
+                       "h2d_bytes_per_layer": copied / n_layers, "h2d_GBs": copied / (ms * 1e-3) / 1e9,
+                       "misses_per_layer": (cache.misses - m0) / steps / n_layers}
+        del offs, cache
+    return res
+
+
 def emit(out: dict) -> None:
     """Write the result line to the real stdout (see main)."""
     os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(out) + "\n").encode())
@@ -626,6 +667,7 @@ def main():
                           "frac_fp4_nominal_9000": flops / (gemm_ms * 1e-3) / 1e12 / 9000.0,
                           "stages_ms": st_p, "zipf": zipf}
         del gp
+        out["offload"] = offload_bench(layer)
     del g
     if rank == 0:
         emit(out)

@@ -289,6 +289,20 @@ MOSAIC_API int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, con
                       const float* expert_weights, const mosaic_expert_bank* bank, void* y, void* workspace,
                       size_t workspace_bytes, mosaic_stream_t stream);
 
+/* mosaic_moe_routed over an expert cache: the weights and scales of logical
+ * expert e (0..n_experts-1, and n_experts = the shared expert when has_shared)
+ * are bank entry expert_slot[e] of a bank of bank_slots entries (int32 device
+ * table of n_experts + has_shared entries; an entry outside [0, bank_slots)
+ * records MOSAIC_ERR_RANGE and reads entry 0).  Everything else uses the
+ * logical ids, so the result equals mosaic_moe_routed on a bank that holds the
+ * same experts in logical order.  Replaces the per-selected-expert loading of
+ * the reference's streaming forward (mosaicvm/runtime/streaming_model.py:209-257,
+ * runtime/loader.py:48-71 ExpertLRU) with a device-resident cache. */
+MOSAIC_API int mosaic_moe_routed_slots(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,
+                                       const float* expert_weights, const mosaic_expert_bank* bank,
+                                       const int32_t* expert_slot, int32_t bank_slots, void* y, void* workspace,
+                                       size_t workspace_bytes, mosaic_stream_t stream);
+
 /* ---- Expert parallelism -------------------------------------------------
  * Rank d of `world` owns the contiguous experts [d*E/world, (d+1)*E/world)
  * (.mosaicvm/source/inference_model.py:620-627) plus a replica of the shared

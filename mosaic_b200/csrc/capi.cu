@@ -206,7 +206,9 @@ void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
 // partial_out, row r at out_row[r] (out_row null: row r).
 int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const LayoutParams& lp,
               const mosaic_expert_bank* bank, int shared_expert, const int* out_row, void* partial_out,
-              cudaStream_t stream, void* const* ev, const EpPeersDev* ep = nullptr) {
+              cudaStream_t stream, void* const* ev, const EpPeersDev* ep = nullptr,
+              const int* expert_slot = nullptr, int bank_slots = 0) {
+  const int n_map = expert_slot ? bank_slots : w.n_bank;  // bank entries the weight maps cover
   const int H = d->hidden, I = d->inter;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
   const int sms = sm_count();
@@ -228,10 +230,12 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   gp.brows = w.tt;
   gp.nbuf = w.nbuf;
   gp.swiglu_limit = d->swiglu_limit;
+  gp.expert_slot = expert_slot;
+  gp.bank_slots = n_map;
   gp.err = lp.err;
 
   // gate/up
-  int st = make_weight_map(&tw, bank->gu_tiled, w.n_bank, 2 * I, H, 2);
+  int st = make_weight_map(&tw, bank->gu_tiled, n_map, 2 * I, H, 2);
   if (st) return st;
   st = make_act_map(&tx, ws + w.xq, w.R_pad, w.planes, H, w.tt, 1);
   if (st) return st;
@@ -247,7 +251,7 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
 
   // down: pairs of hidden blocks (nb, nb + H/256), adjacent in the bank
-  st = make_weight_map(&tw, bank->dn_tiled, w.n_bank, H, I, 2);
+  st = make_weight_map(&tw, bank->dn_tiled, n_map, H, I, 2);
   if (st) return st;
   st = make_act_map(&tx, gp.zq, w.R_pad, w.planes, I, w.tt, 1);
   if (st) return st;
@@ -275,7 +279,7 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
 
 int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const void* x, const int64_t* idx,
                 const float* weights, const mosaic_expert_bank* bank, void* y, cudaStream_t stream,
-                void* const* ev = nullptr) {
+                void* const* ev = nullptr, const int* expert_slot = nullptr, int bank_slots = 0) {
   const int T = d->tokens, H = d->hidden, E = d->n_experts, k = d->top_k;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
   const int shared_base = d->has_shared ? T * k : -1;
@@ -296,7 +300,8 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
     return MOSAIC_ERR_CUDA;
   if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
 
-  const int st = run_gemms(d, w, ws, lp, bank, d->has_shared ? E : -1, nullptr, ws + w.partial, stream, ev);
+  const int st = run_gemms(d, w, ws, lp, bank, d->has_shared ? E : -1, nullptr, ws + w.partial, stream, ev, nullptr,
+                           expert_slot, bank_slots);
   if (st) return st;
 
   if (launch_combine(ws + w.partial, w.partial_f32, lp.row_sorted, T, k, H, shared_base, y, stream) != cudaSuccess)
@@ -727,6 +732,26 @@ int mosaic_moe_routed(const mosaic_moe_dims* dims, const void* x, const int64_t*
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   return run_experts(dims, w, ws, x, expert_ids, expert_weights, bank, y, s);
+}
+
+int mosaic_moe_routed_slots(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,
+                            const float* expert_weights, const mosaic_expert_bank* bank, const int32_t* expert_slot,
+                            int32_t bank_slots, void* y, void* workspace, size_t workspace_bytes,
+                            mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!x || !expert_ids || !expert_slot || !y || !workspace) return MOSAIC_ERR_SHAPE;
+  if (bank_slots < 1) return MOSAIC_ERR_SHAPE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(workspace, 256) || !aligned(expert_slot, 4))
+    return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  return run_experts(dims, w, ws, x, expert_ids, expert_weights, bank, y, s, nullptr, expert_slot, bank_slots);
 }
 
 int mosaic_ep_dispatch(const mosaic_moe_dims* dims, int32_t world, const void* x, const int64_t* idx,

@@ -35,6 +35,9 @@
 // decode sizes three issuer pairs take the stages in turn (stage parity modulo
 // 3), each accumulating into its own TMEM chain with its own scale-factor
 // columns.  The epilogue sums the chains in a fixed order.
+// With an expert slot table the producers read logical expert e's weights and
+// scales from bank entry expert_slot[e] (an offload cache); everything else
+// uses the logical id, so results do not depend on where the expert sits.
 // Reference behaviour: mosaicvm/kernels/qpa_mma.py:337-486 (grouped ordered
 // gate/up and down kernels), mosaicvm/kernels/mxint.py:1301-1346 (fused
 // SwiGLU / route weight / bf16 / act_quant epilogue).
@@ -197,9 +200,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
       const Item m = get_item(p, item);
+      // bank entry of the item's expert (offload: through the slot table)
+      int em = m.e;
+      if (p.expert_slot) {
+        em = __ldg(p.expert_slot + m.e);
+        if (em < 0 || em >= p.bank_slots) {
+          if (lane == 0) set_error(p.err, MOSAIC_ERR_RANGE);
+          em = 0;
+        }
+      }
       // tile index of (expert, block pair, K-tile 0, first of the pair); the two
       // tiles of the pair are adjacent for every K-tile
-      const int wtile = ((m.e * p.n_blocks + m.nb) * KT) * 2;
+      const int wtile = ((em * p.n_blocks + m.nb) * KT) * 2;
       for (int kt = 0; kt < KT; ++kt, ++it) {
         const int s = it % S;
         const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;

@@ -43,6 +43,10 @@ struct GemmParams {
   const int* ep_src_pos;
   size_t ep_ret_off;
   uint8_t* ep_regions[MOSAIC_EP_MAX_WORLD];
+  // expert offload: the weights of logical expert e are bank entry
+  // expert_slot[e] (< bank_slots); null = entry e
+  const int* expert_slot;
+  int bank_slots;
   int* err;
 };
 size_t gemm_smem_bytes(int planes, int brows);
