@@ -216,7 +216,10 @@ class PinnedStager:
     """
 
     def __init__(self, device, chunk_bytes: int = 64 << 20, n_buffers: int = 2):
-        self.device = torch.device(device)
+        dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
         self.chunk = int(chunk_bytes)
         self.bufs = [torch.empty(self.chunk, dtype=torch.uint8, pin_memory=True) for _ in range(n_buffers)]
         self.events = [None] * n_buffers

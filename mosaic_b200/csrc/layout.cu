@@ -8,9 +8,11 @@
 // stable order; the reference's argsort leaves that order unspecified.
 //
 // One CTA of 1024 threads does everything in shared memory, so the layer
-// needs no host round trip.  Ranks inside a 1024-token chunk come from
-// per-warp bit masks (one bit per lane, per expert) and a scan over the 32
-// warps; chunks are processed in order and carry per-expert running bases.
+// needs no host round trip.  Ranks inside a chunk of 1024 assignments come
+// from per-warp bit masks (one bit per lane, per expert) and a scan over the
+// 32 warps; chunks are processed in order and carry per-expert running bases.
+// A token may name an expert more than once (the reference's gather-based
+// path allows it): each assignment still gets a row of its own.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -81,79 +83,83 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
   warp0_exclusive_scan(ntile, toff, NE);
   __syncthreads();
 
-  for (int c0 = 0; c0 < T; c0 += 1024) {
-    const int t = c0 + tid;
+  // Ranks: 1024 assignments per chunk in flat (token-major, slot-minor) order.
+  // One bit per lane per expert marks the chunk's assignments; a token that
+  // names an expert twice (hash tables may) simply has two bits, so every
+  // assignment gets its own row and the order inside an expert stays the flat
+  // index order.
+  for (int c0 = 0; c0 < A; c0 += 1024) {
+    const int a = c0 + tid;
     for (int i = tid; i < 32 * E; i += 1024) masks[i] = 0u;
     __syncthreads();
-    int ev[8];
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      ev[s] = -1;
-      if (s < k && t < T) {
-        const int64_t e = p.idx[static_cast<size_t>(t) * k + s];
-        if (e >= 0 && e < E) {
-          ev[s] = static_cast<int>(e);
-          atomicOr(&masks[warp * E + ev[s]], 1u << lane);
-        }
+    int e = -1;
+    if (a < A) {
+      const int64_t v = p.idx[a];
+      if (v >= 0 && v < E) {
+        e = static_cast<int>(v);
+        atomicOr(&masks[warp * E + e], 1u << lane);
       }
     }
     __syncthreads();
-    for (int e = tid; e < E; e += 1024) {
-      int run = base[e];
+    for (int ex = tid; ex < E; ex += 1024) {
+      int run = base[ex];
       for (int w = 0; w < 32; ++w) {
-        pre[w * E + e] = run;
-        run += __popc(masks[w * E + e]);
+        pre[w * E + ex] = run;
+        run += __popc(masks[w * E + ex]);
       }
-      base[e] = run;
+      base[ex] = run;
     }
     __syncthreads();
-    if (t < T) {
-      int rows[8];
-      const unsigned lt = (1u << lane) - 1u;
+    if (a < A) {
+      int row = -1;
+      if (e >= 0) {
+        const int t = a / k;
+        const unsigned lt = (1u << lane) - 1u;
+        const int rank = pre[warp * E + e] + __popc(masks[warp * E + e] & lt);
+        row = offs[e] + rank;
+        if (p.row_token) p.row_token[row] = t;
+        if (p.row_tile) {
+          const int tt = p.tt_routed;
+          const int ti = rank / tt;
+          const int rows_t = min(tt, hist[e] - ti * tt);
+          p.row_tile[row] = toff[e] + ti;
+          p.row_pos[row] = ((p.rpad_to_tile ? tt : (rows_t + 15) & ~15) << 8) | (rank - ti * tt);
+        }
+        if (p.row_weight) p.row_weight[row] = p.weights ? p.weights[a] : 1.0f;
+        if (x.perm) x.perm[row] = a;
+        if (x.sorted_ids) x.sorted_ids[row] = e;
+      }
+      if (p.row_of) p.row_of[a] = row;
+    }
+    __syncthreads();
+  }
+  // Per token, its rows in ascending expert id (the combine order); equal ids
+  // (repeated by a hash table) hold equal partials, so their order is free.
+  if (p.row_sorted && p.row_of) {
+    for (int t = tid; t < T; t += 1024) {
+      int ke[8], kr[8];
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
-        if (s >= k) break;
-        const int e = ev[s];
-        int row = -1;
-        if (e >= 0) {
-          const int rank = pre[warp * E + e] + __popc(masks[warp * E + e] & lt);
-          row = offs[e] + rank;
-          if (p.row_token) p.row_token[row] = t;
-          if (p.row_tile) {
-            const int tt = p.tt_routed;
-            const int ti = rank / tt;
-            const int rows_t = min(tt, hist[e] - ti * tt);
-            p.row_tile[row] = toff[e] + ti;
-            p.row_pos[row] = ((p.rpad_to_tile ? tt : (rows_t + 15) & ~15) << 8) | (rank - ti * tt);
-          }
-          if (p.row_weight) p.row_weight[row] = p.weights ? p.weights[static_cast<size_t>(t) * k + s] : 1.0f;
-          if (x.perm) x.perm[row] = static_cast<int64_t>(t) * k + s;
-          if (x.sorted_ids) x.sorted_ids[row] = e;
+        ke[s] = 0x7FFFFFFF;
+        kr[s] = 0;
+        if (s < k) {
+          const int64_t v = p.idx[static_cast<size_t>(t) * k + s];
+          ke[s] = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+          kr[s] = p.row_of[static_cast<size_t>(t) * k + s];
         }
-        rows[s] = row;
-        if (p.row_of) p.row_of[static_cast<size_t>(t) * k + s] = row;
       }
-      if (p.row_sorted) {
-        // ascending expert id (ids of one token are distinct)
-        int ke[8], kr[8];
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          ke[s] = (s < k) ? ev[s] : 0x7FFFFFFF;
-          kr[s] = (s < k) ? rows[s] : 0;
+      for (int i = 1; i < k; ++i) {
+        const int ce = ke[i], cr = kr[i];
+        int j = i - 1;
+        while (j >= 0 && ke[j] > ce) {
+          ke[j + 1] = ke[j];
+          kr[j + 1] = kr[j];
+          --j;
         }
-        for (int i = 1; i < k; ++i) {
-          const int ce = ke[i], cr = kr[i];
-          int j = i - 1;
-          while (j >= 0 && ke[j] > ce) {
-            ke[j + 1] = ke[j];
-            kr[j + 1] = kr[j];
-            --j;
-          }
-          ke[j + 1] = ce;
-          kr[j + 1] = cr;
-        }
-        for (int s = 0; s < k; ++s) p.row_sorted[static_cast<size_t>(t) * k + s] = kr[s];
+        ke[j + 1] = ce;
+        kr[j + 1] = cr;
       }
+      for (int s = 0; s < k; ++s) p.row_sorted[static_cast<size_t>(t) * k + s] = kr[s];
     }
     __syncthreads();
   }
