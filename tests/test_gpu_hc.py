@@ -1,10 +1,15 @@
 """Hyper-connection pre-mix + RMSNorm (+ act_quant) and post-mix on the GPU.
 
 Bars: post / comb within rtol 1e-4, atol 1e-6 (the mixing dot products run over
-hc*D products in another order than torch's CPU GEMM); bf16 outputs within one
-bf16 ulp of the reference everywhere and bit-equal on at least 98 % of the
-elements; the fused E4M3 act_quant bit-equal to act_quant_ref applied to the
-kernel's own bf16 output.
+hc*D products in another order than torch's CPU GEMM); bf16 outputs bit-equal on
+at least 98 % of the elements and everywhere within two bf16 ulps of the value
+(the pre-mix is rounded to bf16 before the RMSNorm rounds again, so a one-ulp
+flip in the first becomes up to two in the second) plus 2^-14 of the row's
+RMS.  The absolute term covers cancellation: an output
+sum_m pre_m * x_m of terms ~1 that nearly cancels carries the fp32 error of its
+terms (pre differs from the reference in its last bits), which is large
+relative to the tiny result but not to the row.  The fused E4M3 act_quant is
+bit-equal to act_quant_ref applied to the kernel's own bf16 output.
 """
 from __future__ import annotations
 
@@ -25,8 +30,9 @@ GOLD = Path(__file__).parent / "golden"
 def _bf16_close(got, ref, what):
     got = np.asarray(got, dtype=np.float32)
     ref = np.asarray(ref, dtype=np.float32)
-    ulp = np.maximum(np.abs(ref), np.abs(got)) * 2.0 ** -7 + 1e-30
-    assert np.all(np.abs(got - ref) <= ulp), (what, float(np.max(np.abs(got - ref) / ulp)))
+    rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2, axis=-1, keepdims=True))
+    tol = np.maximum(np.abs(ref), np.abs(got)) * 2.0 ** -6 + rms * 2.0 ** -14 + 1e-30
+    assert np.all(np.abs(got - ref) <= tol), (what, float(np.max(np.abs(got - ref) / tol)))
     assert np.mean(got == ref) >= 0.98, (what, float(np.mean(got == ref)))
 
 
