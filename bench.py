@@ -548,6 +548,35 @@ def offload_bench(layer, n_layers=4, steps=10, warmup=3):
     return res
 
 
+def hc_bench(hbm, steps=20, warmup=3):
+    """The fused hyper-connection pre-mix + RMSNorm (+ E4M3 act_quant) in front of
+    the MoE at the V3 hidden size, hc = 4: HBM-bound on the residual copies."""
+    from mosaic_b200.hc import HyperConnections, RMSNorm, ffn_pre_norm
+
+    d, hcm = 7168, 4
+    hc = HyperConnections(d, hc_mult=hcm).cuda()
+    norm = RMSNorm(d).cuda()
+    res = {}
+    for t in (128, 8192):
+        g = torch.Generator(device="cuda").manual_seed(t)
+        x = torch.randn(t, hcm, d, generator=g, device="cuda").to(torch.bfloat16)
+        for quant in (False, True):
+            for _ in range(warmup):
+                ffn_pre_norm(x, hc, norm, quant=quant)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                ffn_pre_norm(x, hc, norm, quant=quant)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            nbytes = t * (hcm * d * 2 + d * 2 + (d + d // 32 if quant else 0))
+            res[f"T{t}" + ("_quant" if quant else "")] = {
+                "ms": ms, "GBs": nbytes / (ms * 1e-3) / 1e9, "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm,
+                "fma_tflops": t * 24 * hcm * d / (ms * 1e-3) / 1e12}
+    return res
+
+
 def emit(out: dict) -> None:
     """Write the result line to the real stdout (see main)."""
     os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(out) + "\n").encode())
@@ -668,6 +697,7 @@ def main():
                           "stages_ms": st_p, "zipf": zipf}
         del gp
         out["offload"] = offload_bench(layer)
+        out["hc_pre_norm"] = hc_bench(hbm)
     del g
     if rank == 0:
         emit(out)
