@@ -511,6 +511,7 @@ def offload_bench(layer, n_layers=4, steps=10, warmup=3):
     """Experts streamed from pinned host memory through an LRU expert cache that
     holds about one layer's selection: every layer of a step misses, so the step
     time is the host-to-device copy of the selected experts plus the expert path."""
+    from mosaic_b200 import synthetic
     from mosaic_b200.offload import ExpertCache, HostBank, OffloadedMoELayer
 
     host = HostBank.from_bank(layer.bank)
