@@ -240,11 +240,14 @@ MOSAIC_API int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32
  *   y           bf16 [T, D] = RMSNorm(sum_m pre_m * x_m), the MoE input
  *   post        fp32 [T, hc], comb fp32 [T, hc, hc]: for mosaic_hc_post
  *   q, q_scale  E4M3 [T, D] and fp32 [T, D/128] = act_quant_ref(y), or both NULL
- * hc 1..4; D a multiple of 128 (x, y, q 16-byte aligned; fn, norm_weight too). */
+ * hc 1..4; D a multiple of 128 (x, y, q 16-byte aligned; fn, norm_weight too).
+ * The workspace (256-B aligned, mosaic_hc_pre_norm_workspace_bytes) holds the
+ * split-K partials of the mixing products. */
+MOSAIC_API size_t mosaic_hc_pre_norm_workspace_bytes(int32_t T, int32_t D, int32_t hc);
 MOSAIC_API int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const float* scale,
                                   const float* norm_weight, int32_t T, int32_t D, int32_t hc, int32_t sinkhorn_iters,
                                   float hc_eps, float norm_eps, void* y, float* post, float* comb, uint8_t* q,
-                                  float* q_scale, mosaic_stream_t stream);
+                                  float* q_scale, void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
 
 /* The step behind the MoE: out[t, m] = post[t, m] * y[t] + sum_n comb[t, m, n] * residual[t, n]
  * (fp32, rounded to bf16); y bf16 [T, D] (the MoE output), residual and out bf16 [T, hc, D]. */

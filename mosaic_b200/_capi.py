@@ -55,6 +55,7 @@ EXPORTED = (
     "mosaic_pack_mxfp4",
     "mosaic_repack_weights",
     "mosaic_prepack_scales",
+    "mosaic_hc_pre_norm_workspace_bytes",
     "mosaic_hc_pre_norm",
     "mosaic_hc_post",
     "mosaic_moe_workspace_bytes",
@@ -159,8 +160,9 @@ _SIGS = {
     "mosaic_pack_mxfp4": ([_P, _I, _I, _P, _P, _P], ctypes.c_int),
     "mosaic_repack_weights": ([_P, _I, _I, _I, _I, _P, _P], ctypes.c_int),
     "mosaic_prepack_scales": ([_P, _I, _I, _I, _I, _P, _P], ctypes.c_int),
+    "mosaic_hc_pre_norm_workspace_bytes": ([_I, _I, _I], _SZ),
     "mosaic_hc_pre_norm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float, _P, _P, _P, _P, _P,
-                            _P], ctypes.c_int),
+                            _P, _SZ, _P], ctypes.c_int),
     "mosaic_hc_post": ([_P, _P, _P, _P, _I, _I, _I, _P, _P], ctypes.c_int),
     "mosaic_moe_workspace_bytes": ([ctypes.POINTER(MoEDims)], _SZ),
     "mosaic_moe_forward": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _P, _P, _SZ, _P],

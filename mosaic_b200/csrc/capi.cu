@@ -605,20 +605,29 @@ int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, in
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
+size_t mosaic_hc_pre_norm_workspace_bytes(int32_t T, int32_t D, int32_t hc) {
+  if (T < 1 || D < 128 || D % 128 || hc < 1 || hc > 4) return 0;
+  const int sms = sm_count();
+  return hc_pre_norm_workspace_bytes(T, D, hc, sms > 0 ? sms : 148);
+}
+
 int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const float* scale,
                        const float* norm_weight, int32_t T, int32_t D, int32_t hc, int32_t sinkhorn_iters,
                        float hc_eps, float norm_eps, void* y, float* post, float* comb, uint8_t* q, float* q_scale,
-                       mosaic_stream_t stream) {
-  if (!x || !fn || !base || !scale || !y || !post || !comb) return MOSAIC_ERR_SHAPE;
+                       void* workspace, size_t workspace_bytes, mosaic_stream_t stream) {
+  if (!x || !fn || !base || !scale || !y || !post || !comb || !workspace) return MOSAIC_ERR_SHAPE;
   if ((q == nullptr) != (q_scale == nullptr)) return MOSAIC_ERR_SHAPE;
   if (T < 1 || D < 128 || D % 128 || hc < 1 || hc > 4 || sinkhorn_iters < 1) return MOSAIC_ERR_SHAPE;
   if (!aligned(x, 16) || !aligned(fn, 16) || (norm_weight && !aligned(norm_weight, 16)) || !aligned(y, 16) ||
       (q && !aligned(q, 16)))
     return MOSAIC_ERR_ALIGN;
+  if (!aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   if (hc_pre_norm_smem_bytes(hc_tokens_per_cta(T, sms), D) > 227u * 1024u) return MOSAIC_ERR_UNSUPPORTED;
+  if (workspace_bytes < hc_pre_norm_workspace_bytes(T, D, hc, sms)) return MOSAIC_ERR_WORKSPACE;
   HcParams p{};
+  p.partial = static_cast<float*>(workspace);
   p.x = x;
   p.fn = fn;
   p.base = base;

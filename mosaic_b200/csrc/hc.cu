@@ -8,12 +8,15 @@
 //   act_quant_ref           mosaicvm/kernels/fp4_source.py:110-129
 //   HyperConnections.post   mosaicvm/model/layers.py:269-271
 //
-// hc_pre_norm: a CTA takes TT tokens at a time.  Pass A streams the tokens'
-// hc residual copies (x_flat, hc*D bf16) once and accumulates the sum of
-// squares and the (2+hc)*hc mixing dot products against fn (fp32, read from
-// L2, shared by the TT tokens).  One thread per token then runs the Sinkhorn
-// normalisation of the 4x4 combination.  Pass B forms y = sum_m pre_m x_m
-// (bf16) into shared memory with its sum of squares, pass C applies the
+// Two launches.  hc_mix_kernel is a split-K fp32 GEMM of the residual copies
+// x_flat [T, hc*D] (bf16) against fn [(2+hc)*hc, hc*D]: a CTA takes 128 tokens
+// x one K range, stages 32-wide K slices of x (transposed) and fn in shared
+// memory, and each thread accumulates a 4-token x 4-mix tile (plus the tokens'
+// sums of squares), so fn is read once per 128 tokens instead of once per
+// token.  Each split writes its own partials; hc_pre_norm_kernel (TT tokens
+// per CTA) adds them in split order (deterministic), runs the Sinkhorn
+// normalisation of the 4x4 combination (one thread per token), forms the
+// pre-mix y = sum_m pre_m x_m (bf16) in shared memory, then applies the
 // RMSNorm (skipped without a norm weight) and writes the MoE input (and its
 // E4M3 act_quant).
 #include "common.cuh"
@@ -31,11 +34,89 @@ constexpr int kRed = kMaxMix + 1;         // mixes + sum of squares per token
 
 __device__ __forceinline__ float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
 
+constexpr int kMixTok = 128;     // tokens per hc_mix CTA
+constexpr int kMixK = 32;        // K slice staged per step
+constexpr int kMixThreads = 192; // 32 token groups of 4 x 6 mix groups of 4
+
+__global__ void __launch_bounds__(kMixThreads) hc_mix_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            const float* __restrict__ fn, int T, int KD, int nmix,
+                                                            int kchunk, float* __restrict__ partial) {
+  __shared__ __align__(16) float xs[kMixK][kMixTok];  // x slice, transposed: [k][token]
+  __shared__ __align__(16) float fs[kMixK][kMaxMix];  // fn slice, transposed: [k][mix]
+  const int tid = threadIdx.x;
+  const int t0 = blockIdx.x * kMixTok;
+  const int ks = blockIdx.y;
+  const int k_begin = ks * kchunk;
+  const int k_end = min(KD, k_begin + kchunk);
+  const int tg = tid / 6, mg = tid % 6;  // tokens 4tg..4tg+3, mixes 4mg..4mg+3
+  float acc[4][4], ssq[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    ssq[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  }
+  for (int k0 = k_begin; k0 < k_end; k0 += kMixK) {
+    // x: 128 tokens x 32 k = 512 vectors of 8 bf16
+    for (int i = tid; i < kMixTok * (kMixK / 8); i += kMixThreads) {
+      const int row = i >> 2, seg = i & 3;
+      const int t = t0 + row, k = k0 + seg * 8;
+      float v[8];
+      if (t < T && k < k_end) {
+        load8_bf16(x + static_cast<size_t>(t) * KD + k, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xs[seg * 8 + j][row] = v[j];
+    }
+    // fn: 24 mixes x 32 k = 192 float4 (one per thread)
+    {
+      const int mix = tid >> 3, kseg = tid & 7;
+      const int k = k0 + kseg * 4;
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (mix < nmix && k < k_end) f = __ldg(reinterpret_cast<const float4*>(fn + static_cast<size_t>(mix) * KD + k));
+      fs[kseg * 4 + 0][mix] = f.x;
+      fs[kseg * 4 + 1][mix] = f.y;
+      fs[kseg * 4 + 2][mix] = f.z;
+      fs[kseg * 4 + 3][mix] = f.w;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kMixK; ++kk) {
+      const float4 xv = *reinterpret_cast<const float4*>(&xs[kk][4 * tg]);
+      const float4 fv = *reinterpret_cast<const float4*>(&fs[kk][4 * mg]);
+      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+      const float fa[4] = {fv.x, fv.y, fv.z, fv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], fa[j], acc[i][j]);
+        ssq[i] = fmaf(xa[i], xa[i], ssq[i]);
+      }
+    }
+    __syncthreads();
+  }
+  float* out = partial + static_cast<size_t>(ks) * T * kRed;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + 4 * tg + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int mix = 4 * mg + j;
+      if (mix < nmix) out[static_cast<size_t>(t) * kRed + mix] = acc[i][j];
+    }
+    if (mg == 0) out[static_cast<size_t>(t) * kRed + kMaxMix] = ssq[i];
+  }
+}
+
 template <int TT>
 __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* ybuf = reinterpret_cast<__nv_bfloat16*>(smem);                   // [TT][D]
-  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(TT) * p.D * 2);  // [warps][TT][kRed]
+  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(TT) * p.D * 2);  // [warps][TT]
   float* tot = red + kHcWarps * TT * kRed;                                          // [TT][kRed]
   float* pre_s = tot + TT * kRed;                                                   // [TT][4]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -43,59 +124,12 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
   const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
   __nv_bfloat16* yout = static_cast<__nv_bfloat16*>(p.y);
   for (int t0 = blockIdx.x * TT; t0 < p.T; t0 += gridDim.x * TT) {
-    // ---- pass A: mixing dot products and sum of squares of x_flat
-    float acc[TT][kMaxMix];
-    float ss[TT];
-#pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      ss[t] = 0.f;
-#pragma unroll
-      for (int r = 0; r < kMaxMix; ++r) acc[t][r] = 0.f;
-    }
-    for (int c0 = 0; c0 < KD; c0 += kHcChunk) {
-      const int col = c0 + tid * 8;
-      if (col >= KD) continue;
-      float xv[TT][8];
-#pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        if (t0 + t < p.T) {
-          load8_bf16(x + static_cast<size_t>(t0 + t) * KD + col, xv[t]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xv[t][i] = 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ss[t] = fmaf(xv[t][i], xv[t][i], ss[t]);
-      }
-#pragma unroll
-      for (int r = 0; r < kMaxMix; ++r) {
-        if (r < nmix) {
-          const float4 a = __ldg(reinterpret_cast<const float4*>(p.fn + static_cast<size_t>(r) * KD + col));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(p.fn + static_cast<size_t>(r) * KD + col + 4));
-          const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-          for (int t = 0; t < TT; ++t)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[t][r] = fmaf(xv[t][i], f[i], acc[t][r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < TT; ++t) {
-#pragma unroll
-      for (int r = 0; r < kMaxMix; ++r) {
-        if (r < nmix) {
-          const float v = warp_sum(acc[t][r]);
-          if (lane == 0) red[(warp * TT + t) * kRed + r] = v;
-        }
-      }
-      const float v = warp_sum(ss[t]);
-      if (lane == 0) red[(warp * TT + t) * kRed + kMaxMix] = v;
-    }
-    __syncthreads();
+    // ---- mixing dot products and sums of squares: the splits' partials, in split order
     for (int i = tid; i < TT * kRed; i += kHcThreads) {
+      const int t = t0 + i / kRed, r = i % kRed;
       float s = 0.f;
-      for (int w = 0; w < kHcWarps; ++w) s += red[w * TT * kRed + i];
+      if (t < p.T && (r < nmix || r == kMaxMix))
+        for (int sp = 0; sp < p.splits; ++sp) s += p.partial[(static_cast<size_t>(sp) * p.T + t) * kRed + r];
       tot[i] = s;
     }
     __syncthreads();
@@ -300,7 +334,33 @@ size_t hc_pre_norm_smem_bytes(int tt, int D) {
 
 int hc_tokens_per_cta(int T, int num_sms) { return T >= 4 * num_sms ? 4 : (T >= 2 * num_sms ? 2 : 1); }
 
-cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream) {
+// K split of hc_mix_kernel: about two CTAs per SM, K ranges of whole 32-wide slices.
+void hc_mix_split(int T, int KD, int num_sms, int* splits, int* kchunk) {
+  const int tiles = (T + kMixTok - 1) / kMixTok;
+  int s = (2 * num_sms + tiles - 1) / tiles;
+  const int smax = KD / (4 * kMixK);  // at least four slices per split
+  if (s > smax) s = smax;
+  if (s < 1) s = 1;
+  int kc = (KD + s - 1) / s;
+  kc = (kc + kMixK - 1) / kMixK * kMixK;
+  *kchunk = kc;
+  *splits = (KD + kc - 1) / kc;
+}
+
+size_t hc_pre_norm_workspace_bytes(int T, int D, int hc, int num_sms) {
+  int splits = 0, kchunk = 0;
+  hc_mix_split(T, hc * D, num_sms, &splits, &kchunk);
+  return sizeof(float) * static_cast<size_t>(splits) * T * kRed;
+}
+
+cudaError_t launch_hc_pre_norm(const HcParams& p_in, int num_sms, cudaStream_t stream) {
+  HcParams p = p_in;
+  const int KD = p.hc * p.D;
+  int kchunk = 0;
+  hc_mix_split(p.T, KD, num_sms, &p.splits, &kchunk);
+  dim3 gm((p.T + kMixTok - 1) / kMixTok, p.splits);
+  hc_mix_kernel<<<gm, kMixThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(p.x), p.fn, p.T, KD,
+                                                (2 + p.hc) * p.hc, kchunk, p.partial);
   const int tt = hc_tokens_per_cta(p.T, num_sms);
   const int groups = (p.T + tt - 1) / tt;
   const int grid = groups < num_sms ? groups : num_sms;

@@ -83,8 +83,11 @@ struct HcParams {
   float* comb;           // [T][hc][hc]
   uint8_t* q;            // E4M3 [T][D] or null
   float* q_scale;        // [T][D/128]
+  float* partial;        // workspace: [splits][T][25] mixing partials (+ sum of squares)
+  int splits;            // set by the launcher
 };
 size_t hc_pre_norm_smem_bytes(int tt, int D);
+size_t hc_pre_norm_workspace_bytes(int T, int D, int hc, int num_sms);
 int hc_tokens_per_cta(int T, int num_sms);
 cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream);
 cudaError_t launch_hc_post(const void* y, const void* residual, const float* post, const float* comb, int T, int D,

@@ -95,9 +95,11 @@ def _pre_norm(hc_mod: HyperConnections, norm: RMSNorm | None, x, *, quant: bool)
     comb = torch.empty(t, hc, hc, dtype=torch.float32, device=dev)
     q = torch.empty(t, d, dtype=torch.uint8, device=dev) if quant else None
     qs = torch.empty(t, d // 128, dtype=torch.float32, device=dev) if quant else None
-    st = C.lib().mosaic_hc_pre_norm(ops._ptr(xf), ops._ptr(fn), ops._ptr(base), ops._ptr(scale), ops._ptr(w), t, d, hc,
-                                    hc_mod.iters, float(hc_mod.eps), float(hc_mod.norm_eps), ops._ptr(y),
-                                    ops._ptr(post), ops._ptr(comb), ops._ptr(q), ops._ptr(qs), ops._stream())
+    lib = C.lib()
+    ws = torch.empty(max(lib.mosaic_hc_pre_norm_workspace_bytes(t, d, hc), 256), dtype=torch.uint8, device=dev)
+    st = lib.mosaic_hc_pre_norm(ops._ptr(xf), ops._ptr(fn), ops._ptr(base), ops._ptr(scale), ops._ptr(w), t, d, hc,
+                                hc_mod.iters, float(hc_mod.eps), float(hc_mod.norm_eps), ops._ptr(y), ops._ptr(post),
+                                ops._ptr(comb), ops._ptr(q), ops._ptr(qs), ops._ptr(ws), ws.numel(), ops._stream())
     C.check(st, "mosaic_hc_pre_norm")
     out = (y.view(*lead, d), post.view(*lead, hc), comb.view(*lead, hc, hc))
     if quant:

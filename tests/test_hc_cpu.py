@@ -42,11 +42,17 @@ def test_hc_validation_before_launch():
     lib = C.lib()
     f = 1 << 20
     # D not a multiple of 128, hc out of range, iters 0, q without its scale, misaligned x
-    assert lib.mosaic_hc_pre_norm(f, f, f, f, f, 4, 200, 4, 20, 1e-6, 1e-6, f, f, f, None, None, None) == 1
-    assert lib.mosaic_hc_pre_norm(f, f, f, f, f, 4, 256, 5, 20, 1e-6, 1e-6, f, f, f, None, None, None) == 1
-    assert lib.mosaic_hc_pre_norm(f, f, f, f, f, 4, 256, 4, 0, 1e-6, 1e-6, f, f, f, None, None, None) == 1
-    assert lib.mosaic_hc_pre_norm(f, f, f, f, f, 4, 256, 4, 20, 1e-6, 1e-6, f, f, f, f, None, None) == 1
-    assert lib.mosaic_hc_pre_norm(f + 8, f, f, f, f, 4, 256, 4, 20, 1e-6, 1e-6, f, f, f, None, None, None) == 3
+    def call(*a):
+        return lib.mosaic_hc_pre_norm(*a, f, 1 << 30, None)
+
+    assert call(f, f, f, f, f, 4, 200, 4, 20, 1e-6, 1e-6, f, f, f, None, None) == 1
+    assert call(f, f, f, f, f, 4, 256, 5, 20, 1e-6, 1e-6, f, f, f, None, None) == 1
+    assert call(f, f, f, f, f, 4, 256, 4, 0, 1e-6, 1e-6, f, f, f, None, None) == 1
+    assert call(f, f, f, f, f, 4, 256, 4, 20, 1e-6, 1e-6, f, f, f, f, None) == 1
+    assert call(f + 8, f, f, f, f, 4, 256, 4, 20, 1e-6, 1e-6, f, f, f, None, None) == 3
+    assert lib.mosaic_hc_pre_norm(f, f, f, f, f, 4, 256, 4, 20, 1e-6, 1e-6, f, f, f, None, None, None, 0,
+                                  None) == 1  # no workspace
+    assert lib.mosaic_hc_pre_norm_workspace_bytes(4, 200, 4) == 0
     assert lib.mosaic_hc_post(f, f, f, f, 4, 12, 4, f, None) == 1
     assert lib.mosaic_hc_post(f, f + 2, f, f, 4, 256, 4, f, None) == 3
 
