@@ -124,13 +124,16 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
   const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
   __nv_bfloat16* yout = static_cast<__nv_bfloat16*>(p.y);
   for (int t0 = blockIdx.x * TT; t0 < p.T; t0 += gridDim.x * TT) {
-    // ---- mixing dot products and sums of squares: the splits' partials, in split order
-    for (int i = tid; i < TT * kRed; i += kHcThreads) {
+    // ---- mixing dot products and sums of squares: the splits' partials.  Warp w
+    // reduces values w, w+8, ...; lane l adds splits l, l+32, ... in order and
+    // a butterfly adds the lanes, so the order is fixed (deterministic).
+    for (int i = warp; i < TT * kRed; i += kHcWarps) {
       const int t = t0 + i / kRed, r = i % kRed;
       float s = 0.f;
       if (t < p.T && (r < nmix || r == kMaxMix))
-        for (int sp = 0; sp < p.splits; ++sp) s += p.partial[(static_cast<size_t>(sp) * p.T + t) * kRed + r];
-      tot[i] = s;
+        for (int sp = lane; sp < p.splits; sp += 32) s += p.partial[(static_cast<size_t>(sp) * p.T + t) * kRed + r];
+      s = warp_sum(s);
+      if (lane == 0) tot[i] = s;
     }
     __syncthreads();
     // ---- Sinkhorn split, one thread per token
@@ -332,13 +335,19 @@ size_t hc_pre_norm_smem_bytes(int tt, int D) {
   return static_cast<size_t>(tt) * D * 2 + sizeof(float) * (kHcWarps * tt * kRed + tt * kRed + tt * 4);
 }
 
-int hc_tokens_per_cta(int T, int num_sms) { return T >= 4 * num_sms ? 4 : (T >= 2 * num_sms ? 2 : 1); }
+// One token per CTA: the per-token kernel reads nothing that tokens could share,
+// and small CTAs keep many loads in flight on every SM.
+int hc_tokens_per_cta(int T, int num_sms) {
+  (void)T;
+  (void)num_sms;
+  return 1;
+}
 
 // K split of hc_mix_kernel: about two CTAs per SM, K ranges of whole 32-wide slices.
 void hc_mix_split(int T, int KD, int num_sms, int* splits, int* kchunk) {
   const int tiles = (T + kMixTok - 1) / kMixTok;
   int s = (2 * num_sms + tiles - 1) / tiles;
-  const int smax = KD / (4 * kMixK);  // at least four slices per split
+  const int smax = KD / (8 * kMixK);  // at least eight slices per split
   if (s > smax) s = smax;
   if (s < 1) s = 1;
   int kc = (KD + s - 1) / s;
@@ -363,7 +372,7 @@ cudaError_t launch_hc_pre_norm(const HcParams& p_in, int num_sms, cudaStream_t s
                                                 (2 + p.hc) * p.hc, kchunk, p.partial);
   const int tt = hc_tokens_per_cta(p.T, num_sms);
   const int groups = (p.T + tt - 1) / tt;
-  const int grid = groups < num_sms ? groups : num_sms;
+  const int grid = groups < 16 * num_sms ? groups : 16 * num_sms;
   const size_t smem = hc_pre_norm_smem_bytes(tt, p.D);
 #define MOSAIC_HC(TT)                                                                                     \
   do {                                                                                                    \
