@@ -56,33 +56,48 @@ __global__ void __launch_bounds__(kMixThreads) hc_mix_kernel(const __nv_bfloat16
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
   }
-  for (int k0 = k_begin; k0 < k_end; k0 += kMixK) {
-    // x: 128 tokens x 32 k = 512 vectors of 8 bf16
-    for (int i = tid; i < kMixTok * (kMixK / 8); i += kMixThreads) {
-      const int row = i >> 2, seg = i & 3;
-      const int t = t0 + row, k = k0 + seg * 8;
-      float v[8];
-      if (t < T && k < k_end) {
-        load8_bf16(x + static_cast<size_t>(t) * KD + k, v);
-      } else {
+  // The next slice is loaded into registers while the current one is used, so
+  // the HBM latency of x overlaps the FMAs.  x: 128 tokens x 32 k = 512 vectors
+  // of 8 bf16 (threads < 128 take three, the others two); fn: 24 x 32 = 192 float4.
+  uint4 xr[3];
+  float4 fr;
+  const int fmix = tid >> 3, fseg = tid & 7;
+  auto load_slice = [&](int k0) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    for (int u = 0; u < 3; ++u) {
+      const int i = tid + u * kMixThreads;
+      xr[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (i < kMixTok * (kMixK / 8)) {
+        const int t = t0 + (i >> 2), k = k0 + (i & 3) * 8;
+        if (t < T && k < k_end) xr[u] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * KD + k));
       }
+    }
+    const int k = k0 + fseg * 4;
+    fr = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (fmix < nmix && k < k_end) fr = __ldg(reinterpret_cast<const float4*>(fn + static_cast<size_t>(fmix) * KD + k));
+  };
+  if (k_begin < k_end) load_slice(k_begin);
+  for (int k0 = k_begin; k0 < k_end; k0 += kMixK) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) xs[seg * 8 + j][row] = v[j];
+    for (int u = 0; u < 3; ++u) {
+      const int i = tid + u * kMixThreads;
+      if (i < kMixTok * (kMixK / 8)) {
+        const int row = i >> 2, seg = i & 3;
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&xr[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h2[j]);
+          xs[seg * 8 + 2 * j][row] = f.x;
+          xs[seg * 8 + 2 * j + 1][row] = f.y;
+        }
+      }
     }
-    // fn: 24 mixes x 32 k = 192 float4 (one per thread)
-    {
-      const int mix = tid >> 3, kseg = tid & 7;
-      const int k = k0 + kseg * 4;
-      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (mix < nmix && k < k_end) f = __ldg(reinterpret_cast<const float4*>(fn + static_cast<size_t>(mix) * KD + k));
-      fs[kseg * 4 + 0][mix] = f.x;
-      fs[kseg * 4 + 1][mix] = f.y;
-      fs[kseg * 4 + 2][mix] = f.z;
-      fs[kseg * 4 + 3][mix] = f.w;
-    }
+    fs[fseg * 4 + 0][fmix] = fr.x;
+    fs[fseg * 4 + 1][fmix] = fr.y;
+    fs[fseg * 4 + 2][fmix] = fr.z;
+    fs[fseg * 4 + 3][fmix] = fr.w;
     __syncthreads();
+    if (k0 + kMixK < k_end) load_slice(k0 + kMixK);
 #pragma unroll 8
     for (int kk = 0; kk < kMixK; ++kk) {
       const float4 xv = *reinterpret_cast<const float4*>(&xs[kk][4 * tg]);
@@ -170,24 +185,25 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) c[i][j] = (i < hc && j < hc) ? c[i][j] / sum + p.hc_eps : 0.f;
       }
+      // row / column normalisations: products with the reciprocal of each sum
       for (int it = 1; it < p.iters; ++it) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           float s = 0.f;
 #pragma unroll
           for (int j = 0; j < 4; ++j) s += c[i][j];
-          s += p.hc_eps;
+          const float inv = 1.0f / (s + p.hc_eps);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) c[i][j] /= s;
+          for (int j = 0; j < 4; ++j) c[i][j] *= inv;
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           float s = 0.f;
 #pragma unroll
           for (int i = 0; i < 4; ++i) s += c[i][j];
-          s += p.hc_eps;
+          const float inv = 1.0f / (s + p.hc_eps);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) c[i][j] /= s;
+          for (int i = 0; i < 4; ++i) c[i][j] *= inv;
         }
       }
 #pragma unroll
