@@ -15,7 +15,7 @@
 // sums of squares), so fn is read once per 128 tokens instead of once per
 // token.  Each split writes its own partials; hc_pre_norm_kernel (TT tokens
 // per CTA) adds them in split order (deterministic), runs the Sinkhorn
-// normalisation of the 4x4 combination (one thread per token), forms the
+// normalisation of the 4x4 combination (one warp per token), forms the
 // pre-mix y = sum_m pre_m x_m (bf16) in shared memory, then applies the
 // RMSNorm (skipped without a norm weight) and writes the MoE input (and its
 // E4M3 act_quant).
@@ -151,66 +151,36 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
       if (lane == 0) tot[i] = s;
     }
     __syncthreads();
-    // ---- Sinkhorn split, one thread per token
-    if (tid < TT && t0 + tid < p.T) {
-      const int t = t0 + tid;
-      const float* mt = tot + tid * kRed;
+    // ---- Sinkhorn split: warp tt takes token tt; lane 4i+j (< 16) holds comb[i][j],
+    // rows are 4-lane groups (xor 1, 2), columns stride 4 (xor 4, 8)
+    if (warp < TT && t0 + warp < p.T) {
+      const int t = t0 + warp;
+      const float* mt = tot + warp * kRed;
       const float rs = 1.0f / sqrtf(mt[kMaxMix] / static_cast<float>(KD) + p.norm_eps);
-      float mix[kMaxMix];
-#pragma unroll
-      for (int r = 0; r < kMaxMix; ++r) mix[r] = r < nmix ? mt[r] * rs : 0.f;
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        if (m < hc) {
-          pre_s[tid * 4 + m] = sigmoidf(mix[m] * p.scale[0] + p.base[m]) + p.hc_eps;
-          p.post[static_cast<size_t>(t) * hc + m] = 2.0f * sigmoidf(mix[hc + m] * p.scale[1] + p.base[hc + m]);
-        }
+      if (lane < hc) {
+        pre_s[warp * 4 + lane] = sigmoidf(mt[lane] * rs * p.scale[0] + p.base[lane]) + p.hc_eps;
+        p.post[static_cast<size_t>(t) * hc + lane] = 2.0f * sigmoidf(mt[hc + lane] * rs * p.scale[1] + p.base[hc + lane]);
       }
-      // comb rows: softmax + eps, then iters - 1 rounds of row / column normalisation
-      float c[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          c[i][j] = (i < hc && j < hc) ? mix[2 * hc + i * hc + j] * p.scale[2] + p.base[2 * hc + i * hc + j] : 0.f;
-          if (i < hc && j < hc) mx = fmaxf(mx, c[i][j]);
-        }
-        float sum = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          c[i][j] = (i < hc && j < hc) ? expf(c[i][j] - mx) : 0.f;
-          sum += c[i][j];
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) c[i][j] = (i < hc && j < hc) ? c[i][j] / sum + p.hc_eps : 0.f;
-      }
+      const int ci = (lane >> 2) & 3, cj = lane & 3;
+      const bool on = lane < 16 && ci < hc && cj < hc;
+      const int r = 2 * hc + ci * hc + cj;
+      const float v = on ? mt[r] * rs * p.scale[2] + p.base[r] : -INFINITY;
+      float mx = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+      float c = on ? expf(v - mx) : 0.f;
+      float sum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+      sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+      c = on ? c / sum + p.hc_eps : 0.f;
       // row / column normalisations: products with the reciprocal of each sum
       for (int it = 1; it < p.iters; ++it) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) s += c[i][j];
-          const float inv = 1.0f / (s + p.hc_eps);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) c[i][j] *= inv;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float s = 0.f;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) s += c[i][j];
-          const float inv = 1.0f / (s + p.hc_eps);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) c[i][j] *= inv;
-        }
+        float rsum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+        rsum += __shfl_xor_sync(0xFFFFFFFFu, rsum, 2);
+        c *= 1.0f / (rsum + p.hc_eps);
+        float csum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 4);
+        csum += __shfl_xor_sync(0xFFFFFFFFu, csum, 8);
+        c *= 1.0f / (csum + p.hc_eps);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (i < hc && j < hc) p.comb[(static_cast<size_t>(t) * hc + i) * hc + j] = c[i][j];
+      if (on) p.comb[(static_cast<size_t>(t) * hc + ci) * hc + cj] = c;
     }
     __syncthreads();
     // ---- pass B: y = sum_m pre_m x_m (products rounded, summed in m order), bf16
@@ -359,10 +329,10 @@ int hc_tokens_per_cta(int T, int num_sms) {
   return 1;
 }
 
-// K split of hc_mix_kernel: about two CTAs per SM, K ranges of whole 32-wide slices.
+// K split of hc_mix_kernel: K ranges of whole 32-wide slices.
 void hc_mix_split(int T, int KD, int num_sms, int* splits, int* kchunk) {
   const int tiles = (T + kMixTok - 1) / kMixTok;
-  int s = (2 * num_sms + tiles - 1) / tiles;
+  int s = (8 * num_sms + tiles - 1) / tiles;  // about eight CTAs per SM
   const int smax = KD / (8 * kMixK);  // at least eight slices per split
   if (s > smax) s = smax;
   if (s < 1) s = 1;
