@@ -564,13 +564,19 @@ def hc_bench(hbm, steps=20, warmup=3):
         for quant in (False, True):
             for _ in range(warmup):
                 ffn_pre_norm(x, hc, norm, quant=quant)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()  # replayed: device time without the host's launch gaps
+            with torch.cuda.graph(graph):
+                ffn_pre_norm(x, hc, norm, quant=quant)
+            graph.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(steps):
-                ffn_pre_norm(x, hc, norm, quant=quant)
+                graph.replay()
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / steps
+            del graph
             nbytes = t * (hcm * d * 2 + d * 2 + (d + d // 32 if quant else 0))
             res[f"T{t}" + ("_quant" if quant else "")] = {
                 "ms": ms, "GBs": nbytes / (ms * 1e-3) / 1e9, "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm,
