@@ -27,14 +27,17 @@
 // overlaps the MMAs of the next.  The epilogue stages its output in shared
 // memory and writes whole token rows with 16-byte stores.
 //
-// Warp roles (384 threads): warp 0 = weight producer, warp 6 = activation /
-// scale producer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31),
+// Warp roles (416 threads): warp 0 = weight producer, warp 6 = activation /
+// scale producer, warp 12 = scale-factor copier (tcgen05.cp of each stage's
+// weight and token scale chunks into a TMEM ring, one slot per smem stage),
+// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31),
 // warps 1, 7..11 = up to three pairs of MMA issuers (warp 1 also owns TMEM).  A
 // tcgen05.mma costs its issuing thread ~150-200 cycles whatever its size, so
 // each stage is split into two units (the two blocks of the pair), and at
 // decode sizes three issuer pairs take the stages in turn (stage parity modulo
-// 3), each accumulating into its own TMEM chain with its own scale-factor
-// columns.  The epilogue sums the chains in a fixed order.
+// 3), each accumulating into its own TMEM chain.  The copier keeps the scale
+// copies off the issuers (a copy costs its issuing thread about a quarter of
+// an MMA).  The epilogue sums the chains in a fixed order.
 // With an expert slot table the producers read logical expert e's weights and
 // scales from bank entry expert_slot[e] (an offload cache); everything else
 // uses the logical id, so results do not depend on where the expert sits.
@@ -48,20 +51,21 @@ namespace mosaic {
 
 namespace {
 
-constexpr int kThreads = 384;
+constexpr int kThreads = 416;  // + warp 12: scale-factor copier
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 225 * 1024;
 constexpr int kEpiBytes = 16 * 256 * 4;  // epilogue staging: 16 token columns x 256 values (fp32)
 constexpr int kMaxParities = 3;          // issuer pairs (two MMA warps each)
-constexpr uint32_t kSfCols = 8u * 2 * kMaxParities;  // TMEM scale columns: 8 per issuer
+constexpr uint32_t kSfSlotCols = 12u;  // TMEM scale columns per ring stage: 2 weight chunks + token chunk
 
 struct Ctrl {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
-  uint64_t drain[6];
+  uint64_t drain[7];
+  uint64_t sf_ready[kMaxStages];
   uint32_t tmem_base;
   int abort;
   float red[4][16];
@@ -155,11 +159,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nbuf = p.nbuf;
   const int P = p.parities;  // stage parities split across issuer pairs (1 or 2)
   // TMEM: accumulator pair of (buffer b, chain c) at column (b*P + c) * acc_w,
-  // the second block of the pair at +max_n.  Issuer i's scale factors: weight
-  // chunk at sf_base + 8i, token chunk at +4.
+  // the second block of the pair at +max_n.  Scale factors of ring stage s:
+  // the pair's two weight chunks at sf_base + 12s (+4) and the token chunk at +8.
   const uint32_t acc_w = static_cast<uint32_t>(2 * p.max_n);
   const uint32_t half_off = static_cast<uint32_t>(p.max_n);
-  const uint32_t sf_base = kTmemCols - kSfCols;
+  const uint32_t sf_base = kTmemCols - kSfSlotCols * static_cast<uint32_t>(S);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -170,7 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ctrl->acc_full[b], 2 * P);  // one commit from each issuer
       mbar_init(&ctrl->acc_empty[b], 128);
     }
-    for (int i = 0; i < 6; ++i) mbar_init(&ctrl->drain[i], 1);
+    for (int i = 0; i < 7; ++i) mbar_init(&ctrl->drain[i], 1);
+    for (int s = 0; s < S; ++s) mbar_init(&ctrl->sf_ready[s], 1);
     ctrl->abort = 0;
     fence_mbar_init();
   }
@@ -251,8 +256,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int issuer = (warp == 1) ? 0 : warp - 6;  // 0 .. 2P-1
     const int ip = issuer >> 1;                     // stage parity this issuer takes
     const int iu = issuer & 1;                      // unit: block of the pair
-    const uint32_t col_sfw = tmem + sf_base + 8u * issuer;  // weight scale chunk
-    const uint32_t col_sfx = col_sfw + 4u;                  // token scale chunk
     int it = 0, li = 0;
     bool issued = false, ok = true;
     for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++li) {
@@ -272,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // consumes.  A parity wait that skipped phases could match the phase two
         // fills back and read a stage before it lands; requiring every issuer's
         // arrival before a refill keeps all four within one phase of the ring.
-        if (!mbar_wait(&ctrl->full[s], ph, abort)) {
+        if (!mbar_wait(&ctrl->sf_ready[s], ph, abort)) {
           ok = false;
           break;
         }
@@ -286,8 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sw = smem_u32(smem + s * pl.stage_bytes);
           const bool first = (kt < P);  // first stage of this issuer's chain in the item
           const uint32_t d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
-          tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
-          tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
+          const uint32_t col_sfw = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 4u * iu;
+          const uint32_t col_sfx = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 8u;
           const uint32_t a = sw + 16384 * iu, bb = sw + pl.off_b;
 #pragma unroll
           for (uint32_t kb = 0; kb < 4; ++kb) {
@@ -315,6 +318,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&ctrl->drain[issuer]);
       volatile int never = 0;
       mbar_wait(&ctrl->drain[issuer], 0, &never);
+    }
+    __syncwarp();
+  } else if (warp == 12) {
+    // -------------------------------------------------- scale-factor copier
+    int it = 0;
+    bool issued = false, ok = true;
+    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % S;
+        const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+        if (!mbar_wait(&ctrl->full[s], ph, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sw = smem_u32(smem + s * pl.stage_bytes);
+          const uint32_t c0 = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s);
+          tc_cp_32x128b_x4(c0, desc_sf(sw + pl.off_sfa));
+          tc_cp_32x128b_x4(c0 + 4u, desc_sf(sw + pl.off_sfa + 512));
+          tc_cp_32x128b_x4(c0 + 8u, desc_sf(sw + pl.off_sfb));
+          tc_commit(&ctrl->sf_ready[s]);
+          issued = true;
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok) {
+      if (lane == 0) set_error(p.err, MOSAIC_ERR_TIMEOUT);
+      ctrl->abort = 1;
+    }
+    if (lane == 0 && issued) {
+      tc_commit(&ctrl->drain[6]);
+      volatile int never = 0;
+      mbar_wait(&ctrl->drain[6], 0, &never);
     }
     __syncwarp();
   } else if (warp >= 2 && warp <= 5) {
@@ -489,7 +527,11 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
     return cudaErrorInvalidValue;
   const int planes = p.hilo ? 2 : 1;
   if (p.brows * planes != p.max_n || p.brows % 16 || p.brows > 128) return cudaErrorInvalidValue;
-  if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols - kSfCols)) return cudaErrorInvalidValue;
+  {
+    const Plan pl0 = make_plan(p.hilo ? 2 : 1, p.brows);
+    if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols - kSfSlotCols * pl0.stages))
+      return cudaErrorInvalidValue;
+  }
   if (p.K % 128 || p.K < 128) return cudaErrorInvalidValue;
   if (p.mode == 1 && p.H % 256) return cudaErrorInvalidValue;
   const Plan pl = make_plan(planes, p.brows);
