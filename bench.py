@@ -59,6 +59,8 @@ def parse():
                    help="activation mode of the main layer (bf16: decode configs; fp8: prefill configs)")
     p.add_argument("--profile-small", action="store_true",
                    help="small case for ncu captures: no extras, no CPU baseline, 2 profiled stage runs")
+    p.add_argument("--hc-only", action="store_true",
+                   help="only the hyper-connection pre-mix + RMSNorm timing (prints its JSON; for ncu captures)")
     return p.parse_args()
 
 
@@ -611,6 +613,9 @@ def main():
     if dist_on:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, bf16_tf, peak_src = peaks()
+    if args.hc_only:
+        emit({"hc_pre_norm": hc_bench(hbm)})
+        return
     if dist_on:
         run_ep(args, rank, world, local, hbm, peak_src)
         return
