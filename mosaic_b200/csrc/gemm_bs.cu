@@ -57,7 +57,8 @@ constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 225 * 1024;
 constexpr int kEpiBytes = 16 * 256 * 4;  // epilogue staging: 16 token columns x 256 values (fp32)
 constexpr int kMaxParities = 3;          // issuer pairs (two MMA warps each)
-constexpr uint32_t kSfSlotCols = 12u;  // TMEM scale columns per ring stage: 2 weight chunks + token chunk
+constexpr uint32_t kSfSlotCols = 12u;  // copier: TMEM scale columns per ring stage (2 weight chunks + token)
+constexpr uint32_t kSfIssuerCols = 8u * 2 * kMaxParities;  // no copier: 8 columns per issuer
 
 struct Ctrl {
   uint64_t full[kMaxStages];
@@ -160,10 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int P = p.parities;  // stage parities split across issuer pairs (1 or 2)
   // TMEM: accumulator pair of (buffer b, chain c) at column (b*P + c) * acc_w,
   // the second block of the pair at +max_n.  Scale factors of ring stage s:
-  // the pair's two weight chunks at sf_base + 12s (+4) and the token chunk at +8.
+  // the pair's two weight chunks at sf_base + 12s (+4) and the token chunk at +8
+  // (with the copier); without it, issuer i's weight chunk at sf_base + 8i and
+  // the token chunk at +4.
   const uint32_t acc_w = static_cast<uint32_t>(2 * p.max_n);
   const uint32_t half_off = static_cast<uint32_t>(p.max_n);
-  const uint32_t sf_base = kTmemCols - kSfSlotCols * static_cast<uint32_t>(S);
+  const bool copier = p.sf_copier != 0;
+  const uint32_t sf_base = kTmemCols - (copier ? kSfSlotCols * static_cast<uint32_t>(S) : kSfIssuerCols);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -275,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // consumes.  A parity wait that skipped phases could match the phase two
         // fills back and read a stage before it lands; requiring every issuer's
         // arrival before a refill keeps all four within one phase of the ring.
-        if (!mbar_wait(&ctrl->sf_ready[s], ph, abort)) {
+        if (!mbar_wait(copier ? &ctrl->sf_ready[s] : &ctrl->full[s], ph, abort)) {
           ok = false;
           break;
         }
@@ -289,8 +293,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sw = smem_u32(smem + s * pl.stage_bytes);
           const bool first = (kt < P);  // first stage of this issuer's chain in the item
           const uint32_t d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
-          const uint32_t col_sfw = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 4u * iu;
-          const uint32_t col_sfx = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 8u;
+          uint32_t col_sfw, col_sfx;
+          if (copier) {
+            col_sfw = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 4u * iu;
+            col_sfx = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 8u;
+          } else {
+            col_sfw = tmem + sf_base + 8u * issuer;
+            col_sfx = col_sfw + 4u;
+            tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
+            tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
+          }
           const uint32_t a = sw + 16384 * iu, bb = sw + pl.off_b;
 #pragma unroll
           for (uint32_t kb = 0; kb < 4; ++kb) {
@@ -320,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&ctrl->drain[issuer], 0, &never);
     }
     __syncwarp();
-  } else if (warp == 12) {
+  } else if (warp == 12 && copier) {
     // -------------------------------------------------- scale-factor copier
     int it = 0;
     bool issued = false, ok = true;
@@ -529,7 +541,8 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   if (p.brows * planes != p.max_n || p.brows % 16 || p.brows > 128) return cudaErrorInvalidValue;
   {
     const Plan pl0 = make_plan(p.hilo ? 2 : 1, p.brows);
-    if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols - kSfSlotCols * pl0.stages))
+    const int sf_cols = p.sf_copier ? static_cast<int>(kSfSlotCols) * pl0.stages : static_cast<int>(kSfIssuerCols);
+    if (p.nbuf * p.parities * 2 * p.max_n > static_cast<int>(kTmemCols) - sf_cols)
       return cudaErrorInvalidValue;
   }
   if (p.K % 128 || p.K < 128) return cudaErrorInvalidValue;

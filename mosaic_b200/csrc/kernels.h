@@ -47,6 +47,8 @@ struct GemmParams {
   // expert_slot[e] (< bank_slots); null = entry e
   const int* expert_slot;
   int bank_slots;
+  int sf_copier;      // 1: warp 12 copies the scale chunks into a TMEM ring (double-buffered
+                      // accumulators); 0: each issuer copies its own (single buffer)
   int* err;
 };
 size_t gemm_smem_bytes(int planes, int brows);
