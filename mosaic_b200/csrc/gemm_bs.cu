@@ -29,7 +29,9 @@
 //
 // Warp roles (416 threads): warp 0 = weight producer, warp 6 = activation /
 // scale producer, warp 12 = scale-factor copier (tcgen05.cp of each stage's
-// weight and token scale chunks into a TMEM ring, one slot per smem stage),
+// weight and token scale chunks into a TMEM ring, one slot per smem stage;
+// the 384-thread instance for single-buffered launches has no copier and the
+// issuers copy their own chunks),
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31),
 // warps 1, 7..11 = up to three pairs of MMA issuers (warp 1 also owns TMEM).  A
 // tcgen05.mma costs its issuing thread ~150-200 cycles whatever its size, so
@@ -51,7 +53,8 @@ namespace mosaic {
 
 namespace {
 
-constexpr int kThreads = 416;  // + warp 12: scale-factor copier
+constexpr int kThreadsCopier = 416;  // 13 warps: + warp 12, the scale-factor copier (128 registers)
+constexpr int kThreadsPlain = 384;   // 12 warps: issuers copy their own scale chunks (up to 168 registers)
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 225 * 1024;
@@ -144,7 +147,8 @@ __device__ __forceinline__ Item get_item(const GemmParams& p, int item) {
   return it;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NT>
+__global__ void __launch_bounds__(NT, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -166,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the token chunk at +4.
   const uint32_t acc_w = static_cast<uint32_t>(2 * p.max_n);
   const uint32_t half_off = static_cast<uint32_t>(p.max_n);
-  const bool copier = p.sf_copier != 0;
+  constexpr bool copier = (NT == kThreadsCopier);
   const uint32_t sf_base = kTmemCols - (copier ? kSfSlotCols * static_cast<uint32_t>(S) : kSfIssuerCols);
 
   if (threadIdx.x == 0) {
@@ -550,10 +554,11 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   const Plan pl = make_plan(planes, p.brows);
   if (pl.stages < 2) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes(planes, p.brows);
-  cudaError_t err = cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  auto kernel = p.sf_copier ? moe_gemm_kernel<kThreadsCopier> : moe_gemm_kernel<kThreadsPlain>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  moe_gemm_kernel<<<grid, kThreads, smem, stream>>>(tmap_w, tmap_x, p);
+  kernel<<<grid, p.sf_copier ? kThreadsCopier : kThreadsPlain, smem, stream>>>(tmap_w, tmap_x, p);
   return cudaGetLastError();
 }
 

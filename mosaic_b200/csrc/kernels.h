@@ -47,8 +47,9 @@ struct GemmParams {
   // expert_slot[e] (< bank_slots); null = entry e
   const int* expert_slot;
   int bank_slots;
-  int sf_copier;      // 1: warp 12 copies the scale chunks into a TMEM ring (double-buffered
-                      // accumulators); 0: each issuer copies its own (single buffer)
+  int sf_copier;      // 1: the 416-thread kernel, whose warp 12 copies the scale chunks into a
+                      // TMEM ring (double-buffered launches); 0: the 384-thread kernel, whose
+                      // issuers copy their own (single-buffered wide decode tiles)
   int* err;
 };
 size_t gemm_smem_bytes(int planes, int brows);
