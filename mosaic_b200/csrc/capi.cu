@@ -88,7 +88,7 @@ struct WsPlan {
   int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32, max_n, nbuf, parities;
   size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, row_tile, row_pos, tiles,
       n_tiles;
-  size_t xq, x_sft, zq, z_sft, partial, row_idx, row_w, total;
+  size_t xq, x_sft, zq, z_sft, partial, row_idx, row_w, lay_scratch, total;
 };
 
 int check_dims(const mosaic_moe_dims* d) {
@@ -164,6 +164,7 @@ WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   w.partial = take(rows_mode ? 0 : static_cast<size_t>(w.R) * H * (w.partial_f32 ? 4 : 2));
   w.row_idx = take(rows_mode ? sizeof(int64_t) * static_cast<size_t>(T) : 0);
   w.row_w = take(rows_mode ? sizeof(float) * static_cast<size_t>(T) : 0);
+  w.lay_scratch = take(sizeof(int) * layout_scratch_ints(T, k, E));
   w.total = o;
   return w;
 }
@@ -199,6 +200,7 @@ void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
   lp.tiles = reinterpret_cast<int*>(ws + w.tiles);
   lp.n_tiles = reinterpret_cast<int*>(ws + w.n_tiles);
   lp.err = reinterpret_cast<int*>(ws + w.err);
+  lp.scratch = layout_scratch_ints(lp.T, lp.k, lp.E) ? reinterpret_cast<int*>(ws + w.lay_scratch) : nullptr;
 }
 
 // Gate/up (+ SwiGLU, route weight, re-quantisation) then down over the packed

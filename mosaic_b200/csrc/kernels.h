@@ -117,7 +117,10 @@ struct LayoutParams {
   int* tiles;             // [max_tiles][3]
   int* n_tiles;
   int* err;
+  int* scratch;           // layout_scratch_ints(T, k, E) ints: the multi-CTA layout of
+                          // batches above 1024 assignments (null: the single-CTA kernel)
 };
+size_t layout_scratch_ints(int T, int k, int E);
 cudaError_t launch_layout(const LayoutParams& p, cudaStream_t stream);
 cudaError_t launch_layout_assignments(const int64_t* ids, int A, int E, int64_t* sorted_ids, int64_t* perm,
                                       int32_t* offsets, int32_t* counts, cudaStream_t stream);

@@ -200,6 +200,206 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
   }
 }
 
+// ---- multi-CTA layout for large batches (more than one chunk of 1024 assignments).
+// The single-CTA kernel above walks the chunks one after another; here each
+// chunk is a CTA: (1) count its assignments per expert, (2) one CTA scans the
+// counts over chunks (per expert) and over experts and writes the tile list,
+// (3) each chunk ranks its assignments from its chunk base, (4) per token: the
+// combine order and the shared expert's rows.  Ranks are those of the
+// single-CTA kernel: stable by flat assignment index inside each expert.
+struct LayoutScratch {
+  int* chunk;  // [nchunks][E]: counts, then exclusive chunk bases
+  int* hist;   // [NE]
+  int* offs;   // [NE + 1]
+  int* toff;   // [NE + 1]
+};
+
+__device__ __forceinline__ LayoutScratch scratch_of(const LayoutParams& p, int nchunks) {
+  const int NE = p.E + (p.with_shared ? 1 : 0);
+  LayoutScratch s;
+  s.chunk = p.scratch;
+  s.hist = p.scratch + static_cast<size_t>(nchunks) * p.E;
+  s.offs = s.hist + NE;
+  s.toff = s.offs + NE + 1;
+  return s;
+}
+
+__global__ void __launch_bounds__(1024) layout_count_kernel(LayoutParams p, int nchunks) {
+  __shared__ int cnt[260];  // E <= 257 (the per-row pass counts the shared expert as an id)
+  const int E = p.E, k = p.k, tid = threadIdx.x, c = blockIdx.x;
+  const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
+  const int A = T * k;
+  const LayoutScratch sc = scratch_of(p, nchunks);
+  for (int e = tid; e < E; e += 1024) cnt[e] = 0;
+  __syncthreads();
+  const int a = c * 1024 + tid;
+  if (a < A) {
+    const int64_t v = p.idx[a];
+    if (v >= 0 && v < E) {
+      atomicAdd(&cnt[static_cast<int>(v)], 1);
+    } else {
+      set_error(p.err, MOSAIC_ERR_RANGE);
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += 1024) sc.chunk[static_cast<size_t>(c) * E + e] = cnt[e];
+}
+
+__global__ void __launch_bounds__(1024) layout_scan_kernel(LayoutParams p, int nchunks) {
+  extern __shared__ int sm[];
+  const int E = p.E, tid = threadIdx.x;
+  const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
+  const int NE = E + (p.with_shared ? 1 : 0);
+  const LayoutScratch sc = scratch_of(p, nchunks);
+  int* hist = sm;           // NE
+  int* offs = hist + NE;    // NE + 1
+  int* ntile = offs + NE + 1;  // NE
+  int* toff = ntile + NE;   // NE + 1
+  for (int e = tid; e < E; e += 1024) {
+    int run = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      int* q = sc.chunk + static_cast<size_t>(c) * E + e;
+      const int v = *q;
+      *q = run;
+      run += v;
+    }
+    hist[e] = run;
+  }
+  if (tid == 0 && p.with_shared) hist[E] = T;
+  __syncthreads();
+  warp0_exclusive_scan(hist, offs, NE);
+  for (int i = tid; i < NE; i += 1024) {
+    const int tt = (p.with_shared && i == E) ? p.tt_shared : p.tt_routed;
+    ntile[i] = (tt > 0) ? (hist[i] + tt - 1) / tt : 0;
+  }
+  __syncthreads();
+  warp0_exclusive_scan(ntile, toff, NE);
+  __syncthreads();
+  for (int i = tid; i < NE; i += 1024) {
+    sc.hist[i] = hist[i];
+    if (p.counts) p.counts[i] = hist[i];
+  }
+  for (int i = tid; i <= NE; i += 1024) {
+    sc.offs[i] = offs[i];
+    sc.toff[i] = toff[i];
+    if (p.offsets) p.offsets[i] = offs[i];
+  }
+  if (p.tiles) {
+    for (int e = tid; e < NE; e += 1024) {
+      const int tt = (p.with_shared && e == E) ? p.tt_shared : p.tt_routed;
+      for (int i = 0; i < ntile[e]; ++i) {
+        const int j = toff[e] + i;
+        if (j < p.max_tiles) {
+          p.tiles[3 * j + 0] = e;
+          p.tiles[3 * j + 1] = offs[e] + i * tt;
+          p.tiles[3 * j + 2] = min(tt, hist[e] - i * tt);
+        }
+      }
+    }
+    if (tid == 0) {
+      *p.n_tiles = toff[NE];
+      if (toff[NE] > p.max_tiles) set_error(p.err, MOSAIC_ERR_WORKSPACE);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) layout_rank_kernel(LayoutParams p, int nchunks, LayoutExtra x) {
+  extern __shared__ int sm[];
+  const int E = p.E, k = p.k, c = blockIdx.x;
+  const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
+  const int A = T * k;
+  if (c * 1024 >= A) return;
+  const LayoutScratch sc = scratch_of(p, nchunks);
+  unsigned* masks = reinterpret_cast<unsigned*>(sm);         // 32 * E
+  int* pre = reinterpret_cast<int*>(masks + 32 * E);          // 32 * E
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 32 * E; i += 1024) masks[i] = 0u;
+  __syncthreads();
+  const int a = c * 1024 + tid;
+  int e = -1;
+  if (a < A) {
+    const int64_t v = p.idx[a];
+    if (v >= 0 && v < E) {
+      e = static_cast<int>(v);
+      atomicOr(&masks[warp * E + e], 1u << lane);
+    }
+  }
+  __syncthreads();
+  for (int ex = tid; ex < E; ex += 1024) {
+    int run = sc.chunk[static_cast<size_t>(c) * E + ex];
+    for (int w = 0; w < 32; ++w) {
+      pre[w * E + ex] = run;
+      run += __popc(masks[w * E + ex]);
+    }
+  }
+  __syncthreads();
+  if (a < A) {
+    int row = -1;
+    if (e >= 0) {
+      const unsigned lt = (1u << lane) - 1u;
+      const int rank = pre[warp * E + e] + __popc(masks[warp * E + e] & lt);
+      row = sc.offs[e] + rank;
+      if (p.row_token) p.row_token[row] = a / k;
+      if (p.row_tile) {
+        const int tt = p.tt_routed;
+        const int ti = rank / tt;
+        const int rows_t = min(tt, sc.hist[e] - ti * tt);
+        p.row_tile[row] = sc.toff[e] + ti;
+        p.row_pos[row] = ((p.rpad_to_tile ? tt : (rows_t + 15) & ~15) << 8) | (rank - ti * tt);
+      }
+      if (p.row_weight) p.row_weight[row] = p.weights ? p.weights[a] : 1.0f;
+      if (x.perm) x.perm[row] = a;
+      if (x.sorted_ids) x.sorted_ids[row] = e;
+    }
+    if (p.row_of) p.row_of[a] = row;
+  }
+}
+
+__global__ void __launch_bounds__(256) layout_finish_kernel(LayoutParams p, int nchunks) {
+  const int E = p.E, k = p.k;
+  const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
+  const LayoutScratch sc = scratch_of(p, nchunks);
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+    if (p.row_sorted && p.row_of) {
+      int ke[8], kr[8];
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        ke[s] = 0x7FFFFFFF;
+        kr[s] = 0;
+        if (s < k) {
+          const int64_t v = p.idx[static_cast<size_t>(t) * k + s];
+          ke[s] = (v >= 0 && v < E) ? static_cast<int>(v) : -1;
+          kr[s] = p.row_of[static_cast<size_t>(t) * k + s];
+        }
+      }
+      for (int i = 1; i < k; ++i) {
+        const int ce = ke[i], cr = kr[i];
+        int j = i - 1;
+        while (j >= 0 && ke[j] > ce) {
+          ke[j + 1] = ke[j];
+          kr[j + 1] = kr[j];
+          --j;
+        }
+        ke[j + 1] = ce;
+        kr[j + 1] = cr;
+      }
+      for (int s = 0; s < k; ++s) p.row_sorted[static_cast<size_t>(t) * k + s] = kr[s];
+    }
+    if (p.with_shared && p.row_token && p.row_weight) {
+      const int row = sc.offs[E] + t;
+      p.row_token[row] = t;
+      p.row_weight[row] = 1.0f;
+      if (p.row_tile) {
+        const int tt = p.tt_shared;
+        const int ti = t / tt;
+        const int rows_t = min(tt, T - ti * tt);
+        p.row_tile[row] = sc.toff[E] + ti;
+        p.row_pos[row] = ((p.rpad_to_tile ? tt : (rows_t + 15) & ~15) << 8) | (t - ti * tt);
+      }
+    }
+  }
+}
+
 size_t layout_smem(int E, int with_shared) {
   const int NE = E + (with_shared ? 1 : 0);
   return sizeof(int) * (static_cast<size_t>(NE) * 4 + 2 + E + 64 * static_cast<size_t>(E));
@@ -230,7 +430,26 @@ __global__ void emit_tiles_kernel(const int32_t* counts, int E, int block_m, int
 
 }  // namespace
 
+size_t layout_scratch_ints(int T, int k, int E) {
+  const int nchunks = (T * k + 1023) / 1024;
+  return nchunks > 1 ? static_cast<size_t>(nchunks) * E + 3 * static_cast<size_t>(E + 3) : 0;
+}
+
 cudaError_t launch_layout(const LayoutParams& p, cudaStream_t stream) {
+  const int nchunks = (p.T * p.k + 1023) / 1024;
+  if (nchunks > 1 && p.scratch) {
+    const int NE = p.E + (p.with_shared ? 1 : 0);
+    layout_count_kernel<<<nchunks, 1024, 0, stream>>>(p, nchunks);
+    layout_scan_kernel<<<1, 1024, sizeof(int) * (4 * NE + 2), stream>>>(p, nchunks);
+    const size_t rsmem = sizeof(int) * 64 * static_cast<size_t>(p.E);
+    cudaError_t e = cudaFuncSetAttribute(layout_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(rsmem));
+    if (e != cudaSuccess) return e;
+    layout_rank_kernel<<<nchunks, 1024, rsmem, stream>>>(p, nchunks, LayoutExtra{nullptr, nullptr});
+    const int fb = (p.T + 255) / 256;
+    layout_finish_kernel<<<fb < 1184 ? fb : 1184, 256, 0, stream>>>(p, nchunks);
+    return cudaGetLastError();
+  }
   const size_t smem = layout_smem(p.E, p.with_shared);
   cudaError_t err = cudaFuncSetAttribute(layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
