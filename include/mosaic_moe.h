@@ -166,8 +166,8 @@ MOSAIC_API int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, con
                                  int32_t topk_group, float route_scale, int32_t norm_topk_prob, float* weights_out,
                                  int64_t* idx_out, void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
 
-/* Size of the fixed device scratch of mosaic_router_noalloc (16 MiB). */
-#define MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES (16u << 20)
+/* Size of the fixed device scratch of mosaic_router_noalloc (32 MiB). */
+#define MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES (32u << 20)
 
 /* mosaic_router without a caller workspace; it has no counterpart in the
  * reference (whose Router.forward allocates through torch).  The split-K
@@ -176,8 +176,8 @@ MOSAIC_API int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, con
  * device memory (no cudaMalloc/cudaFree, no torch allocator); results are
  * bit-identical to mosaic_router on the same inputs.  Inputs whose partials
  * need more than the scratch (mosaic_router_workspace_bytes(T, H, E) >
- * MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES, e.g. T = 16384, E = 256) return
- * MOSAIC_ERR_WORKSPACE without launching.
+ * MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES, e.g. T = 32768, H = 7168, E = 256)
+ * return MOSAIC_ERR_WORKSPACE without launching.
  * - One scratch per device: calls that overlap on a device (two streams, two
  *   host threads, or two launches in one graph that may run concurrently)
  *   race on it and give undefined results.  Serialise them.

@@ -28,7 +28,7 @@ def ep_row_bytes(hidden: int) -> int:
 
 
 # include/mosaic_moe.h MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
-MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 16 << 20
+MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 MOSAIC_ACT_BF16 = 0
 MOSAIC_ACT_FP8 = 1

@@ -84,9 +84,59 @@ int make_act_map(CUtensorMap* map, const uint8_t* q, int R_pad, int planes, int 
   return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
+// Router logits on the tensor cores (router_tc.cu) for batches that take one
+// pass over K: x bf16 [T][H] and the three bf16 parts of W [3E][H], both as
+// 2-D maps with 64-value (128-byte, swizzled) x 128-row boxes.
+bool router_tc_ok(int T, int H, int E, int sms) {
+  return router_large_batch(T, E, sms) && H % 64 == 0 && E % 16 == 0;
+}
+
+size_t router_parts_bytes(int T, int H, int E, int sms) {
+  return router_tc_ok(T, H, E, sms) ? up256(sizeof(uint16_t) * 3 * static_cast<size_t>(E) * H) : 0;
+}
+
+int make_bf16_rows_map(CUtensorMap* map, const void* base, int rows, int K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return MOSAIC_ERR_CUDA;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+// Logits + top-k.  parts (router_parts_bytes, or null) selects the tensor-core
+// logits where they apply; the split-K FMA kernels otherwise.
+int run_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k, int n_group,
+               int topk_group, float route_scale, int norm, float* weights_out, int64_t* idx_out, float* partial,
+               void* parts, int splits, int* err, cudaStream_t stream, const RouteVariant* rv) {
+  const RouteVariant r = rv ? *rv : RouteVariant{};
+  const int sms = sm_count();
+  if (parts && !(r.hash && !r.tid2eid) && sms > 0 && router_tc_ok(T, H, E, sms)) {
+    if (launch_router_split_w(w, E, H, parts, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+    CUtensorMap tx, tw;
+    int st = make_bf16_rows_map(&tx, x, T, H);
+    if (st) return st;
+    st = make_bf16_rows_map(&tw, parts, 3 * E, H);
+    if (st) return st;
+    if (launch_router_logits_tc(tx, tw, T, H, E, partial, err, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+    return launch_router_topk(partial, 1, bias, T, E, top_k, n_group, topk_group, route_scale, norm, weights_out,
+                              idx_out, err, stream, rv) == cudaSuccess
+               ? MOSAIC_OK
+               : MOSAIC_ERR_CUDA;
+  }
+  return launch_router(x, w, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm, weights_out, idx_out,
+                       partial, splits, err, stream, rv) == cudaSuccess
+             ? MOSAIC_OK
+             : MOSAIC_ERR_CUDA;
+}
+
 struct WsPlan {
   int R, R_pad, planes, max_tiles, splits, tt, n_bank, partial_f32, max_n, nbuf, parities;
-  size_t err, router_part, counts, offsets, row_of, row_sorted, row_token, row_weight, row_tile, row_pos, tiles,
+  size_t err, router_part, router_parts, counts, offsets, row_of, row_sorted, row_token, row_weight, row_tile, row_pos, tiles,
       n_tiles;
   size_t xq, x_sft, zq, z_sft, partial, row_idx, row_w, lay_scratch, total;
 };
@@ -147,6 +197,7 @@ WsPlan plan_ws(const mosaic_moe_dims* d, bool rows_mode = false) {
   };
   w.err = take(16);
   w.router_part = take(rows_mode ? 0 : sizeof(float) * static_cast<size_t>(w.splits) * T * E);
+  w.router_parts = take(rows_mode ? 0 : router_parts_bytes(T, H, E, sms > 0 ? sms : 148));
   w.counts = take(sizeof(int) * (E + 1));
   w.offsets = take(sizeof(int) * (E + 2));
   w.row_of = take(sizeof(int) * static_cast<size_t>(T) * k);
@@ -480,7 +531,8 @@ size_t mosaic_router_workspace_bytes(int32_t T, int32_t H, int32_t E) {
   if (T < 1 || H < 1 || E < 1) return 0;
   const int sms = sm_count();
   const int splits = router_splits(T, H, E, sms > 0 ? sms : 148);
-  return up256(16) + up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
+  return up256(16) + up256(sizeof(float) * static_cast<size_t>(splits) * T * E) +
+         router_parts_bytes(T, H, E, sms > 0 ? sms : 148);
 }
 
 int mosaic_router(const void* x, const float* weight, const float* bias, int32_t T, int32_t H, int32_t E,
@@ -496,10 +548,10 @@ int mosaic_router(const void* x, const float* weight, const float* bias, int32_t
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   const int splits = router_splits(T, H, E, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
-                                weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
-                                reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  const size_t part_bytes = up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
+  return run_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob, weights_out,
+                    idx_out, reinterpret_cast<float*>(ws + up256(16)), ws + up256(16) + part_bytes, splits,
+                    reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream), nullptr);
 }
 
 int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, const float* weight, const float* bias, int32_t T,
@@ -526,10 +578,10 @@ int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, const float* w
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   const int splits = router_splits(T, H, E, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
-                                weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
-                                reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream), &rv);
-  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  const size_t part_bytes = up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
+  return run_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob, weights_out,
+                    idx_out, reinterpret_cast<float*>(ws + up256(16)), ws + up256(16) + part_bytes, splits,
+                    reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream), &rv);
 }
 
 int mosaic_router_noalloc(const void* x, const float* weight, const float* bias, int32_t T, int32_t H, int32_t E,
@@ -548,10 +600,10 @@ int mosaic_router_noalloc(const void* x, const float* weight, const float* bias,
   const int sst = router_scratch(dev, &ws);
   if (sst != MOSAIC_OK) return sst;
   const int splits = router_splits(T, H, E, sms);
-  cudaError_t e = launch_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob,
-                                weights_out, idx_out, reinterpret_cast<float*>(ws + up256(16)), splits,
-                                reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  const size_t part_bytes = up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
+  return run_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob, weights_out,
+                    idx_out, reinterpret_cast<float*>(ws + up256(16)), ws + up256(16) + part_bytes, splits,
+                    reinterpret_cast<int*>(ws), reinterpret_cast<cudaStream_t>(stream), nullptr);
 }
 
 int mosaic_layout_assignments(const int64_t* expert_ids, int32_t A, int32_t E, int64_t* sorted_ids, int64_t* perm,
@@ -694,12 +746,11 @@ int moe_forward_impl(const mosaic_moe_dims* dims, const mosaic_route_ext* ext, c
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (!rec(stage_events, 0, s)) return MOSAIC_ERR_CUDA;
-  cudaError_t e = launch_router(x, router_weight, rv.hash ? nullptr : router_bias, dims->tokens, dims->hidden,
-                                dims->n_experts, dims->top_k, dims->n_group, dims->topk_group, dims->route_scale,
-                                dims->norm_topk_prob, weights_out, idx_out,
-                                reinterpret_cast<float*>(ws + w.router_part), w.splits,
-                                reinterpret_cast<int*>(ws + w.err), s, &rv);
-  if (e != cudaSuccess) return MOSAIC_ERR_CUDA;
+  st = run_router(x, router_weight, rv.hash ? nullptr : router_bias, dims->tokens, dims->hidden, dims->n_experts,
+                  dims->top_k, dims->n_group, dims->topk_group, dims->route_scale, dims->norm_topk_prob, weights_out,
+                  idx_out, reinterpret_cast<float*>(ws + w.router_part), ws + w.router_parts, w.splits,
+                  reinterpret_cast<int*>(ws + w.err), s, &rv);
+  if (st) return st;
   if (!rec(stage_events, 1, s)) return MOSAIC_ERR_CUDA;
   return run_experts(dims, w, ws, x, idx_out, weights_out, bank, y, s, stage_events);
 }

@@ -67,6 +67,15 @@ struct RouteVariant {
   const int64_t* token_ids = nullptr;  // [T]; null = 0..T-1
 };
 int router_splits(int T, int H, int E, int num_sms);
+bool router_large_batch(int T, int E, int num_sms);  // one-pass logits (split factor 1)
+cudaError_t launch_router_topk(const float* partial, int splits, const float* bias, int T, int E, int top_k,
+                               int n_group, int topk_group, float route_scale, int norm, float* weights_out,
+                               int64_t* idx_out, int* err, cudaStream_t stream, const RouteVariant* variant);
+// tensor-core logits (router_tc.cu): W fp32 -> three bf16 parts, then logits [T][E] fp32
+size_t router_tc_smem_bytes();
+cudaError_t launch_router_split_w(const float* w, int E, int H, void* parts, int num_sms, cudaStream_t stream);
+cudaError_t launch_router_logits_tc(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, int T, int H, int E,
+                                    float* logits, int* err, cudaStream_t stream);
 cudaError_t launch_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
                           int n_group, int topk_group, float route_scale, int norm, float* weights_out,
                           int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream,

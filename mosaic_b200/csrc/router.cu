@@ -441,6 +441,8 @@ __global__ void router_hash_salted_kernel(const int64_t* __restrict__ token_ids,
 
 }  // namespace
 
+bool router_large_batch(int T, int E, int num_sms) { return use_big_tiles(T, E, num_sms); }
+
 // Split-K factor of the logits kernel for small batches: ~2 CTAs per SM with
 // K ranges of at least 256 (more splits only add partials for the top-k pass).
 int router_splits(int T, int H, int E, int num_sms) {
@@ -473,6 +475,15 @@ cudaError_t launch_router(const void* x, const float* w, const float* bias, int 
     dim3 g1((T + kTileT - 1) / kTileT, (E + kTileE - 1) / kTileE, used);
     router_logits_kernel<<<g1, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), w, T, H, E, kchunk, partial);
   }
+  return launch_router_topk(partial, used, bias, T, E, top_k, n_group, topk_group, route_scale, norm, weights_out,
+                            idx_out, err, stream, &rv);
+}
+
+cudaError_t launch_router_topk(const float* partial, int splits, const float* bias, int T, int E, int top_k,
+                               int n_group, int topk_group, float route_scale, int norm, float* weights_out,
+                               int64_t* idx_out, int* err, cudaStream_t stream, const RouteVariant* variant) {
+  const RouteVariant rv = variant ? *variant : RouteVariant{};
+  const int used = splits;
   // warps per block: spread small batches over the SMs, pack large ones
   const int wpb = T >= 8 * 148 ? 8 : (T >= 4 * 148 ? 4 : (T >= 2 * 148 ? 2 : 1));
   dim3 g2((T + wpb - 1) / wpb);

@@ -143,7 +143,7 @@ def test_router_noalloc_validation_before_launch():
     assert st == C.MOSAIC_ERR_SHAPE
     st = lib.mosaic_router_noalloc(fake + 4, fake, None, 4, 512, 32, 4, 1, 1, 1.0, 1, fake, fake, None)
     assert st == C.MOSAIC_ERR_ALIGN
-    # T = 16384 tokens over 256 experts needs 16 MiB of partials + the error word
-    assert lib.mosaic_router_workspace_bytes(16384, 7168, 256) > C.MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
-    st = lib.mosaic_router_noalloc(fake, fake, None, 16384, 7168, 256, 8, 8, 4, 2.5, 1, fake, fake, None)
+    # T = 32768 tokens over 256 experts: 32 MiB of logits + the W parts of the tensor-core path
+    assert lib.mosaic_router_workspace_bytes(32768, 7168, 256) > C.MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
+    st = lib.mosaic_router_noalloc(fake, fake, None, 32768, 7168, 256, 8, 8, 4, 2.5, 1, fake, fake, None)
     assert st == C.MOSAIC_ERR_WORKSPACE

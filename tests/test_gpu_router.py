@@ -104,3 +104,12 @@ def test_router_ragged_expert_counts(ops, e):
     the scalar partial-sum path; all must match the oracle."""
     x, wt, bias = make_gate_case(24, 1024, e, seed=300 + e)
     _check(ops, x, wt, bias, 4, 1, 1, 1.0, max_ties=1)
+
+
+@pytest.mark.parametrize("t", [4736, 8192])
+def test_router_tensor_core_logits(ops, t):
+    """Batches that take one pass over K use the tensor-core logits (x . (hi + mid +
+    lo) with W split into three bf16 parts, fp32 accumulation): the same bar as the
+    FMA kernels, ids exact outside fp32 ties."""
+    x, wt, bias = make_gate_case(t, 7168, 256, seed=7000 + t)
+    _check(ops, x, wt, bias, 8, 8, 4, 2.5, max_ties=max(1, t // 32))

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 # (T, H, E, top_k, n_group, topk_group): decode and prefill V3 routing, and a
 # small ungrouped case whose split count differs.
-CASES = [(128, 7168, 256, 8, 8, 4), (2048, 7168, 256, 8, 8, 4), (5, 512, 32, 4, 1, 1)]
+CASES = [(128, 7168, 256, 8, 8, 4), (2048, 7168, 256, 8, 8, 4), (8192, 7168, 256, 8, 8, 4), (5, 512, 32, 4, 1, 1)]
 
 
 def _inputs(t, h, e, seed):
@@ -67,7 +67,7 @@ def test_noalloc_allocates_no_device_memory():
 def test_noalloc_rejects_oversize_without_launch():
     from mosaic_b200 import ops
 
-    t, h, e = 16384, 7168, 256
+    t, h, e = 32768, 7168, 256
     x = torch.zeros(t, h, dtype=torch.bfloat16, device="cuda")
     w = torch.zeros(e, h, device="cuda")
     wo = torch.empty(t, 8, device="cuda")
