@@ -84,15 +84,15 @@ int make_act_map(CUtensorMap* map, const uint8_t* q, int R_pad, int planes, int 
   return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
-// Router logits on the tensor cores (router_tc.cu) for batches that take one
-// pass over K: x bf16 [T][H] and the three bf16 parts of W [3E][H], both as
-// 2-D maps with 64-value (128-byte, swizzled) x 128-row boxes.
-bool router_tc_ok(int T, int H, int E, int sms) {
-  return router_large_batch(T, E, sms) && H % 64 == 0 && E % 16 == 0;
+// Router logits on the tensor cores (router_tc.cu) wherever the shape allows.
+// W is split into three bf16 parts once per call into the workspace, except
+// for the smallest batches, whose logits kernel splits it in shared memory.
+bool router_tc_parts(int T, int H, int E, int sms) {
+  return router_tc_applies(H, E) && !router_tc_convert(T, H, E, sms);
 }
 
 size_t router_parts_bytes(int T, int H, int E, int sms) {
-  return router_tc_ok(T, H, E, sms) ? up256(sizeof(uint16_t) * 3 * static_cast<size_t>(E) * H) : 0;
+  return router_tc_parts(T, H, E, sms) ? up256(sizeof(uint16_t) * 3 * static_cast<size_t>(E) * H) : 0;
 }
 
 int make_bf16_rows_map(CUtensorMap* map, const void* base, int rows, int K) {
@@ -108,22 +108,43 @@ int make_bf16_rows_map(CUtensorMap* map, const void* base, int rows, int K) {
   return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
-// Logits + top-k.  parts (router_parts_bytes, or null) selects the tensor-core
-// logits where they apply; the split-K FMA kernels otherwise.
+// W fp32 [E][H] as a 2-D map with unswizzled 64-value x 128-row boxes.
+int make_f32_rows_map(CUtensorMap* map, const float* base, int rows, int K) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return MOSAIC_ERR_CUDA;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 4};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+// Logits + top-k.  splits = router_splits(T, H, E, sms) sizes the partials;
+// parts (router_parts_bytes) is the large-batch split of W.
 int run_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k, int n_group,
                int topk_group, float route_scale, int norm, float* weights_out, int64_t* idx_out, float* partial,
                void* parts, int splits, int* err, cudaStream_t stream, const RouteVariant* rv) {
   const RouteVariant r = rv ? *rv : RouteVariant{};
   const int sms = sm_count();
-  if (parts && !(r.hash && !r.tid2eid) && sms > 0 && router_tc_ok(T, H, E, sms)) {
-    if (launch_router_split_w(w, E, H, parts, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (!(r.hash && !r.tid2eid) && sms > 0 && router_tc_applies(H, E)) {
+    const bool use_parts = router_tc_parts(T, H, E, sms);
+    if (use_parts && !parts) return MOSAIC_ERR_WORKSPACE;
     CUtensorMap tx, tw;
     int st = make_bf16_rows_map(&tx, x, T, H);
     if (st) return st;
-    st = make_bf16_rows_map(&tw, parts, 3 * E, H);
+    if (use_parts) {
+      if (launch_router_split_w(w, E, H, parts, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+      st = make_bf16_rows_map(&tw, parts, 3 * E, H);
+    } else {
+      st = make_f32_rows_map(&tw, w, E, H);
+    }
     if (st) return st;
-    if (launch_router_logits_tc(tx, tw, T, H, E, partial, err, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
-    return launch_router_topk(partial, 1, bias, T, E, top_k, n_group, topk_group, route_scale, norm, weights_out,
+    if (launch_router_logits_tc(tx, tw, !use_parts, T, H, E, splits, partial, err, stream) != cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+    return launch_router_topk(partial, splits, bias, T, E, top_k, n_group, topk_group, route_scale, norm, weights_out,
                               idx_out, err, stream, rv) == cudaSuccess
                ? MOSAIC_OK
                : MOSAIC_ERR_CUDA;

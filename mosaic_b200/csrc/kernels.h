@@ -66,16 +66,22 @@ struct RouteVariant {
   long long table_rows = 0;
   const int64_t* token_ids = nullptr;  // [T]; null = 0..T-1
 };
+// Split-K factor of the router logits (tensor-core split count where
+// router_tc_applies, else the FMA kernels'); the partials are [splits][T][E].
 int router_splits(int T, int H, int E, int num_sms);
-bool router_large_batch(int T, int E, int num_sms);  // one-pass logits (split factor 1)
 cudaError_t launch_router_topk(const float* partial, int splits, const float* bias, int T, int E, int top_k,
                                int n_group, int topk_group, float route_scale, int norm, float* weights_out,
                                int64_t* idx_out, int* err, cudaStream_t stream, const RouteVariant* variant);
-// tensor-core logits (router_tc.cu): W fp32 -> three bf16 parts, then logits [T][E] fp32
-size_t router_tc_smem_bytes();
+// tensor-core logits (router_tc.cu): x . (hi + mid + lo) with W split into three
+// bf16 parts, fp32 partials [splits][T][E].  convert = false: tmap_w maps the
+// parts [3E][H] (launch_router_split_w); true: tmap_w maps W fp32 [E][H] and
+// the kernel splits it in shared memory.
+bool router_tc_applies(int H, int E);
+int router_tc_splits(int T, int H, int E, int num_sms);
+bool router_tc_convert(int T, int H, int E, int num_sms);
 cudaError_t launch_router_split_w(const float* w, int E, int H, void* parts, int num_sms, cudaStream_t stream);
-cudaError_t launch_router_logits_tc(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, int T, int H, int E,
-                                    float* logits, int* err, cudaStream_t stream);
+cudaError_t launch_router_logits_tc(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, bool convert, int T, int H,
+                                    int E, int splits, float* out, int* err, cudaStream_t stream);
 cudaError_t launch_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
                           int n_group, int topk_group, float route_scale, int norm, float* weights_out,
                           int64_t* idx_out, float* partial, int splits, int* err, cudaStream_t stream,

@@ -189,33 +189,19 @@ __device__ __forceinline__ bool better(float v, int e, float v2, int e2) {
 // sqrt(softplus(l)) with torch's softplus (beta 1, threshold 20: l itself above 20).
 __device__ __forceinline__ float sqrt_softplus(float l) { return sqrtf(l > 20.f ? l : log1pf(expf(l))); }
 
+// Adds splits sp0, sp0 + step, ... of this lane's PER logits in ascending order.
 template <int PER>
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits,
-                                                          const float* __restrict__ bias, int T, int E, int top_k,
-                                                          int n_group, int topk_group, float route_scale,
-                                                          int norm, float* __restrict__ w_out,
-                                                          int64_t* __restrict__ idx_out, int* err, RouteVariant rv) {
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // one warp per token
-  if (t >= T) return;
-  float s[PER], sel[PER];
-  // logits: partials added in split order; a lane's PER experts are contiguous,
-  // so each split is PER/4 16-byte loads, and eight splits are in flight at once
-  float logit[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) logit[i] = 0.f;
-  // vector path: this lane's experts in range and every row start 16-byte aligned
-  const bool full = (lane + 1) * PER <= E && (PER % 4 == 0) && (E % 4 == 0);
-  const float* pp = partial + static_cast<size_t>(t) * E + lane * PER;
-  const size_t stride = static_cast<size_t>(T) * E;
+__device__ __forceinline__ void add_splits(const float* __restrict__ pp, size_t stride, int splits, int sp0, int step,
+                                           bool full, int lane, int E, float (&logit)[PER]) {
   if (full) {
-    int sp = 0;
-    for (; sp + 8 <= splits; sp += 8) {
+    int sp = sp0;
+    for (; sp + 7 * step < splits; sp += 8 * step) {
       float4 v[8][PER / 4 > 0 ? PER / 4 : 1];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
 #pragma unroll
-        for (int q = 0; q < PER / 4; ++q) v[u][q] = *reinterpret_cast<const float4*>(pp + (sp + u) * stride + 4 * q);
+        for (int q = 0; q < PER / 4; ++q)
+          v[u][q] = *reinterpret_cast<const float4*>(pp + static_cast<size_t>(sp + u * step) * stride + 4 * q);
 #pragma unroll
       for (int u = 0; u < 8; ++u)
 #pragma unroll
@@ -226,10 +212,10 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
           logit[4 * q + 3] += v[u][q].w;
         }
     }
-    for (; sp < splits; ++sp)
+    for (; sp < splits; sp += step)
 #pragma unroll
       for (int q = 0; q < PER / 4; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(pp + sp * stride + 4 * q);
+        const float4 v = *reinterpret_cast<const float4*>(pp + static_cast<size_t>(sp) * stride + 4 * q);
         logit[4 * q + 0] += v.x;
         logit[4 * q + 1] += v.y;
         logit[4 * q + 2] += v.z;
@@ -239,7 +225,48 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 #pragma unroll
     for (int i = 0; i < PER; ++i)
       if (lane * PER + i < E)
-        for (int sp = 0; sp < splits; ++sp) logit[i] += pp[sp * stride + i];
+        for (int sp = sp0; sp < splits; sp += step) logit[i] += pp[static_cast<size_t>(sp) * stride + i];
+  }
+}
+
+constexpr int kTopkWays = 8;  // warps adding one token's splits when there are many
+
+// One warp per token selects; with ways = kTopkWays a block of that many warps
+// serves one token, warp w adding splits w, w + ways, ... and warp 0 adding
+// the warps' sums in order w = 0, 1, ... (a fixed order: deterministic).
+template <int PER>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits, int ways,
+                                                          const float* __restrict__ bias, int T, int E, int top_k,
+                                                          int n_group, int topk_group, float route_scale,
+                                                          int norm, float* __restrict__ w_out,
+                                                          int64_t* __restrict__ idx_out, int* err, RouteVariant rv) {
+  __shared__ float red[kTopkWays][32 * 8];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t = ways > 1 ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + warp;  // one token per warp / block
+  if (t >= T) return;
+  float s[PER], sel[PER];
+  float logit[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) logit[i] = 0.f;
+  // vector path: this lane's experts in range and every row start 16-byte aligned
+  const bool full = (lane + 1) * PER <= E && (PER % 4 == 0) && (E % 4 == 0);
+  const float* pp = partial + static_cast<size_t>(t) * E + lane * PER;
+  const size_t stride = static_cast<size_t>(T) * E;
+  if (ways > 1) {
+    add_splits<PER>(pp, stride, splits, warp, ways, full, lane, E, logit);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) red[warp][lane * PER + i] = logit[i];
+    __syncthreads();
+    if (warp != 0) return;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      float v = 0.f;
+      for (int w = 0; w < ways; ++w) v += red[w][lane * PER + i];
+      logit[i] = v;
+    }
+  } else {
+    add_splits<PER>(pp, stride, splits, 0, 1, full, lane, E, logit);
   }
   if (rv.score_func == MOSAIC_SCORE_SOFTMAX) {
     // max-shifted exponentials times the reciprocal of their sum
@@ -441,11 +468,11 @@ __global__ void router_hash_salted_kernel(const int64_t* __restrict__ token_ids,
 
 }  // namespace
 
-bool router_large_batch(int T, int E, int num_sms) { return use_big_tiles(T, E, num_sms); }
-
-// Split-K factor of the logits kernel for small batches: ~2 CTAs per SM with
-// K ranges of at least 256 (more splits only add partials for the top-k pass).
+// Split-K factor of the logits: the tensor-core kernel's where it applies;
+// for the FMA kernels ~2 CTAs per SM with K ranges of at least 256 (more splits
+// only add partials for the top-k pass).
 int router_splits(int T, int H, int E, int num_sms) {
+  if (router_tc_applies(H, E)) return router_tc_splits(T, H, E, num_sms);
   if (use_big_tiles(T, E, num_sms)) return 1;
   const int tiles = ((T + kTileT - 1) / kTileT) * ((E + kTileE - 1) / kTileE);
   int s = (2 * num_sms + tiles - 1) / tiles;
@@ -484,12 +511,15 @@ cudaError_t launch_router_topk(const float* partial, int splits, const float* bi
                                int64_t* idx_out, int* err, cudaStream_t stream, const RouteVariant* variant) {
   const RouteVariant rv = variant ? *variant : RouteVariant{};
   const int used = splits;
-  // warps per block: spread small batches over the SMs, pack large ones
-  const int wpb = T >= 8 * 148 ? 8 : (T >= 4 * 148 ? 4 : (T >= 2 * 148 ? 2 : 1));
-  dim3 g2((T + wpb - 1) / wpb);
+  // many splits: a block of kTopkWays warps per token adds them; otherwise a
+  // warp per token, with the warps per block spreading small batches over the
+  // SMs and packing large ones
+  const int ways = splits >= 2 * kTopkWays ? kTopkWays : 1;
+  const int wpb = ways > 1 ? kTopkWays : (T >= 8 * 148 ? 8 : (T >= 4 * 148 ? 4 : (T >= 2 * 148 ? 2 : 1)));
+  dim3 g2(ways > 1 ? T : (T + wpb - 1) / wpb);
   const int per = (E + 31) / 32;
 #define MOSAIC_TOPK(P)                                                                                      \
-  router_topk_kernel<P><<<g2, 32 * wpb, 0, stream>>>(partial, used, bias, T, E, top_k, n_group, topk_group,     \
+  router_topk_kernel<P><<<g2, 32 * wpb, 0, stream>>>(partial, used, ways, bias, T, E, top_k, n_group, topk_group, \
                                                 route_scale, norm, weights_out, idx_out, err, rv)
   if (per <= 1)
     MOSAIC_TOPK(1);

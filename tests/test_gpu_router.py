@@ -108,8 +108,32 @@ def test_router_ragged_expert_counts(ops, e):
 
 @pytest.mark.parametrize("t", [4736, 8192])
 def test_router_tensor_core_logits(ops, t):
-    """Batches that take one pass over K use the tensor-core logits (x . (hi + mid +
-    lo) with W split into three bf16 parts, fp32 accumulation): the same bar as the
-    FMA kernels, ids exact outside fp32 ties."""
+    """Large batches use the tensor-core logits with W split into three bf16 parts
+    by a separate pass (x . (hi + mid + lo), fp32 accumulation; 2 and 1 K splits
+    here): the same bar as the FMA kernels, ids exact outside fp32 ties."""
     x, wt, bias = make_gate_case(t, 7168, 256, seed=7000 + t)
     _check(ops, x, wt, bias, 8, 8, 4, 2.5, max_ties=max(1, t // 32))
+
+
+@pytest.mark.parametrize("t", [1, 7, 129, 300, 1000, 2048])
+def test_router_tensor_core_split_k(ops, t):
+    """Smaller batches split K over up to 64 CTAs per 128 x 128 tile.  T <= 128
+    (at most two K slices per CTA) also split W inside the kernel (the swizzled
+    part tiles written by the converter warps); the top-k pass adds the splits
+    (8 warps per token from 16 splits up)."""
+    x, wt, bias = make_gate_case(t, 7168, 256, seed=7100 + t)
+    _check(ops, x, wt, bias, 8, 8, 4, 2.5, max_ties=max(1, t // 32))
+
+
+@pytest.mark.parametrize("e", [16, 48, 144, 208])
+def test_router_tensor_core_expert_tiles(ops, e):
+    """Expert counts that leave a partial 128-expert tile (N = E mod 128) or a
+    single small one; rows past E read as zeros."""
+    x, wt, bias = make_gate_case(200, 1024, e, seed=7200 + e)
+    _check(ops, x, wt, bias, 4, 1, 1, 1.0, max_ties=1)
+
+
+def test_router_fma_path_hidden_not_multiple_of_64(ops):
+    """H = 992 (a multiple of 32, not of 64) keeps the split-K FMA kernels."""
+    x, wt, bias = make_gate_case(128, 992, 256, seed=7300)
+    _check(ops, x, wt, bias, 8, 8, 4, 2.5, max_ties=4)
