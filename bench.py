@@ -61,6 +61,9 @@ def parse():
                    help="small case for ncu captures: no extras, no CPU baseline, 2 profiled stage runs")
     p.add_argument("--hc-only", action="store_true",
                    help="only the hyper-connection pre-mix + RMSNorm timing (prints its JSON; for ncu captures)")
+    p.add_argument("--router-only", action="store_true",
+                   help="only the router (V3: H 7168, E 256, groups 8/4, top 8) at T = 1, 128, 2048, 8192, "
+                        "or at --tokens when given (prints its JSON; for ncu captures)")
     return p.parse_args()
 
 
@@ -586,6 +589,51 @@ def hc_bench(hbm, steps=20, warmup=3):
     return res
 
 
+def router_bench(tokens, steps=20, warmup=3):
+    """mosaic_router alone at the V3 router dims: logits on the tensor cores
+    (split-K; the W split in-kernel up to T = 128) and the group-limited top 8.
+    Each timed call is a CUDA-graph replay of 10 router calls."""
+    import ctypes
+    from mosaic_b200 import _capi as C
+    from mosaic_b200.ops import _ptr
+
+    lib = C.lib()
+    h, e = 7168, 256
+    res = {}
+    for t in tokens:
+        g = torch.Generator(device="cuda").manual_seed(t)
+        x = torch.randn(t, h, generator=g, device="cuda").to(torch.bfloat16)
+        w = (torch.rand(e, h, generator=g, device="cuda") * 2 - 1) / h ** 0.5
+        b = torch.randn(e, generator=g, device="cuda") * 0.01
+        ws = torch.empty(lib.mosaic_router_workspace_bytes(t, h, e), dtype=torch.uint8, device="cuda")
+        wo = torch.empty(t, 8, device="cuda")
+        io = torch.empty(t, 8, dtype=torch.int64, device="cuda")
+
+        def call():
+            st = lib.mosaic_router(_ptr(x), _ptr(w), _ptr(b), t, h, e, 8, 8, 4, 2.5, 1, _ptr(wo), _ptr(io), _ptr(ws),
+                                   ws.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            C.check(st, "mosaic_router")
+
+        for _ in range(warmup):
+            call()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(10):
+                call()
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        us = e0.elapsed_time(e1) / (10 * steps) * 1e3
+        res[f"T{t}"] = {"us": us, "logit_tflops": 2 * t * e * h / (us * 1e-6) / 1e12}
+    return res
+
+
 def emit(out: dict) -> None:
     """Write the result line to the real stdout (see main)."""
     os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(out) + "\n").encode())
@@ -615,6 +663,10 @@ def main():
     hbm, bf16_tf, peak_src = peaks()
     if args.hc_only:
         emit({"hc_pre_norm": hc_bench(hbm)})
+        return
+    if args.router_only:
+        tokens = [args.tokens] if "--tokens" in sys.argv else [1, 128, 2048, 8192]
+        emit({"router": router_bench(tokens, steps=max(args.steps // 20, 5), warmup=max(args.warmup, 3))})
         return
     if dist_on:
         run_ep(args, rank, world, local, hbm, peak_src)
