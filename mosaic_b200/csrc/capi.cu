@@ -95,12 +95,12 @@ size_t router_parts_bytes(int T, int H, int E, int sms) {
   return router_tc_parts(T, H, E, sms) ? up256(sizeof(uint16_t) * 3 * static_cast<size_t>(E) * H) : 0;
 }
 
-int make_bf16_rows_map(CUtensorMap* map, const void* base, int rows, int K) {
+int make_bf16_rows_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows = 128) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return MOSAIC_ERR_CUDA;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -683,10 +683,24 @@ int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, in
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 
+// Workspace of mosaic_hc_pre_norm: [error word][partials][fn parts].
+struct HcWs {
+  int splits;
+  size_t partial, parts, total;
+};
+HcWs hc_ws(int T, int D, int hc, int sms) {
+  HcWs w{};
+  w.splits = hc_mix_tc_splits(T, hc * D, sms);
+  w.partial = 256;
+  w.parts = w.partial + up256(hc_partials_bytes(T, w.splits));
+  w.total = w.parts + up256(hc_fn_parts_bytes(hc * D));
+  return w;
+}
+
 size_t mosaic_hc_pre_norm_workspace_bytes(int32_t T, int32_t D, int32_t hc) {
   if (T < 1 || D < 128 || D % 128 || hc < 1 || hc > 4) return 0;
   const int sms = sm_count();
-  return hc_pre_norm_workspace_bytes(T, D, hc, sms > 0 ? sms : 148);
+  return hc_ws(T, D, hc, sms > 0 ? sms : 148).total;
 }
 
 int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const float* scale,
@@ -703,9 +717,24 @@ int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const 
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   if (hc_pre_norm_smem_bytes(hc_tokens_per_cta(T, sms), D) > 227u * 1024u) return MOSAIC_ERR_UNSUPPORTED;
-  if (workspace_bytes < hc_pre_norm_workspace_bytes(T, D, hc, sms)) return MOSAIC_ERR_WORKSPACE;
+  const HcWs w = hc_ws(T, D, hc, sms);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int KD = hc * D, nmix = (2 + hc) * hc;
+  CUtensorMap tx, tf;
+  int st = make_bf16_rows_map(&tx, x, T, KD);
+  if (st) return st;
+  st = make_bf16_rows_map(&tf, ws + w.parts, 3 * 32, KD, 32);
+  if (st) return st;
+  if (cudaMemsetAsync(ws, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (launch_hc_split_fn(fn, nmix, KD, ws + w.parts, sms, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  if (launch_hc_mix_tc(tx, tf, T, KD, nmix, w.splits, reinterpret_cast<float*>(ws + w.partial),
+                       reinterpret_cast<int*>(ws), s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
   HcParams p{};
-  p.partial = static_cast<float*>(workspace);
+  p.partial = reinterpret_cast<float*>(ws + w.partial);
+  p.splits = w.splits;
   p.x = x;
   p.fn = fn;
   p.base = base;
@@ -722,7 +751,7 @@ int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const 
   p.comb = comb;
   p.q = q;
   p.q_scale = q_scale;
-  cudaError_t e = launch_hc_pre_norm(p, sms, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_hc_pre_norm(p, sms, s);
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 

@@ -1,5 +1,5 @@
 // Hyper-connection pre-mix + RMSNorm (+ act_quant) in front of the MoE, and
-// the hyper-connection post-mix behind it (fp32 CUDA cores, HBM-bound).
+// the hyper-connection post-mix behind it.
 //
 // Reference behaviour:
 //   HyperConnections.pre    mosaicvm/model/layers.py:258-267, with the Sinkhorn
@@ -8,17 +8,14 @@
 //   act_quant_ref           mosaicvm/kernels/fp4_source.py:110-129
 //   HyperConnections.post   mosaicvm/model/layers.py:269-271
 //
-// Two launches.  hc_mix_kernel is a split-K fp32 GEMM of the residual copies
-// x_flat [T, hc*D] (bf16) against fn [(2+hc)*hc, hc*D]: a CTA takes 128 tokens
-// x one K range, stages 32-wide K slices of x (transposed) and fn in shared
-// memory, and each thread accumulates a 4-token x 4-mix tile (plus the tokens'
-// sums of squares), so fn is read once per 128 tokens instead of once per
-// token.  Each split writes its own partials; hc_pre_norm_kernel (TT tokens
-// per CTA) adds them in split order (deterministic), runs the Sinkhorn
-// normalisation of the 4x4 combination (one warp per token), forms the
-// pre-mix y = sum_m pre_m x_m (bf16) in shared memory, then applies the
-// RMSNorm (skipped without a norm weight) and writes the MoE input (and its
-// E4M3 act_quant).
+// Three launches.  hc_split_fn_kernel and hc_mix_tc_kernel (hc_tc.cu) make the
+// split-K partials of the mixing dot products x_flat . fn^T (x_flat [T, hc*D]
+// bf16, fn [(2+hc)*hc, hc*D]) and of the tokens' sums of squares on the tensor
+// cores.  hc_pre_norm_kernel (TT tokens per CTA) adds the partials in a fixed
+// order (deterministic), runs the Sinkhorn normalisation of the 4x4
+// combination (one warp per token), forms the pre-mix y = sum_m pre_m x_m
+// (bf16) in shared memory, then applies the RMSNorm (skipped without a norm
+// weight) and writes the MoE input (and its E4M3 act_quant).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -33,99 +30,6 @@ constexpr int kMaxMix = 24;               // (2 + hc) * hc at hc = 4
 constexpr int kRed = kMaxMix + 1;         // mixes + sum of squares per token
 
 __device__ __forceinline__ float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
-
-constexpr int kMixTok = 128;     // tokens per hc_mix CTA
-constexpr int kMixK = 32;        // K slice staged per step
-constexpr int kMixThreads = 192; // 32 token groups of 4 x 6 mix groups of 4
-
-__global__ void __launch_bounds__(kMixThreads) hc_mix_kernel(const __nv_bfloat16* __restrict__ x,
-                                                            const float* __restrict__ fn, int T, int KD, int nmix,
-                                                            int kchunk, float* __restrict__ partial) {
-  __shared__ __align__(16) float xs[kMixK][kMixTok];  // x slice, transposed: [k][token]
-  __shared__ __align__(16) float fs[kMixK][kMaxMix];  // fn slice, transposed: [k][mix]
-  const int tid = threadIdx.x;
-  const int t0 = blockIdx.x * kMixTok;
-  const int ks = blockIdx.y;
-  const int k_begin = ks * kchunk;
-  const int k_end = min(KD, k_begin + kchunk);
-  const int tg = tid / 6, mg = tid % 6;  // tokens 4tg..4tg+3, mixes 4mg..4mg+3
-  float acc[4][4], ssq[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    ssq[i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  }
-  // The next slice is loaded into registers while the current one is used, so
-  // the HBM latency of x overlaps the FMAs.  x: 128 tokens x 32 k = 512 vectors
-  // of 8 bf16 (threads < 128 take three, the others two); fn: 24 x 32 = 192 float4.
-  uint4 xr[3];
-  float4 fr;
-  const int fmix = tid >> 3, fseg = tid & 7;
-  auto load_slice = [&](int k0) {
-#pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      const int i = tid + u * kMixThreads;
-      xr[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (i < kMixTok * (kMixK / 8)) {
-        const int t = t0 + (i >> 2), k = k0 + (i & 3) * 8;
-        if (t < T && k < k_end) xr[u] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * KD + k));
-      }
-    }
-    const int k = k0 + fseg * 4;
-    fr = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (fmix < nmix && k < k_end) fr = __ldg(reinterpret_cast<const float4*>(fn + static_cast<size_t>(fmix) * KD + k));
-  };
-  if (k_begin < k_end) load_slice(k_begin);
-  for (int k0 = k_begin; k0 < k_end; k0 += kMixK) {
-#pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      const int i = tid + u * kMixThreads;
-      if (i < kMixTok * (kMixK / 8)) {
-        const int row = i >> 2, seg = i & 3;
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&xr[u]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(h2[j]);
-          xs[seg * 8 + 2 * j][row] = f.x;
-          xs[seg * 8 + 2 * j + 1][row] = f.y;
-        }
-      }
-    }
-    fs[fseg * 4 + 0][fmix] = fr.x;
-    fs[fseg * 4 + 1][fmix] = fr.y;
-    fs[fseg * 4 + 2][fmix] = fr.z;
-    fs[fseg * 4 + 3][fmix] = fr.w;
-    __syncthreads();
-    if (k0 + kMixK < k_end) load_slice(k0 + kMixK);
-#pragma unroll 8
-    for (int kk = 0; kk < kMixK; ++kk) {
-      const float4 xv = *reinterpret_cast<const float4*>(&xs[kk][4 * tg]);
-      const float4 fv = *reinterpret_cast<const float4*>(&fs[kk][4 * mg]);
-      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-      const float fa[4] = {fv.x, fv.y, fv.z, fv.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], fa[j], acc[i][j]);
-        ssq[i] = fmaf(xa[i], xa[i], ssq[i]);
-      }
-    }
-    __syncthreads();
-  }
-  float* out = partial + static_cast<size_t>(ks) * T * kRed;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + 4 * tg + i;
-    if (t >= T) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int mix = 4 * mg + j;
-      if (mix < nmix) out[static_cast<size_t>(t) * kRed + mix] = acc[i][j];
-    }
-    if (mg == 0) out[static_cast<size_t>(t) * kRed + kMaxMix] = ssq[i];
-  }
-}
 
 template <int TT>
 __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
@@ -329,33 +233,10 @@ int hc_tokens_per_cta(int T, int num_sms) {
   return 1;
 }
 
-// K split of hc_mix_kernel: K ranges of whole 32-wide slices.
-void hc_mix_split(int T, int KD, int num_sms, int* splits, int* kchunk) {
-  const int tiles = (T + kMixTok - 1) / kMixTok;
-  int s = (8 * num_sms + tiles - 1) / tiles;  // about eight CTAs per SM
-  const int smax = KD / (8 * kMixK);  // at least eight slices per split
-  if (s > smax) s = smax;
-  if (s < 1) s = 1;
-  int kc = (KD + s - 1) / s;
-  kc = (kc + kMixK - 1) / kMixK * kMixK;
-  *kchunk = kc;
-  *splits = (KD + kc - 1) / kc;
-}
-
-size_t hc_pre_norm_workspace_bytes(int T, int D, int hc, int num_sms) {
-  int splits = 0, kchunk = 0;
-  hc_mix_split(T, hc * D, num_sms, &splits, &kchunk);
-  return sizeof(float) * static_cast<size_t>(splits) * T * kRed;
-}
+size_t hc_partials_bytes(int T, int splits) { return sizeof(float) * static_cast<size_t>(splits) * T * kRed; }
 
 cudaError_t launch_hc_pre_norm(const HcParams& p_in, int num_sms, cudaStream_t stream) {
-  HcParams p = p_in;
-  const int KD = p.hc * p.D;
-  int kchunk = 0;
-  hc_mix_split(p.T, KD, num_sms, &p.splits, &kchunk);
-  dim3 gm((p.T + kMixTok - 1) / kMixTok, p.splits);
-  hc_mix_kernel<<<gm, kMixThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(p.x), p.fn, p.T, KD,
-                                                (2 + p.hc) * p.hc, kchunk, p.partial);
+  const HcParams& p = p_in;
   const int tt = hc_tokens_per_cta(p.T, num_sms);
   const int groups = (p.T + tt - 1) / tt;
   const int grid = groups < 16 * num_sms ? groups : 16 * num_sms;

@@ -102,12 +102,21 @@ struct HcParams {
   uint8_t* q;            // E4M3 [T][D] or null
   float* q_scale;        // [T][D/128]
   float* partial;        // workspace: [splits][T][25] mixing partials (+ sum of squares)
-  int splits;            // set by the launcher
+  int splits;
 };
 size_t hc_pre_norm_smem_bytes(int tt, int D);
-size_t hc_pre_norm_workspace_bytes(int T, int D, int hc, int num_sms);
+size_t hc_partials_bytes(int T, int splits);
 int hc_tokens_per_cta(int T, int num_sms);
+// the per-token kernel: adds p.splits partials, Sinkhorn, pre-mix, RMSNorm (+ act_quant)
 cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream);
+// mixing partials on the tensor cores (hc_tc.cu): fn [nmix][KD] -> parts bf16
+// [3][32][KD]; x_flat [T][KD] and the parts as 128-byte-swizzled 64-wide maps
+// (128-row and 32-row boxes)
+int hc_mix_tc_splits(int T, int KD, int num_sms);
+size_t hc_fn_parts_bytes(int KD);
+cudaError_t launch_hc_split_fn(const float* fn, int nmix, int KD, void* parts, int num_sms, cudaStream_t stream);
+cudaError_t launch_hc_mix_tc(const CUtensorMap& tmap_x, const CUtensorMap& tmap_f, int T, int KD, int nmix,
+                             int splits, float* partial, int* err, cudaStream_t stream);
 cudaError_t launch_hc_post(const void* y, const void* residual, const float* post, const float* comb, int T, int D,
                            int hc, void* out, int num_sms, cudaStream_t stream);
 
