@@ -54,77 +54,83 @@ __device__ __forceinline__ uint32_t gather_word(int e) {
   return w;
 }
 
-// grid (T, ceil(H / 1024)), 128 threads: each warp quantises 256 values of one token
-// and writes them to every packed row of the token; the scale words go into the
-// row's token-tile chunk (word (n%32)*4 + n/32 of chunk [tile][kt]; the lo plane
-// of a bf16 tile sits at rows rpad + n of the same chunk).
-__device__ __forceinline__ void quant_token_row(const __nv_bfloat16* __restrict__ x, int t, int H, int ldx, int k,
-                                                const int* __restrict__ row_of, int shared_base, int hilo, int R_pad,
-                                                const int* __restrict__ row_tile, const int* __restrict__ row_pos,
-                                                uint8_t* __restrict__ xq, uint32_t* __restrict__ sft) {
-  const int lane = threadIdx.x & 31;
-  const int k0 = blockIdx.y * 1024 + (threadIdx.x >> 5) * 256 + lane * 8;
-  const bool valid = k0 < H;
-  float v[8];
-  if (valid) {
-    load8_bf16(x + static_cast<size_t>(t) * ldx + k0, v);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
-  }
-  const int nrows = k + (shared_base >= 0 ? 1 : 0);
-  const int KT = H / 128;
-  const int kt = k0 / 128;
-  if (!hilo) {
-    uint8_t q[8];
-    const int e = quant_block128(v, q);
-    if (!valid) return;
-    const uint2 pq = pack8(q);
-    const uint32_t word = (static_cast<uint32_t>(e + 127) & 0xFFu) * 0x01010101u;
-    for (int s = 0; s < nrows; ++s) {
-      const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
-      if (r < 0) continue;
-      *reinterpret_cast<uint2*>(xq + (static_cast<size_t>(kt) * R_pad + r) * 128 + (k0 & 127)) = pq;
-      if ((lane & 15) == 0) {
-        const int n = row_pos[r] & 0xFF;
-        sft[(static_cast<size_t>(row_tile[r]) * KT + kt) * 128 + (n & 31) * 4 + (n >> 5)] = word;
-      }
-    }
-  } else {
-    uint8_t hi[8], lo[8];
-    int eh, el;
-    split_block32(v, hi, lo, eh, el);
-    const uint32_t wh = gather_word(eh);
-    const uint32_t wl = gather_word(el);
-    if (!valid) return;
-    const uint2 ph = pack8(hi), pl = pack8(lo);
-    for (int s = 0; s < nrows; ++s) {
-      const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
-      if (r < 0) continue;
-      *reinterpret_cast<uint2*>(xq + ((static_cast<size_t>(kt) * 2 + 0) * R_pad + r) * 128 + (k0 & 127)) = ph;
-      *reinterpret_cast<uint2*>(xq + ((static_cast<size_t>(kt) * 2 + 1) * R_pad + r) * 128 + (k0 & 127)) = pl;
-      if ((lane & 15) == 0) {
-        const int pos = row_pos[r];
-        const int n = pos & 0xFF, rp = pos >> 8, n2 = rp + n;
-        uint32_t* c = sft + (static_cast<size_t>(row_tile[r]) * KT + kt) * 128;
-        c[(n & 31) * 4 + (n >> 5)] = wh;
-        c[(n2 & 31) * 4 + (n2 >> 5)] = wl;
-      }
-    }
-  }
-}
+// A block per token row (grid-stride over rows; with T_dev only the first
+// *T_dev rows exist, the grid being sized for T); small batches give a row
+// gridDim.y blocks, each taking every gridDim.y-th group of 8 chunks.  The row's destinations --
+// its k packed rows (row_of) and the shared expert's row -- and their tile
+// positions are looked up once into shared memory; each warp then quantises
+// 256-value chunks of the row (H % 256 == 0) and writes them to every
+// destination row: K-tile-major planes [kt][plane][R_pad][128 B], the scale
+// words into the row's token-tile chunk (word (n % 32) * 4 + n / 32 of chunk
+// [tile][kt], n = the row's position in its tile; the lo plane of a bf16 tile
+// sits at positions rpad + n of the same chunk).
+constexpr int kRqThreads = 256;
+constexpr int kRqMaxRows = 16;  // top_k (<= 8) + the shared expert's row
 
-// grid-stride over token rows: blockIdx.y picks the 1024-value slab of H; with
-// T_dev only the first *T_dev rows exist (the grid is sized for T)
-__global__ void __launch_bounds__(128) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T,
-                                                         const int* __restrict__ T_dev, int H, int ldx, int k,
-                                                         const int* __restrict__ row_of, int shared_base, int hilo,
-                                                         int R_pad, const int* __restrict__ row_tile,
-                                                         const int* __restrict__ row_pos, uint8_t* __restrict__ xq,
-                                                         uint32_t* __restrict__ sft) {
+__global__ void __launch_bounds__(kRqThreads) rows_quant_kernel(const __nv_bfloat16* __restrict__ x, int T,
+                                                                const int* __restrict__ T_dev, int H, int ldx, int k,
+                                                                const int* __restrict__ row_of, int shared_base,
+                                                                int hilo, int R_pad, const int* __restrict__ row_tile,
+                                                                const int* __restrict__ row_pos,
+                                                                uint8_t* __restrict__ xq, uint32_t* __restrict__ sft) {
+  __shared__ int s_row[kRqMaxRows], s_pos[kRqMaxRows], s_tile[kRqMaxRows];
   const int rows = T_dev ? min(*T_dev, T) : T;
-  for (int t = blockIdx.x; t < rows; t += gridDim.x)
-    quant_token_row(x, t, H, ldx, k, row_of, shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
+  const int nrows = k + (shared_base >= 0 ? 1 : 0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int KT = H / 128;
+  for (int t = blockIdx.x; t < rows; t += gridDim.x) {
+    if (threadIdx.x < nrows) {
+      const int s = threadIdx.x;
+      const int r = (s < k) ? row_of[static_cast<size_t>(t) * k + s] : shared_base + t;
+      s_row[s] = r;
+      s_pos[s] = r >= 0 ? row_pos[r] : 0;
+      s_tile[s] = r >= 0 ? row_tile[r] : 0;
+    }
+    __syncthreads();
+    // small batches spread a row over gridDim.y blocks
+    for (int c = blockIdx.y * (kRqThreads / 32) + warp; c < H / 256; c += gridDim.y * (kRqThreads / 32)) {
+      const int k0 = c * 256 + lane * 8;
+      const int kt = k0 / 128;
+      float v[8];
+      load8_bf16(x + static_cast<size_t>(t) * ldx + k0, v);
+      if (!hilo) {
+        uint8_t q[8];
+        const int e = quant_block128(v, q);
+        const uint2 pq = pack8(q);
+        const uint32_t word = (static_cast<uint32_t>(e + 127) & 0xFFu) * 0x01010101u;
+        for (int s = 0; s < nrows; ++s) {
+          const int r = s_row[s];
+          if (r < 0) continue;
+          *reinterpret_cast<uint2*>(xq + (static_cast<size_t>(kt) * R_pad + r) * 128 + (k0 & 127)) = pq;
+          if ((lane & 15) == 0) {
+            const int n = s_pos[s] & 0xFF;
+            sft[(static_cast<size_t>(s_tile[s]) * KT + kt) * 128 + (n & 31) * 4 + (n >> 5)] = word;
+          }
+        }
+      } else {
+        uint8_t hi[8], lo[8];
+        int eh, el;
+        split_block32(v, hi, lo, eh, el);
+        const uint32_t wh = gather_word(eh);
+        const uint32_t wl = gather_word(el);
+        const uint2 ph = pack8(hi), pl = pack8(lo);
+        for (int s = 0; s < nrows; ++s) {
+          const int r = s_row[s];
+          if (r < 0) continue;
+          *reinterpret_cast<uint2*>(xq + ((static_cast<size_t>(kt) * 2 + 0) * R_pad + r) * 128 + (k0 & 127)) = ph;
+          *reinterpret_cast<uint2*>(xq + ((static_cast<size_t>(kt) * 2 + 1) * R_pad + r) * 128 + (k0 & 127)) = pl;
+          if ((lane & 15) == 0) {
+            const int pos = s_pos[s];
+            const int n = pos & 0xFF, rp = pos >> 8, n2 = rp + n;
+            uint32_t* cw = sft + (static_cast<size_t>(s_tile[s]) * KT + kt) * 128;
+            cw[(n & 31) * 4 + (n >> 5)] = wh;
+            cw[(n2 & 31) * 4 + (n2 >> 5)] = wl;
+          }
+        }
+      }
+    }
+    __syncthreads();  // s_row / s_pos / s_tile are rewritten for the next row
+  }
 }
 
 // act_quant_ref: grid (M, ceil(K / 1024)), 128 threads.
@@ -270,10 +276,16 @@ cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int
                               int shared_base,
                               int hilo, int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq,
                               uint32_t* sft, cudaStream_t stream) {
-  // a block per token row, or a bounded grid looping over a device-side count
-  dim3 grid(T_dev ? (T < 1184 ? T : 1184) : T, (H + 1023) / 1024);
-  rows_quant_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k, row_of,
-                                               shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
+  if (H % 256 || k + (shared_base >= 0 ? 1 : 0) > kRqMaxRows) return cudaErrorInvalidValue;
+  // a block per row, at most 8 per SM of 148 at once (the rest loop); below
+  // that, up to one warp per 256-value chunk of a row
+  const int gx = T < 1184 ? T : 1184;
+  const int warps_per_row = kRqThreads / 32, chunks = H / 256;
+  int gy = (1184 + gx - 1) / gx;
+  const int gy_max = (chunks + warps_per_row - 1) / warps_per_row;
+  if (gy > gy_max) gy = gy_max;
+  rows_quant_kernel<<<dim3(gx, gy), kRqThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k,
+                                                      row_of, shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
   return cudaGetLastError();
 }
 
