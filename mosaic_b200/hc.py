@@ -50,6 +50,7 @@ class HyperConnections(nn.Module):
         self.fn = nn.Parameter(torch.empty(mix, hc_mult * hidden_size), requires_grad=False)
         self.base = nn.Parameter(torch.zeros(mix), requires_grad=False)
         self.scale = nn.Parameter(torch.ones(3), requires_grad=False)
+        self.last_workspace = None  # the last fused call's workspace (error word at byte 0)
         nn.init.normal_(self.fn, std=0.01)
 
     def pre(self, x):
@@ -101,6 +102,7 @@ def _pre_norm(hc_mod: HyperConnections, norm: RMSNorm | None, x, *, quant: bool)
                                 hc_mod.iters, float(hc_mod.eps), float(hc_mod.norm_eps), ops._ptr(y), ops._ptr(post),
                                 ops._ptr(comb), ops._ptr(q), ops._ptr(qs), ops._ptr(ws), ws.numel(), ops._stream())
     C.check(st, "mosaic_hc_pre_norm")
+    hc_mod.last_workspace = ws  # its error word: ops.read_error(hc.last_workspace)
     out = (y.view(*lead, d), post.view(*lead, hc), comb.view(*lead, hc, hc))
     if quant:
         out += (q.view(torch.float8_e4m3fn).view(*lead, d), qs.view(*lead, d // 128))

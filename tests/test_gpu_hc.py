@@ -62,6 +62,9 @@ def test_hc_matches_reference_golden(name):
     np.testing.assert_allclose(comb.cpu().numpy(), gold[name + "_comb"], rtol=1e-4, atol=1e-6)
     yn, post2, comb2, q, qs = ffn_pre_norm(xg, hc, norm, quant=True)
     torch.cuda.synchronize()
+    from mosaic_b200 import ops
+
+    assert ops.read_error(hc.last_workspace) == 0
     assert torch.equal(post2, post) and torch.equal(comb2, comb)
     _bf16_close(yn.float().cpu(), gold[name + "_y_norm"], "y_norm")
     q_ref, s_ref = act_quant_ref(yn.float().cpu().numpy().reshape(-1, d))
@@ -84,6 +87,9 @@ def test_hc_pre_norm_v3_dims(t):
     hc, norm = _modules(hcm, d, 20, fn, base, scale, norm_w)
     yn, post, comb = ffn_pre_norm(x.cuda(), hc, norm)
     torch.cuda.synchronize()
+    from mosaic_b200 import ops
+
+    assert ops.read_error(hc.last_workspace) == 0  # no pipeline wait of the mixing kernel ran out
     y_pre, post_r, comb_r = hc_pre(x, fn, base, scale, iters=20, eps=1e-6, norm_eps=1e-6)
     ref = rms_norm(y_pre, norm_w, 1e-6)
     np.testing.assert_allclose(post.cpu().numpy(), post_r.numpy(), rtol=1e-4, atol=1e-6)
