@@ -147,3 +147,33 @@ def test_router_noalloc_validation_before_launch():
     assert lib.mosaic_router_workspace_bytes(32768, 7168, 256) > C.MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
     st = lib.mosaic_router_noalloc(fake, fake, None, 32768, 7168, 256, 8, 8, 4, 2.5, 1, fake, fake, None)
     assert st == C.MOSAIC_ERR_WORKSPACE
+
+
+def test_router_workspace_follows_the_split_plan():
+    """Without a device the plan assumes 148 SMs.  V3 router (H 7168, E 256):
+    the tensor-core logits take one wave of 128 x 128 tiles, up to 64 K splits
+    (the partials are [splits][T][E] fp32 after a 256-byte error block); from
+    T = 129 on W's three bf16 parts (3·E·H·2 B) follow them."""
+    lib = C.lib()
+    h, e = 7168, 256
+    up = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    parts = up(3 * e * h * 2)
+    assert lib.mosaic_router_workspace_bytes(1, h, e) == 256 + up(64 * 1 * e * 4)
+    assert lib.mosaic_router_workspace_bytes(128, h, e) == 256 + up(64 * 128 * e * 4)
+    assert lib.mosaic_router_workspace_bytes(2048, h, e) == 256 + up(4 * 2048 * e * 4) + parts
+    assert lib.mosaic_router_workspace_bytes(8192, h, e) == 256 + up(1 * 8192 * e * 4) + parts
+    # H % 64 != 0 keeps the FMA kernels: no parts
+    assert lib.mosaic_router_workspace_bytes(128, 992, e) % 256 == 0
+    assert lib.mosaic_router_workspace_bytes(128, 992, e) < 256 + up(64 * 128 * e * 4)
+
+
+def test_hc_workspace_follows_the_split_plan():
+    """Error block, split-K mixing partials [splits][T][25] (one wave of 128-token
+    tiles over 148 SMs, at most one 64-wide slice per split), fn's parts [3][32][hc·D]."""
+    lib = C.lib()
+    d, hc = 7168, 4
+    up = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    parts = up(3 * 32 * hc * d * 2)
+    assert lib.mosaic_hc_pre_norm_workspace_bytes(128, d, hc) == 256 + up(148 * 128 * 25 * 4) + parts
+    assert lib.mosaic_hc_pre_norm_workspace_bytes(8192, d, hc) == 256 + up(2 * 8192 * 25 * 4) + parts
+    assert lib.mosaic_hc_pre_norm_workspace_bytes(1, 128, 1) == 256 + up(2 * 1 * 25 * 4) + up(3 * 32 * 128 * 2)
