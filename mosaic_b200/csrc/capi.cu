@@ -123,7 +123,8 @@ int make_f32_rows_map(CUtensorMap* map, const float* base, int rows, int K) {
 }
 
 // Logits + top-k.  splits = router_splits(T, H, E, sms) sizes the partials;
-// parts (router_parts_bytes) is the large-batch split of W.
+// parts (router_parts_bytes) holds W's bf16 split when the logits kernel does
+// not split W itself.
 int run_router(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k, int n_group,
                int topk_group, float route_scale, int norm, float* weights_out, int64_t* idx_out, float* partial,
                void* parts, int splits, int* err, cudaStream_t stream, const RouteVariant* rv) {

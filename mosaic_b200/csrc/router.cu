@@ -1,4 +1,5 @@
-// Group-limited top-k router and hash router (fp32 CUDA cores).
+// Group-limited top-k router and hash router: the top-k pass, and fp32 FMA
+// logits for shapes the tensor-core kernel does not take.
 //
 // Reference behaviour: mosaicvm/model/layers.py:127-150 (Router.forward) and
 // the vendored Gate, .mosaicvm/source/inference_model.py:569-589, whose three
@@ -10,12 +11,14 @@
 // the ids from a token-id table instead of the top-k, and without a table uses
 // the salted multiplicative hash of layers.py:180-184.
 //
-// Kernel 1 computes fp32 logits x . W^T with a deterministic split-K: every
-// split sums its K range sequentially with FMAs and writes its own partial;
-// kernel 2 (one warp per token) adds the partials in split order, so a
-// logit never depends on scheduling.  Kernel 2 then applies the score function
-// + bias, the group limit and the top-k (or the table lookup), and normalises
-// the unbiased weights.
+// The logits x . W^T come from the tensor cores (router_tc.cu) wherever
+// H % 64 == 0 and E % 16 == 0, else from the FMA kernels here; both write
+// deterministic split-K partials [splits][T][E] (every split sums its K
+// range in a fixed order).  router_topk_kernel (one warp per token, or 8 per
+// token when there are many splits) adds the partials in a fixed order, so a
+// logit never depends on scheduling, then applies the score function + bias,
+// the group limit and the top-k (or the table lookup), and normalises the
+// unbiased weights.
 #include "common.cuh"
 #include "kernels.h"
 
