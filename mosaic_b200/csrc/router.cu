@@ -287,10 +287,12 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     const float inv = 1.0f / warp_sum(sum);
 #pragma unroll
     for (int i = 0; i < PER; ++i) s[i] *= inv;
+  } else if (rv.score_func == MOSAIC_SCORE_SQRTSOFTPLUS) {  // a warp-uniform branch around each loop
+#pragma unroll
+    for (int i = 0; i < PER; ++i) s[i] = sqrt_softplus(logit[i]);
   } else {
 #pragma unroll
-    for (int i = 0; i < PER; ++i)
-      s[i] = rv.score_func == MOSAIC_SCORE_SQRTSOFTPLUS ? sqrt_softplus(logit[i]) : 1.0f / (1.0f + expf(-logit[i]));
+    for (int i = 0; i < PER; ++i) s[i] = 1.0f / (1.0f + expf(-logit[i]));
   }
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
