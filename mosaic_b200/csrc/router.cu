@@ -190,6 +190,13 @@ __device__ __forceinline__ bool better(float v, int e, float v2, int e2) {
 }
 
 // sqrt(softplus(l)) with torch's softplus (beta 1, threshold 20: l itself above 20).
+// Order-preserving unsigned key of a score (larger score, larger key); NaN
+// maps to 0, below every number, so it is never selected.
+__device__ __forceinline__ unsigned sel_key(float v) {
+  const unsigned u = __float_as_uint(v);
+  return isnan(v) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+}
+
 __device__ __forceinline__ float sqrt_softplus(float l) { return sqrtf(l > 20.f ? l : log1pf(expf(l))); }
 
 // Adds splits sp0, sp0 + step, ... of this lane's PER logits in ascending order.
@@ -392,26 +399,20 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
         be = 0;
       }
     } else {
-      float bv = -INFINITY;
-      be = 0x7FFFFFFF;
+      // the largest biased score (an order-preserving key; NaN never wins), then
+      // the lowest expert id holding it: two warp reductions
+      unsigned bk = 0u;
+      int bi = -1;
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
-        const int e = lane * PER + i;
-        if (e < E && better(sel[i], e, bv, be)) {
-          bv = sel[i];
-          be = e;
+        if (lane * PER + i < E && sel_key(sel[i]) > bk) {  // strict: the lane's lowest id among equals
+          bk = sel_key(sel[i]);
+          bi = i;
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-        const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-        if (better(ov, oe, bv, be)) {
-          bv = ov;
-          be = oe;
-        }
-      }
-      if (be >= E || bv == -INFINITY) {
+      const unsigned mk = __reduce_max_sync(0xFFFFFFFFu, bk);
+      be = __reduce_min_sync(0xFFFFFFFFu, (bi >= 0 && bk == mk) ? lane * PER + bi : 0x7FFFFFFF);
+      if (be >= E || mk <= sel_key(-INFINITY)) {
         if (lane == 0) set_error(err, MOSAIC_ERR_RANGE);
         be = 0;
       }
