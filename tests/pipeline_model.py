@@ -1,7 +1,8 @@
-"""Discrete-event model of the barrier protocol of ``hc_mix_tc_kernel``
-(``mosaic_b200/csrc/hc_tc.cu``), for CPU tests of its ordering.
+"""Discrete-event models of the mbarrier protocols of the tensor-core kernels,
+for CPU tests of their ordering: ``run`` models ``hc_mix_tc_kernel``
+(``mosaic_b200/csrc/hc_tc.cu``), ``run_gemm`` the grouped GEMM.
 
-The model follows the kernel's roles and waits one for one:
+``run`` follows the mixing kernel's roles and waits one for one:
 
 - the producer waits ``empty[s]`` (parity of the previous use) and issues a
   stage fill that lands after a random delay (TMA complete_tx on ``full[s]``);
@@ -119,6 +120,167 @@ def run(stages: int, issuers: int, nit: int, seed: int, warps: int = 4, max_step
             yield
 
     alive = [producer()] + [issuer(i) for i in range(issuers)] + [summing_warp(w) for w in range(warps)]
+    steps = 0
+    while alive or events:
+        steps += 1
+        if steps > max_steps:
+            errors.append(("no progress",))
+            break
+        clock[0] += 1
+        for e in sorted(e for e in events if e[0] <= clock[0]):
+            events.remove(e)
+            e[2]()
+        rnd.shuffle(alive)
+        for a in list(alive):
+            if rnd.random() < 0.5:
+                continue
+            try:
+                next(a)
+            except StopIteration:
+                alive.remove(a)
+    return errors
+
+
+def run_gemm(stages: int, parities: int, nbuf: int, copier: bool, n_items: int, kt: int, seed: int,
+             observe_all: bool = True, max_steps: int = 400_000) -> list:
+    """The barrier protocol of ``moe_gemm_kernel`` (``mosaic_b200/csrc/gemm_bs.cu``).
+
+    - Two producers (weights, activations + scale chunks) arm ``full[s]`` (count
+      2); their copies land after random delays.
+    - With ``copier`` one warp waits ``full[s]`` for every fill, copies the
+      stage's scale chunks into TMEM slot s and commits ``sf_ready[s]``; the
+      issuers then wait ``sf_ready[s]`` instead of ``full[s]``.
+    - 2P issuers: issuer i takes the stages with kt % P == i // 2 (both blocks
+      of a pair).  With ``observe_all`` (the kernel) it also waits on every
+      other stage and arrives on its ``empty`` (count 2P).  Without it, an
+      issuer skips the other parities' stages and ``empty`` counts only the
+      two consumers (an earlier scheme of the kernel).
+    - Per item an issuer waits its accumulator buffer's ``acc_empty``, issues,
+      and commits ``acc_full`` (count 2P) after its last stage; a commit
+      arrives when the issuer's MMAs so far have completed (in issue order).
+    - The epilogue (128 threads) waits ``acc_full``, reads the buffer and
+      arrives on ``acc_empty``.
+
+    Checks: the stage's data and TMEM scale slot belong to the fill an MMA is
+    for, at issue and at completion; an item's MMAs start on a buffer only
+    after the epilogue released the buffer's previous item; the epilogue reads
+    a buffer only when every chain of its item is complete and no later item
+    has started on it.
+    """
+    rnd = random.Random(seed)
+    P = parities
+    n_iss = 2 * P
+    full = [Barrier(2) for _ in range(stages)]
+    empty = [Barrier(n_iss if observe_all else 2) for _ in range(stages)]
+    sf_ready = [Barrier(1) for _ in range(stages)]
+    acc_full = [Barrier(n_iss) for _ in range(nbuf)]
+    acc_empty = [Barrier(128) for _ in range(nbuf)]
+    sf_slot: list = [None] * stages  # fill whose scales sit in TMEM slot s
+    owner: list = [None] * nbuf      # latest item that issued into buffer b
+    done: dict = {}                  # item -> issuers whose chains completed
+    released = [-1] * nbuf           # latest item the epilogue released from buffer b
+    events: list = []
+    clock = [0]
+    errors: list = []
+    last_done = [0] * n_iss          # completion time of each issuer's latest MMA
+
+    def at(time, fn):
+        events.append((time, rnd.random(), fn))
+
+    def holds(s, it):  # full[s] has completed the phase of fill it and no later one
+        return full[s].phase == it // stages + 1
+
+    def producer():
+        it = 0
+        for _ in range(n_items * kt):
+            s = it % stages
+            while not empty[s].passed(((it // stages) & 1) ^ 1):
+                yield
+            full[s].expect_tx(1)
+            at(clock[0] + rnd.randint(1, 40), lambda s=s: full[s].complete_tx(1))
+            it += 1
+            yield
+
+    def copier_warp():
+        for it in range(n_items * kt):
+            s = it % stages
+            while not full[s].passed((it // stages) & 1):
+                yield
+            if not holds(s, it):
+                errors.append(("copier reads another fill", it, s))
+
+            def copied(s=s, it=it):
+                sf_slot[s] = it
+                sf_ready[s].arrive()
+
+            at(clock[0] + rnd.randint(1, 10), copied)
+            yield
+
+    def issuer(i):
+        ip = i >> 1
+        it = 0
+        for li in range(n_items):
+            b = li % nbuf
+            while not acc_empty[b].passed(((li // nbuf) & 1) ^ 1):
+                yield
+            for k in range(kt):
+                s = it % stages
+                mine = (k % P) == ip
+                if not observe_all and not mine:
+                    it += 1
+                    continue
+                bar = sf_ready[s] if copier else full[s]
+                while not bar.passed((it // stages) & 1):
+                    yield
+                if not mine:
+                    empty[s].arrive()
+                    it += 1
+                    yield
+                    continue
+                if not holds(s, it):
+                    errors.append(("MMA issued on another fill", i, it, s))
+                if copier and sf_slot[s] != it:
+                    errors.append(("MMA issued with another fill's scales", i, it, s, sf_slot[s]))
+                if li >= nbuf and released[b] < li - nbuf:
+                    errors.append(("accumulator written before the epilogue released it", i, li, b))
+                owner[b] = li if owner[b] is None else max(owner[b], li)
+                last_done[i] = max(clock[0], last_done[i]) + rnd.randint(1, 25)
+
+                def complete(s=s, it=it, i=i):
+                    if not holds(s, it):
+                        errors.append(("stage refilled under an MMA", i, it, s))
+                    if copier and sf_slot[s] != it:
+                        errors.append(("scale slot rewritten under an MMA", i, it, s))
+                    empty[s].arrive()
+
+                at(last_done[i], complete)
+                it += 1
+                yield
+
+            def chains_done(b=b, li=li, i=i):
+                done.setdefault(li, set()).add(i)
+                acc_full[b].arrive()
+
+            at(max(clock[0], last_done[i]) + 1, chains_done)
+            yield
+
+    def epilogue():
+        for li in range(n_items):
+            b = li % nbuf
+            while not acc_full[b].passed((li // nbuf) & 1):
+                yield
+            if len(done.get(li, ())) != n_iss or owner[b] != li:
+                errors.append(("epilogue reads an unfinished accumulator", li, b, owner[b]))
+            yield  # reading takes time
+            if owner[b] != li:
+                errors.append(("accumulator overwritten during the epilogue", li, b, owner[b]))
+            released[b] = li
+            acc_empty[b].arrive(128)
+            yield
+
+    alive = [producer(), producer()] + [issuer(i) for i in range(n_iss)] + [epilogue()]
+    if copier:
+        alive.append(copier_warp())
     steps = 0
     while alive or events:
         steps += 1
