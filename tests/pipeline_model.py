@@ -300,3 +300,141 @@ def run_gemm(stages: int, parities: int, nbuf: int, copier: bool, n_items: int, 
             except StopIteration:
                 alive.remove(a)
     return errors
+
+
+def run_router(stages: int, nit: int, convert: bool, seed: int, wait_conv: bool = True,
+               max_steps: int = 200_000) -> list:
+    """The barrier protocol of ``router_logits_tc_kernel`` (``mosaic_b200/csrc/router_tc.cu``).
+
+    - The producer waits ``empty[s]`` and fills stage s (x and W, as parts or
+      as the fp32 tile), landing after a random delay.
+    - With ``convert`` warps 2-5 wait ``full[s]`` for every slice, write the
+      stage's part tiles from its fp32 tile and arrive on ``conv[s]`` (32 each).
+    - One issuer waits ``full[s]`` (and ``conv[s]``) and the slice's
+      accumulator buffer (j % 2), issues, and its commits arrive on ``empty[s]``
+      and ``acc_full`` when the MMAs complete.
+    - Warps 2-5 add slice j - 1's buffer after converting slice j (and the last
+      one after the loop), then arrive on ``acc_empty`` (128).
+    Checks: the converters read the fp32 tile of their fill and write parts
+    the MMAs of the stage's previous fill no longer read; every MMA sees the
+    x tile and parts of its fill from issue to completion; a buffer is added
+    only after its slice's MMAs and rewritten only after it was added.
+    ``wait_conv=False`` drops the issuer's wait on ``conv`` (a planted fault).
+    """
+    rnd = random.Random(seed)
+    full = [Barrier(1) for _ in range(stages)]
+    empty = [Barrier(1) for _ in range(stages)]
+    conv = [Barrier(128) for _ in range(stages)]
+    acc_full = [Barrier(1) for _ in range(2)]
+    acc_empty = [Barrier(128) for _ in range(2)]
+    parts: list = [None] * stages    # fill whose parts the stage holds
+    reading: list = [set() for _ in range(stages)]  # fills whose MMAs are in flight on stage s
+    acc: list = [None] * 2           # slice whose MMAs wrote buffer b
+    acc_complete: list = [None] * 2  # slice whose MMAs into buffer b completed
+    added = [-1]                     # slices added so far (in order)
+    events: list = []
+    clock = [0]
+    errors: list = []
+    last = [0]
+
+    def at(time, fn):
+        events.append((time, rnd.random(), fn))
+
+    def holds(s, j):
+        return full[s].phase == j // stages + 1
+
+    def producer():
+        for j in range(nit):
+            s = j % stages
+            while not empty[s].passed(((j // stages) & 1) ^ 1):
+                yield
+            full[s].expect_tx(1)
+            if not convert:
+                def land(s=s, j=j):
+                    parts[s] = j
+                    full[s].complete_tx(1)
+            else:
+                def land(s=s):
+                    full[s].complete_tx(1)
+            at(clock[0] + rnd.randint(1, 40), land)
+            yield
+
+    def issuer():
+        for j in range(nit):
+            s, b = j % stages, j & 1
+            while not full[s].passed((j // stages) & 1):
+                yield
+            if convert and wait_conv:
+                while not conv[s].passed((j // stages) & 1):
+                    yield
+            while not acc_empty[b].passed(((j >> 1) & 1) ^ 1):
+                yield
+            if not holds(s, j) or parts[s] != j:
+                errors.append(("MMA issued on another fill", j, s, parts[s]))
+            if j >= 2 and added[0] < j - 2:
+                errors.append(("buffer rewritten before it was added", j, b))
+            acc[b] = j
+            reading[s].add(j)
+            last[0] = max(clock[0], last[0]) + rnd.randint(1, 25)
+
+            def complete(s=s, j=j, b=b):
+                if not holds(s, j) or parts[s] != j:
+                    errors.append(("stage changed under an MMA", j, s, parts[s]))
+                reading[s].discard(j)
+                acc_complete[b] = j
+                empty[s].arrive()
+                acc_full[b].arrive()
+
+            at(last[0], complete)
+            yield
+
+    def warps():
+        def add(j):
+            b = j & 1
+            while not acc_full[b].passed((j >> 1) & 1):
+                yield
+            if acc_complete[b] != j or acc[b] != j:
+                errors.append(("buffer added before its MMAs", j, b, acc_complete[b]))
+            added[0] = j
+            acc_empty[b].arrive(128)
+
+        for j in range(nit):
+            if convert:
+                s = j % stages
+                while not full[s].passed((j // stages) & 1):
+                    yield
+                if not holds(s, j):
+                    errors.append(("converters read another fill", j, s))
+                if reading[s]:
+                    errors.append(("parts written under the previous fill's MMAs", j, s, sorted(reading[s])))
+                yield  # the split takes time
+                parts[s] = j
+                conv[s].arrive(128)
+            if j > 0:
+                yield from add(j - 1)
+            yield
+        if nit > 0:
+            yield from add(nit - 1)
+
+    alive = [producer(), issuer(), warps()]
+    steps = 0
+    while alive or events:
+        steps += 1
+        if steps > max_steps:
+            errors.append(("no progress",))
+            break
+        clock[0] += 1
+        for e in sorted(e for e in events if e[0] <= clock[0]):
+            events.remove(e)
+            e[2]()
+        rnd.shuffle(alive)
+        for a in list(alive):
+            if rnd.random() < 0.5:
+                continue
+            try:
+                next(a)
+            except StopIteration:
+                alive.remove(a)
+    if added[0] != nit - 1:
+        errors.append(("not every slice was added", added[0], nit))
+    return errors
