@@ -4,7 +4,8 @@
   repo's plain-C restatement of the source-exact FP4 linear).
 * ``oracle/_ref/libvnni_source.so`` compiled from the REFERENCE's own source
   file ``mosaicvm/bench/vnni_source_kernel.c`` when the reference checkout is
-  present (``$MOSAIC_REFERENCE``, default ``/root/reference``), with the flags
+  present (``$MOSAIC_REFERENCE``, default: a ``reference`` checkout beside
+  this repository), with the flags
   the reference uses (``mosaicvm/bench/vnni_source.py:31-32``).  The output
   goes to ``oracle/_ref/`` only; no reference source is copied.
 """
@@ -15,7 +16,7 @@ import subprocess
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("MOSAIC_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("MOSAIC_REFERENCE", str(HERE.parent.parent / "reference")))
 VNNI_SRC = REF / "mosaicvm" / "bench" / "vnni_source_kernel.c"
 VNNI_LIB = HERE / "_ref" / "libvnni_source.so"
 PORT_LIB = HERE / "libfp4_linear_port.so"

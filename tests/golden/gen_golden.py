@@ -1,7 +1,8 @@
 """Generate the golden fixtures in this directory by running the REFERENCE itself.
 
 Run in a container that has the reference checkout (read-only) at
-``$MOSAIC_REFERENCE`` (default ``/root/reference``):
+``$MOSAIC_REFERENCE`` (default: a ``reference`` checkout beside this
+repository):
 
     python tests/golden/gen_golden.py
 
@@ -36,7 +37,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = os.environ.get("MOSAIC_REFERENCE", "/root/reference")
+REF = os.environ.get("MOSAIC_REFERENCE", str(HERE.parents[2] / "reference"))
 sys.path.insert(0, REF)
 sys.path.insert(0, str(HERE.parents[1]))
 
