@@ -19,7 +19,7 @@ from .moe import (  # noqa: F401
     exact_target,
     grouped_expert_forward,
 )
-from .ep import ExpertParallelMoELayer, expert_range, shard_bank  # noqa: F401
+from .ep import ExpertParallelMoELayer, PeerFailure, PeerHealth, expert_range, shard_bank  # noqa: F401
 
 __all__ = [
     "ExactContractError",
@@ -29,6 +29,8 @@ __all__ = [
     "HashRouter",
     "MoEConfig",
     "MoELayer",
+    "PeerFailure",
+    "PeerHealth",
     "Router",
     "exact_moe",
     "exact_target",

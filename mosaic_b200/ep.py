@@ -216,6 +216,42 @@ class PeerExchange:
         self._own, self._opened = None, []
 
 
+class PeerFailure(RuntimeError):
+    """A rank of the expert-parallel group left it, or a step's exchange with the
+    other ranks failed (a peer that is gone, or the process group's timeout)."""
+
+
+class PeerHealth:
+    """Host-side liveness of the ranks of an expert-parallel group, kept in a
+    c10d store the ranks share (``torch.distributed.TCPStore`` or any other
+    ``Store``).
+
+    A rank that stops between steps calls ``leave()``.  ``ExpertParallelMoELayer``
+    with ``health=`` calls ``check()`` before it launches a step, which raises
+    ``PeerFailure`` naming the ranks that left: the others stop before their
+    next collective instead of waiting for its timeout.  A rank that stops
+    without ``leave()`` is found by the process group's timeout, which ends the
+    step's next collective with an error (also raised as ``PeerFailure``).
+    """
+
+    def __init__(self, store, world: int, rank: int, *, prefix: str = "mosaic_ep"):
+        self.store, self.world, self.rank, self.prefix = store, world, rank, prefix
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}/left/{r}"
+
+    def leave(self) -> None:
+        self.store.set(self._key(self.rank), "1")
+
+    def left(self) -> list:
+        return [r for r in range(self.world) if r != self.rank and self.store.check([self._key(r)])]
+
+    def check(self) -> None:
+        gone = self.left()
+        if gone:
+            raise PeerFailure(f"rank(s) {gone} left the expert-parallel group")
+
+
 class ExpertParallelMoELayer(nn.Module):
     """``MoELayer`` with its routed experts sharded over the ranks of ``group``.
 
@@ -225,13 +261,16 @@ class ExpertParallelMoELayer(nn.Module):
     returns their layer output; every rank of the group must call it.  With
     ``layer_idx`` the layer is hash-routed (``HashMoELayer``,
     mosaicvm/model/layers.py:376-405): ``.hash_router`` replaces ``.router``
-    and ``forward(x, token_ids)`` routes by token id.
+    and ``forward(x, token_ids)`` routes by token id.  With ``health``
+    (a ``PeerHealth``) every step first checks that no rank has left.  A failed
+    collective of the NCCL / gloo exchange raises ``PeerFailure``.
     """
 
     def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None, exchange: str = "nccl",
                  max_tokens: int | None = None, peer_exchange: "PeerExchange | None" = None,
-                 layer_idx: int | None = None):
+                 layer_idx: int | None = None, health: "PeerHealth | None" = None):
         super().__init__()
+        self.health = health
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.exchange = exchange
@@ -320,8 +359,19 @@ class ExpertParallelMoELayer(nn.Module):
         if self.world == 1:  # no process group needed: the exchange is a copy
             out.copy_(inp)
             return None
-        return dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
-                                      group=self.group, async_op=async_op)
+        try:
+            return dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                                          group=self.group, async_op=async_op)
+        except RuntimeError as e:  # DistBackendError, timeouts
+            raise PeerFailure(f"expert-parallel exchange failed on rank {self.rank}: {e}") from e
+
+    def _wait(self, work) -> None:
+        if work is None:
+            return
+        try:
+            work.wait()
+        except RuntimeError as e:
+            raise PeerFailure(f"expert-parallel exchange failed on rank {self.rank}: {e}") from e
 
     def _forward_p2p(self, xf: torch.Tensor, token_ids=None) -> torch.Tensor:
         """One step with the device-driven peer-memory exchange: no host
@@ -373,6 +423,8 @@ class ExpertParallelMoELayer(nn.Module):
         shape = x.shape
         if token_ids is not None and self.hash_router is None:
             raise ValueError("token_ids are only used by a hash-routed layer")
+        if self.health is not None:
+            self.health.check()  # before anything is launched
         if self.exchange == "p2p":
             xf = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
             return self._forward_p2p(xf, token_ids).to(x.dtype).view(shape)
@@ -405,8 +457,7 @@ class ExpertParallelMoELayer(nn.Module):
         dl = self._local_dims(t)
         if self.has_shared and t > 0:  # overlaps the exchange
             kern.shared_rows(dl, self.bank, xf, partials[t * k:])
-        if work is not None:
-            work.wait()
+        self._wait(work)
         recv_part = torch.empty(n_recv, h, dtype=pdt, device=xf.device)
         kern.expert_rows(dl, self.bank, recv, recv_part)
         self._a2a(partials[:n_send], recv_part, sc, rc)
