@@ -118,3 +118,24 @@ def test_rank_that_stops_ends_the_next_collective_with_an_error(scenario):
     what, dt = res[0]
     assert what.startswith("PeerFailure: expert-parallel exchange failed on rank 0"), res
     assert dt < PG_TIMEOUT_S + 10, res  # bounded by the process group's timeout
+
+
+def test_peer_health_store_semantics():
+    """One store, three ranks' views: a departure is seen by the others (not by the
+    rank itself), every departed rank is named, and prefixes keep groups apart."""
+    from mosaic_b200 import PeerFailure, PeerHealth
+
+    store = dist.HashStore()
+    views = [PeerHealth(store, 3, r) for r in range(3)]
+    other_group = PeerHealth(store, 3, 0, prefix="another_layer_group")
+    for v in views:
+        v.check()  # nobody left
+    views[2].leave()
+    views[2].check()  # its own departure is not a peer failure
+    with pytest.raises(PeerFailure, match=r"\[2\]"):
+        views[0].check()
+    views[1].leave()
+    with pytest.raises(PeerFailure, match=r"\[1, 2\]"):
+        views[0].check()
+    assert views[1].left() == [2] and views[2].left() == [1]
+    other_group.check()  # a different prefix sees nothing
