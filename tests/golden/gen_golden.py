@@ -59,7 +59,7 @@ from mosaicvm.runtime.fp8 import dequant_fp4  # noqa: E402
 
 from tests.golden.recipes import (  # noqa: E402
     GATE_CASES,
-    HC_CASES,
+    HC_ORACLE_CASES,
     MOE_CASES,
     ROUTING_CASES,
     SALTED_CASES,
@@ -219,7 +219,7 @@ def gen_routing():
 
 def gen_hc():
     out = {}
-    for name, (b, s_, hc, d, iters, seed) in HC_CASES.items():
+    for name, (b, s_, hc, d, iters, seed) in HC_ORACLE_CASES.items():
         x, fn, base, scale, norm_w, y = make_hc_case(b, s_, hc, d, seed)
         cfg = V4Config(hidden_size=d, hc_mult=hc, hc_sinkhorn_iters=iters)
         mod = HyperConnections(cfg, "ffn")

@@ -135,6 +135,12 @@ HC_CASES = {
     "hc_v4": (1, 4, 4, 4096, 20, 52),
     "hc_mult2": (1, 5, 2, 512, 7, 53),
 }
+# more residual-copy counts, pinning the oracle (CPU tests) on every hc the C ABI takes
+HC_ORACLE_CASES = {
+    **HC_CASES,
+    "hc_mult1": (1, 3, 1, 256, 20, 54),
+    "hc_mult3": (2, 2, 3, 384, 20, 55),
+}
 
 
 def make_hc_case(b, s, hc, d, seed):

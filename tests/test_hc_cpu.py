@@ -12,7 +12,7 @@ import torch
 from mosaic_b200 import _capi as C
 from oracle.formats import act_quant_ref
 from oracle.hc import hc_post, hc_pre, rms_norm
-from tests.golden.recipes import HC_CASES, make_hc_case
+from tests.golden.recipes import HC_ORACLE_CASES, make_hc_case
 
 GOLD = Path(__file__).parent / "golden"
 
@@ -22,9 +22,9 @@ def gold():
     return np.load(GOLD / "hc.npz")
 
 
-@pytest.mark.parametrize("name", list(HC_CASES))
+@pytest.mark.parametrize("name", list(HC_ORACLE_CASES))
 def test_oracle_hc_matches_reference(gold, name):
-    b, s, hc, d, iters, seed = HC_CASES[name]
+    b, s, hc, d, iters, seed = HC_ORACLE_CASES[name]
     x, fn, base, scale, norm_w, y = make_hc_case(b, s, hc, d, seed)
     y_pre, post, comb = hc_pre(x, fn, base, scale, iters=iters, eps=1e-6, norm_eps=1e-6)
     assert np.array_equal(y_pre.float().numpy(), gold[name + "_y_pre"])
