@@ -27,7 +27,7 @@ from __future__ import annotations
 
 import json
 import struct
-from dataclasses import fields
+from dataclasses import dataclass, fields
 from pathlib import Path
 
 import numpy as np
@@ -152,58 +152,87 @@ def moe_config_from_checkpoint(root: str | Path, act_mode: str = "bf16"):
     return cfg, n_hash, raw
 
 
-def _is_packed_fp4(dt: str) -> bool:
-    return dt in ("I8", "U8")
+@dataclass(frozen=True)
+class TensorRule:
+    """One tensor a layer must (or must not) carry on the exact path.
+
+    ``suffix`` is the name after the layer prefix; ``dtypes`` the accepted
+    safetensors dtypes (None: any); ``shape`` the required shape (None: any);
+    ``forbidden`` marks a tensor whose presence breaks the contract.
+    """
+
+    suffix: str
+    dtypes: frozenset | None = None
+    shape: tuple | None = None
+    forbidden: bool = False
+
+
+_PACKED_E2M1 = frozenset({"U8", "I8"})   # two E2M1 codes per byte, low nibble first
+_E8M0 = frozenset({"F8_E8M0"})
+
+
+def exact_layer_rules(cfg: MoEConfig, hash_layer: bool) -> list[TensorRule]:
+    """The tensor table of one MoE layer under the exact MXFP4 contract.
+
+    Every routed expert carries ``w1`` (gate) and ``w3`` (up) as packed E2M1
+    ``[I, H/2]`` with E8M0 scales ``[I, H/32]``, and ``w2`` (down) as
+    ``[H, I/2]`` with ``[H, I/32]`` scales (mosaicvm/runtime/streaming_model.py:30-100
+    states the same formats for expert 0 at the V4 sizes).  A hash-routed
+    layer has a ``tid2eid`` table and no score bias; a score-routed layer has
+    the bias.
+    """
+    h, i = cfg.hidden_size, cfg.moe_intermediate_size
+    dims = {"w1": (i, h), "w3": (i, h), "w2": (h, i)}
+    rules = []
+    for e in range(cfg.n_routed_experts):
+        for w, (rows, k) in dims.items():
+            rules.append(TensorRule(f"ffn.experts.{e}.{w}.weight", _PACKED_E2M1, (rows, k // 2)))
+            rules.append(TensorRule(f"ffn.experts.{e}.{w}.scale", _E8M0, (rows, k // 32)))
+    if hash_layer:
+        rules.append(TensorRule("ffn.gate.tid2eid"))
+        rules.append(TensorRule("ffn.gate.bias", forbidden=True))
+    else:
+        rules.append(TensorRule("ffn.gate.bias"))
+    return rules
+
+
+def check_tensor_rules(index: ShardIndex, prefix: str, rules: list[TensorRule]) -> list[str]:
+    """Evaluates ``rules`` against the shard headers; returns one line per broken rule."""
+    issues = []
+    for r in rules:
+        name = prefix + r.suffix
+        if r.forbidden:
+            if name in index:
+                issues.append(f"{name}: present, but a hash-routed layer takes no score bias")
+            continue
+        if name not in index:
+            issues.append(f"{name}: not in the checkpoint")
+            continue
+        dt, shape = index.meta(name)
+        if r.dtypes is not None and dt not in r.dtypes:
+            issues.append(f"{name}: dtype {dt}, the exact path needs {' or '.join(sorted(r.dtypes))}")
+        if r.shape is not None and tuple(shape) != tuple(r.shape):
+            issues.append(f"{name}: shape {tuple(shape)}, the exact path needs {tuple(r.shape)}")
+    return issues
 
 
 def validate_exact_v4_tensors(index: ShardIndex, prefix: str, layer_idx: int, cfg: MoEConfig,
                               num_hash_layers: int) -> None:
-    """Exact contract on the tensors of one layer (streaming_model.py:30-100).
+    """Checks one layer's tensors against :func:`exact_layer_rules`.
 
-    FP4 E2M1 packed ``[N, K/2]`` uint8/int8 expert weights with E8M0 ``[N, K/32]``
-    scales; ``tid2eid`` present and bias absent on hash layers, bias present on
-    routed layers.  The sizes are the config's (the reference fixes them at
-    4096 / 2048).  Raises ExactContractError listing every problem.
+    Stricter than the reference's check (mosaicvm/runtime/streaming_model.py:30-100),
+    which inspects expert 0 only: every routed expert of the config is checked,
+    at the config's sizes.  Raises ExactContractError listing every broken rule
+    (a layer without any routed expert tensor is reported once).
     """
-    hidden, inter = cfg.hidden_size, cfg.moe_intermediate_size
-    expected = {"w1": (inter, hidden), "w3": (inter, hidden), "w2": (hidden, inter)}
-    problems = []
-    n_experts = 0
-    while f"{prefix}ffn.experts.{n_experts}.w1.weight" in index:
-        n_experts += 1
-    if n_experts == 0:
-        problems.append(f"no per-expert tensors under {prefix}ffn.experts.*")
-    for w, (n, k) in expected.items():
-        wname = f"{prefix}ffn.experts.0.{w}.weight"
-        sname = f"{prefix}ffn.experts.0.{w}.scale"
-        if wname not in index:
-            problems.append(f"missing {wname}")
-            continue
-        dt, shape = index.meta(wname)
-        if not _is_packed_fp4(dt):
-            problems.append(f"{wname}: expected packed uint8 (FP4 E2M1), got {dt}")
-        if tuple(shape) != (n, k // 2):
-            problems.append(f"{wname}: expected shape ({n}, {k // 2}), got {tuple(shape)}")
-        if sname not in index:
-            problems.append(f"missing {sname}")
-        else:
-            sdt, sshape = index.meta(sname)
-            if sdt != "F8_E8M0":
-                problems.append(f"{sname}: expected E8M0, got {sdt}")
-            if tuple(sshape) != (n, k // 32):
-                problems.append(f"{sname}: expected shape ({n}, {k // 32}), got {tuple(sshape)}")
-    is_hash = layer_idx < num_hash_layers
-    tid_name = f"{prefix}ffn.gate.tid2eid"
-    bias_name = f"{prefix}ffn.gate.bias"
-    if is_hash:
-        if tid_name not in index:
-            problems.append(f"missing {tid_name}")
-        if bias_name in index:
-            problems.append(f"hash layer must not have {bias_name}")
-    elif bias_name not in index:
-        problems.append(f"routed layer missing {bias_name}")
-    if problems:
-        raise ExactContractError(f"exact V4 tensor contract violated at layer {layer_idx}: " + "; ".join(problems))
+    rules = exact_layer_rules(cfg, hash_layer=layer_idx < num_hash_layers)
+    issues = check_tensor_rules(index, prefix, rules)
+    expert_rules = [r for r in rules if r.suffix.startswith("ffn.experts.")]
+    if expert_rules and all(prefix + r.suffix not in index for r in expert_rules):
+        issues = [f"{prefix}ffn.experts.*: no routed expert tensors"] + [
+            m for m in issues if not m.startswith(prefix + "ffn.experts.")]
+    if issues:
+        raise ExactContractError(f"layer {layer_idx} breaks the exact MXFP4 tensor contract: " + "; ".join(issues))
 
 
 class PinnedStager:
@@ -310,7 +339,7 @@ def load_moe_layer(root: str | Path | ShardIndex, layer_idx: int, *, cfg: MoECon
     has_shared = cfg.n_shared_experts > 0
     if has_shared:
         dt, _ = index.meta(shared + "w1.weight")
-        if not _is_packed_fp4(dt) or shared + "w1.scale" not in index or index.meta(shared + "w1.scale")[0] != "F8_E8M0":
+        if dt not in _PACKED_E2M1 or shared + "w1.scale" not in index or index.meta(shared + "w1.scale")[0] != "F8_E8M0":
             raise NotImplementedError(f"layer {layer_idx}: shared expert stored as {dt}; the expert GEMM takes "
                                       "MXFP4 (packed E2M1 + E8M0) weights only")
         names.append(shared)

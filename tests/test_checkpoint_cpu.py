@@ -54,13 +54,13 @@ def test_exact_contract_accepts_the_fixture(tmp_path):
 
 
 @pytest.mark.parametrize("mutation,message", [
-    (dict(extra={"layers.1.ffn.experts.0.w1.weight": torch.zeros(128, 256)}), "expected packed uint8"),
-    (dict(extra={"layers.1.ffn.experts.0.w2.weight": torch.zeros(256, 32, dtype=torch.uint8)}), "expected shape"),
-    (dict(drop=("layers.1.ffn.experts.0.w3.scale",)), "missing layers.1.ffn.experts.0.w3.scale"),
-    (dict(extra={"layers.1.ffn.experts.0.w1.scale": torch.zeros(128, 8)}), "expected E8M0"),
-    (dict(drop=("layers.1.ffn.gate.bias",)), "routed layer missing"),
-    (dict(extra={"layers.0.ffn.gate.bias": torch.zeros(8)}), "hash layer must not have"),
-    (dict(drop=("layers.0.ffn.gate.tid2eid",)), "missing layers.0.ffn.gate.tid2eid"),
+    (dict(extra={"layers.1.ffn.experts.0.w1.weight": torch.zeros(128, 256)}), "w1.weight: dtype F32, the exact path needs I8 or U8"),
+    (dict(extra={"layers.1.ffn.experts.0.w2.weight": torch.zeros(256, 32, dtype=torch.uint8)}), "w2.weight: shape \\(256, 32\\), the exact path needs"),
+    (dict(drop=("layers.1.ffn.experts.0.w3.scale",)), "layers.1.ffn.experts.0.w3.scale: not in the checkpoint"),
+    (dict(extra={"layers.1.ffn.experts.0.w1.scale": torch.zeros(128, 8)}), "w1.scale: dtype F32, the exact path needs F8_E8M0"),
+    (dict(drop=("layers.1.ffn.gate.bias",)), "layers.1.ffn.gate.bias: not in the checkpoint"),
+    (dict(extra={"layers.0.ffn.gate.bias": torch.zeros(8)}), "hash-routed layer takes no score bias"),
+    (dict(drop=("layers.0.ffn.gate.tid2eid",)), "layers.0.ffn.gate.tid2eid: not in the checkpoint"),
 ])
 def test_exact_contract_violations(tmp_path, mutation, message):
     make_checkpoint(tmp_path, **mutation)
@@ -71,11 +71,23 @@ def test_exact_contract_violations(tmp_path, mutation, message):
         validate_exact_v4_tensors(idx, f"layers.{layer}.", layer, cfg, n_hash)
 
 
-def test_exact_contract_no_experts(tmp_path):
+def test_exact_contract_missing_gate_weights(tmp_path):
     e = CKPT["E"]
     drop = tuple(f"layers.1.ffn.experts.{i}.w1.weight" for i in range(e))
     make_checkpoint(tmp_path, drop=drop)
     idx = ShardIndex(tmp_path)
     cfg, n_hash, _ = moe_config_from_checkpoint(tmp_path)
-    with pytest.raises(ExactContractError, match="no per-expert tensors"):
+    with pytest.raises(ExactContractError, match=f"layers.1.ffn.experts.{e - 1}.w1.weight: not in the checkpoint"):
         validate_exact_v4_tensors(idx, "layers.1.", 1, cfg, n_hash)
+
+
+def test_exact_contract_no_experts(tmp_path):
+    e = CKPT["E"]
+    drop = tuple(f"layers.1.ffn.experts.{i}.{w}.{t}" for i in range(e) for w in ("w1", "w2", "w3")
+                 for t in ("weight", "scale"))
+    make_checkpoint(tmp_path, drop=drop)
+    idx = ShardIndex(tmp_path)
+    cfg, n_hash, _ = moe_config_from_checkpoint(tmp_path)
+    with pytest.raises(ExactContractError, match="no routed expert tensors") as info:
+        validate_exact_v4_tensors(idx, "layers.1.", 1, cfg, n_hash)
+    assert "experts.0.w1" not in str(info.value)
