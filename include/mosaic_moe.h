@@ -36,6 +36,7 @@
  *                               hc_split_sinkhorn :222-234) + :19-29 (RMSNorm, the block's
  *                               ffn_norm, :431-433) + fp4_source.py:110-129 (act_quant_ref)
  *   mosaic_hc_post           <- mosaicvm/model/layers.py:269-271 (HyperConnections.post)
+ *   mosaic_rms_norm          <- mosaicvm/model/layers.py:19-29 (RMSNorm.forward)
  *   mosaic_ep_*              <- .mosaicvm/source/inference_model.py:614-650 (MoE.forward,
  *                               expert-sharded; all_reduce replaced by all-to-all)
  */
@@ -120,7 +121,9 @@ MOSAIC_API int mosaic_device_sm_count(void);
  * biased score, weights gathered from the unbiased s, normalised and scaled.
  * x bf16 [T, H]; weight fp32 [E, H]; bias fp32 [E] (NULL = zeros);
  * weights_out fp32 [T, top_k]; idx_out int64 [T, top_k].
- * Equal biased scores are broken towards the lower expert id. */
+ * Equal biased scores are broken towards the lower expert id.  The
+ * workspace's error word (its first 16 bytes) is cleared at the start of
+ * each call; read it afterwards with mosaic_read_error. */
 MOSAIC_API size_t mosaic_router_workspace_bytes(int32_t T, int32_t H, int32_t E);
 MOSAIC_API int mosaic_router(const void* x, const float* weight, const float* bias, int32_t T, int32_t H, int32_t E,
                   int32_t top_k, int32_t n_group, int32_t topk_group, float route_scale, int32_t norm_topk_prob,
@@ -181,12 +184,15 @@ MOSAIC_API int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, con
  * - One scratch per device: calls that overlap on a device (two streams, two
  *   host threads, or two launches in one graph that may run concurrently)
  *   race on it and give undefined results.  Serialise them.
- * - The first call on each device looks up the scratch address
- *   (cudaGetSymbolAddress, which may load the module); make that first call
- *   outside any stream capture.  Later calls are capture-safe.
- * - A non-finite score is recorded in the scratch's error word, which this
- *   entry point does not report; use mosaic_router with mosaic_read_error
- *   where that check is needed. */
+ * - Every call outside stream capture looks up the scratch address
+ *   (cudaGetSymbolAddress, which may load the module); a call under capture
+ *   uses the address its device's last uncaptured call found, so the first
+ *   call on each device must come before any stream capture.
+ * - Device errors (a non-finite score, a pipeline wait of the tensor-core
+ *   logits that ran out) go to the scratch's error word, which each call
+ *   clears first and which this entry point does not report: its outputs
+ *   are then undefined.  Use mosaic_router with mosaic_read_error where that
+ *   check is needed. */
 MOSAIC_API int mosaic_router_noalloc(const void* x, const float* weight, const float* bias, int32_t T, int32_t H,
                                      int32_t E, int32_t top_k, int32_t n_group, int32_t topk_group,
                                      float route_scale, int32_t norm_topk_prob, float* weights_out,
@@ -194,7 +200,9 @@ MOSAIC_API int mosaic_router_noalloc(const void* x, const float* weight, const f
 
 /* ids int64 [A] -> sorted_ids int64 [A], perm int64 [A] (stable: ascending
  * flat index inside each expert segment), offsets int32 [E+1], counts int32 [E].
- * Single-CTA histogram / prefix scan / stable scatter; A <= 1<<20. */
+ * One CTA (histogram, prefix scan, stable scatter in 1024-id chunks); A <= 1<<20.
+ * The MoE layer's own layout (inside mosaic_moe_forward) uses a multi-CTA
+ * count / scan / rank pass above 1024 assignments instead. */
 MOSAIC_API int mosaic_layout_assignments(const int64_t* expert_ids, int32_t A, int32_t E, int64_t* sorted_ids,
                               int64_t* perm, int32_t* offsets, int32_t* counts, mosaic_stream_t stream);
 
@@ -249,6 +257,17 @@ MOSAIC_API int mosaic_hc_pre_norm(const void* x, const float* fn, const float* b
                                   const float* norm_weight, int32_t T, int32_t D, int32_t hc, int32_t sinkhorn_iters,
                                   float hc_eps, float norm_eps, void* y, float* post, float* comb, uint8_t* q,
                                   float* q_scale, void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
+
+/* RMSNorm on its own, mosaicvm/model/layers.py:19-29 (RMSNorm.forward):
+ * y[t] = bf16(x[t] * (1 / sqrt(mean(x[t]^2) + eps)) * weight), all in fp32.
+ *   x, y        bf16 [T, D], 16-byte aligned; D % 8 == 0, D <= MOSAIC_RMS_NORM_MAX_D
+ *   weight      fp32 [D], 16-byte aligned
+ *   q, q_scale  E4M3 [T, D] and fp32 [T, D/128] = act_quant_ref(y) (the FP8 MoE
+ *               input; D % 128 == 0), or both NULL
+ * One row per CTA, read from HBM once; no workspace. */
+#define MOSAIC_RMS_NORM_MAX_D 65536
+MOSAIC_API int mosaic_rms_norm(const void* x, const float* weight, int32_t T, int32_t D, float eps, void* y,
+                               uint8_t* q, float* q_scale, mosaic_stream_t stream);
 
 /* The step behind the MoE: out[t, m] = post[t, m] * y[t] + sum_n comb[t, m, n] * residual[t, n]
  * (fp32, rounded to bf16); y bf16 [T, D] (the MoE output), residual and out bf16 [T, hc, D]. */

@@ -58,6 +58,7 @@ EXPORTED = (
     "mosaic_hc_pre_norm_workspace_bytes",
     "mosaic_hc_pre_norm",
     "mosaic_hc_post",
+    "mosaic_rms_norm",
     "mosaic_moe_workspace_bytes",
     "mosaic_moe_forward",
     "mosaic_moe_forward_profiled",
@@ -164,6 +165,7 @@ _SIGS = {
     "mosaic_hc_pre_norm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float, _P, _P, _P, _P, _P,
                             _P, _SZ, _P], ctypes.c_int),
     "mosaic_hc_post": ([_P, _P, _P, _P, _I, _I, _I, _P, _P], ctypes.c_int),
+    "mosaic_rms_norm": ([_P, _P, _I, _I, ctypes.c_float, _P, _P, _P, _P], ctypes.c_int),
     "mosaic_moe_workspace_bytes": ([ctypes.POINTER(MoEDims)], _SZ),
     "mosaic_moe_forward": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _P, _P, _P, _SZ, _P],
                            ctypes.c_int),

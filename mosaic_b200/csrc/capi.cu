@@ -511,13 +511,18 @@ bool salted_hash(const RouteVariant& rv) { return rv.hash && !rv.tid2eid; }
 
 constexpr int kMaxDevices = 64;
 
-// Device address of g_router_scratch, looked up once per device.
-int router_scratch(int dev, uint8_t** out) {
+// Device address of g_router_scratch on device dev.  Outside stream capture it
+// is looked up again on every call (so a reloaded module after a device reset
+// is followed); under capture the address cached by the last uncaptured call
+// is used, because the lookup may load the module, which capture forbids.
+int router_scratch(int dev, cudaStream_t stream, uint8_t** out) {
   static std::mutex mu;
   static uint8_t* addr[kMaxDevices] = {};
   if (dev < 0 || dev >= kMaxDevices) return MOSAIC_ERR_UNSUPPORTED;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  const bool capturing = cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone;
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  if (!capturing || !addr[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_router_scratch) != cudaSuccess || !p) return MOSAIC_ERR_CUDA;
     addr[dev] = static_cast<uint8_t*>(p);
@@ -570,6 +575,7 @@ int mosaic_router(const void* x, const float* weight, const float* bias, int32_t
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   const int splits = router_splits(T, H, E, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws, 0, 16, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return MOSAIC_ERR_CUDA;
   const size_t part_bytes = up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
   return run_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob, weights_out,
                     idx_out, reinterpret_cast<float*>(ws + up256(16)), ws + up256(16) + part_bytes, splits,
@@ -600,6 +606,7 @@ int mosaic_router_ext(const mosaic_route_ext* ext, const void* x, const float* w
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   const int splits = router_splits(T, H, E, sms);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws, 0, 16, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return MOSAIC_ERR_CUDA;
   const size_t part_bytes = up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
   return run_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob, weights_out,
                     idx_out, reinterpret_cast<float*>(ws + up256(16)), ws + up256(16) + part_bytes, splits,
@@ -619,8 +626,10 @@ int mosaic_router_noalloc(const void* x, const float* weight, const float* bias,
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   uint8_t* ws = nullptr;
-  const int sst = router_scratch(dev, &ws);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int sst = router_scratch(dev, s, &ws);
   if (sst != MOSAIC_OK) return sst;
+  if (cudaMemsetAsync(ws, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;  // this call's error word
   const int splits = router_splits(T, H, E, sms);
   const size_t part_bytes = up256(sizeof(float) * static_cast<size_t>(splits) * T * E);
   return run_router(x, weight, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm_topk_prob, weights_out,
@@ -764,6 +773,18 @@ int mosaic_hc_post(const void* y, const void* residual, const float* post, const
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
   cudaError_t e = launch_hc_post(y, residual, post, comb, T, D, hc, out, sms, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_rms_norm(const void* x, const float* weight, int32_t T, int32_t D, float eps, void* y, uint8_t* q,
+                    float* q_scale, mosaic_stream_t stream) {
+  if (!x || !weight || !y || ((q == nullptr) != (q_scale == nullptr))) return MOSAIC_ERR_SHAPE;
+  if (T < 1 || D < 8 || D % 8 || D > MOSAIC_RMS_NORM_MAX_D) return MOSAIC_ERR_SHAPE;
+  if (q && D % 128) return MOSAIC_ERR_SHAPE;
+  if (!(eps >= 0.f)) return MOSAIC_ERR_RANGE;
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(weight, 16) || (q && (!aligned(q, 8) || !aligned(q_scale, 4))))
+    return MOSAIC_ERR_ALIGN;
+  cudaError_t e = launch_rms_norm(x, weight, T, D, eps, y, q, q_scale, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }
 

@@ -219,6 +219,79 @@ __global__ void __launch_bounds__(256) hc_post_kernel(const __nv_bfloat16* __res
   }
 }
 
+
+// Standalone RMSNorm: y = bf16(x * (1 / sqrt(mean(x^2) + eps)) * w) for one row
+// per CTA, the row staged in shared memory between the sum-of-squares pass and
+// the scaling pass (x is read from HBM once).  Optional act_quant_ref of y.
+// Reference: mosaicvm/model/layers.py:19-29 (RMSNorm.forward).
+constexpr int kNormThreads = 128;
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                const float* __restrict__ w, int D, float eps,
+                                                                __nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q,
+                                                                float* __restrict__ q_scale) {
+  extern __shared__ __align__(16) uint8_t norm_smem[];
+  __shared__ float red[kNormThreads / 32];
+  uint4* row = reinterpret_cast<uint4*>(norm_smem);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t base = static_cast<size_t>(blockIdx.x) * D;
+  const int nvec = D / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x + base);
+  float ss = 0.f;
+  for (int v = tid; v < nvec; v += kNormThreads) {
+    const uint4 raw = __ldg(src + v);
+    row[v] = raw;
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h2[i]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float r = 1.0f / sqrtf(tot / static_cast<float>(D) + eps);
+  // Every lane runs the same iterations (quant_block128 shuffles across 16 lanes).
+  const int steps = (nvec + kNormThreads - 1) / kNormThreads;
+  for (int s = 0; s < steps; ++s) {
+    const int v = s * kNormThreads + tid;
+    const bool valid = v < nvec;
+    float o[8];
+    if (valid) {
+      const uint4 raw = row[v];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * v);
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * v + 1);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      __align__(16) __nv_bfloat16 ob[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        ob[2 * i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(f.x, r), wv[2 * i]));
+        ob[2 * i + 1] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(f.y, r), wv[2 * i + 1]));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = __bfloat162float(ob[i]);
+      reinterpret_cast<uint4*>(y + base)[v] = *reinterpret_cast<const uint4*>(ob);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    }
+    if (q) {
+      uint8_t b[8];
+      const int e = quant_block128(o, b);
+      if (valid) {
+        reinterpret_cast<uint2*>(q + base)[v] = pack8(b);
+        if ((lane & 15) == 0) q_scale[static_cast<size_t>(blockIdx.x) * (D / 128) + v / 16] = exp2i(e);
+      }
+    }
+  }
+}
+
 }  // namespace
 
 size_t hc_pre_norm_smem_bytes(int tt, int D) {
@@ -267,6 +340,19 @@ cudaError_t launch_hc_post(const void* y, const void* residual, const float* pos
   hc_post_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(y), static_cast<const __nv_bfloat16*>(residual), post, comb, T, D, hc,
       static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm(const void* x, const float* w, int T, int D, float eps, void* y, uint8_t* q,
+                            float* q_scale, cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(D) * 2;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  rms_norm_kernel<<<T, kNormThreads, smem, stream>>>(static_cast<const __nv_bfloat16*>(x), w, D, eps,
+                                                     static_cast<__nv_bfloat16*>(y), q, q_scale);
   return cudaGetLastError();
 }
 

@@ -117,6 +117,9 @@ size_t hc_fn_parts_bytes(int KD);
 cudaError_t launch_hc_split_fn(const float* fn, int nmix, int KD, void* parts, int num_sms, cudaStream_t stream);
 cudaError_t launch_hc_mix_tc(const CUtensorMap& tmap_x, const CUtensorMap& tmap_f, int T, int KD, int nmix,
                              int splits, float* partial, int* err, cudaStream_t stream);
+// standalone RMSNorm, one row per CTA (D % 8 == 0; q / q_scale optional: act_quant_ref of y)
+cudaError_t launch_rms_norm(const void* x, const float* w, int T, int D, float eps, void* y, uint8_t* q,
+                            float* q_scale, cudaStream_t stream);
 cudaError_t launch_hc_post(const void* y, const void* residual, const float* post, const float* comb, int T, int D,
                            int hc, void* out, int num_sms, cudaStream_t stream);
 

@@ -6,7 +6,8 @@ Reference API mirrored (paths inside fazin-ahamed/Mosaic):
   ``fn`` [(2+hc)*hc, hc*D], ``base`` [(2+hc)*hc], ``scale`` [3];
   ``pre(x [b, s, hc, D]) -> (y [b, s, D], post [b, s, hc], comb [b, s, hc, hc])``
   and ``post(y, residual, post, comb) -> [b, s, hc, D]``.
-* ``RMSNorm`` <- ``mosaicvm/model/layers.py:19-29``: ``weight`` [D], ``eps``.
+* ``RMSNorm`` <- ``mosaicvm/model/layers.py:19-29``: ``weight`` [D], ``eps``;
+  ``forward`` runs ``mosaic_rms_norm``.
 * ``ffn_pre_norm`` is the fused form of ``y, post, comb = hc_ffn.pre(x);
   y = ffn_norm(y)`` in ``V4Block.forward`` (``layers.py:428-433``), optionally
   with ``act_quant_ref`` of y (the FP8 MoE input), in one kernel
@@ -25,15 +26,41 @@ from . import ops
 
 
 class RMSNorm(nn.Module):
-    """RMSNorm parameters (layers.py:19-29); it runs fused into :func:`ffn_pre_norm`."""
+    """RMSNorm (layers.py:19-29) on the GPU: ``mosaic_rms_norm``, one row per CTA.
+
+    ``forward(x)`` takes bf16 ``[..., D]`` and returns bf16, as the reference
+    does for bf16 activations (fp32 arithmetic, one rounding at the end).
+    ``forward(x, quant=True)`` also returns ``act_quant_ref`` of the result
+    (E4M3 ``[..., D]`` and fp32 scales ``[..., D/128]``), fused.  In front of
+    the MoE the norm runs fused with the hyper-connection pre-mix instead
+    (:func:`ffn_pre_norm`).
+    """
 
     def __init__(self, dim: int, eps: float = 1e-6):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(dim), requires_grad=False)
         self.eps = eps
 
-    def forward(self, x):
-        raise NotImplementedError("RMSNorm runs fused with the hyper-connection pre-mix: use ffn_pre_norm")
+    def forward(self, x, quant: bool = False):
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"RMSNorm on the GPU path takes bf16 activations, got {x.dtype}")
+        d = x.shape[-1]
+        if d != self.weight.numel():
+            raise ValueError(f"RMSNorm of width {self.weight.numel()} given rows of {d}")
+        t = x.numel() // d
+        xf = x.reshape(t, d).contiguous()
+        ops._need_cuda(xf, what="RMSNorm")
+        w = self.weight.detach().float().contiguous().to(xf.device)
+        y = torch.empty_like(xf)
+        q = torch.empty(t, d, dtype=torch.uint8, device=xf.device) if quant else None
+        qs = torch.empty(t, d // 128, dtype=torch.float32, device=xf.device) if quant else None
+        st = C.lib().mosaic_rms_norm(ops._ptr(xf), ops._ptr(w), t, d, float(self.eps), ops._ptr(y), ops._ptr(q),
+                                     ops._ptr(qs), ops._stream())
+        C.check(st, "mosaic_rms_norm")
+        y = y.view(x.shape)
+        if not quant:
+            return y
+        return y, q.view(torch.float8_e4m3fn).view(x.shape), qs.view(*x.shape[:-1], d // 128)
 
 
 class HyperConnections(nn.Module):

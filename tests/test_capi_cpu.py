@@ -177,3 +177,21 @@ def test_hc_workspace_follows_the_split_plan():
     assert lib.mosaic_hc_pre_norm_workspace_bytes(128, d, hc) == 256 + up(148 * 128 * 25 * 4) + parts
     assert lib.mosaic_hc_pre_norm_workspace_bytes(8192, d, hc) == 256 + up(2 * 8192 * 25 * 4) + parts
     assert lib.mosaic_hc_pre_norm_workspace_bytes(1, 128, 1) == 256 + up(2 * 1 * 25 * 4) + up(3 * 32 * 128 * 2)
+
+
+def test_rms_norm_validation_before_launch():
+    """Shape, pairing of q / q_scale, epsilon and alignment are checked on the host."""
+    lib = C.lib()
+    fake = 1 << 20
+    st = lib.mosaic_rms_norm(fake, fake, 4, 12, 1e-6, fake, None, None, None)  # D % 8
+    assert st == C.MOSAIC_ERR_SHAPE
+    st = lib.mosaic_rms_norm(fake, fake, 4, 65544, 1e-6, fake, None, None, None)  # D above the maximum
+    assert st == C.MOSAIC_ERR_SHAPE
+    st = lib.mosaic_rms_norm(fake, fake, 4, 256, 1e-6, fake, fake, None, None)  # q without q_scale
+    assert st == C.MOSAIC_ERR_SHAPE
+    st = lib.mosaic_rms_norm(fake, fake, 4, 136, 1e-6, fake, fake, fake, None)  # act_quant needs D % 128
+    assert st == C.MOSAIC_ERR_SHAPE
+    st = lib.mosaic_rms_norm(fake, fake, 4, 256, -1.0, fake, None, None, None)
+    assert st == C.MOSAIC_ERR_RANGE
+    st = lib.mosaic_rms_norm(fake + 8, fake, 4, 256, 1e-6, fake, None, None, None)
+    assert st == C.MOSAIC_ERR_ALIGN

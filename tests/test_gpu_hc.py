@@ -21,7 +21,7 @@ import torch
 
 from oracle.formats import act_quant_ref
 from oracle.hc import hc_post, hc_pre, rms_norm
-from tests.golden.recipes import HC_CASES, make_hc_case
+from tests.golden.recipes import HC_CASES, HC_ORACLE_CASES, make_hc_case
 
 pytestmark = pytest.mark.gpu
 GOLD = Path(__file__).parent / "golden"
@@ -111,3 +111,53 @@ def test_hc_pre_norm_feeds_the_moe_layer():
     y2 = layer(yn.clone())
     torch.cuda.synchronize()
     assert torch.equal(y1, y2) and torch.isfinite(y1.float()).all()
+
+
+@pytest.mark.parametrize("name", list(HC_ORACLE_CASES))
+def test_rms_norm_matches_reference_golden(name):
+    """Standalone RMSNorm on the reference's own pre-mix output (y_pre, bf16)
+    against the reference RMSNorm's output: the same bf16 input, so only the
+    order of the sum of squares differs; act_quant of the result is bit-equal
+    to act_quant_ref of the kernel's bf16 output."""
+    from mosaic_b200.hc import RMSNorm
+
+    gold = np.load(GOLD / "hc.npz")
+    b, s, hcm, d, iters, seed = HC_ORACLE_CASES[name]
+    _, _, _, _, norm_w, _ = make_hc_case(b, s, hcm, d, seed)
+    x = torch.from_numpy(gold[name + "_y_pre"]).to(torch.bfloat16).cuda()
+    norm = RMSNorm(d)
+    norm.weight.data = norm_w.cuda()
+    y = norm(x)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.bfloat16 and y.shape == x.shape
+    _bf16_close(y.float().cpu(), gold[name + "_y_norm"], "rms_norm")
+    if d % 128 == 0:
+        y2, q, qs = norm(x, quant=True)
+        torch.cuda.synchronize()
+        assert torch.equal(y2, y)
+        q_ref, s_ref = act_quant_ref(y.float().cpu().numpy().reshape(-1, d))
+        assert np.array_equal(q.view(torch.uint8).cpu().numpy().reshape(-1, d), q_ref)
+        assert np.array_equal(qs.cpu().numpy().reshape(-1, d // 128), s_ref)
+
+
+@pytest.mark.parametrize("t,d", [(1, 8), (3, 136), (257, 7168), (64, 16384), (2, 65536)])
+def test_rms_norm_against_oracle(t, d):
+    """Widths from one vector to MOSAIC_RMS_NORM_MAX_D (partial last pass of the
+    block, more passes than one, the widest shared-memory row)."""
+    from mosaic_b200.hc import RMSNorm
+
+    g = torch.Generator().manual_seed(t * 7 + d)
+    x = (torch.randn(t, d, generator=g) * 3).to(torch.bfloat16)
+    w = 1 + 0.1 * torch.randn(d, generator=g)
+    norm = RMSNorm(d, eps=1e-6)
+    norm.weight.data = w.cuda()
+    y = norm(x.cuda())
+    torch.cuda.synchronize()
+    _bf16_close(y.float().cpu(), rms_norm(x, w, 1e-6).float(), "rms_norm")
+
+
+def test_rms_norm_rejects_other_dtypes():
+    from mosaic_b200.hc import RMSNorm
+
+    with pytest.raises(TypeError):
+        RMSNorm(256).cuda()(torch.zeros(2, 256, device="cuda"))

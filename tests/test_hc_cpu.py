@@ -66,7 +66,11 @@ def test_hc_module_contracts():
         hc.pre(torch.zeros(1, 2, 4, 256))
     with pytest.raises(ValueError, match="CUDA"):
         hc.pre(torch.zeros(1, 2, 4, 256, dtype=torch.bfloat16))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(TypeError, match="bf16"):
         RMSNorm(256)(torch.zeros(2, 256))
+    with pytest.raises(ValueError, match="CUDA"):
+        RMSNorm(256)(torch.zeros(2, 256, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="width 256"):
+        RMSNorm(256)(torch.zeros(2, 128, dtype=torch.bfloat16))
     with pytest.raises(ValueError, match="one epsilon"):
         ffn_pre_norm(torch.zeros(1, 2, 4, 256, dtype=torch.bfloat16), hc, RMSNorm(256, eps=1e-5))
