@@ -204,35 +204,40 @@ __global__ void __launch_bounds__(NT, 1)
   const int n_items = n_tiles * p.n_blocks;
   const int KT = p.K / 128;
 
+  // The producer, issuer and copier loops run on lane 0 alone, with the ring
+  // position (stage, phase) and the accumulator position kept as counters and
+  // every per-item operand computed once per item: a warp-wide loop with a
+  // lane-0 branch per stage, or a division per stage, costs each
+  // tcgen05.mma several hundred cycles of issue time.
   if (warp == 0 || warp == 6) {
     // ----------------------------------------------------------- producers
-    const bool wprod = (warp == 0);
-    const uint32_t tx = wprod ? 2u * 8192u  // packed global bytes of the two weight tiles
-                              : 2u * 512u + static_cast<uint32_t>(planes * p.brows) * 128u + 512u;
-    int it = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-      const Item m = get_item(p, item);
-      // bank entry of the item's expert (offload: through the slot table)
-      int em = m.e;
-      if (p.expert_slot) {
-        em = __ldg(p.expert_slot + m.e);
-        if (em < 0 || em >= p.bank_slots) {
-          if (lane == 0) set_error(p.err, MOSAIC_ERR_RANGE);
-          em = 0;
+    if (lane == 0) {
+      const bool wprod = (warp == 0);
+      const uint32_t tx = wprod ? 2u * 8192u  // packed global bytes of the two weight tiles
+                                : 2u * 512u + static_cast<uint32_t>(planes * p.brows) * 128u + 512u;
+      int s = 0, last_s = -1;
+      uint32_t ph = 0, last_ph = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const Item m = get_item(p, item);
+        // bank entry of the item's expert (offload: through the slot table)
+        int em = m.e;
+        if (p.expert_slot) {
+          em = __ldg(p.expert_slot + m.e);
+          if (em < 0 || em >= p.bank_slots) {
+            set_error(p.err, MOSAIC_ERR_RANGE);
+            em = 0;
+          }
         }
-      }
-      // tile index of (expert, block pair, K-tile 0, first of the pair); the two
-      // tiles of the pair are adjacent for every K-tile
-      const int wtile = ((em * p.n_blocks + m.nb) * KT) * 2;
-      for (int kt = 0; kt < KT; ++kt, ++it) {
-        const int s = it % S;
-        const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
-        if (!mbar_wait(&ctrl->empty[s], ph ^ 1u, abort)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
+        // tile index of (expert, block pair, K-tile 0, first of the pair); the two
+        // tiles of the pair are adjacent for every K-tile
+        const int wtile = ((em * p.n_blocks + m.nb) * KT) * 2;
+        const uint8_t* sft = p.x_sft + static_cast<size_t>(m.tile) * KT * 512;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&ctrl->empty[s], ph ^ 1u, abort)) {
+            ok = false;
+            break;
+          }
           uint8_t* st = smem + s * pl.stage_bytes;
           uint64_t* fb = &ctrl->full[s];
           const int t0 = wtile + kt * 2;
@@ -242,133 +247,148 @@ __global__ void __launch_bounds__(NT, 1)
           } else {
             tma_load_4d(st + pl.off_b, &tmap_x, fb, 0, m.row0, 0, kt);
             bulk_load(st + pl.off_sfa, p.w_sf + static_cast<size_t>(t0) * 512, 1024u, fb);
-            bulk_load(st + pl.off_sfb, p.x_sft + (static_cast<size_t>(m.tile) * KT + kt) * 512, 512u, fb);
+            bulk_load(st + pl.off_sfb, sft + static_cast<size_t>(kt) * 512, 512u, fb);
+          }
+          last_s = s;
+          last_ph = ph;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
           }
         }
-        __syncwarp();
       }
-    }
-    if (!ok) {
-      if (lane == 0) set_error(p.err, MOSAIC_ERR_TIMEOUT);
-      ctrl->abort = 1;
-    }
-    // Wait (bounded) for the last armed stage so no copy is in flight at exit.
-    if (it > 0 && lane == 0) {
-      const int s = (it - 1) % S;
-      volatile int never = 0;
-      mbar_wait(&ctrl->full[s], static_cast<uint32_t>((it - 1) / S) & 1u, &never);
+      if (!ok) {
+        set_error(p.err, MOSAIC_ERR_TIMEOUT);
+        ctrl->abort = 1;
+      }
+      // Wait (bounded) for the last armed stage so no copy is in flight at exit.
+      if (last_s >= 0) {
+        volatile int never = 0;
+        mbar_wait(&ctrl->full[last_s], last_ph, &never);
+      }
     }
     __syncwarp();
   } else if ((warp == 1 || warp >= 7) && (warp == 1 ? 0 : warp - 6) < 2 * P) {
     // ----------------------------------------------------------------- MMA
-    const int issuer = (warp == 1) ? 0 : warp - 6;  // 0 .. 2P-1
-    const int ip = issuer >> 1;                     // stage parity this issuer takes
-    const int iu = issuer & 1;                      // unit: block of the pair
-    int it = 0, li = 0;
-    bool issued = false, ok = true;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++li) {
-      const Item m = get_item(p, item);
-      const int b = li % nbuf;
-      const uint32_t aph = static_cast<uint32_t>(li / nbuf) & 1u;
-      if (!mbar_wait(&ctrl->acc_empty[b], aph ^ 1u, abort)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      for (int kt = 0; kt < KT; ++kt, ++it) {
-        const int s = it % S;
-        const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
-        // Every issuer observes every phase of every full barrier and arrives on
-        // the matching empty barrier, including for the stages the other parity
-        // consumes.  A parity wait that skipped phases could match the phase two
-        // fills back and read a stage before it lands; requiring every issuer's
-        // arrival before a refill keeps all four within one phase of the ring.
-        if (!mbar_wait(copier ? &ctrl->sf_ready[s] : &ctrl->full[s], ph, abort)) {
+    if (lane == 0) {
+      const int issuer = (warp == 1) ? 0 : warp - 6;  // 0 .. 2P-1
+      const int ip = issuer >> 1;                     // stage parity this issuer takes
+      const int iu = issuer & 1;                      // unit: block of the pair
+      const uint32_t smem_base = smem_u32(smem);
+      const uint32_t stage_bytes = static_cast<uint32_t>(pl.stage_bytes);
+      const uint32_t a_off = 16384u * static_cast<uint32_t>(iu);
+      const uint32_t b_off = static_cast<uint32_t>(pl.off_b);
+      // scale-factor columns of ring stage 0 (copier) or of this issuer (no copier)
+      const uint32_t sfw0 = copier ? tmem + sf_base + 4u * iu : tmem + sf_base + 8u * issuer;
+      const uint32_t sfx0 = copier ? tmem + sf_base + 8u : tmem + sf_base + 8u * issuer + 4u;
+      const uint32_t sf_step = copier ? kSfSlotCols : 0u;
+      int s = 0, b = 0;
+      uint32_t ph = 0, aph = 0;
+      bool issued = false, ok = true;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const Item m = get_item(p, item);
+        if (!mbar_wait(&ctrl->acc_empty[b], aph ^ 1u, abort)) {
           ok = false;
           break;
         }
-        if (kt % P != ip) {
-          if (lane == 0) mbar_arrive(&ctrl->empty[s]);
-          __syncwarp();
-          continue;
-        }
         tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sw = smem_u32(smem + s * pl.stage_bytes);
-          const bool first = (kt < P);  // first stage of this issuer's chain in the item
-          const uint32_t d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
-          uint32_t col_sfw, col_sfx;
-          if (copier) {
-            col_sfw = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 4u * iu;
-            col_sfx = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s) + 8u;
+        const uint32_t d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
+        const uint32_t id0 = idesc_mxf8f6f4(m.n, 0);
+        int par = 0;  // kt % P
+        for (int kt = 0; kt < KT; ++kt) {
+          // Every issuer observes every phase of every full barrier and arrives on
+          // the matching empty barrier, including for the stages the other parity
+          // consumes.  A parity wait that skipped phases could match the phase two
+          // fills back and read a stage before it lands; requiring every issuer's
+          // arrival before a refill keeps all of them within one phase of the ring.
+          if (!mbar_wait(copier ? &ctrl->sf_ready[s] : &ctrl->full[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          if (par != ip) {
+            mbar_arrive(&ctrl->empty[s]);
           } else {
-            col_sfw = tmem + sf_base + 8u * issuer;
-            col_sfx = col_sfw + 4u;
-            tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
-            tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
-          }
-          const uint32_t a = sw + 16384 * iu, bb = sw + pl.off_b;
+            tc_fence_after();
+            const uint32_t sw = smem_base + static_cast<uint32_t>(s) * stage_bytes;
+            const uint32_t col_sfw = sfw0 + sf_step * static_cast<uint32_t>(s);
+            const uint32_t col_sfx = sfx0 + sf_step * static_cast<uint32_t>(s);
+            if (!copier) {
+              tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
+              tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
+            }
+            const uint64_t ad = desc_sw128(sw + a_off), bd = desc_sw128(sw + b_off);
+            const uint32_t first = (kt < P) ? 1u : 0u;  // first stage of this issuer's chain in the item
 #pragma unroll
-          for (uint32_t kb = 0; kb < 4; ++kb) {
-            tc_mma_mxf8f6f4(d, desc_sw128(a + kb * 32), desc_sw128(bb + kb * 32), idesc_mxf8f6f4(m.n, kb),
-                            (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
+            for (uint32_t kb = 0; kb < 4; ++kb) {
+              // kb * 32 bytes along K: +2 in the descriptor's 16-byte address units
+              tc_mma_mxf8f6f4(d, ad + 2u * kb, bd + 2u * kb, id0 | (kb << 4) | (kb << 29),
+                              (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
+            }
+            tc_commit(&ctrl->empty[s]);
+            issued = true;
           }
-          tc_commit(&ctrl->empty[s]);
-          issued = true;
+          if (++par == P) par = 0;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-        __syncwarp();
-      }
-      if (!ok) break;
-      if (lane == 0) {
+        if (!ok) break;
         tc_commit(&ctrl->acc_full[b]);
         issued = true;
+        if (++b == nbuf) {
+          b = 0;
+          aph ^= 1u;
+        }
       }
-      __syncwarp();
-    }
-    if (!ok) {
-      if (lane == 0) set_error(p.err, MOSAIC_ERR_TIMEOUT);
-      ctrl->abort = 1;
-    }
-    // Drain: every MMA / copy this warp issued has completed before TMEM is freed.
-    if (lane == 0 && issued) {
-      tc_commit(&ctrl->drain[issuer]);
-      volatile int never = 0;
-      mbar_wait(&ctrl->drain[issuer], 0, &never);
+      if (!ok) {
+        set_error(p.err, MOSAIC_ERR_TIMEOUT);
+        ctrl->abort = 1;
+      }
+      // Drain: every MMA / copy this thread issued has completed before TMEM is freed.
+      if (issued) {
+        tc_commit(&ctrl->drain[issuer]);
+        volatile int never = 0;
+        mbar_wait(&ctrl->drain[issuer], 0, &never);
+      }
     }
     __syncwarp();
   } else if (warp == 12 && copier) {
     // -------------------------------------------------- scale-factor copier
-    int it = 0;
-    bool issued = false, ok = true;
-    for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-      for (int kt = 0; kt < KT; ++kt, ++it) {
-        const int s = it % S;
-        const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
-        if (!mbar_wait(&ctrl->full[s], ph, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sw = smem_u32(smem + s * pl.stage_bytes);
+    if (lane == 0) {
+      const uint32_t smem_base = smem_u32(smem);
+      int s = 0;
+      uint32_t ph = 0;
+      bool issued = false, ok = true;
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&ctrl->full[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sw = smem_base + static_cast<uint32_t>(s) * static_cast<uint32_t>(pl.stage_bytes);
           const uint32_t c0 = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s);
           tc_cp_32x128b_x4(c0, desc_sf(sw + pl.off_sfa));
           tc_cp_32x128b_x4(c0 + 4u, desc_sf(sw + pl.off_sfa + 512));
           tc_cp_32x128b_x4(c0 + 8u, desc_sf(sw + pl.off_sfb));
           tc_commit(&ctrl->sf_ready[s]);
           issued = true;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
-        __syncwarp();
       }
-    }
-    if (!ok) {
-      if (lane == 0) set_error(p.err, MOSAIC_ERR_TIMEOUT);
-      ctrl->abort = 1;
-    }
-    if (lane == 0 && issued) {
-      tc_commit(&ctrl->drain[6]);
-      volatile int never = 0;
-      mbar_wait(&ctrl->drain[6], 0, &never);
+      if (!ok) {
+        set_error(p.err, MOSAIC_ERR_TIMEOUT);
+        ctrl->abort = 1;
+      }
+      if (issued) {
+        tc_commit(&ctrl->drain[6]);
+        volatile int never = 0;
+        mbar_wait(&ctrl->drain[6], 0, &never);
+      }
     }
     __syncwarp();
   } else if (warp >= 2 && warp <= 5) {

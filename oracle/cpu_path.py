@@ -96,6 +96,32 @@ class FP4LinearCPU:
         return y
 
 
+class F32LinearCPU:
+    """y fp32 [M, N] = x fp32 [M, K] against the dequantised MXFP4 matrix
+    (``fp4_linear_f32`` of ``oracle/fp4_linear_port.c``: double accumulation,
+    one rounding).  The oracle's bf16-path linear at V3 sizes, where numpy's
+    dequantise-then-matmul is too slow for tens of experts."""
+
+    def __init__(self):
+        if not PORT_LIB.exists():
+            raise RuntimeError(f"{PORT_LIB} missing: run `python oracle/build.py`")
+        ptr = lambda dt: np.ctypeslib.ndpointer(dt, flags="C_CONTIGUOUS")  # noqa: E731
+        self.lib = ctypes.CDLL(str(PORT_LIB))
+        self.lib.fp4_linear_f32.argtypes = [ptr(np.float32), ptr(np.uint8), ptr(np.float32), ptr(np.float32)] + \
+            [ctypes.c_int] * 3
+        self.lib.fp4_linear_f32.restype = None
+
+    def __call__(self, x: np.ndarray, packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        sw = np.ascontiguousarray(e8m0_to_fp32(scale), dtype=np.float32)
+        m, k = x.shape
+        n = packed.shape[0]
+        y = np.empty((m, n), dtype=np.float32)
+        self.lib.fp4_linear_f32(x, packed, sw, y, m, n, k)
+        return y
+
+
 def _silu(x):
     return F.silu(torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))).numpy()
 

@@ -50,3 +50,38 @@ void fp4_linear_port(const uint8_t *q, const float *sa, const uint8_t *packed, c
     }
   }
 }
+
+/*
+ * fp32-activation linear on the dequantised weights (the bf16 path of the
+ * oracle, mosaicvm/model/layers.py:348-366 on runtime/fp8.py:19-34 weights):
+ * y[m][n] = sum_k x[m][k] * E2M1(code[n][k]) * sw[n][k/32], accumulated in
+ * double and rounded once to fp32 (every product is exact in double).
+ */
+static const float E2M1_F[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
+                                 -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
+
+void fp4_linear_f32(const float *x, const uint8_t *packed, const float *sw, float *y, int M, int N, int K) {
+  const int G = K / 32;
+  #pragma omp parallel
+  {
+    double *wrow = (double *)__builtin_alloca(sizeof(double) * (size_t)K);
+    #pragma omp for schedule(static)
+    for (int n = 0; n < N; n++) {
+      const uint8_t *pw = packed + (size_t)n * (K / 2);
+      for (int g = 0; g < G; g++) {
+        const double s = (double)sw[(size_t)n * G + g];
+        for (int i = 0; i < 16; i++) {
+          const uint8_t b = pw[g * 16 + i];
+          wrow[g * 32 + 2 * i] = (double)E2M1_F[b & 0xF] * s;
+          wrow[g * 32 + 2 * i + 1] = (double)E2M1_F[b >> 4] * s;
+        }
+      }
+      for (int m = 0; m < M; m++) {
+        const float *xr = x + (size_t)m * K;
+        double acc = 0.0;
+        for (int k = 0; k < K; k++) acc += (double)xr[k] * wrow[k];
+        y[(size_t)m * N + n] = (float)acc;
+      }
+    }
+  }
+}

@@ -47,33 +47,46 @@ def _swiglu(gate, up, w, limit: float):
     return (z * w[:, None].astype(np.float32)).astype(np.float32)
 
 
+def _linear_f32(x, packed, scale, fast):
+    if fast is not None:
+        return fast(x, packed, scale)
+    return (x.astype(np.float32) @ dequant_fp4(packed, scale).T).astype(np.float32)
+
+
 def expert_bf16(x, gu_packed, gu_scale, dn_packed, dn_scale, w, limit: float,
-                shared: bool = False) -> np.ndarray:
-    """One expert on bf16 activations x [M, H] (fp32 values of bf16) -> fp32 [M, H]."""
+                shared: bool = False, fast=None) -> np.ndarray:
+    """One expert on bf16 activations x [M, H] (fp32 values of bf16) -> fp32 [M, H].
+    ``fast``: an ``oracle.cpu_path.F32LinearCPU`` for the two linears (the same
+    products summed in double instead of numpy's fp32 order)."""
     inter = gu_packed.shape[0] // 2
-    wgu = dequant_fp4(gu_packed, gu_scale)
-    wd = dequant_fp4(dn_packed, dn_scale)
-    gu = (x.astype(np.float32) @ wgu.T).astype(np.float32)
+    gu = _linear_f32(x, gu_packed, gu_scale, fast)
     if shared:
         gu = to_bf16(gu)
     z = _swiglu(gu[:, :inter], gu[:, inter:], w, limit)
     zd = to_bf16(z)
-    y = (zd @ wd.T).astype(np.float32)
+    y = _linear_f32(zd, dn_packed, dn_scale, fast)
     return to_bf16(y) if shared else y
 
 
-def expert_fp8(xq, xs, gu_packed, gu_scale, dn_packed, dn_scale, w, limit: float) -> np.ndarray:
-    """One expert on E4M3 activations (bytes [M, H], pow2 scales [M, H/128]) -> bf16-valued fp32 [M, H]."""
+def _linear_src(q, s, packed, scale, fast):
+    if fast is not None:
+        return fast(q, s, fast.prepare(packed, scale))
+    return fp4_linear_source(q, s, packed, scale)
+
+
+def expert_fp8(xq, xs, gu_packed, gu_scale, dn_packed, dn_scale, w, limit: float, fast=None) -> np.ndarray:
+    """One expert on E4M3 activations (bytes [M, H], pow2 scales [M, H/128]) -> bf16-valued fp32 [M, H].
+    ``fast``: an ``oracle.cpu_path.FP4LinearCPU`` (bit-equal to ``fp4_linear_source``)."""
     inter = gu_packed.shape[0] // 2
-    gu = to_bf16(fp4_linear_source(xq, xs, gu_packed, gu_scale))
+    gu = to_bf16(_linear_src(xq, xs, gu_packed, gu_scale, fast))
     z = _swiglu(gu[:, :inter], gu[:, inter:], w, limit)
     zd = to_bf16(z)
     zq, zs = act_quant_ref(zd)
-    return to_bf16(fp4_linear_source(zq, zs, dn_packed, dn_scale))
+    return to_bf16(_linear_src(zq, zs, dn_packed, dn_scale, fast))
 
 
 def moe_layer(x, weights, idx, bank: dict, *, mode: str = "bf16", swiglu_limit: float = 0.0,
-              with_shared: bool = True, return_parts: bool = False):
+              with_shared: bool = True, return_parts: bool = False, fast: bool = False):
     """x [T, H] (bf16 values as fp32 or a bf16 tensor), weights fp32 [T, k], idx [T, k].
 
     bank: dict of numpy uint8 arrays ``gu_packed [E, 2I, H/2]``,
@@ -81,7 +94,14 @@ def moe_layer(x, weights, idx, bank: dict, *, mode: str = "bf16", swiglu_limit: 
     and, with ``with_shared``, ``sh_gu_packed [2I, H/2]``, ``sh_gu_scale``,
     ``sh_dn_packed [H, I/2]``, ``sh_dn_scale``.
     Returns the bf16-valued fp32 output [T, H] (and the parts if asked).
+    ``fast`` runs the linears in the C checkers of ``oracle/cpu_path.py``
+    (V3 sizes: the FP8 path bit-equal, the bf16 path summed in double).
     """
+    lin = None
+    if fast:
+        from .cpu_path import F32LinearCPU, FP4LinearCPU
+
+        lin = F32LinearCPU() if mode == "bf16" else FP4LinearCPU("port")
     if isinstance(x, torch.Tensor):
         x = x.detach().to(torch.float32).cpu().numpy()
     x = np.ascontiguousarray(x, dtype=np.float32)
@@ -97,9 +117,9 @@ def moe_layer(x, weights, idx, bank: dict, *, mode: str = "bf16", swiglu_limit: 
         w = weights[tok, slot]
         args = (bank["gu_packed"][e], bank["gu_scale"][e], bank["dn_packed"][e], bank["dn_scale"][e])
         if mode == "bf16":
-            y = expert_bf16(x[tok], *args, w, swiglu_limit)
+            y = expert_bf16(x[tok], *args, w, swiglu_limit, fast=lin)
         elif mode == "fp8":
-            y = expert_fp8(xq[tok], xs[tok], *args, w, swiglu_limit)
+            y = expert_fp8(xq[tok], xs[tok], *args, w, swiglu_limit, fast=lin)
         else:
             raise ValueError(f"unknown mode {mode}")
         partials[tok, slot] = y
@@ -113,9 +133,9 @@ def moe_layer(x, weights, idx, bank: dict, *, mode: str = "bf16", swiglu_limit: 
     one = np.ones(t, dtype=np.float32)
     sargs = (bank["sh_gu_packed"], bank["sh_gu_scale"], bank["sh_dn_packed"], bank["sh_dn_scale"])
     if mode == "bf16":
-        shared = expert_bf16(x, *sargs, one, swiglu_limit, shared=True)
+        shared = expert_bf16(x, *sargs, one, swiglu_limit, shared=True, fast=lin)
     else:
-        shared = expert_fp8(xq, xs, *sargs, one, swiglu_limit)
+        shared = expert_fp8(xq, xs, *sargs, one, swiglu_limit, fast=lin)
     out = to_bf16(shared + routed)
     if return_parts:
         return out, partials, routed, shared

@@ -45,3 +45,28 @@ def test_cpu_linear_matches_oracle_fp32(kind):
     y = lin(q, sa, lin.prepare(p, s))
     ref = fm.fp4_linear_source(q, sa, p, s)
     assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.skipif(not PORT_LIB.exists(), reason="oracle C checkers not built")
+def test_fast_oracle_layer_matches_numpy_oracle():
+    """moe_layer(fast=True) (the C linears used at V3 sizes) against the numpy
+    oracle pinned to the reference goldens: FP8 path bit-equal, bf16 path
+    within fp32 summation-order noise."""
+    import torch
+
+    from oracle.moe import moe_layer
+    from tests.golden.recipes import MOE_CASES, make_moe_case
+    from tests.helpers import pack_case, rel_l2
+
+    case = make_moe_case(**MOE_CASES["S"])
+    obank, _ = pack_case(case)
+    c = case["cfg"]
+    for mode in ("fp8", "bf16"):
+        a = moe_layer(case["x"], case["weights"], case["idx"], obank, mode=mode, swiglu_limit=c["swiglu_limit"])
+        b = moe_layer(case["x"], case["weights"], case["idx"], obank, mode=mode, swiglu_limit=c["swiglu_limit"],
+                      fast=True)
+        if mode == "fp8":
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        else:
+            assert rel_l2(b, a) < 1e-3
+    assert isinstance(case["x"], torch.Tensor)
