@@ -72,7 +72,10 @@ struct Ctrl {
   uint64_t sf_ready[kMaxStages];
   uint32_t tmem_base;
   int abort;
-  float red[4][16];
+  float4 red4[2][16];  // gate/up act_quant: column maxima of the four epilogue warps, two blocks
+  float meta_w[128];   // gate/up: route weight of each row of the item's token tile
+  int meta_o[128];     // down: output row (EP: row in the source's return buffer)
+  int meta_r[128];     // down, EP: source rank of the row
 };
 
 // Per stage: the two 16 KB (unpacked) weight tiles of the pair for one
@@ -82,8 +85,8 @@ struct Plan {
   int stage_bytes, off_b, off_sfa, off_sfb, stages, epi;
 };
 
-__host__ __device__ inline Plan make_plan(int planes, int brows) {
-  Plan pl;
+__host__ __device__ constexpr Plan make_plan(int planes, int brows) {
+  Plan pl{};
   pl.off_b = 32768;
   pl.off_sfa = pl.off_b + ((planes * brows * 128 + 1023) / 1024) * 1024;
   pl.off_sfb = pl.off_sfa + 1024;
@@ -95,6 +98,16 @@ __host__ __device__ inline Plan make_plan(int planes, int brows) {
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of the four epilogue warps that also ANDs a predicate over them.
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
 
 // 4-D tensor load (activation rows: {128 B, rows, planes, K-tiles}).
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
@@ -126,6 +139,56 @@ __device__ __forceinline__ void tmem_sum16(uint32_t taddr, int C, uint32_t acc_w
   }
 }
 
+// tmem_sum16 of two column groups (the pair's blocks, half_off apart), with all
+// loads of a chain issued before one wait.
+__device__ __forceinline__ void tmem_sum16x2(uint32_t taddr, uint32_t half_off, int C, uint32_t acc_w, int lo_off,
+                                             float (&out0)[16], float (&out1)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) out0[j] = out1[j] = 0.f;
+  for (int c = 0; c < C; ++c) {
+    uint32_t r0[16], r1[16];
+    tmem_ld16(taddr + c * acc_w, r0);
+    tmem_ld16(taddr + half_off + c * acc_w, r1);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      out0[j] += __uint_as_float(r0[j]);
+      out1[j] += __uint_as_float(r1[j]);
+    }
+    if (lo_off) {
+      tmem_ld16(taddr + c * acc_w + lo_off, r0);
+      tmem_ld16(taddr + half_off + c * acc_w + lo_off, r1);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        out0[j] += __uint_as_float(r0[j]);
+        out1[j] += __uint_as_float(r1[j]);
+      }
+    }
+  }
+}
+
+// Maximum over the warp of each of 16 per-lane values by a transposed
+// butterfly (16 shuffles instead of 80): lane l returns the maximum of value
+// (l >> 1) & 15; both lanes of a pair hold it.
+__device__ __forceinline__ float warp_colmax16(const float (&in)[16]) {
+  const int lane = threadIdx.x & 31;
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = in[i];
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {  // 16 -> 8 -> 4 -> 2 -> 1 values per lane
+    const bool up = (lane & (2 * w)) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? v[i] : v[i + w];
+      const float keep = up ? v[i + w] : v[i];
+      v[i] = fmaxf(keep, __shfl_xor_sync(0xFFFFFFFFu, send, 2 * w));
+    }
+  }
+  return fmaxf(v[0], __shfl_xor_sync(0xFFFFFFFFu, v[0], 1));
+}
+
 // Word index, inside a 512-byte scale chunk, of token row n (< 128).
 __device__ __forceinline__ int sf_word(int n) { return (n & 31) * 4 + (n >> 5); }
 
@@ -147,15 +210,20 @@ __device__ __forceinline__ Item get_item(const GemmParams& p, int item) {
   return it;
 }
 
-template <int NT>
+// The ring layout is a compile-time constant of each instance (planes x token
+// rows per tile), so the issuer and copier loops, unrolled over the ring, give
+// every tcgen05 instruction its shared-memory and TMEM operands as immediate
+// offsets from per-kernel bases.
+template <int NT, int PLANES, int BROWS>
 __global__ void __launch_bounds__(NT, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int planes = p.hilo ? 2 : 1;
-  const Plan pl = make_plan(planes, p.brows);
-  const int S = pl.stages;
+  constexpr int planes = PLANES;
+  constexpr Plan pl = make_plan(PLANES, BROWS);
+  constexpr int S = pl.stages;
+  static_assert(S >= 2 && S <= kMaxStages, "ring");
   uint8_t* epi = smem + pl.epi;
   Ctrl* ctrl = reinterpret_cast<Ctrl*>(epi + kEpiBytes);
   const int warp = threadIdx.x >> 5;
@@ -171,7 +239,7 @@ __global__ void __launch_bounds__(NT, 1)
   const uint32_t acc_w = static_cast<uint32_t>(2 * p.max_n);
   const uint32_t half_off = static_cast<uint32_t>(p.max_n);
   constexpr bool copier = (NT == kThreadsCopier);
-  const uint32_t sf_base = kTmemCols - (copier ? kSfSlotCols * static_cast<uint32_t>(S) : kSfIssuerCols);
+  constexpr uint32_t sf_base = kTmemCols - (copier ? kSfSlotCols * static_cast<uint32_t>(S) : kSfIssuerCols);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -270,162 +338,207 @@ __global__ void __launch_bounds__(NT, 1)
     __syncwarp();
   } else if ((warp == 1 || warp >= 7) && (warp == 1 ? 0 : warp - 6) < 2 * P) {
     // ----------------------------------------------------------------- MMA
-    if (lane == 0) {
+    // The whole warp runs the loop (warp-uniform operands); elect.sync inside
+    // each tcgen05 instruction picks the issuing lane.
+    {
       const int issuer = (warp == 1) ? 0 : warp - 6;  // 0 .. 2P-1
       const int ip = issuer >> 1;                     // stage parity this issuer takes
       const int iu = issuer & 1;                      // unit: block of the pair
       const uint32_t smem_base = smem_u32(smem);
-      const uint32_t stage_bytes = static_cast<uint32_t>(pl.stage_bytes);
-      const uint32_t a_off = 16384u * static_cast<uint32_t>(iu);
-      const uint32_t b_off = static_cast<uint32_t>(pl.off_b);
+      // descriptors of ring stage 0; stage s adds s * stage_bytes (16-byte units)
+      const uint64_t ad0 = desc_sw128(smem_base + 16384u * static_cast<uint32_t>(iu));
+      const uint64_t bd0 = desc_sw128(smem_base + static_cast<uint32_t>(pl.off_b));
       // scale-factor columns of ring stage 0 (copier) or of this issuer (no copier)
       const uint32_t sfw0 = copier ? tmem + sf_base + 4u * iu : tmem + sf_base + 8u * issuer;
       const uint32_t sfx0 = copier ? tmem + sf_base + 8u : tmem + sf_base + 8u * issuer + 4u;
-      const uint32_t sf_step = copier ? kSfSlotCols : 0u;
-      int s = 0, b = 0;
-      uint32_t ph = 0, aph = 0;
-      bool issued = false, ok = true;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-        const Item m = get_item(p, item);
-        if (!mbar_wait(&ctrl->acc_empty[b], aph ^ 1u, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
-        const uint32_t id0 = idesc_mxf8f6f4(m.n, 0);
-        int par = 0;  // kt % P
-        for (int kt = 0; kt < KT; ++kt) {
+      constexpr uint32_t sf_step = copier ? kSfSlotCols : 0u;
+      int item = blockIdx.x, b = 0, kt = 0, par = 0;
+      uint32_t ph = 0, aph = 0, d = 0, id0 = 0;
+      bool issued = false, ok = true, live = false, done = false;
+      while (!done && ok) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+          if (!live) {  // next work item: its accumulator buffer must be free
+            if (item >= n_items) {
+              done = true;
+              break;
+            }
+            const Item m = get_item(p, item);
+            if (!mbar_wait_warp(&ctrl->acc_empty[b], aph ^ 1u, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d = tmem + static_cast<uint32_t>(b * P + ip) * acc_w + (iu ? half_off : 0u);
+            id0 = idesc_mxf8f6f4(m.n, 0);
+            kt = 0;
+            par = 0;
+            live = true;
+          }
           // Every issuer observes every phase of every full barrier and arrives on
           // the matching empty barrier, including for the stages the other parity
           // consumes.  A parity wait that skipped phases could match the phase two
           // fills back and read a stage before it lands; requiring every issuer's
           // arrival before a refill keeps all of them within one phase of the ring.
-          if (!mbar_wait(copier ? &ctrl->sf_ready[s] : &ctrl->full[s], ph, abort)) {
+          if (!mbar_wait_warp(copier ? &ctrl->sf_ready[s] : &ctrl->full[s], ph, abort)) {
             ok = false;
             break;
           }
           if (par != ip) {
-            mbar_arrive(&ctrl->empty[s]);
+            mbar_arrive_elect(&ctrl->empty[s]);
           } else {
             tc_fence_after();
-            const uint32_t sw = smem_base + static_cast<uint32_t>(s) * stage_bytes;
             const uint32_t col_sfw = sfw0 + sf_step * static_cast<uint32_t>(s);
             const uint32_t col_sfx = sfx0 + sf_step * static_cast<uint32_t>(s);
             if (!copier) {
-              tc_cp_32x128b_x4(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
-              tc_cp_32x128b_x4(col_sfx, desc_sf(sw + pl.off_sfb));
+              const uint32_t sw = smem_base + static_cast<uint32_t>(s * pl.stage_bytes);
+              tc_cp_32x128b_x4_elect(col_sfw, desc_sf(sw + pl.off_sfa + 512 * iu));
+              tc_cp_32x128b_x4_elect(col_sfx, desc_sf(sw + pl.off_sfb));
             }
-            const uint64_t ad = desc_sw128(sw + a_off), bd = desc_sw128(sw + b_off);
+            const uint64_t so = static_cast<uint64_t>((s * pl.stage_bytes) >> 4);
             const uint32_t first = (kt < P) ? 1u : 0u;  // first stage of this issuer's chain in the item
 #pragma unroll
             for (uint32_t kb = 0; kb < 4; ++kb) {
               // kb * 32 bytes along K: +2 in the descriptor's 16-byte address units
-              tc_mma_mxf8f6f4(d, ad + 2u * kb, bd + 2u * kb, id0 | (kb << 4) | (kb << 29),
-                              (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
+              tc_mma_mxf8f6f4_elect(d, ad0 + so + 2u * kb, bd0 + so + 2u * kb, id0 | (kb << 4) | (kb << 29),
+                                    (first && kb == 0) ? 0u : 1u, col_sfw | (kb << 30), col_sfx | (kb << 30));
             }
-            tc_commit(&ctrl->empty[s]);
+            tc_commit_elect(&ctrl->empty[s]);
             issued = true;
           }
           if (++par == P) par = 0;
-          if (++s == S) {
-            s = 0;
-            ph ^= 1u;
+          if (++kt == KT) {  // item done: its accumulators go to the epilogue
+            tc_commit_elect(&ctrl->acc_full[b]);
+            issued = true;
+            if (++b == nbuf) {
+              b = 0;
+              aph ^= 1u;
+            }
+            live = false;
+            item += gridDim.x;
           }
         }
-        if (!ok) break;
-        tc_commit(&ctrl->acc_full[b]);
-        issued = true;
-        if (++b == nbuf) {
-          b = 0;
-          aph ^= 1u;
-        }
+        ph ^= 1u;
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         set_error(p.err, MOSAIC_ERR_TIMEOUT);
         ctrl->abort = 1;
       }
-      // Drain: every MMA / copy this thread issued has completed before TMEM is freed.
+      // Drain: every MMA / copy this warp issued has completed before TMEM is freed.
       if (issued) {
-        tc_commit(&ctrl->drain[issuer]);
+        tc_commit_elect(&ctrl->drain[issuer]);
         volatile int never = 0;
-        mbar_wait(&ctrl->drain[issuer], 0, &never);
+        mbar_wait_warp(&ctrl->drain[issuer], 0, &never);
       }
     }
     __syncwarp();
   } else if (warp == 12 && copier) {
     // -------------------------------------------------- scale-factor copier
-    if (lane == 0) {
+    {
       const uint32_t smem_base = smem_u32(smem);
-      int s = 0;
+      const uint64_t sd0 = desc_sf(smem_base + static_cast<uint32_t>(pl.off_sfa));
+      const uint64_t xd0 = desc_sf(smem_base + static_cast<uint32_t>(pl.off_sfb));
+      int item = blockIdx.x, kt = 0;
       uint32_t ph = 0;
-      bool issued = false, ok = true;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-        for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&ctrl->full[s], ph, abort)) {
+      bool issued = false, ok = true, done = item >= n_items;
+      while (!done && ok) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+          if (!mbar_wait_warp(&ctrl->full[s], ph, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sw = smem_base + static_cast<uint32_t>(s) * static_cast<uint32_t>(pl.stage_bytes);
+          const uint64_t so = static_cast<uint64_t>((s * pl.stage_bytes) >> 4);
           const uint32_t c0 = tmem + sf_base + kSfSlotCols * static_cast<uint32_t>(s);
-          tc_cp_32x128b_x4(c0, desc_sf(sw + pl.off_sfa));
-          tc_cp_32x128b_x4(c0 + 4u, desc_sf(sw + pl.off_sfa + 512));
-          tc_cp_32x128b_x4(c0 + 8u, desc_sf(sw + pl.off_sfb));
-          tc_commit(&ctrl->sf_ready[s]);
+          tc_cp_32x128b_x4_elect(c0, sd0 + so);
+          tc_cp_32x128b_x4_elect(c0 + 4u, sd0 + so + 32u);  // + 512 bytes
+          tc_cp_32x128b_x4_elect(c0 + 8u, xd0 + so);
+          tc_commit_elect(&ctrl->sf_ready[s]);
           issued = true;
-          if (++s == S) {
-            s = 0;
-            ph ^= 1u;
+          if (++kt == KT) {
+            kt = 0;
+            item += gridDim.x;
+            if (item >= n_items) {
+              done = true;
+              break;
+            }
           }
         }
+        ph ^= 1u;
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         set_error(p.err, MOSAIC_ERR_TIMEOUT);
         ctrl->abort = 1;
       }
       if (issued) {
-        tc_commit(&ctrl->drain[6]);
+        tc_commit_elect(&ctrl->drain[6]);
         volatile int never = 0;
-        mbar_wait(&ctrl->drain[6], 0, &never);
+        mbar_wait_warp(&ctrl->drain[6], 0, &never);
       }
     }
     __syncwarp();
   } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------ epilogue
+    // Warp w reads TMEM lanes 32*(w%4).. (weight rows); each thread holds one
+    // weight row of 16 token columns at a time.  Per item, the rows' route
+    // weights (gate/up) or output rows (down) are loaded into shared memory
+    // once; per 16-column block, column maxima use transposed butterflies and
+    // the staging buffers alternate between blocks, so a gate/up block takes
+    // two named barriers.
     const int q = warp & 3;
     const int lrow = q * 32 + lane;
     const int et = threadIdx.x - 64;  // 0..127: this thread's index among the epilogue warps
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const size_t z_plane = static_cast<size_t>(p.R_pad) * 128;    // bytes per (K-tile, plane) of z rows
     const size_t z_ktile = static_cast<size_t>(planes) * z_plane;  // bytes per K-tile of z rows
-    float* stage_f = reinterpret_cast<float*>(epi);                // [16 tokens][256 values]
-    uint8_t* stage_b = epi;                                        // [planes][16 tokens][128 B]
+    float* stage_f = reinterpret_cast<float*>(epi);                // down: [16 tokens][256 values]
     const int P_used = KT < P ? KT : P;                            // chains that received MMAs
-    int li = 0;
+    int li = 0, blk = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
       const Item m = get_item(p, item);
       const bool round_mid = p.fp8 || (m.e == p.shared_expert);
       const int b = li % nbuf;
       const uint32_t aph = static_cast<uint32_t>(li / nbuf) & 1u;
-      if (!mbar_wait(&ctrl->acc_full[b], aph, abort)) {
-        if (lane == 0) set_error(p.err, MOSAIC_ERR_TIMEOUT);
-        ctrl->abort = 1;
+      // row metadata of the item (read by every warp after the barrier below)
+      if (et < m.rows) {
+        const int r = m.row0 + et;
+        if (gu) {
+          ctrl->meta_w[et] = p.row_weight[r];
+        } else {
+          const int orow = p.out_row ? p.out_row[r] : r;
+          if (p.ep_world) {  // receive row orow of source s goes to s's send position of it
+            int sr = 0;
+            while (sr + 1 < p.ep_world && orow >= p.ep_recv_start[sr + 1]) ++sr;
+            ctrl->meta_r[et] = sr;
+            ctrl->meta_o[et] = p.ep_src_pos[sr] + orow - p.ep_recv_start[sr];
+          } else {
+            ctrl->meta_o[et] = orow;
+          }
+        }
+      }
+      // every epilogue warp takes the same branch (a warp that left while the
+      // others wait at a named barrier would hold them there)
+      if (!epi_all(mbar_wait_warp(&ctrl->acc_full[b], aph, abort))) {  // also makes the metadata visible
+        if (lane == 0) {
+          set_error(p.err, MOSAIC_ERR_TIMEOUT);
+          ctrl->abort = 1;
+        }
         break;
       }
       tc_fence_after();
       const uint32_t c_buf = static_cast<uint32_t>(b * P) * acc_w;
       const int lo = p.hilo ? m.rpad : 0;
-      for (int c0 = 0; c0 < m.rpad; c0 += 16) {
+      for (int c0 = 0; c0 < m.rpad; c0 += 16, ++blk) {
         float s0[16], s1[16];
-        tmem_sum16(tq + c_buf + c0, P_used, acc_w, lo, s0);
-        tmem_sum16(tq + c_buf + half_off + c0, P_used, acc_w, lo, s1);
+        tmem_sum16x2(tq + c_buf + c0, half_off, P_used, acc_w, lo, s0, s1);
         const int ncol = min(16, m.rows - c0);  // token columns of this block that exist
         if (gu) {
+          uint8_t* stage_b = epi + (blk & 1) * 4096;  // [planes][16 tokens][128 B], alternating
+          float4* red = ctrl->red4[blk & 1];
           float zd[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int col = c0 + j;
             float gv = s0[j];
             float uv = s1[j];
             if (round_mid) {
@@ -436,7 +549,7 @@ __global__ void __launch_bounds__(NT, 1)
               gv = fminf(gv, p.swiglu_limit);
               uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
             }
-            const float w = (j < ncol) ? p.row_weight[m.row0 + col] : 0.f;
+            const float w = (j < ncol) ? ctrl->meta_w[c0 + j] : 0.f;
             float z = gv / (1.0f + expf(-gv)) * uv;
             z = z * w;
             zd[j] = (j < ncol) ? bf16r(z) : 0.f;
@@ -444,39 +557,56 @@ __global__ void __launch_bounds__(NT, 1)
           // quantised bytes staged as [plane][token][128 B] (this thread: byte lrow)
           uint32_t* zsf = p.z_sft + (static_cast<size_t>(m.tile) * (p.I / 128) + m.nb) * 128;
           if (p.fp8) {
+            // act_quant per 128 rows: column maxima of the four warps meet in shared memory
+            float a[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float mx = warp_max(fabsf(zd[j]));
-              if (lane == 0) ctrl->red[q][j] = mx;
-            }
+            for (int j = 0; j < 16; ++j) a[j] = fabsf(zd[j]);
+            const float cm = warp_colmax16(a);
+            if ((lane & 1) == 0) reinterpret_cast<float*>(&red[(lane >> 1) & 15])[q] = cm;
             epi_bar();
+            int my_ex = 0;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float amax =
-                  fmaxf(fmaxf(ctrl->red[0][j], ctrl->red[1][j]), fmaxf(ctrl->red[2][j], ctrl->red[3][j]));
+              const float4 r4 = red[j];
+              const float amax = fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w));
               const int ex = pow2_scale_exp(amax, 1e-4f);
+              if (j == lrow) my_ex = ex;
               const float y = fminf(fmaxf(zd[j] * exp2i(-ex), -448.f), 448.f);
               stage_b[j * 128 + lrow] = f32_to_e4m3(y);
-              if (lrow == 0 && j < ncol) zsf[sf_word(c0 + j)] = (static_cast<uint32_t>(ex + 127) & 0xFFu) * 0x01010101u;
             }
+            if (lrow < ncol) zsf[sf_word(c0 + lrow)] = (static_cast<uint32_t>(my_ex + 127) & 0xFFu) * 0x01010101u;
           } else {
+            // hi + lo planes with per-32-row (per-warp) scales
+            float a[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) a[j] = fabsf(zd[j]);
+            const float cm = warp_colmax16(a);
+            float res[16];
+            int eh[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float mx = warp_max(fabsf(zd[j]));
-              int eh = pow2_scale_exp(mx, 1e-30f);
-              eh = max(-126, min(127, eh));
-              const uint8_t hb = f32_to_e4m3(zd[j] * exp2i(-eh));
-              const float res = zd[j] - e4m3_to_f32(hb) * exp2i(eh);
-              const float m2 = warp_max(fabsf(res));
-              int el = pow2_scale_exp(m2, fmaxf(mx * 1e-7f, 1e-30f));
-              el = max(-126, min(127, el));
-              const uint8_t lb = f32_to_e4m3(res * exp2i(-el));
+              const float mx = __shfl_sync(0xFFFFFFFFu, cm, 2 * j);
+              eh[j] = max(-126, min(127, pow2_scale_exp(mx, 1e-30f)));
+              const uint8_t hb = f32_to_e4m3(zd[j] * exp2i(-eh[j]));
+              res[j] = zd[j] - e4m3_to_f32(hb) * exp2i(eh[j]);
               stage_b[j * 128 + lrow] = hb;
-              stage_b[2048 + j * 128 + lrow] = lb;
-              if (lane == 0 && j < ncol) {
-                reinterpret_cast<uint8_t*>(zsf + sf_word(c0 + j))[q] = static_cast<uint8_t>(eh + 127);
-                reinterpret_cast<uint8_t*>(zsf + sf_word(m.rpad + c0 + j))[q] = static_cast<uint8_t>(el + 127);
-              }
+              a[j] = fabsf(res[j]);
+              s0[j] = mx;  // keep the hi maximum for the lo floor
+            }
+            const float cm2 = warp_colmax16(a);
+            int my_e = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float m2 = __shfl_sync(0xFFFFFFFFu, cm2, 2 * j);
+              const int el = max(-126, min(127, pow2_scale_exp(m2, fmaxf(s0[j] * 1e-7f, 1e-30f))));
+              stage_b[2048 + j * 128 + lrow] = f32_to_e4m3(res[j] * exp2i(-el));
+              if ((lane & 15) == j) my_e = (lane < 16) ? eh[j] : el;
+            }
+            // lane j writes the hi exponent of column j, lane 16 + j the lo one
+            const int jc = lane & 15;
+            if (jc < ncol) {
+              const int col = (lane < 16) ? c0 + jc : m.rpad + c0 + jc;
+              reinterpret_cast<uint8_t*>(zsf + sf_word(col))[q] = static_cast<uint8_t>(my_e + 127);
             }
           }
           epi_bar();
@@ -488,7 +618,7 @@ __global__ void __launch_bounds__(NT, 1)
               *reinterpret_cast<uint4*>(zq + pl_ * z_plane + static_cast<size_t>(m.row0 + c0 + j) * 128 + off) =
                   *reinterpret_cast<const uint4*>(stage_b + pl_ * 2048 + j * 128 + off);
           }
-          epi_bar();  // the staging buffer is rewritten by the next column block
+          // the next block writes the other staging buffer and the other maxima
         } else {
           // partials of the two hidden blocks, staged as [token][256 values]
 #pragma unroll
@@ -510,17 +640,10 @@ __global__ void __launch_bounds__(NT, 1)
             const int per = p.out_f32 ? 32 : 16;
             const int j = v / (2 * per), h = (v / per) & 1, w16 = v % per;
             if (j >= ncol) continue;
-            const int orow = p.out_row ? p.out_row[m.row0 + c0 + j] : m.row0 + c0 + j;
-            uint8_t* row_base;
-            if (p.ep_world) {
-              // receive row orow of source s goes to s's send position of it
-              int sr = 0;
-              while (sr + 1 < p.ep_world && orow >= p.ep_recv_start[sr + 1]) ++sr;
-              row_base = p.ep_regions[sr] + p.ep_ret_off +
-                         static_cast<size_t>(p.ep_src_pos[sr] + orow - p.ep_recv_start[sr]) * p.H * esz;
-            } else {
-              row_base = static_cast<uint8_t*>(p.out) + static_cast<size_t>(orow) * p.H * esz;
-            }
+            const int orow = ctrl->meta_o[c0 + j];
+            uint8_t* row_base = p.ep_world ? p.ep_regions[ctrl->meta_r[c0 + j]] + p.ep_ret_off +
+                                                 static_cast<size_t>(orow) * p.H * esz
+                                           : static_cast<uint8_t*>(p.out) + static_cast<size_t>(orow) * p.H * esz;
             uint4* dst = reinterpret_cast<uint4*>(row_base + static_cast<size_t>(h * hb + m.nb * 128) * esz) + w16;
             const float* src = stage_f + j * 256 + h * 128;
             if (p.out_f32) {
@@ -538,12 +661,12 @@ __global__ void __launch_bounds__(NT, 1)
       }
       tc_fence_before();
       mbar_arrive(&ctrl->acc_empty[b]);
+      epi_bar();  // every warp is done with this item's metadata before the next item's is written
     }
     // partials stored into other ranks' memory are made visible at system
     // scope before the kernel ends (the next kernel stamps their flags)
     if (p.ep_world) __threadfence_system();
   }
-
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -574,7 +697,14 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   const Plan pl = make_plan(planes, p.brows);
   if (pl.stages < 2) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes(planes, p.brows);
-  auto kernel = p.sf_copier ? moe_gemm_kernel<kThreadsCopier> : moe_gemm_kernel<kThreadsPlain>;
+  // the three tile shapes the workspace plans use: E4M3 tiles of 112 rows
+  // (double-buffered), two-plane tiles of 16 rows (double-buffered) and of 32
+  // rows (single-buffered, no copier)
+  void (*kernel)(const CUtensorMap, const CUtensorMap, const GemmParams) = nullptr;
+  if (planes == 1 && p.brows == 112 && p.sf_copier) kernel = moe_gemm_kernel<kThreadsCopier, 1, 112>;
+  if (planes == 2 && p.brows == 16 && p.sf_copier) kernel = moe_gemm_kernel<kThreadsCopier, 2, 16>;
+  if (planes == 2 && p.brows == 32 && !p.sf_copier) kernel = moe_gemm_kernel<kThreadsPlain, 2, 32>;
+  if (!kernel) return cudaErrorInvalidValue;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
