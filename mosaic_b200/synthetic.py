@@ -109,36 +109,67 @@ def make_layer(tokens: int, seed: int = 0, act_mode: str = "bf16", n_experts: in
     return layer, x
 
 
-def zipf_targets(n_experts: int, alpha: float, assignments: int, seed: int) -> np.ndarray:
-    """Per-expert target loads proportional to rank^-alpha, ranks assigned by a seeded permutation."""
+def zipf_targets(n_experts: int, alpha: float, assignments: int, seed: int, cap: float | None = None) -> np.ndarray:
+    """Per-expert target loads proportional to rank^-alpha, ranks assigned by a seeded permutation.
+
+    With ``cap`` (the token count: an expert takes at most one slot of a token)
+    the loads above it are clipped and the excess is spread over the other
+    experts in proportion to their Zipf shares, until none exceeds the cap
+    (Zipf(1.2) over 256 experts asks 25 % of all slots of rank 1, more than
+    one per token at top-8)."""
     rng = np.random.default_rng(seed)
     ranks = rng.permutation(n_experts) + 1
-    p = ranks.astype(np.float64) ** (-alpha)
-    return p / p.sum() * assignments
+    share = ranks.astype(np.float64) ** (-alpha)
+    t = share / share.sum() * assignments
+    if cap is not None:
+        for _ in range(n_experts):
+            over = t > cap
+            if not over.any():
+                break
+            excess = float((t[over] - cap).sum())
+            t[over] = cap
+            free = ~over & (t < cap)
+            t[free] += excess * share[free] / share[free].sum()
+    return t
 
 
-def calibrate_zipf_bias(layer: MoELayer, alpha: float = 1.2, tokens: int = 8192, steps: int = 60,
-                        gamma: float = 2e-3, seed: int = 0) -> dict:
-    """Sign-update the selection bias so per-expert load approaches Zipf(alpha) on a
-    separate calibration batch (b_e += gamma * sign(target_e - load_e)).
-    Returns the final histogram and the fitted exponent."""
-    cfg = layer.cfg
-    dev = layer.router.weight.device
-    xc = make_tokens(tokens, cfg.hidden_size, seed + 1000, dev)
-    target = torch.from_numpy(zipf_targets(cfg.n_routed_experts, alpha, tokens * cfg.num_experts_per_tok, seed)).to(dev)
-    bias = layer.router.e_score_correction_bias.data
-    load = None
-    for _ in range(steps):
-        _, idx = layer.router(xc)
-        load = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).double()
-        bias += gamma * torch.sign(target - load).float()
-    _, idx = layer.router(xc)
-    load = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).double().cpu().numpy()
+def _fit_alpha(load: np.ndarray) -> float:
     srt = np.sort(load)[::-1]
     r = np.arange(1, len(srt) + 1)
     nz = srt > 0
-    slope = np.polyfit(np.log(r[nz]), np.log(srt[nz]), 1)[0] if nz.sum() > 2 else float("nan")
-    return {"load_max": float(srt[0]), "load_min": float(srt[-1]), "fitted_alpha": float(-slope)}
+    return float(-np.polyfit(np.log(r[nz]), np.log(srt[nz]), 1)[0]) if nz.sum() > 2 else float("nan")
+
+
+def calibrate_zipf_bias(layer: MoELayer, alpha: float = 1.2, tokens: int = 8192, steps: int = 300,
+                        seed: int = 0) -> dict:
+    """Fit the selection bias so the per-expert load approaches the clipped
+    Zipf(alpha) target of :func:`zipf_targets` on a separate calibration batch.
+
+    Each step moves b_e by lr_i * clip(log((target_e + 1) / (load_e + 1)), -1, 1),
+    with lr decaying from 0.05 to 0.002: large moves first (the bias has to
+    span about the spread of the sigmoid scores), fine ones last.  Returns the
+    final histogram's summary: fitted exponent, max / min load, the target's
+    maximum and the relative L1 distance sum|load - target| / sum target.
+    """
+    cfg = layer.cfg
+    dev = layer.router.weight.device
+    xc = make_tokens(tokens, cfg.hidden_size, seed + 1000, dev)
+    a = tokens * cfg.num_experts_per_tok
+    target_np = zipf_targets(cfg.n_routed_experts, alpha, a, seed, cap=float(tokens))
+    target = torch.from_numpy(target_np).to(dev)
+    bias = layer.router.e_score_correction_bias.data
+    for i in range(steps):
+        _, idx = layer.router(xc)
+        load = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).double()
+        lr = 0.048 * (0.985 ** i) + 0.002
+        bias += (lr * torch.clamp(torch.log((target + 1.0) / (load + 1.0)), -1.0, 1.0)).float()
+    _, idx = layer.router(xc)
+    load = torch.bincount(idx.reshape(-1), minlength=cfg.n_routed_experts).double().cpu().numpy()
+    return {"alpha": alpha, "target": "Zipf(alpha) clipped at one slot per token, excess re-spread",
+            "load_max": float(load.max()), "load_min": float(load.min()), "target_max": float(target_np.max()),
+            "fitted_alpha": _fit_alpha(load), "target_fitted_alpha": _fit_alpha(target_np),
+            "l1_rel": float(np.abs(load - target_np).sum() / target_np.sum()), "steps": steps,
+            "calibration_tokens": tokens}
 
 
 def bank_to_oracle(bank: ExpertBank, experts) -> dict:

@@ -48,3 +48,23 @@ def rel_l2(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def oracle_subset(layer, x, y, sel, mode):
+    """Relative L2 of the layer output y on the tokens ``sel`` against the CPU
+    oracle, run with the routing the layer used (its last call) on a bank of
+    just the experts those tokens touch (the C linears of oracle/cpu_path.py:
+    V3-size experts in seconds)."""
+    from mosaic_b200 import synthetic
+    from oracle.moe import moe_layer
+
+    sel = np.sort(np.asarray(sel))
+    idx = layer.last_idx[torch.as_tensor(sel, device=layer.last_idx.device)].cpu()
+    w = layer.last_weights[torch.as_tensor(sel, device=layer.last_idx.device)].cpu()
+    experts = np.unique(idx.numpy())
+    obank = synthetic.bank_to_oracle(layer.bank, experts)
+    remap = {int(e): i for i, e in enumerate(experts)}
+    idx_l = torch.tensor([[remap[int(v)] for v in row] for row in idx.numpy()])
+    xs = x[torch.as_tensor(sel, device=x.device)].cpu()
+    ref = moe_layer(xs, w, idx_l, obank, mode=mode, swiglu_limit=layer.cfg.swiglu_limit, fast=True)
+    return rel_l2(y[torch.as_tensor(sel, device=y.device)].float().cpu().numpy(), ref)

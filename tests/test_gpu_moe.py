@@ -7,7 +7,7 @@ Bars (written in each assert):
   follows the reference's integer-exact source semantics, is also held to a
   much tighter 2e-3, and the bf16 mode (hi + lo E4M3 carrying each bf16) to 5e-3;
 * full-size configs (V3 decode T=128, prefill T=2048..8192): the oracle is run on a
-  random subset of tokens (a token's output depends only on that token), plus
+  random subset of 32 tokens (a token's output depends only on that token), plus
   bit-exact token-permutation equivariance and run-to-run determinism.
 """
 from __future__ import annotations
@@ -19,7 +19,7 @@ import torch
 from oracle.moe import moe_layer
 from oracle.router import route_ties
 from tests.golden.recipes import MOE_CASES, make_moe_case
-from tests.helpers import gpu_bank, layer_for, pack_case, rel_l2
+from tests.helpers import gpu_bank, layer_for, oracle_subset, pack_case, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -146,19 +146,10 @@ def _v3_case(t, seed, n_bank_experts=256, act_mode="bf16"):
 
 
 def _oracle_subset(layer, x, y, n_tok, mode, seed):
-    from mosaic_b200 import synthetic
-
+    """Oracle check on n_tok random tokens of the layer's last call."""
     rng = np.random.default_rng(seed)
-    sel = np.sort(rng.choice(x.shape[0], size=min(n_tok, x.shape[0]), replace=False))
-    idx = layer.last_idx[sel].cpu()
-    w = layer.last_weights[sel].cpu()
-    experts = np.unique(idx.numpy())
-    obank = synthetic.bank_to_oracle(layer.bank, experts)
-    # remap expert ids to the subset bank
-    remap = {int(e): i for i, e in enumerate(experts)}
-    idx_l = torch.tensor([[remap[int(v)] for v in row] for row in idx.numpy()])
-    ref = moe_layer(x[sel].cpu(), w, idx_l, obank, mode=mode, swiglu_limit=layer.cfg.swiglu_limit)
-    return rel_l2(y[sel].float().cpu().numpy(), ref)
+    sel = rng.choice(x.shape[0], size=min(n_tok, x.shape[0]), replace=False)
+    return oracle_subset(layer, x, y, sel, mode)
 
 
 @pytest.mark.parametrize("t", [1, 8, 128])
@@ -166,7 +157,7 @@ def test_v3_decode_subset_parity(t):
     layer, x = _v3_case(t, seed=100 + t)
     y = layer(x)
     torch.cuda.synchronize()
-    rel = _oracle_subset(layer, x, y, 6, "bf16", seed=t)
+    rel = _oracle_subset(layer, x, y, 32, "bf16", seed=t)
     assert rel <= TOL["bf16"], rel
 
 
@@ -177,7 +168,7 @@ def test_v3_prefill_subset_parity_and_properties():
     y = layer(x)
     torch.cuda.synchronize()
     assert ops.read_error(layer.workspace(x.shape[0], x.device)) == 0
-    rel = _oracle_subset(layer, x, y, 6, "fp8", seed=3)  # uses the routing of this call
+    rel = _oracle_subset(layer, x, y, 32, "fp8", seed=3)  # uses the routing of this call
     assert rel <= TOL["fp8"], rel
     y2 = layer(x)
     assert torch.equal(y, y2), "run-to-run determinism"
@@ -247,5 +238,5 @@ def test_v4_dims_subset_parity(t, mode):
         else:
             assert np.array_equal(got[ti], i_ref.numpy()[ti]), ti
     assert sel_tie.sum() <= max(1, t // 32)
-    rel = _oracle_subset(layer, x, y, 6, mode, seed=t)
+    rel = _oracle_subset(layer, x, y, 32, mode, seed=t)
     assert rel <= TOL[mode], rel
