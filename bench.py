@@ -1,20 +1,28 @@
 #!/usr/bin/env python
-"""MoE-layer benchmark: tokens/s of one DeepSeek-V3-dimension MoE layer on B200.
+"""MoE-layer benchmark: tokens/s of DeepSeek-V3-dimension MoE layers on B200.
 
-Workload (the one the metric is quoted on): hidden 7168,
-256 routed + 1 shared experts, moe_intermediate 2048, 8 groups / top-4 groups,
-top-8, sigmoid + bias routing, routed_scaling 2.5, MXFP4 experts drawn from
-N(0, 0.02), bf16 tokens ~ N(0, 1), uniform-random router, T = 128 tokens
-(decode).  A step is one full layer (router -> layout -> expert gate/up ->
-down -> combine, shared expert included) replayed from a CUDA graph.  The
-expert weights the step touches (~5.9 GB) are far larger than L2 (126 MB),
-so no L2 flush is needed between steps.
+Headline, at every GPU count N (BASELINE config 4's per-GPU workload): one
+expert-parallel V3 MoE layer step with 4096 FP8 tokens per GPU.  The 256
+routed MXFP4 experts (N(0, 0.02)) are split evenly over the N GPUs (N = 1:
+the whole layer on one GPU, the single-GPU ``MoELayer``), the shared expert is
+replicated, the router is uniform-random.  A step is router -> dispatch
+(N > 1: the device-driven NVLink peer-memory exchange) -> grouped expert GEMMs
+(gate/up + SwiGLU + route weight + act_quant, then down) -> return -> combine,
+replayed from one CUDA graph; ``value`` = 4096 * N / step time (max over
+ranks), weak scaling.  Every step touches the whole layer's expert weights
+(6 GB at N = 1, 0.75 GB per GPU at N = 8) plus ~60 MB of activations per
+GPU, far above the 126 MB L2, so no L2 flush is needed between steps.
 
-Prints ONE JSON line (rank 0).  With N > 1 (torchrun) the layer runs expert
-parallel: each rank holds 256/N routed experts plus the shared expert and its
-own T = 128 tokens (weak scaling), dispatch and combine are NCCL all-to-alls,
-and the time is the max over ranks.  ``--impl reference`` times the reference
-CPU expert path instead.
+Extras in the same line: BASELINE config 2 (decode, T = 128 bf16 tokens, the
+whole layer on one GPU) with its HBM roofline, the decode sweep T in
+{1, 8, 32}, config 3 (prefill, T = 8192 FP8 tokens, router bias fitted to a
+clipped Zipf(1.2) load), the hyper-connection step and the offload step; at
+N > 1 the expert-parallel decode step, the NCCL all-to-all path for
+comparison and (N >= 4) the 58-layer decode stack (config 5).
+
+``--impl reference`` runs the reference's CPU expert path (its AVX-VNNI
+kernel compiled from its own source) on the same seeded layer on the host
+cores, rank 0 only.
 """
 from __future__ import annotations
 
@@ -28,6 +36,7 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
+import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -37,28 +46,60 @@ EXPERT_BYTES = 23_396_352          # MXFP4 codes + E8M0 scales of one V3 expert 
 GU_BYTES = 2 * 2048 * 3584 + 2 * 2048 * 224
 DN_BYTES = 7168 * 1024 + 7168 * 64
 ROUTER_BYTES = 256 * 7168 * 4
-# DRAM traffic / algorithmic bytes of the gate/up launch: dram__bytes_read.sum +
+GU_FLOP_PER_ROW = 2 * (2 * 2048) * 7168   # gate + up rows of one token row
+DN_FLOP_PER_ROW = 2 * 7168 * 2048
+LAYER_FLOP_PER_TOKEN = 9 * (GU_FLOP_PER_ROW + DN_FLOP_PER_ROW)  # 8 routed + 1 shared expert rows
+# DRAM traffic / algorithmic bytes of the decode gate/up launch: dram__bytes_read.sum +
 # dram__bytes_write.sum of one ncu capture of `bench.py --experts 64 --profile-small`
 # (65 experts streamed).  Traffic grows with the number of experts streamed, so the
 # full launch's traffic is this ratio times its algorithmic bytes.
 GU_TRAFFIC_RATIO = (1.0408e9 + 7.37e6) / 1_013_841_920
+HEAD_T = 4096        # tokens per GPU of the headline
+CPU_SAMPLE_T = 512   # tokens per step of the CPU reference path
+SEED = 1234
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; % of HBM / FP4 tensor roofline"
+
+
+def headline_config(world: int) -> dict:
+    """The headline workload; the reference arm reports the same dict."""
+    return {"workload": "BASELINE config 4 per GPU: expert-parallel V3 MoE layer step, 4096 FP8 tokens per GPU, "
+                        "256 routed + 1 shared MXFP4 experts split over the GPUs (N=1: the whole layer on one GPU)",
+            "tokens_per_gpu": HEAD_T, "hidden": 7168, "inter": 2048, "experts": 256, "shared": 1, "top_k": 8,
+            "groups": "8/4", "act": "fp8", "routing": "uniform", "parallelism": f"ep{world}"}
+
+
+def layer_launches(t: int, world: int) -> int:
+    """Kernels one layer step launches (the C ABI's launch sequence).
+
+    Router: tensor-core logits + top-k, plus the W split above 128 tokens.
+    Layout: one CTA up to 1024 assignments, else count / scan / rank / finish.
+    One GPU: router, layout, rows_quant, gate/up, down, combine.  Expert
+    parallel: router, dispatch (layout, pack, destination counts), exchange
+    (counts, send, wait), the shared expert and the received rows (per-row
+    metadata, layout, rows_quant, gate/up, down each), return (signal, wait),
+    combine."""
+    router = 3 if t > 128 else 2
+    lay = lambda a: 4 if a > 1024 else 1  # noqa: E731
+    if world == 1:
+        return router + lay(t * 8) + 4
+    return router + (lay(t * 8) + 2) + 3 + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=400)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["mosaic", "reference"], default="mosaic")
-    p.add_argument("--tokens", type=int, default=128)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--no-extras", action="store_true", help="skip the T sweep and the prefill line")
+    p.add_argument("--no-extras", action="store_true", help="headline only")
     p.add_argument("--experts", type=int, default=256, help="routed experts in the bank (V3: 256)")
-    p.add_argument("--act", choices=["bf16", "fp8"], default="bf16",
-                   help="activation mode of the main layer (bf16: decode configs; fp8: prefill configs)")
+    p.add_argument("--tokens", type=int, default=None, help="tokens of a single-layer run (with --act)")
+    p.add_argument("--act", choices=["bf16", "fp8"], default=None,
+                   help="single-layer run at --tokens in this activation mode instead of the headline "
+                        "(small cases for ncu captures)")
     p.add_argument("--profile-small", action="store_true",
-                   help="small case for ncu captures: no extras, no CPU baseline, 2 profiled stage runs")
+                   help="with --act: no extras, no CPU baseline, 2 profiled stage runs")
     p.add_argument("--hc-only", action="store_true",
                    help="only the hyper-connection pre-mix + RMSNorm timing (prints its JSON; for ncu captures)")
     p.add_argument("--router-only", action="store_true",
@@ -68,6 +109,8 @@ def parse():
 
 
 def peaks():
+    """HBM GB/s, bf16 dense TF/s (measured on this pool when MEASURED_PEAKS.json
+    is present) and the source."""
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
@@ -152,11 +195,13 @@ def timed_graph(graph, steps, warmup, dist_on):
     return ms
 
 
-def check_device_error(layer, t, where):
-    """Fail loudly if a kernel of the timed region recorded an error (e.g. a bounded wait that ran out)."""
+def check_device_error(layer, x, where):
+    """Fail loudly if a kernel of the timed region recorded an error (e.g. a bounded wait that ran out).
+    The workspace is looked up with the device of the layer's own calls (a different
+    device key would allocate a new, uninitialised workspace)."""
     from mosaic_b200 import ops
 
-    code = ops.read_error(layer.workspace(t, torch.device("cuda")))
+    code = ops.read_error(layer.workspace(x.shape[0], x.device))
     if code:
         raise RuntimeError(f"device error {code} recorded during {where}")
 
@@ -232,81 +277,216 @@ def e2e(layer, x, steps, dist_on):
     return ms, xh.numel() * xh.element_size(), yh.numel() * yh.element_size()
 
 
-def cpu_baseline(layer, x, idx, w, n_sample=16, seed=0):
-    import numpy as np
 
+
+def fp8_roofline(gemm_ms: float, rows: int, tf_peak: float, peak_src: str) -> dict:
+    """Gate/up launch against the tensor-core peak.  kind::mxf8f6f4 (E2M1 x E4M3)
+    runs at the FP8 rate, twice the bf16 rate: the denominator is twice the
+    measured dense bf16 peak (cuBLAS, MEASURED_PEAKS.json)."""
+    flops = rows * GU_FLOP_PER_ROW
+    achieved = flops / (gemm_ms * 1e-3) / 1e12
+    peak = 2.0 * tf_peak
+    return {"kernel": "moe_gemm_kernel (gate/up + SwiGLU + act_quant, tcgen05 kind::mxf8f6f4 block-scaled)",
+            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": None, "algorithmic_flops": flops,
+            "peak_source": f"2 x {peak_src} dense bf16 ({tf_peak:.1f} TF/s): the FP8 MMA rate is twice the bf16 rate",
+            "frac_of_nominal_fp8_4500": achieved / 4500.0, "frac_of_nominal_fp4_9000": achieved / 9000.0}
+
+
+def cpu_layer_baseline(layer, x, y_gpu, *, n_tok=CPU_SAMPLE_T, steps=2, warmup=1) -> dict:
+    """The reference CPU expert path on the first n_tok tokens of x, through the
+    whole layer (every touched expert, no extrapolation), timed on the host
+    cores; its output is checked against the GPU's."""
     from mosaic_b200 import synthetic
-    from oracle.cpu_path import time_layer_sample
+    from oracle.cpu_path import LayerCPU, _cpu_model
 
-    rng = np.random.default_rng(seed)
-    touched = np.unique(idx.cpu().numpy())
-    sample = np.sort(rng.choice(touched, size=min(n_sample, len(touched)), replace=False))
-    bank = synthetic.bank_to_oracle(layer.bank, sample)
-    bank["experts"] = sample
+    torch.set_num_threads(os.cpu_count() or 1)
+    bank = synthetic.bank_to_oracle(layer.bank, np.arange(layer.cfg.n_routed_experts))
+    cpu = LayerCPU(bank)
+    del bank
+    xs = x[:n_tok].cpu()
+    rw = layer.router.weight.data.cpu()
+    rb = layer.router.e_score_correction_bias.data.cpu()
     c = layer.cfg
-    r = time_layer_sample(x.cpu(), layer.router.weight.data.cpu(), layer.router.e_score_correction_bias.data.cpu(),
-                          bank, idx.cpu().numpy(), w.cpu().numpy(), top_k=c.num_experts_per_tok, n_group=c.n_group,
-                          topk_group=c.topk_group, route_scale=c.routed_scaling_factor, n_sample=len(sample))
-    r["sample"] = (f"T={x.shape[0]} tokens, router on all tokens, {len(sample)} of {r['distinct_experts']} touched "
-                   f"experts timed on their own tokens (+ shared expert on all tokens), best of {r['reps']} reps, "
-                   f"scaled to the full layer; FP8-activation semantics (VNNI consumes E4M3)")
-    return r
+    kw = dict(top_k=c.num_experts_per_tok, n_group=c.n_group, topk_group=c.topk_group,
+              route_scale=c.routed_scaling_factor, limit=c.swiglu_limit)
+    for _ in range(warmup):
+        cpu.step(xs, rw, rb, **kw)
+    secs, y = [], None
+    for _ in range(steps):
+        y, s, _ = cpu.step(xs, rw, rb, **kw)
+        secs.append(s)
+    sec = statistics.mean(secs)
+    yg = y_gpu[:n_tok].float().cpu().numpy()
+    rel = float(np.linalg.norm(yg - y) / max(np.linalg.norm(y), 1e-30))
+    return {"value": n_tok / sec, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": cpu.kind,
+            "sample": (f"{n_tok} of the {x.shape[0]} tokens per step through the whole layer (router, every touched "
+                       f"expert on its rows, shared expert, ordered combine), mean of {steps} steps after {warmup} "
+                       "warm-up; no extrapolation (the CPU kernel's time is linear in rows per expert)"),
+            "cpu": _cpu_model(), "step_s": sec, "gpu_vs_cpu_rel_l2": rel}
 
 
 def run_reference(args):
-    """--impl reference: the reference CPU expert path on the host cores (rank 0 only)."""
+    """--impl reference: the reference CPU expert path (its AVX-VNNI kernel compiled
+    from its own source; oracle/_ref) on the headline's seeded layer, rank 0 only.
+    Each step: CPU_SAMPLE_T tokens of rank 0's batch through the whole layer."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    import numpy as np
+    from mosaic_b200 import synthetic
+    from oracle.cpu_path import LayerCPU, _cpu_model
 
-    from oracle import formats as fm
-    from oracle.cpu_path import time_layer_sample
-    from oracle.router import route
-
+    same_layer = torch.cuda.is_available()
+    if same_layer:
+        # the GPU arm's bank, router and tokens, generated from the same seeds on the
+        # device and copied to host memory; only the CPU path below is timed
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        layer, x = synthetic.make_layer(tokens=HEAD_T, seed=SEED, act_mode="fp8", n_experts=256)
+        bank = synthetic.bank_to_oracle(layer.bank, np.arange(256))
+        rw, rb = layer.router.weight.data.cpu(), layer.router.e_score_correction_bias.data.cpu()
+        xs = x[:CPU_SAMPLE_T].cpu()
+        del layer, x
+        torch.cuda.empty_cache()
+    else:
+        raise RuntimeError("the reference arm builds the GPU arm's seeded layer on the device")
     torch.set_num_threads(os.cpu_count() or 1)
-    t, h, inter, e = args.tokens, 7168, 2048, 256
-    g = torch.Generator().manual_seed(1234)
-    bound = 1.0 / h ** 0.5
-    rw = (torch.rand(e, h, generator=g) * 2 - 1) * bound
-    bias = torch.randn(e, generator=g) * 0.01
-    x = torch.randn(t, h, generator=g).to(torch.bfloat16)
-    w, idx = route(x, rw, bias, top_k=8, n_group=8, topk_group=4, route_scale=2.5)
-    touched = np.unique(idx.numpy())
-    rng = np.random.default_rng(0)
-    n_sample = 8
-    sample = np.sort(rng.choice(touched, size=min(n_sample, len(touched)), replace=False))
-    gu, dn = [], []
-    for _ in list(sample) + ["shared"]:
-        gu.append(fm.pack_mxfp4_nk(torch.randn(2 * inter, h, generator=g) * 0.02))
-        dn.append(fm.pack_mxfp4_nk(torch.randn(h, inter, generator=g) * 0.02))
-    bank = {"gu_packed": np.stack([p for p, _ in gu[:-1]]), "gu_scale": np.stack([s for _, s in gu[:-1]]),
-            "dn_packed": np.stack([p for p, _ in dn[:-1]]), "dn_scale": np.stack([s for _, s in dn[:-1]]),
-            "sh_gu_packed": gu[-1][0], "sh_gu_scale": gu[-1][1], "sh_dn_packed": dn[-1][0],
-            "sh_dn_scale": dn[-1][1], "experts": sample}
-    time_layer_sample(x, rw, bias, bank, idx.numpy(), w.numpy(), top_k=8, n_group=8, topk_group=4,
-                      route_scale=2.5, reps=1)  # warm-up
+    cpu = LayerCPU(bank)
+    del bank
+    kw = dict(top_k=8, n_group=8, topk_group=4, route_scale=2.5, limit=0.0)
+    for _ in range(args.warmup):
+        cpu.step(xs, rw, rb, **kw)
     secs = []
-    r = None
-    steps = max(1, min(args.steps, 5))
-    for _ in range(steps):
-        r = time_layer_sample(x, rw, bias, bank, idx.numpy(), w.numpy(), top_k=8, n_group=8, topk_group=4,
-                              route_scale=2.5, reps=1)
-        secs.append(r["layer_seconds"])
-    ms = 1e3 * sum(secs) / len(secs)
-    value = t / (ms / 1e3)
-    sample_desc = (f"T={t} decode tokens (V3 dims), router on all tokens, {len(sample)} of {r['distinct_experts']} "
-                   f"touched experts timed on their own tokens + shared expert, scaled to the full layer, "
-                   f"{steps} steps; FP8-activation semantics")
-    out = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
-           "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "mxfp4*fp8 (cpu)", "data": "synthetic (seeded, CPU-generated)",
-           "config": {"workload": "V3 MoE layer decode, T=128, 256+1 experts, top-8, groups 8/4",
-                      "tokens": t, "hidden": h, "inter": inter, "experts": e, "parallelism": "cpu"},
-           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["cores"], "kind": r["kind"],
-                            "sample": sample_desc, "cpu": r["cpu"]},
+    for _ in range(args.steps):
+        _, s, _ = cpu.step(xs, rw, rb, **kw)
+        secs.append(s)
+    sec = statistics.mean(secs)
+    value = CPU_SAMPLE_T / sec
+    sample = (f"{CPU_SAMPLE_T} of rank 0's {HEAD_T} tokens per step through the whole layer (router, every touched "
+              "expert on its rows, shared expert, ordered combine); no extrapolation (the CPU kernel's time is "
+              "linear in rows per expert); the same seeded layer as the GPU arm")
+    out = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "mxfp4*fp8 (cpu)",
+           "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)", "config": headline_config(world),
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": cpu.kind,
+                            "sample": sample, "cpu": _cpu_model()},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(out)
+
+
+def headline_single(args, local, hbm, tf_peak, peak_src, bank):
+    """N = 1: the whole layer on one GPU (MoELayer, FP8 activations), one CUDA graph per step."""
+    from mosaic_b200 import synthetic
+
+    layer, x = synthetic.make_layer(tokens=HEAD_T, seed=SEED, act_mode="fp8", n_experts=args.experts, bank=bank)
+    g, sx, sy = capture(layer, x)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    with Clocks(gpu_index(local)) as clk:
+        ms = timed_graph(g, steps, warmup, False)
+    clocks = clk.summary()
+    check_device_error(layer, x, "graph replays")
+    g.replay()
+    y = sy.clone()
+    stages, idx = stage_times(layer, x, reps=10)
+    rows = HEAD_T * 9
+    e2e_ms, bi, bo = e2e(layer, x, max(steps // 4, 10), False)
+    check_device_error(layer, x, "e2e")
+    flops = HEAD_T * LAYER_FLOP_PER_TOKEN
+    out = {
+        "metric": METRIC, "value": HEAD_T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4*fp8 (e4m3, per-128 pow2 scales, fp32 accumulate)",
+        "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)",
+        "config": headline_config(1),
+        "notes": {"l2": "no flush: every step streams the layer's 6 GB of expert weights (>> 126 MB L2)",
+                  "graph": "one CUDA graph per layer step"},
+        "clocks": clocks,
+        "gpu_launches": layer_launches(HEAD_T, 1) * steps,
+        "roofline": fp8_roofline(stages["gemm_gate_up"], rows, tf_peak, peak_src),
+        "layer_tflops": flops / (ms * 1e-3) / 1e12,
+        "stages_ms": stages,
+        "e2e": {"value": HEAD_T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
+                "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms},
+    }
+    del g
+    return out, layer, x, y
+
+
+def decode_extra(bank, local, hbm, steps, warmup):
+    """decode, T = 128 bf16 tokens, the whole layer on one GPU."""
+    from mosaic_b200 import synthetic
+
+    t = 128
+    layer, x = synthetic.make_layer(tokens=t, seed=SEED, act_mode="bf16", n_experts=256, bank=bank)
+    g, _, _ = capture(layer, x)
+    with Clocks(gpu_index(local)) as clk:
+        ms = timed_graph(g, steps, warmup, False)
+    check_device_error(layer, x, "decode graph replays")
+    stages, idx = stage_times(layer, x, reps=20)
+    u = int(torch.unique(idx).numel())
+    layer_bytes = (u + 1) * EXPERT_BYTES + ROUTER_BYTES + 2 * t * 7168 * 2
+    gu_bytes = (u + 1) * GU_BYTES
+    achieved = gu_bytes / (stages["gemm_gate_up"] * 1e-3) / 1e9
+    e2e_ms, bi, bo = e2e(layer, x, max(steps // 4, 10), False)
+    del g
+    return {"workload": "BASELINE config 2: V3 MoE layer decode, T=128 bf16 tokens, 256+1 experts, one GPU",
+            "tokens_per_s": t / (ms / 1e3), "ms_per_step": ms, "steps": steps, "clocks": clk.summary(),
+            "dtype": "mxfp4*bf16 (bf16 as hi+lo e4m3, fp32 accumulate)", "gpu_launches_per_step": layer_launches(t, 1),
+            "roofline": {"kernel": "moe_gemm_kernel (gate/up, tcgen05 mxf8f6f4)", "bound": "hbm",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": GU_TRAFFIC_RATIO * gu_bytes,
+                         "traffic_source": "ncu dram bytes of a 65-expert launch scaled by experts streamed",
+                         "algorithmic_bytes": gu_bytes,
+                         "note": "algorithmic bytes = (distinct experts + shared) x gate/up MXFP4 codes + scales"},
+            "layer_roofline": {"bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms * 1e-3) / 1e9,
+                               "frac": layer_bytes / (ms * 1e-3) / 1e9 / hbm, "distinct_experts": u},
+            "stages_ms": stages,
+            "e2e": {"value": t / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
+                    "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms}}, layer
+
+
+def decode_sweep(layer, hbm):
+    from mosaic_b200 import MoELayer, synthetic
+
+    sweep = {}
+    for tt in (1, 8, 32):
+        lt = MoELayer(layer.cfg, layer.bank)
+        lt.router.weight.data = layer.router.weight.data
+        lt.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
+        xt = synthetic.make_tokens(tt, 7168, 99 + tt)
+        gt, _, _ = capture(lt, xt)
+        mst = timed_graph(gt, 200, 10, False)
+        st_t, idx_t = stage_times(lt, xt, reps=5)
+        ut = int(torch.unique(idx_t).numel())
+        bt = (ut + 1) * EXPERT_BYTES + ROUTER_BYTES + 2 * tt * 7168 * 2
+        sweep[str(tt)] = {"ms": mst, "tokens_per_s": tt / (mst / 1e3), "distinct_experts": ut,
+                          "layer_hbm_frac": bt / (mst * 1e-3) / 1e9 / hbm,
+                          "gate_up_hbm_frac": (ut + 1) * GU_BYTES / (st_t["gemm_gate_up"] * 1e-3) / 1e9 / hbm,
+                          "stages_ms": st_t}
+        del gt
+    return sweep
+
+
+def prefill_extra(bank, tf_peak, peak_src):
+    """prefill, T = 8192 FP8 tokens, router bias fitted to a clipped Zipf(1.2) load."""
+    from mosaic_b200 import synthetic
+
+    t = 8192
+    lp, _ = synthetic.make_layer(tokens=1, seed=SEED, act_mode="fp8", n_experts=256, bank=bank)
+    zipf = synthetic.calibrate_zipf_bias(lp, alpha=1.2, tokens=t, seed=5)
+    xp = synthetic.make_tokens(t, 7168, 555)
+    gp, _, _ = capture(lp, xp)
+    msp = timed_graph(gp, 20, 3, False)
+    st_p, _ = stage_times(lp, xp, reps=5)
+    del gp
+    flops = t * LAYER_FLOP_PER_TOKEN
+    gemm_ms = st_p["gemm_gate_up"] + st_p["gemm_down"]
+    return {"workload": "BASELINE config 3: V3 MoE layer prefill, T=8192 FP8 tokens, clipped Zipf(1.2) load",
+            "tokens": t, "ms": msp, "tokens_per_s": t / (msp / 1e3),
+            "expert_tflops": flops / (gemm_ms * 1e-3) / 1e12,
+            "roofline_gate_up": fp8_roofline(st_p["gemm_gate_up"], t * 9, tf_peak, peak_src),
+            "stages_ms": st_p, "zipf": zipf}
 
 
 def timed_eager(fn, steps, warmup):
@@ -328,131 +508,6 @@ def timed_eager(fn, steps, warmup):
     ms = torch.tensor([a.elapsed_time(b) / steps], device="cuda")
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     return float(ms.item())
-
-
-def run_ep(args, rank, world, local, hbm, peak_src):
-    """N > 1: expert parallelism (BASELINE configs 4/5 layout).  Every rank holds
-    E/N routed experts + the shared expert and its own decode tokens.  The
-    headline step uses the device-driven peer-memory exchange and runs as one
-    CUDA graph; the NCCL all-to-all path (host-synchronised split sizes) is
-    timed beside it.  Times are the max over ranks."""
-    from mosaic_b200 import synthetic
-    from mosaic_b200.ep import ExpertParallelMoELayer
-
-    dist = torch.distributed
-    n_exp, t, h = args.experts, args.tokens, 7168
-    # the same bank on every rank (same seed), each rank keeps its own shard
-    layer, _ = synthetic.make_layer(tokens=1, seed=1234, act_mode="bf16", n_experts=n_exp)
-    ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=t)
-    ep_nccl = ExpertParallelMoELayer(layer.cfg, ep.bank)
-    ep_nccl.router = ep.router
-    layer.bank = None  # drop the full bank: only the local shard stays resident
-    torch.cuda.empty_cache()
-    x = synthetic.make_tokens(t, h, 1234 + rank)
-    steps, warmup = args.steps, max(args.warmup, 3)
-
-    # one CUDA graph per layer step (peer exchange: no host synchronisation)
-    xs = x.clone()
-    for _ in range(3):
-        ep(xs)
-    torch.cuda.synchronize()
-    dist.barrier()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        ys = ep(xs)
-    with Clocks(gpu_index(local)) as clk:
-        ms = timed_graph(g, steps, warmup, True)
-    clocks = clk.summary()
-    if ep.peer_exchange().error():
-        raise RuntimeError("device error recorded in the peer exchange")
-    idx = ep.last_idx.clone()
-    lo, hi = ep.e_lo, ep.e_hi
-    # distinct local experts this rank streamed in a step, from every rank's routing
-    all_idx = [torch.empty_like(idx) for _ in range(world)]
-    dist.all_gather(all_idx, idx)
-    ids = torch.unique(torch.cat(all_idx))
-    u_local = int(((ids >= lo) & (ids < hi)).sum().item())
-    rank_bytes = (u_local + 1) * EXPERT_BYTES + ROUTER_BYTES
-    frac = torch.tensor([rank_bytes / (ms * 1e-3) / 1e9 / hbm], device="cuda")
-    dist.all_reduce(frac, op=dist.ReduceOp.MIN)
-
-    # e2e through the public API with host buffers: pinned H2D, the graph-replayed
-    # step, D2H of the result, every step
-    xh = x.cpu().pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
-
-    def step_e2e():
-        xs.copy_(xh, non_blocking=True)
-        g.replay()
-        yh.copy_(ys, non_blocking=True)
-
-    e2e_ms = timed_eager(step_e2e, max(steps // 4, 10), 3)
-    # the NCCL all-to-all path, eager (split sizes read on the host every step)
-    nccl_ms = timed_eager(lambda: ep_nccl(x), max(steps // 4, 10), 3)
-    sc, rc = ep_nccl.last_counts
-    if ep.peer_exchange().error():
-        raise RuntimeError("device error recorded in the peer exchange")
-    out = {
-        "metric": METRIC, "value": t * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
-        "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "mxfp4*bf16 (bf16 as hi+lo e4m3, fp32 accumulate)",
-        "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)",
-        "config": {"workload": f"V3 MoE layer decode, expert parallel over {world} GPUs, T={t} per rank",
-                   "tokens_per_gpu": t, "hidden": h, "inter": 2048, "experts": n_exp,
-                   "experts_per_gpu": n_exp // world, "shared": "replicated", "top_k": 8, "groups": "8/4",
-                   "parallelism": f"ep{world}",
-                   "exchange": "NVLink peer-memory stores with device-side counts and flags (CUDA IPC)",
-                   "l2": "no flush: every rank streams its touched experts (>> 126 MB L2) each step",
-                   "graph": "one CUDA graph per layer step"},
-        "clocks": clocks,
-        # router 2, dispatch 3, exchange 3, shared expert 5, received rows 5, return 2, combine 1
-        "gpu_launches": 21 * steps,
-        "roofline": {"kernel": "whole EP layer step per rank (HBM: local experts streamed)", "bound": "hbm",
-                     "achieved": rank_bytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": float(frac.item()), "traffic": None, "peak_source": peak_src,
-                     "distinct_local_experts": u_local},
-        "exchange_bytes_per_rank": {"dispatch": sum(sc) * (2 * h + 16), "return": sum(sc) * h * 4},
-        "nccl_path": {"ms_per_step": nccl_ms, "tokens_per_s": t * world / (nccl_ms / 1e3),
-                      "exchange": "NCCL all_to_all_single, eager"},
-        "e2e": {"value": t * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": xh.numel() * 2,
-                "d2h_bytes_per_step": yh.numel() * 2, "ms_per_step": e2e_ms},
-    }
-    del g
-    if not args.no_extras:
-        # BASELINE config 4: 4096 FP8 tokens per rank, uniform routing (NCCL exchange)
-        from mosaic_b200 import MoEConfig
-
-        cfgp = MoEConfig(act_mode="fp8", **{k: v for k, v in synthetic.V3.items()})
-        epp = ExpertParallelMoELayer(cfgp, ep.bank)
-        epp.router.weight.data = ep.router.weight.data
-        epp.router.e_score_correction_bias.data = ep.router.e_score_correction_bias.data
-        tp = 4096
-        xp = synthetic.make_tokens(tp, h, 4321 + rank)
-        msp = timed_eager(lambda: epp(xp), 10, 3)
-        flops = tp * world * 9 * 88_080_384
-        out["ep_prefill"] = {"tokens_per_gpu": tp, "ms": msp, "tokens_per_s": tp * world / (msp / 1e3),
-                             "expert_tflops_per_gpu": flops / world / (msp * 1e-3) / 1e12,
-                             "act": "fp8 (e4m3, per-128 pow2 scales)", "routing": "uniform",
-                             "exchange": "NCCL all_to_all_single"}
-        del epp, xp
-    if not args.no_extras and world >= 4:
-        # BASELINE config 5: the 58-layer decode stack, expert parallel, one CUDA graph
-        del ep_nccl
-        ep.close()
-        del ep
-        torch.cuda.empty_cache()
-        out["stack"] = run_stack(58, t, world, rank)
-        if rank == 0:
-            emit(out)
-        dist.barrier()
-        dist.destroy_process_group()
-        return
-    if rank == 0:
-        emit(out)
-    ep.close()
-    del ep, ep_nccl
-    dist.barrier()
-    dist.destroy_process_group()
 
 
 def run_stack(n_layers, t, world, rank):
@@ -635,6 +690,136 @@ def router_bench(tokens, steps=20, warmup=3):
     return res
 
 
+
+
+def headline_ep(args, rank, world, local, hbm, tf_peak, peak_src):
+    """N > 1: every rank holds 256/N routed experts + the shared expert and its own
+    4096 FP8 tokens; one CUDA graph per step with the device-driven peer-memory
+    exchange (the down GEMM stores partials straight into the sources' return
+    buffers).  Times are the max over ranks."""
+    from mosaic_b200 import MoEConfig, synthetic
+    from mosaic_b200.ep import ExpertParallelMoELayer
+
+    dist = torch.distributed
+    h = 7168
+    # the same bank on every rank (same seed); each rank keeps its shard
+    layer, _ = synthetic.make_layer(tokens=1, seed=SEED, act_mode="fp8", n_experts=256)
+    ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=HEAD_T)
+    layer.bank = None
+    del layer
+    torch.cuda.empty_cache()
+    x = synthetic.make_tokens(HEAD_T, h, SEED + rank)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    xs = x.clone()
+    for _ in range(3):
+        ep(xs)
+    torch.cuda.synchronize()
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ys = ep(xs)
+    with Clocks(gpu_index(local)) as clk:
+        ms = timed_graph(g, steps, warmup, True)
+    clocks = clk.summary()
+    if ep.peer_exchange().error():
+        raise RuntimeError("device error recorded in the peer exchange")
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+
+    def step_e2e():
+        xs.copy_(xh, non_blocking=True)
+        g.replay()
+        yh.copy_(ys, non_blocking=True)
+
+    e2e_ms = timed_eager(step_e2e, max(steps // 4, 10), 3)
+    if ep.peer_exchange().error():
+        raise RuntimeError("device error recorded in the peer exchange")
+    idx = ep.last_idx
+    rows = torch.tensor([float(((idx >= r * (256 // world)) & (idx < (r + 1) * (256 // world))).sum().item())
+                         for r in range(world)], device="cuda")
+    dist.all_reduce(rows)  # routed rows each rank receives in a step
+    recv_rows = rows.tolist()
+    flops_rank = HEAD_T * LAYER_FLOP_PER_TOKEN  # mean over ranks
+    achieved = flops_rank / (ms * 1e-3) / 1e12
+    out = {
+        "metric": METRIC, "value": HEAD_T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mxfp4*fp8 (e4m3, per-128 pow2 scales, fp32 accumulate)",
+        "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)",
+        "config": headline_config(world),
+        "notes": {"exchange": "device-driven NVLink peer-memory stores (CUDA IPC, no multicast); the down GEMM's "
+                              "epilogue writes every partial into its source rank's return buffer",
+                  "l2": "no flush: every rank streams its 32-256 experts' weights (>> 126 MB L2) each step",
+                  "graph": "one CUDA graph per layer step"},
+        "clocks": clocks,
+        "gpu_launches": layer_launches(HEAD_T, world) * steps,
+        "roofline": {"kernel": "whole expert-parallel layer step per rank: expert FLOPs / step time", "bound": "tensor",
+                     "achieved": achieved, "peak": 2.0 * tf_peak, "unit": "TFLOP/s",
+                     "frac": achieved / (2.0 * tf_peak), "traffic": None,
+                     "peak_source": f"2 x {peak_src} dense bf16 ({tf_peak:.1f} TF/s): the FP8 MMA rate"},
+        "routed_rows_received_per_rank": recv_rows,
+        "e2e": {"value": HEAD_T * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": xh.numel() * 2,
+                "d2h_bytes_per_step": yh.numel() * 2, "ms_per_step": e2e_ms},
+    }
+    del g
+    if not args.no_extras:
+        # the same step with the NCCL all-to-all exchange (host-read split sizes, eager)
+        cfgp = MoEConfig(act_mode="fp8", **synthetic.V3)
+        epn = ExpertParallelMoELayer(cfgp, ep.bank)
+        epn.router.weight.data = ep.router.weight.data
+        epn.router.e_score_correction_bias.data = ep.router.e_score_correction_bias.data
+        msn = timed_eager(lambda: epn(x), 10, 3)
+        out["nccl_path"] = {"ms_per_step": msn, "tokens_per_s": HEAD_T * world / (msn / 1e3),
+                            "exchange": "NCCL all_to_all_single, split sizes read on the host, eager"}
+        del epn
+        # BASELINE config 2 sizes, expert parallel: 128 decode tokens per rank, bf16
+        cfgd = MoEConfig(act_mode="bf16", **synthetic.V3)
+        epd = ExpertParallelMoELayer(cfgd, ep.bank, exchange="p2p", max_tokens=128)
+        epd.router.weight.data = ep.router.weight.data
+        epd.router.e_score_correction_bias.data = ep.router.e_score_correction_bias.data
+        xd = synthetic.make_tokens(128, h, 4321 + rank)
+        for _ in range(3):
+            epd(xd)
+        torch.cuda.synchronize()
+        dist.barrier()
+        gd = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gd):
+            epd(xd)
+        msd = timed_graph(gd, 200, 10, True)
+        if epd.peer_exchange().error():
+            raise RuntimeError("device error recorded in the decode peer exchange")
+        out["decode_ep"] = {"tokens_per_gpu": 128, "ms_per_step": msd, "tokens_per_s": 128 * world / (msd / 1e3),
+                            "act": "bf16", "graph": "one CUDA graph per layer step"}
+        del gd
+        epd.close()
+        del epd
+    ep.close()
+    del ep
+    torch.cuda.empty_cache()
+    if not args.no_extras and world >= 4:
+        out["stack"] = run_stack(58, 128, world, rank)
+    if rank == 0:
+        emit(out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def single_layer_run(args, local, hbm, tf_peak, peak_src):
+    """--act: one layer at --tokens in that activation mode (small cases for ncu captures)."""
+    from mosaic_b200 import synthetic
+
+    t = args.tokens or 128
+    layer, x = synthetic.make_layer(tokens=t, seed=SEED, act_mode=args.act, n_experts=args.experts)
+    g, _, _ = capture(layer, x)
+    ms = timed_graph(g, args.steps, max(args.warmup, 3), False)
+    check_device_error(layer, x, "graph replays")
+    stages, idx = stage_times(layer, x, reps=2 if args.profile_small else 10)
+    del g
+    return {"single_layer": {"tokens": t, "act": args.act, "experts": args.experts, "ms_per_step": ms,
+                             "tokens_per_s": t / (ms / 1e3), "stages_ms": stages,
+                             "distinct_experts": int(torch.unique(idx).numel())}}
+
+
 def emit(out: dict) -> None:
     """Write the result line to the real stdout (see main)."""
     os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(out) + "\n").encode())
@@ -652,138 +837,58 @@ def main():
     if args.impl == "reference":
         run_reference(args)
         return
-    from mosaic_b200 import MoELayer, synthetic
+    from mosaic_b200 import synthetic
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dist_on = world > 1
-    if dist_on:
+    if world > 1:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
-    hbm, bf16_tf, peak_src = peaks()
+    hbm, tf_peak, peak_src = peaks()
     if args.hc_only:
         emit({"hc_pre_norm": hc_bench(hbm)})
         return
     if args.router_only:
-        tokens = [args.tokens] if "--tokens" in sys.argv else [1, 128, 2048, 8192]
+        tokens = [args.tokens] if args.tokens else [1, 128, 2048, 8192]
         emit({"router": router_bench(tokens, steps=max(args.steps // 20, 5), warmup=max(args.warmup, 3))})
         return
-    if dist_on:
-        run_ep(args, rank, world, local, hbm, peak_src)
+    if args.act:
+        emit(single_layer_run(args, local, hbm, tf_peak, peak_src))
         return
-    n_exp = args.experts
-    t = args.tokens
-    layer, x = synthetic.make_layer(tokens=t, seed=1234 + rank, act_mode=args.act, n_experts=n_exp)
-
-    g, sx, sy = capture(layer, x)
-    steps, warmup = args.steps, max(args.warmup, 3)
-    with Clocks(gpu_index(local)) as clk:
-        ms = timed_graph(g, steps, warmup, dist_on)
-    clocks = clk.summary()
-    check_device_error(layer, t, "graph replays")
-    stages, idx = stage_times(layer, x, reps=2 if args.profile_small else 20)
-    u = int(torch.unique(idx).numel())
-    w_last = layer.last_weights
-    layer_bytes = (u + 1) * EXPERT_BYTES + ROUTER_BYTES + 2 * t * 7168 * 2
-    gu_bytes = (u + 1) * GU_BYTES
-    achieved = gu_bytes / (stages["gemm_gate_up"] * 1e-3) / 1e9
-    e2e_ms, bi, bo = e2e(layer, x, max(steps // 4, 10), dist_on)
-    check_device_error(layer, t, "e2e")
-    value = t * world / (ms / 1e3)
-    out = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": ("mxfp4*bf16 (bf16 as hi+lo e4m3, fp32 accumulate)" if args.act == "bf16"
-                  else "mxfp4*fp8 (e4m3, per-128 pow2 scales, fp32 accumulate)"), "data": "synthetic (seeded N(0,0.02) experts, N(0,1) tokens)",
-        "config": {"workload": (f"V3 MoE layer decode (BASELINE config 2), T={t}" if args.act == "bf16"
-                                else f"V3 MoE layer, FP8 activations, T={t}, uniform routing"),
-                   "tokens_per_gpu": t, "hidden": 7168,
-                   "inter": 2048, "experts": n_exp, "shared": 1, "top_k": 8, "groups": "8/4",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "no flush: ~5.9 GB of touched expert weights per step >> 126 MB L2",
-                   "graph": "one CUDA graph per layer step"},
-        "clocks": clocks,
-        "gpu_launches": 7 * steps,
-        "roofline": {"kernel": "moe_gemm_kernel (gate/up, tcgen05 mxf8f6f4)", "bound": "hbm",
-                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": GU_TRAFFIC_RATIO * gu_bytes,
-                     "traffic_source": "ncu dram bytes of a 65-expert launch scaled by experts streamed",
-                     "algorithmic_bytes": gu_bytes, "peak_source": peak_src,
-                     "note": "algorithmic bytes = (distinct experts + shared) x gate/up MXFP4 codes + scales"},
-        "layer_roofline": {"bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms * 1e-3) / 1e9,
-                           "frac": layer_bytes / (ms * 1e-3) / 1e9 / hbm, "distinct_experts": u},
-        "stages_ms": stages,
-        "e2e": {"value": t * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
-                "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms},
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile_small:
+    if world > 1:
+        headline_ep(args, rank, world, local, hbm, tf_peak, peak_src)
+        return
+    bank = synthetic.make_bank(7168, 2048, args.experts, SEED)
+    out, layer, x, y = headline_single(args, local, hbm, tf_peak, peak_src, bank)
+    if not args.no_cpu_baseline:
         try:
-            r = cpu_baseline(layer, x, idx, w_last)
-            out["cpu_baseline"] = {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": r["cores"],
-                                   "kind": r["kind"], "sample": r["sample"], "cpu": r["cpu"],
-                                   "layer_ms": r["layer_seconds"] * 1e3}
+            out["cpu_baseline"] = cpu_layer_baseline(layer, x, y)
         except Exception as exc:  # report, do not hide
             out["cpu_baseline"] = {"value": None, "error": f"{type(exc).__name__}: {exc}"}
-    if not args.no_extras and not args.profile_small:
-        # each extra is reported on its own: one that fails records its error
-        # in the line and the headline numbers above are still printed
+    del layer, x, y
+    if not args.no_extras:
+        # each extra is reported on its own: one that fails records its error in
+        # the line and the headline numbers above are still printed
         def extra(key, fn):
             try:
                 out[key] = fn()
             except Exception as exc:  # report, do not hide
                 out[key] = {"error": f"{type(exc).__name__}: {exc}"}
 
-        def decode_sweep():
-            sweep = {}
-            for tt in (1, 8, 32):
-                lt = MoELayer(layer.cfg, layer.bank)
-                lt.router.weight.data = layer.router.weight.data
-                lt.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data
-                xt = synthetic.make_tokens(tt, 7168, 99 + tt)
-                gt, _, _ = capture(lt, xt)
-                mst = timed_graph(gt, 200, 10, dist_on)
-                st_t, idx_t = stage_times(lt, xt, reps=5)
-                ut = int(torch.unique(idx_t).numel())
-                bt = (ut + 1) * EXPERT_BYTES + ROUTER_BYTES + 2 * tt * 7168 * 2
-                sweep[str(tt)] = {"ms": mst, "tokens_per_s": tt * world / (mst / 1e3), "distinct_experts": ut,
-                                  "layer_hbm_frac": bt / (mst * 1e-3) / 1e9 / hbm,
-                                  "gate_up_hbm_frac": (ut + 1) * GU_BYTES / (st_t["gemm_gate_up"] * 1e-3) / 1e9
-                                  / hbm}
-                del gt
-            return sweep
+        holder = {}
 
-        def prefill():
-            # 8192 tokens, FP8 activations, Zipf(1.2) load
-            from mosaic_b200 import MoEConfig
+        def dec():
+            d, holder["layer"] = decode_extra(bank, local, hbm, max(args.steps, 100), max(args.warmup, 5))
+            return d
 
-            cfgp = MoEConfig(act_mode="fp8", **{k: v for k, v in synthetic.V3.items()})
-            lp = MoELayer(cfgp, layer.bank)
-            lp.router.weight.data = layer.router.weight.data.clone()
-            lp.router.e_score_correction_bias.data = layer.router.e_score_correction_bias.data.clone()
-            zipf = synthetic.calibrate_zipf_bias(lp, alpha=1.2, tokens=8192, seed=5)
-            xp = synthetic.make_tokens(8192, 7168, 555)
-            gp, _, _ = capture(lp, xp)
-            msp = timed_graph(gp, 20, 3, dist_on)
-            st_p, _ = stage_times(lp, xp, reps=5)
-            del gp
-            flops = 8192 * 9 * 88_080_384
-            gemm_ms = st_p["gemm_gate_up"] + st_p["gemm_down"]
-            return {"tokens": 8192, "ms": msp, "tokens_per_s": 8192 * world / (msp / 1e3),
-                    "expert_tflops": flops / (gemm_ms * 1e-3) / 1e12,
-                    "frac_fp8_nominal_4500": flops / (gemm_ms * 1e-3) / 1e12 / 4500.0,
-                    "frac_fp4_nominal_9000": flops / (gemm_ms * 1e-3) / 1e12 / 9000.0,
-                    "stages_ms": st_p, "zipf": zipf}
-
-        extra("decode_sweep", decode_sweep)
-        extra("prefill", prefill)
-        extra("offload", lambda: offload_bench(layer))
+        extra("decode", dec)
+        if "layer" in holder:
+            extra("decode_sweep", lambda: decode_sweep(holder["layer"], hbm))
+            extra("offload", lambda: offload_bench(holder["layer"]))
+        extra("prefill", lambda: prefill_extra(bank, tf_peak, peak_src))
         extra("hc_pre_norm", lambda: hc_bench(hbm))
-    del g
-    if rank == 0:
-        emit(out)
-    if dist_on:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    emit(out)
 
 
 if __name__ == "__main__":

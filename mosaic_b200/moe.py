@@ -164,6 +164,9 @@ class _Workspace:
         self.buf = None
 
     def get(self, dims: C.MoEDims, device) -> torch.Tensor:
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:  # "cuda" and "cuda:<current>" are one workspace
+            device = torch.device("cuda", torch.cuda.current_device())
         key = (bytes(dims), device)
         if key != self._key:
             n = C.lib().mosaic_moe_workspace_bytes(ctypes.byref(dims))

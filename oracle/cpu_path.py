@@ -50,6 +50,11 @@ class FP4LinearCPU:
             kind = "reference" if (VNNI_LIB.exists() and host_has_avx_vnni()) else "port"
         self.kind = kind
         ptr = lambda dt: np.ctypeslib.ndpointer(dt, flags="C_CONTIGUOUS")  # noqa: E731
+        self._prep = None
+        if PORT_LIB.exists():
+            self._prep = ctypes.CDLL(str(PORT_LIB))
+            self._prep.vnni_prepare.argtypes = [ptr(np.uint8), ctypes.c_int, ctypes.c_int, ptr(np.int8), ptr(np.int32)]
+            self._prep.vnni_prepare.restype = None
         if kind == "reference":
             self.lib = ctypes.CDLL(str(VNNI_LIB))
             self.lib.vnni_source_gemm.argtypes = [ptr(np.uint8), ptr(np.float32), ptr(np.int8), ptr(np.float32),
@@ -72,6 +77,11 @@ class FP4LinearCPU:
         sw = np.ascontiguousarray(e8m0_to_fp32(scale), dtype=np.float32)
         if self.kind == "port":
             return ("port", packed, sw, n, k)
+        if self._prep is not None:
+            tiled = np.empty((n // 8, k // 4, 8, 4), dtype=np.int8)
+            sums = np.empty((n, k // 32), dtype=np.int32)
+            self._prep.vnni_prepare(packed, n, k, tiled, sums)
+            return ("reference", tiled, sw, sums, n, k)
         qw = np.rint(decode_e2m1(packed) * 2.0).astype(np.int8)
         tiled = np.ascontiguousarray(qw.reshape(n // 8, 8, k // 4, 4).transpose(0, 2, 1, 3))
         sums = np.ascontiguousarray(qw.reshape(n, k // 32, 32).sum(-1, dtype=np.int32))
@@ -137,57 +147,57 @@ def expert_fp8_cpu(lin: FP4LinearCPU, xq, xs, w, prep_gu, prep_dn, inter: int, l
     return to_bf16(lin(zq, zs, prep_dn))
 
 
-def time_layer_sample(x, router_w, bias, bank: dict, idx_all, weights_all, *, top_k, n_group, topk_group,
-                      route_scale, n_sample: int = 8, limit: float = 0.0, kind: str | None = None,
-                      reps: int = 3, seed: int = 0) -> dict:
-    """Time the reference CPU expert path on a bounded sample and scale it to one layer.
+class LayerCPU:
+    """The reference CPU expert path over one whole MoE layer.
 
-    x [T, H] (bf16 values), router fp32; bank: oracle layout holding the
-    SAMPLED experts only (``bank["experts"]`` = their global ids) plus the
-    shared expert; idx_all / weights_all: the layer's routing [T, k].
-    Layer time = router time (all T tokens) + mean expert time (its own tokens)
-    x (distinct experts touched + 1 shared).  Returns the estimate and how it
-    was sampled.
+    Every expert's operands are prepared once (the reference prepares its
+    weights once too, ``vnni_source.prepare_weights``); ``step`` then runs the
+    path on a batch of tokens: the router on every token, ``act_quant_ref``,
+    each touched expert on its own tokens (gate/up, SwiGLU, route weight,
+    re-quantise, down), the shared expert on every token, and the combine in
+    ascending expert id, all on the host cores.
+
+    bank: oracle layout with every routed expert (``gu_packed [E, 2I, H/2]``
+    ...) and the shared expert (``sh_*``).
     """
-    lin = FP4LinearCPU(kind)
-    threads = torch.get_num_threads()
-    xn = torch.as_tensor(x).float().numpy()
-    t = xn.shape[0]
-    inter = bank["gu_packed"].shape[1] // 2
-    experts = list(bank["experts"])
-    preps = [(lin.prepare(bank["gu_packed"][i], bank["gu_scale"][i]), lin.prepare(bank["dn_packed"][i], bank["dn_scale"][i]))
-             for i in range(len(experts))]
-    sh = (lin.prepare(bank["sh_gu_packed"], bank["sh_gu_scale"]), lin.prepare(bank["sh_dn_packed"], bank["sh_dn_scale"]))
-    idx_np = np.asarray(idx_all)
-    w_np = np.asarray(weights_all, dtype=np.float32)
-    # warm-up
-    route(torch.as_tensor(x), router_w, bias, top_k=top_k, n_group=n_group, topk_group=topk_group,
-          route_scale=route_scale)
-    best_router, best_expert, best_shared = float("inf"), float("inf"), float("inf")
-    for _ in range(reps):
+
+    def __init__(self, bank: dict, kind: str | None = None):
+        self.lin = FP4LinearCPU(kind)
+        self.kind = self.lin.kind
+        lin = self.lin
+        self.inter = bank["gu_packed"].shape[1] // 2
+        self.n_experts = bank["gu_packed"].shape[0]
+        self.prep = [(lin.prepare(bank["gu_packed"][e], bank["gu_scale"][e]),
+                      lin.prepare(bank["dn_packed"][e], bank["dn_scale"][e])) for e in range(self.n_experts)]
+        self.shared = (lin.prepare(bank["sh_gu_packed"], bank["sh_gu_scale"]),
+                       lin.prepare(bank["sh_dn_packed"], bank["sh_dn_scale"]))
+
+    def step(self, x, router_w, bias, *, top_k, n_group, topk_group, route_scale, limit: float = 0.0):
+        """One layer step on x [T, H] (bf16 values).  Returns (y fp32 [T, H]
+        holding bf16 values, seconds, routing (w, idx))."""
         t0 = time.perf_counter()
-        route(torch.as_tensor(x), router_w, bias, top_k=top_k, n_group=n_group, topk_group=topk_group,
-              route_scale=route_scale)
+        xt = torch.as_tensor(x)
+        w, idx = route(xt, router_w, bias, top_k=top_k, n_group=n_group, topk_group=topk_group,
+                       route_scale=route_scale)
+        xn = xt.float().numpy()
+        t = xn.shape[0]
+        idx_np = idx.numpy()
+        w_np = w.numpy().astype(np.float32)
         xq, xs = act_quant_ref(xn)
-        t1 = time.perf_counter()
-        tot = 0.0
-        for i, e in enumerate(experts):
+        partials = np.zeros((t, top_k, xn.shape[1]), dtype=np.float32)
+        for e in np.unique(idx_np):
             tok, slot = np.nonzero(idx_np == e)
-            s0 = time.perf_counter()
-            expert_fp8_cpu(lin, xq[tok], xs[tok], w_np[tok, slot], preps[i][0], preps[i][1], inter, limit)
-            tot += time.perf_counter() - s0
-        s0 = time.perf_counter()
-        expert_fp8_cpu(lin, xq, xs, np.ones(t, np.float32), sh[0], sh[1], inter, limit)
-        s1 = time.perf_counter()
-        best_router = min(best_router, t1 - t0)
-        best_expert = min(best_expert, tot / max(len(experts), 1))
-        best_shared = min(best_shared, s1 - s0)
-    u = len(np.unique(idx_np))
-    layer_s = best_router + best_expert * u + best_shared
-    return {"layer_seconds": layer_s, "tokens_per_s": t / layer_s, "kind": lin.kind, "cores": threads,
-            "router_s": best_router, "expert_s_mean": best_expert, "shared_s": best_shared,
-            "distinct_experts": int(u), "sampled_experts": len(experts), "reps": reps,
-            "cpu": _cpu_model()}
+            pg, pd = self.prep[e]
+            partials[tok, slot] = expert_fp8_cpu(self.lin, xq[tok], xs[tok], w_np[tok, slot], pg, pd, self.inter,
+                                                 limit)
+        order = np.argsort(idx_np, axis=1, kind="stable")
+        acc = np.zeros((t, xn.shape[1]), dtype=np.float32)
+        for s_ in range(top_k):
+            acc = acc + partials[np.arange(t), order[:, s_]]
+        shared = expert_fp8_cpu(self.lin, xq, xs, np.ones(t, np.float32), self.shared[0], self.shared[1],
+                                self.inter, limit)
+        y = to_bf16(shared + to_bf16(acc))
+        return y, time.perf_counter() - t0, (w, idx)
 
 
 def _cpu_model() -> str:

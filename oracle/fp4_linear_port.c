@@ -85,3 +85,28 @@ void fp4_linear_f32(const float *x, const uint8_t *packed, const float *sw, floa
     }
   }
 }
+
+/*
+ * Operand preparation of the reference's AVX-VNNI CPU kernel, in C (its own
+ * numpy preparation, mosaicvm/bench/vnni_source.py:38-54, takes ~0.3 s per
+ * V3 gate/up matrix): weights as 2*E2M1 int8 tiled [N/8][K/4][8][4] and the
+ * per-32 int32 weight sums [N][K/32].
+ */
+void vnni_prepare(const uint8_t *packed, int N, int K, int8_t *tiled, int32_t *sums) {
+  const int G = K / 32;
+  #pragma omp parallel for schedule(static)
+  for (int n = 0; n < N; n++) {
+    const uint8_t *pw = packed + (size_t)n * (K / 2);
+    for (int g = 0; g < G; g++) {
+      int32_t s = 0;
+      for (int i = 0; i < 32; i++) {
+        const int c = g * 32 + i;
+        const uint8_t b = pw[c >> 1];
+        const int8_t q = E2M1_Q2[(c & 1) ? (b >> 4) : (b & 0xF)];
+        s += q;
+        tiled[(((size_t)(n >> 3) * (K >> 2) + (c >> 2)) << 5) + ((n & 7) << 2) + (c & 3)] = q;
+      }
+      sums[(size_t)n * G + g] = s;
+    }
+  }
+}

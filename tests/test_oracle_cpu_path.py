@@ -70,3 +70,43 @@ def test_fast_oracle_layer_matches_numpy_oracle():
         else:
             assert rel_l2(b, a) < 1e-3
     assert isinstance(case["x"], torch.Tensor)
+
+
+@pytest.mark.skipif(not KINDS, reason="oracle C checkers not built")
+def test_cpu_layer_path_matches_the_fp8_oracle():
+    """The whole-layer CPU baseline (router, every touched expert through the
+    reference CPU kernel, shared expert, ordered combine) equals the FP8 oracle
+    layer bit for bit and routes like the golden recipe."""
+    import torch
+
+    from oracle.cpu_path import LayerCPU
+    from oracle.moe import moe_layer
+    from tests.golden.recipes import MOE_CASES, make_moe_case
+    from tests.helpers import pack_case
+
+    case = make_moe_case(**MOE_CASES["S"])
+    obank, _ = pack_case(case)
+    c = case["cfg"]
+    cpu = LayerCPU(obank)
+    y, sec, (w, idx) = cpu.step(case["x"], case["router_w"], case["bias"], top_k=c["k"], n_group=c["n_group"],
+                                topk_group=c["topk_group"], route_scale=c["scale"], limit=c["swiglu_limit"])
+    assert torch.equal(idx, case["idx"]) and sec > 0
+    ref = moe_layer(case["x"], w, idx, obank, mode="fp8", swiglu_limit=c["swiglu_limit"])
+    assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.skipif(not KINDS, reason="oracle C checkers not built")
+def test_vnni_operand_preparation_matches_the_layout():
+    """The C preparation of the reference kernel's weight operands equals the
+    numpy restatement of mosaicvm/bench/vnni_source.py:38-54."""
+    from oracle.cpu_path import decode_e2m1
+
+    rng = np.random.default_rng(3)
+    p, s = fm.pack_mxfp4_nk(rng.standard_normal((64, 256)).astype(np.float32) * 0.02)
+    lin = FP4LinearCPU(KINDS[-1])
+    if lin.kind != "reference":
+        pytest.skip("the reference kernel's layout is prepared for the reference kind only")
+    prep = lin.prepare(p, s)
+    qw = np.rint(decode_e2m1(p) * 2.0).astype(np.int8)
+    assert np.array_equal(prep[1], qw.reshape(8, 8, 64, 4).transpose(0, 2, 1, 3))
+    assert np.array_equal(prep[3], qw.reshape(64, 8, 32).sum(-1, dtype=np.int32))
