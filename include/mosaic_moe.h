@@ -411,7 +411,9 @@ typedef struct mosaic_ep_peers {
   int32_t max_tokens;     /* T_max (shared-expert rows of the return buffer) */
   int32_t hidden;         /* H */
   int32_t partial_f32;    /* 1: fp32 partials (MOSAIC_ACT_BF16), 0: bf16 (MOSAIC_ACT_FP8) */
-  int32_t reserved;
+  int32_t wait_us;        /* budget of each device-side wait on a peer's flag, in microseconds
+                             (0: about 2 s); a wait that runs out records MOSAIC_ERR_TIMEOUT in
+                             this rank's region and the kernel returns */
   void* regions[MOSAIC_EP_MAX_WORLD];  /* rank r's region as mapped in this process (own at [rank]) */
 } mosaic_ep_peers;
 

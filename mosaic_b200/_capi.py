@@ -133,7 +133,7 @@ class EpPeersC(ctypes.Structure):
         ("max_tokens", ctypes.c_int32),
         ("hidden", ctypes.c_int32),
         ("partial_f32", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("wait_us", ctypes.c_int32),
         ("regions", ctypes.c_void_p * EP_MAX_WORLD),
     ]
 

@@ -957,6 +957,7 @@ int check_peers(const mosaic_ep_peers* p) {
     return MOSAIC_ERR_SHAPE;
   if (p->max_recv_rows < 1 || p->max_send_rows < 1 || p->max_tokens < 1) return MOSAIC_ERR_SHAPE;
   if (p->hidden < 256 || p->hidden % 256) return MOSAIC_ERR_SHAPE;
+  if (p->wait_us < 0) return MOSAIC_ERR_RANGE;
   return MOSAIC_OK;
 }
 
@@ -975,6 +976,7 @@ EpPeersDev ep_dev(const mosaic_ep_peers* p) {
   d.ret_row_bytes = ep_ret_row_bytes(p);
   d.recv_off = kEpHeaderBytes;
   d.ret_off = up256(kEpHeaderBytes + ep_recv_bytes(p));
+  d.wait_ns = p->wait_us > 0 ? static_cast<unsigned long long>(p->wait_us) * 1000ull : 2000000000ull;
   for (int r = 0; r < p->world; ++r) d.regions[r] = static_cast<uint8_t*>(p->regions[r]);
   return d;
 }

@@ -95,13 +95,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 // true once *flag has reached epoch (epochs only grow; the signed difference
-// handles wrap-around)
-__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch) {
+// handles wrap-around); false after budget_ns of the global timer
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, unsigned long long budget_ns) {
   if (static_cast<int>(ld_acquire_sys(flag) - epoch) >= 0) return true;
-  const long long t0 = clock64();
+  const unsigned long long t0 = global_ns();
   while (static_cast<int>(ld_acquire_sys(flag) - epoch) < 0) {
-    if (clock64() - t0 > MOSAIC_WAIT_CYCLES) return false;
+    if (global_ns() - t0 > budget_ns) return false;
     __nanosleep(64);
   }
   return true;
@@ -129,7 +134,7 @@ __global__ void ep_counts_kernel(const EpPeersDev P, const int* __restrict__ des
     st_release_sys(&ph->count_flag[P.rank], epoch);
   }
   __syncthreads();
-  if (p < P.world && !wait_epoch(&own->count_flag[p], epoch)) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
+  if (p < P.world && !wait_epoch(&own->count_flag[p], epoch, P.wait_ns)) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -256,7 +261,7 @@ __global__ void ep_wait_kernel(const EpPeersDev P, int which) {
   const int p = threadIdx.x;
   if (p < P.world) {
     const uint32_t* f = (which == 0) ? &own->data_flag[p] : &own->ret_flag[p];
-    if (!wait_epoch(f, epoch)) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
+    if (!wait_epoch(f, epoch, P.wait_ns)) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
   }
 }
 

@@ -212,6 +212,7 @@ static_assert(sizeof(EpRegionHeader) <= kEpHeaderBytes, "EP region header");
 
 struct EpPeersDev {
   int world, rank, max_recv_rows, row_bytes, ret_row_bytes;
+  unsigned long long wait_ns;  // budget of each wait on a peer's flag (global timer, ns)
   size_t recv_off, ret_off;  // byte offsets of the receive rows / return partials in a region
   uint8_t* regions[MOSAIC_EP_MAX_WORLD];
 };

@@ -145,11 +145,13 @@ class PeerExchange:
     the flags, the count matrix, the receive rows and the return partials of
     the device-driven exchange (``mosaic_ep_exchange_rows`` /
     ``mosaic_ep_return_partials``).  Capacity: ``max_tokens`` tokens per rank;
-    the receive side is sized for any routing.
+    the receive side is sized for any routing.  ``wait_us`` bounds every
+    device-side wait on another rank's flag; a wait that runs out records
+    MOSAIC_ERR_TIMEOUT in this rank's region (``error()``) and the kernel returns.
     """
 
     def __init__(self, *, group=None, max_tokens: int, top_k: int, n_experts: int, hidden: int,
-                 partial_f32: bool):
+                 partial_f32: bool, wait_us: int = 0):
         lib = C.lib()
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -166,6 +168,7 @@ class PeerExchange:
         pe.max_tokens = max_tokens
         pe.hidden = hidden
         pe.partial_f32 = int(bool(partial_f32))
+        pe.wait_us = int(wait_us)  # budget of each device-side wait on a peer (0: about 2 s)
         nbytes = lib.mosaic_ep_region_bytes(ctypes.byref(pe))
         if nbytes == 0:
             raise ValueError("invalid peer-exchange geometry")

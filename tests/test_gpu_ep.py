@@ -172,6 +172,21 @@ def test_ep_two_gpus_nccl():
     assert r.stdout.count("EP_OK") == 2, r.stdout[-2000:]
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus_rank_departure_seen_before_the_next_step():
+    """One of two GPU ranks leaves between steps (PeerHealth.leave) and exits;
+    the other's next step raises PeerFailure before launching anything."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29534",
+           os.path.join(ROOT, "tests", "ep_failure_gpu_check.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, cwd=ROOT)
+    out = r.stdout + r.stderr
+    assert r.returncode == 0, out[-3000:]
+    assert out.count("STEP1_OK") == 2 and "rank 1 LEFT" in out, out[-3000:]
+    assert "rank 0 PEER_FAILURE_SEEN" in out, out[-3000:]
+
+
 @pytest.mark.parametrize("act_mode", ["bf16", "fp8"])
 def test_ep_p2p_world1_bit_identical_and_graph_capturable(act_mode):
     """The device-driven exchange path (own region only at world 1): eager
