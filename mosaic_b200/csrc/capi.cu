@@ -145,6 +145,7 @@ int run_router(const void* x, const float* w, const float* bias, int T, int H, i
     if (st) return st;
     if (launch_router_logits_tc(tx, tw, !use_parts, T, H, E, splits, partial, err, stream) != cudaSuccess)
       return MOSAIC_ERR_CUDA;
+    PdlScope pdl(true);  // the top-k follows the logits kernel in the stream
     return launch_router_topk(partial, splits, bias, T, E, top_k, n_group, topk_group, route_scale, norm, weights_out,
                               idx_out, err, stream, rv) == cudaSuccess
                ? MOSAIC_OK
@@ -355,9 +356,12 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   return MOSAIC_OK;
 }
 
+// after_kernel: the layout follows a kernel of the layer (the router's top-k)
+// in the stream, so it may launch programmatically too.
 int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const void* x, const int64_t* idx,
                 const float* weights, const mosaic_expert_bank* bank, void* y, cudaStream_t stream,
-                void* const* ev = nullptr, const int* expert_slot = nullptr, int bank_slots = 0) {
+                void* const* ev = nullptr, const int* expert_slot = nullptr, int bank_slots = 0,
+                bool after_kernel = false) {
   const int T = d->tokens, H = d->hidden, E = d->n_experts, k = d->top_k;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
   const int shared_base = d->has_shared ? T * k : -1;
@@ -370,7 +374,15 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   lp.E = E;
   lp.with_shared = d->has_shared ? 1 : 0;
   fill_layout(lp, w, ws);
-  if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  // layout -> quantise -> gate/up -> down -> combine: each kernel follows the
+  // previous one in the stream, so they launch programmatically (the layout
+  // only when the router's top-k precedes it); with stage events in between,
+  // none does
+  {
+    PdlScope pdl_layout(ev == nullptr && after_kernel);
+    if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  }
+  PdlScope pdl(ev == nullptr);
   if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
 
   if (launch_rows_quant(x, T, nullptr, H, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos,
@@ -824,7 +836,7 @@ int moe_forward_impl(const mosaic_moe_dims* dims, const mosaic_route_ext* ext, c
                   reinterpret_cast<int*>(ws + w.err), s, &rv);
   if (st) return st;
   if (!rec(stage_events, 1, s)) return MOSAIC_ERR_CUDA;
-  return run_experts(dims, w, ws, x, idx_out, weights_out, bank, y, s, stage_events);
+  return run_experts(dims, w, ws, x, idx_out, weights_out, bank, y, s, stage_events, nullptr, 0, true);
 }
 
 }  // namespace

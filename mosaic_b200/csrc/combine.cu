@@ -36,6 +36,8 @@ template <bool F32>
 __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ partial,
                                                       const int* __restrict__ row_sorted, int T, int k, int H,
                                                       int shared_base, __nv_bfloat16* __restrict__ y) {
+  griddep_wait();  // the down GEMM's partials are visible
+  griddep_launch();
   const int t = blockIdx.x;
   const int h0 = (blockIdx.y * 256 + threadIdx.x) * 8;
   if (h0 >= H) return;
@@ -71,12 +73,11 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ p
 cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,
                            int shared_base, void* y, cudaStream_t stream) {
   dim3 grid(T, (H + 2047) / 2048);
-  if (partial_f32)
-    combine_kernel<true><<<grid, 256, 0, stream>>>(partial, row_sorted, T, k, H, shared_base,
-                                                   static_cast<__nv_bfloat16*>(y));
-  else
-    combine_kernel<false><<<grid, 256, 0, stream>>>(partial, row_sorted, T, k, H, shared_base,
-                                                    static_cast<__nv_bfloat16*>(y));
+  const cudaError_t e = partial_f32 ? launch_k(combine_kernel<true>, grid, dim3(256), 0, stream, partial, row_sorted, T,
+                                               k, H, shared_base, static_cast<__nv_bfloat16*>(y))
+                                    : launch_k(combine_kernel<false>, grid, dim3(256), 0, stream, partial, row_sorted,
+                                               T, k, H, shared_base, static_cast<__nv_bfloat16*>(y));
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

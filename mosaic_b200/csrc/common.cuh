@@ -24,6 +24,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ------------------------------------------------ programmatic launches ---
+// A kernel of the MoE layer's chain may be launched before its predecessor in
+// the stream has finished (programmatic dependent launch): griddep_wait()
+// returns once the predecessor has completed and its writes are visible, and
+// must come before the kernel reads or writes anything the predecessor
+// touches; griddep_launch() lets the successor be scheduled.  Both are no-ops
+// for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- errors ---
 // Device error word: the first error code wins, later ones are dropped.
 __device__ __forceinline__ void set_error(int* err, int code) {

@@ -266,6 +266,10 @@ __global__ void __launch_bounds__(NT, 1)
   tc_fence_after();
   const uint32_t tmem = ctrl->tmem_base;
   volatile int* abort = &ctrl->abort;
+  // the set-up above (barriers, TMEM, tensor-map prefetch) overlaps the previous
+  // kernel's tail; everything below reads what it wrote
+  griddep_wait();
+  griddep_launch();
 
   int n_tiles = *p.n_tiles;
   if (n_tiles > p.max_tiles) n_tiles = p.max_tiles;
@@ -708,7 +712,9 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  kernel<<<grid, p.sf_copier ? kThreadsCopier : kThreadsPlain, smem, stream>>>(tmap_w, tmap_x, p);
+  err = launch_k(kernel, dim3(grid), dim3(p.sf_copier ? kThreadsCopier : kThreadsPlain), smem, stream, tmap_w, tmap_x,
+                 p);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -8,6 +8,34 @@
 
 namespace mosaic {
 
+// ---- launches
+// Inside a PdlScope(true) the chain kernels below are launched with
+// programmatic stream serialization: each starts with griddep_wait(), so it
+// may be scheduled while its predecessor (a kernel of the same chain) drains.
+// Only the single-GPU layer's chain, whose every kernel follows another of its
+// kernels in the stream, turns it on.
+inline thread_local bool g_pdl_chain = false;
+struct PdlScope {
+  bool prev;
+  explicit PdlScope(bool on) : prev(g_pdl_chain) { g_pdl_chain = on; }
+  ~PdlScope() { g_pdl_chain = prev; }
+};
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl_chain ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---- grouped block-scaled expert GEMM (gemm_bs.cu)
 struct GemmParams {
   int mode;           // 0 = gate/up (+SwiGLU, re-quantise), 1 = down (partials)

@@ -46,6 +46,8 @@ struct LayoutExtra {
 };
 
 __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtra x) {
+  griddep_wait();  // the previous kernel of the chain has finished
+  griddep_launch();
   extern __shared__ int sm[];
   const int E = p.E, k = p.k;
   const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;  // device-side count (EP receive side)
@@ -225,6 +227,8 @@ __device__ __forceinline__ LayoutScratch scratch_of(const LayoutParams& p, int n
 }
 
 __global__ void __launch_bounds__(1024) layout_count_kernel(LayoutParams p, int nchunks) {
+  griddep_wait();  // the previous kernel of the chain has finished
+  griddep_launch();
   __shared__ int cnt[260];  // E <= 257 (the per-row pass counts the shared expert as an id)
   const int E = p.E, k = p.k, tid = threadIdx.x, c = blockIdx.x;
   const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
@@ -246,6 +250,8 @@ __global__ void __launch_bounds__(1024) layout_count_kernel(LayoutParams p, int 
 }
 
 __global__ void __launch_bounds__(1024) layout_scan_kernel(LayoutParams p, int nchunks) {
+  griddep_wait();  // the previous kernel of the chain has finished
+  griddep_launch();
   extern __shared__ int sm[];
   const int E = p.E, tid = threadIdx.x;
   const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
@@ -304,6 +310,8 @@ __global__ void __launch_bounds__(1024) layout_scan_kernel(LayoutParams p, int n
 }
 
 __global__ void __launch_bounds__(1024) layout_rank_kernel(LayoutParams p, int nchunks, LayoutExtra x) {
+  griddep_wait();  // the previous kernel of the chain has finished
+  griddep_launch();
   extern __shared__ int sm[];
   const int E = p.E, k = p.k, c = blockIdx.x;
   const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
@@ -356,6 +364,8 @@ __global__ void __launch_bounds__(1024) layout_rank_kernel(LayoutParams p, int n
 }
 
 __global__ void __launch_bounds__(256) layout_finish_kernel(LayoutParams p, int nchunks) {
+  griddep_wait();  // the previous kernel of the chain has finished
+  griddep_launch();
   const int E = p.E, k = p.k;
   const int T = p.T_dev ? max(0, min(*p.T_dev, p.T)) : p.T;
   const LayoutScratch sc = scratch_of(p, nchunks);
@@ -437,24 +447,29 @@ size_t layout_scratch_ints(int T, int k, int E) {
 
 cudaError_t launch_layout(const LayoutParams& p, cudaStream_t stream) {
   const int nchunks = (p.T * p.k + 1023) / 1024;
+  cudaError_t e = cudaSuccess;
   if (nchunks > 1 && p.scratch) {
     const int NE = p.E + (p.with_shared ? 1 : 0);
-    layout_count_kernel<<<nchunks, 1024, 0, stream>>>(p, nchunks);
-    layout_scan_kernel<<<1, 1024, sizeof(int) * (4 * NE + 2), stream>>>(p, nchunks);
-    const size_t rsmem = sizeof(int) * 64 * static_cast<size_t>(p.E);
-    cudaError_t e = cudaFuncSetAttribute(layout_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(rsmem));
+    e = launch_k(layout_count_kernel, dim3(nchunks), dim3(1024), 0, stream, p, nchunks);
     if (e != cudaSuccess) return e;
-    layout_rank_kernel<<<nchunks, 1024, rsmem, stream>>>(p, nchunks, LayoutExtra{nullptr, nullptr});
+    e = launch_k(layout_scan_kernel, dim3(1), dim3(1024), sizeof(int) * (4 * NE + 2), stream, p, nchunks);
+    if (e != cudaSuccess) return e;
+    const size_t rsmem = sizeof(int) * 64 * static_cast<size_t>(p.E);
+    e = cudaFuncSetAttribute(layout_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(rsmem));
+    if (e != cudaSuccess) return e;
+    e = launch_k(layout_rank_kernel, dim3(nchunks), dim3(1024), rsmem, stream, p, nchunks,
+                 LayoutExtra{nullptr, nullptr});
+    if (e != cudaSuccess) return e;
     const int fb = (p.T + 255) / 256;
-    layout_finish_kernel<<<fb < 1184 ? fb : 1184, 256, 0, stream>>>(p, nchunks);
+    e = launch_k(layout_finish_kernel, dim3(fb < 1184 ? fb : 1184), dim3(256), 0, stream, p, nchunks);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
   const size_t smem = layout_smem(p.E, p.with_shared);
-  cudaError_t err = cudaFuncSetAttribute(layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-  if (err != cudaSuccess) return err;
-  layout_kernel<<<1, 1024, smem, stream>>>(p, LayoutExtra{nullptr, nullptr});
+  e = cudaFuncSetAttribute(layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  e = launch_k(layout_kernel, dim3(1), dim3(1024), smem, stream, p, LayoutExtra{nullptr, nullptr});
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(kRqThreads) rows_quant_kernel(const __nv_bfloa
                                                                 int hilo, int R_pad, const int* __restrict__ row_tile,
                                                                 const int* __restrict__ row_pos,
                                                                 uint8_t* __restrict__ xq, uint32_t* __restrict__ sft) {
+  griddep_wait();  // the layout's row maps are visible
+  griddep_launch();
   __shared__ int s_row[kRqMaxRows], s_pos[kRqMaxRows], s_tile[kRqMaxRows];
   const int rows = T_dev ? min(*T_dev, T) : T;
   const int nrows = k + (shared_base >= 0 ? 1 : 0);
@@ -284,8 +286,10 @@ cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int
   int gy = (1184 + gx - 1) / gx;
   const int gy_max = (chunks + warps_per_row - 1) / warps_per_row;
   if (gy > gy_max) gy = gy_max;
-  rows_quant_kernel<<<dim3(gx, gy), kRqThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k,
-                                                      row_of, shared_base, hilo, R_pad, row_tile, row_pos, xq, sft);
+  const cudaError_t e = launch_k(rows_quant_kernel, dim3(gx, gy), dim3(kRqThreads), 0, stream,
+                                 static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k, row_of, shared_base, hilo,
+                                 R_pad, row_tile, row_pos, xq, sft);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

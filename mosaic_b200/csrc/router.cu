@@ -250,6 +250,8 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
                                                           int n_group, int topk_group, float route_scale,
                                                           int norm, float* __restrict__ w_out,
                                                           int64_t* __restrict__ idx_out, int* err, RouteVariant rv) {
+  griddep_wait();  // the logits kernel's partials are visible
+  griddep_launch();
   __shared__ float red[kTopkWays][32 * 8];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -524,9 +526,10 @@ cudaError_t launch_router_topk(const float* partial, int splits, const float* bi
   const int wpb = ways > 1 ? kTopkWays : (T >= 8 * 148 ? 8 : (T >= 4 * 148 ? 4 : (T >= 2 * 148 ? 2 : 1)));
   dim3 g2(ways > 1 ? T : (T + wpb - 1) / wpb);
   const int per = (E + 31) / 32;
-#define MOSAIC_TOPK(P)                                                                                      \
-  router_topk_kernel<P><<<g2, 32 * wpb, 0, stream>>>(partial, used, ways, bias, T, E, top_k, n_group, topk_group, \
-                                                route_scale, norm, weights_out, idx_out, err, rv)
+  cudaError_t e = cudaSuccess;
+#define MOSAIC_TOPK(P)                                                                                          \
+  e = launch_k(router_topk_kernel<P>, g2, dim3(32 * wpb), 0, stream, partial, used, ways, bias, T, E, top_k, n_group, \
+               topk_group, route_scale, norm, weights_out, idx_out, err, rv)
   if (per <= 1)
     MOSAIC_TOPK(1);
   else if (per <= 2)
@@ -536,6 +539,7 @@ cudaError_t launch_router_topk(const float* partial, int splits, const float* bi
   else
     MOSAIC_TOPK(8);
 #undef MOSAIC_TOPK
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
