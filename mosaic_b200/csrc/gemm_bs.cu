@@ -72,10 +72,11 @@ struct Ctrl {
   uint64_t sf_ready[kMaxStages];
   uint32_t tmem_base;
   int abort;
-  float4 red4[2][16];  // gate/up act_quant: column maxima of the four epilogue warps, two blocks
-  float meta_w[128];   // gate/up: route weight of each row of the item's token tile
-  int meta_o[128];     // down: output row (EP: row in the source's return buffer)
-  int meta_r[128];     // down, EP: source rank of the row
+  // per epilogue group (two in the E4M3 instance, one otherwise):
+  float4 red4[2][2][16];  // gate/up act_quant: column maxima of the group's four warps, two blocks
+  float meta_w[2][128];   // gate/up: route weight of each row of the item's token tile
+  int meta_o[2][128];     // down: output row (EP: row in the source's return buffer)
+  int meta_r[2][128];     // down, EP: source rank of the row
 };
 
 // Per stage: the two 16 KB (unpacked) weight tiles of the pair for one
@@ -97,14 +98,15 @@ __host__ __device__ constexpr Plan make_plan(int planes, int brows) {
   return pl;
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// Named barrier of the four epilogue warps that also ANDs a predicate over them.
-__device__ __forceinline__ bool epi_all(bool v) {
+// Named barrier (1 + g) of epilogue group g's four warps.
+__device__ __forceinline__ void epi_bar(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
+// The same barrier, also ANDing a predicate over the group.
+__device__ __forceinline__ bool epi_all(int g, bool v) {
   uint32_t r;
   asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(v))
+      : "r"(static_cast<uint32_t>(v)), "r"(1 + g)
       : "memory");
   return r != 0;
 }
@@ -221,6 +223,9 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int planes = PLANES;
+  // E4M3 (prefill) tiles have one issuer pair, so warps 8-11 form a second
+  // epilogue group: each group takes every other 16-column block of an item
+  constexpr int kGroups = PLANES == 1 ? 2 : 1;
   constexpr Plan pl = make_plan(PLANES, BROWS);
   constexpr int S = pl.stages;
   static_assert(S >= 2 && S <= kMaxStages, "ring");
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctrl->acc_full[b], 2 * P);  // one commit from each issuer
-      mbar_init(&ctrl->acc_empty[b], 128);
+      mbar_init(&ctrl->acc_empty[b], 128 * kGroups);
     }
     for (int i = 0; i < 7; ++i) mbar_init(&ctrl->drain[i], 1);
     for (int s = 0; s < S; ++s) mbar_init(&ctrl->sf_ready[s], 1);
@@ -482,21 +487,29 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
     __syncwarp();
-  } else if (warp >= 2 && warp <= 5) {
+  } else if ((warp >= 2 && warp <= 5) || (kGroups == 2 && warp >= 8 && warp <= 11)) {
     // ------------------------------------------------------------ epilogue
     // Warp w reads TMEM lanes 32*(w%4).. (weight rows); each thread holds one
     // weight row of 16 token columns at a time.  Per item, the rows' route
     // weights (gate/up) or output rows (down) are loaded into shared memory
     // once; per 16-column block, column maxima use transposed butterflies and
     // the staging buffers alternate between blocks, so a gate/up block takes
-    // two named barriers.
+    // two named barriers.  With two groups (warps 2-5 and 8-11), group g takes
+    // the blocks starting at columns 16g, 16g + 32, ... with its own barrier,
+    // metadata and half of the staging area.
+    const int g = warp >= 8 ? 1 : 0;
     const int q = warp & 3;
     const int lrow = q * 32 + lane;
-    const int et = threadIdx.x - 64;  // 0..127: this thread's index among the epilogue warps
+    const int et = (warp - (g ? 8 : 2)) * 32 + lane;  // 0..127: this thread's index in its group
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const size_t z_plane = static_cast<size_t>(p.R_pad) * 128;    // bytes per (K-tile, plane) of z rows
     const size_t z_ktile = static_cast<size_t>(planes) * z_plane;  // bytes per K-tile of z rows
-    float* stage_f = reinterpret_cast<float*>(epi);                // down: [16 tokens][256 values]
+    uint8_t* epi_g = epi + g * (kEpiBytes / kGroups);
+    float* stage_f = reinterpret_cast<float*>(epi_g);              // down, fp32: [16 tokens][256 values]
+    __nv_bfloat16* stage_h = reinterpret_cast<__nv_bfloat16*>(epi_g);  // down, bf16: [16 tokens][256 values]
+    float* meta_w = ctrl->meta_w[g];
+    int* meta_o = ctrl->meta_o[g];
+    int* meta_r = ctrl->meta_r[g];
     const int P_used = KT < P ? KT : P;                            // chains that received MMAs
     int li = 0, blk = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
@@ -508,22 +521,22 @@ __global__ void __launch_bounds__(NT, 1)
       if (et < m.rows) {
         const int r = m.row0 + et;
         if (gu) {
-          ctrl->meta_w[et] = p.row_weight[r];
+          meta_w[et] = p.row_weight[r];
         } else {
           const int orow = p.out_row ? p.out_row[r] : r;
           if (p.ep_world) {  // receive row orow of source s goes to s's send position of it
             int sr = 0;
             while (sr + 1 < p.ep_world && orow >= p.ep_recv_start[sr + 1]) ++sr;
-            ctrl->meta_r[et] = sr;
-            ctrl->meta_o[et] = p.ep_src_pos[sr] + orow - p.ep_recv_start[sr];
+            meta_r[et] = sr;
+            meta_o[et] = p.ep_src_pos[sr] + orow - p.ep_recv_start[sr];
           } else {
-            ctrl->meta_o[et] = orow;
+            meta_o[et] = orow;
           }
         }
       }
       // every epilogue warp takes the same branch (a warp that left while the
       // others wait at a named barrier would hold them there)
-      if (!epi_all(mbar_wait_warp(&ctrl->acc_full[b], aph, abort))) {  // also makes the metadata visible
+      if (!epi_all(g, mbar_wait_warp(&ctrl->acc_full[b], aph, abort))) {  // also makes the metadata visible
         if (lane == 0) {
           set_error(p.err, MOSAIC_ERR_TIMEOUT);
           ctrl->abort = 1;
@@ -533,13 +546,13 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_after();
       const uint32_t c_buf = static_cast<uint32_t>(b * P) * acc_w;
       const int lo = p.hilo ? m.rpad : 0;
-      for (int c0 = 0; c0 < m.rpad; c0 += 16, ++blk) {
+      for (int c0 = 16 * g; c0 < m.rpad; c0 += 16 * kGroups, ++blk) {
         float s0[16], s1[16];
         tmem_sum16x2(tq + c_buf + c0, half_off, P_used, acc_w, lo, s0, s1);
         const int ncol = min(16, m.rows - c0);  // token columns of this block that exist
         if (gu) {
-          uint8_t* stage_b = epi + (blk & 1) * 4096;  // [planes][16 tokens][128 B], alternating
-          float4* red = ctrl->red4[blk & 1];
+          uint8_t* stage_b = epi_g + (blk & 1) * 4096;  // [planes][16 tokens][128 B], alternating
+          float4* red = ctrl->red4[g][blk & 1];
           float zd[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -553,7 +566,7 @@ __global__ void __launch_bounds__(NT, 1)
               gv = fminf(gv, p.swiglu_limit);
               uv = fminf(fmaxf(uv, -p.swiglu_limit), p.swiglu_limit);
             }
-            const float w = (j < ncol) ? ctrl->meta_w[c0 + j] : 0.f;
+            const float w = (j < ncol) ? meta_w[c0 + j] : 0.f;
             float z = gv / (1.0f + expf(-gv)) * uv;
             z = z * w;
             zd[j] = (j < ncol) ? bf16r(z) : 0.f;
@@ -567,7 +580,7 @@ __global__ void __launch_bounds__(NT, 1)
             for (int j = 0; j < 16; ++j) a[j] = fabsf(zd[j]);
             const float cm = warp_colmax16(a);
             if ((lane & 1) == 0) reinterpret_cast<float*>(&red[(lane >> 1) & 15])[q] = cm;
-            epi_bar();
+            epi_bar(g);
             int my_ex = 0;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -613,7 +626,7 @@ __global__ void __launch_bounds__(NT, 1)
               reinterpret_cast<uint8_t*>(zsf + sf_word(col))[q] = static_cast<uint8_t>(my_e + 127);
             }
           }
-          epi_bar();
+          epi_bar(g);
           // 16-byte stores of whole 128-byte z rows: planes x 16 tokens x 8 vectors
           uint8_t* zq = p.zq + static_cast<size_t>(m.nb) * z_ktile;
           for (int v = et; v < planes * 128; v += 128) {
@@ -625,6 +638,7 @@ __global__ void __launch_bounds__(NT, 1)
           // the next block writes the other staging buffer and the other maxima
         } else {
           // partials of the two hidden blocks, staged as [token][256 values]
+          // (fp32 partials as fp32, bf16 ones rounded here)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float v0 = s0[j], v1 = s1[j];
@@ -632,40 +646,36 @@ __global__ void __launch_bounds__(NT, 1)
               v0 = bf16r(v0);
               v1 = bf16r(v1);
             }
-            stage_f[j * 256 + lrow] = v0;
-            stage_f[j * 256 + 128 + lrow] = v1;
+            if (p.out_f32) {
+              stage_f[j * 256 + lrow] = v0;
+              stage_f[j * 256 + 128 + lrow] = v1;
+            } else {
+              stage_h[j * 256 + lrow] = __float2bfloat16_rn(v0);
+              stage_h[j * 256 + 128 + lrow] = __float2bfloat16_rn(v1);
+            }
           }
-          epi_bar();
+          epi_bar(g);
           // 16-byte stores: per token, two runs of 128 values (block nb of each half)
           const int hb = p.H / 2;
           const int esz = p.out_f32 ? 4 : 2;
-          for (int v = et; v < (p.out_f32 ? 16 * 64 : 16 * 32); v += 128) {
-            // fp32: 16 tokens x 2 halves x 32 float4; bf16: 16 x 2 x 16 vectors of 8
-            const int per = p.out_f32 ? 32 : 16;
+          const int per = p.out_f32 ? 32 : 16;  // 16-byte vectors per run of 128 values
+          for (int v = et; v < 16 * 2 * per; v += 128) {
             const int j = v / (2 * per), h = (v / per) & 1, w16 = v % per;
             if (j >= ncol) continue;
-            const int orow = ctrl->meta_o[c0 + j];
-            uint8_t* row_base = p.ep_world ? p.ep_regions[ctrl->meta_r[c0 + j]] + p.ep_ret_off +
+            const int orow = meta_o[c0 + j];
+            uint8_t* row_base = p.ep_world ? p.ep_regions[meta_r[c0 + j]] + p.ep_ret_off +
                                                  static_cast<size_t>(orow) * p.H * esz
                                            : static_cast<uint8_t*>(p.out) + static_cast<size_t>(orow) * p.H * esz;
             uint4* dst = reinterpret_cast<uint4*>(row_base + static_cast<size_t>(h * hb + m.nb * 128) * esz) + w16;
-            const float* src = stage_f + j * 256 + h * 128;
-            if (p.out_f32) {
-              *dst = *reinterpret_cast<const uint4*>(src + w16 * 4);
-            } else {
-              uint4 pk;
-              __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(src[w16 * 8 + 2 * i], src[w16 * 8 + 2 * i + 1]);
-              *dst = pk;
-            }
+            *dst = p.out_f32 ? reinterpret_cast<const uint4*>(stage_f + j * 256 + h * 128)[w16]
+                             : reinterpret_cast<const uint4*>(stage_h + j * 256 + h * 128)[w16];
           }
-          epi_bar();
+          epi_bar(g);
         }
       }
       tc_fence_before();
       mbar_arrive(&ctrl->acc_empty[b]);
-      epi_bar();  // every warp is done with this item's metadata before the next item's is written
+      epi_bar(g);  // every warp is done with this item's metadata before the next item's is written
     }
     // partials stored into other ranks' memory are made visible at system
     // scope before the kernel ends (the next kernel stamps their flags)
@@ -698,6 +708,9 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   }
   if (p.K % 128 || p.K < 128) return cudaErrorInvalidValue;
   if (p.mode == 1 && p.H % 256) return cudaErrorInvalidValue;
+  // the E4M3 instance runs two epilogue groups on the warps of the unused issuer
+  // pairs, each staging bf16 partials in half of the staging area
+  if (!p.hilo && (p.parities != 1 || (p.mode == 1 && p.out_f32))) return cudaErrorInvalidValue;
   const Plan pl = make_plan(planes, p.brows);
   if (pl.stages < 2) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes(planes, p.brows);
