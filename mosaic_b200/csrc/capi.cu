@@ -308,9 +308,10 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   gp.swiglu_limit = d->swiglu_limit;
   gp.expert_slot = expert_slot;
   gp.bank_slots = n_map;
-  // the copier pays off when two accumulator buffers keep the issuers busy; with
-  // one buffer (wide decode tiles) its extra hop per stage costs more than it saves
-  gp.sf_copier = w.nbuf == 2 ? 1 : 0;
+  // the copier pays off for double-buffered two-plane (decode) tiles; with one
+  // buffer (wide decode tiles) or E4M3 tiles its extra hop per stage costs more
+  // than it saves
+  gp.sf_copier = (w.nbuf == 2 && hilo) ? 1 : 0;
   gp.err = lp.err;
 
   // gate/up

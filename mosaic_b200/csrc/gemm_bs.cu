@@ -715,10 +715,11 @@ cudaError_t launch_moe_gemm(const CUtensorMap& tmap_w, const CUtensorMap& tmap_x
   if (pl.stages < 2) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes(planes, p.brows);
   // the three tile shapes the workspace plans use: E4M3 tiles of 112 rows
-  // (double-buffered), two-plane tiles of 16 rows (double-buffered) and of 32
-  // rows (single-buffered, no copier)
+  // (double-buffered, no copier: the issuers' own scale copies beat the copier's
+  // extra barrier hop per stage there), two-plane tiles of 16 rows
+  // (double-buffered, with the copier) and of 32 rows (single-buffered, no copier)
   void (*kernel)(const CUtensorMap, const CUtensorMap, const GemmParams) = nullptr;
-  if (planes == 1 && p.brows == 112 && p.sf_copier) kernel = moe_gemm_kernel<kThreadsCopier, 1, 112>;
+  if (planes == 1 && p.brows == 112 && !p.sf_copier) kernel = moe_gemm_kernel<kThreadsPlain, 1, 112>;
   if (planes == 2 && p.brows == 16 && p.sf_copier) kernel = moe_gemm_kernel<kThreadsCopier, 2, 16>;
   if (planes == 2 && p.brows == 32 && !p.sf_copier) kernel = moe_gemm_kernel<kThreadsPlain, 2, 32>;
   if (!kernel) return cudaErrorInvalidValue;
