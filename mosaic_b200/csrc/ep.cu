@@ -17,6 +17,21 @@ namespace {
 
 constexpr int kPackWarps = 8;
 
+// One warp copies one row of n 16-byte vectors, four loads in flight per lane
+// (a copy loop with one load per store waits out a load latency per vector).
+__device__ __forceinline__ void warp_copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int n, int lane) {
+  int c = lane;
+  for (; c + 96 < n; c += 128) {
+    const uint4 a = src[c], b = src[c + 32], d = src[c + 64], e = src[c + 96];
+    dst[c] = a;
+    dst[c + 32] = b;
+    dst[c + 64] = d;
+    dst[c + 96] = e;
+  }
+  for (; c < n; c += 32) dst[c] = src[c];
+}
+
+
 // One warp per send row: 16-byte vector copies of the token row, then the tail.
 __global__ void __launch_bounds__(kPackWarps * 32) ep_pack_kernel(const uint4* __restrict__ x, int H, int A, int E,
                                                                   int E_local, const int* __restrict__ offsets,
@@ -36,7 +51,7 @@ __global__ void __launch_bounds__(kPackWarps * 32) ep_pack_kernel(const uint4* _
     const int t = row_token[r];
     const uint4* src = x + static_cast<size_t>(t) * vec_per_row;
     uint4* dst = send + static_cast<size_t>(r) * stride_vec;
-    for (int v = lane; v < vec_per_row; v += 32) dst[v] = src[v];
+    warp_copy_row(dst, src, vec_per_row, lane);
     if (lane == 0) {
       // expert of sorted row r: the last e with offsets[e] <= r
       int lo = 0, hi = E;  // invariant: offsets[lo] <= r < offsets[hi]
@@ -190,16 +205,17 @@ __global__ void __launch_bounds__(256) ep_send_kernel(const EpPeersDev P, const 
   __syncthreads();
   const uint32_t epoch = own->epoch;
   const int cpr = P.row_bytes / 16;
-  const long long total = static_cast<long long>(g.send_start[P.world]) * cpr;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(i / cpr), c = static_cast<int>(i - static_cast<long long>(r) * cpr);
+  const int rows = g.send_start[P.world];
+  const int lane = threadIdx.x & 31;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  // a warp per row: the row's destination once, then the row's vectors
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nwarps) {
     int d = 0;
     while (r >= g.send_start[d + 1]) ++d;
     if (!g.fits[d]) continue;
     uint4* dst = reinterpret_cast<uint4*>(P.regions[d] + P.recv_off) +
-                 static_cast<size_t>(g.dest_off[d] + r - g.send_start[d]) * cpr + c;
-    *dst = send[static_cast<size_t>(r) * cpr + c];
+                 static_cast<size_t>(g.dest_off[d] + r - g.send_start[d]) * cpr;
+    warp_copy_row(dst, send + static_cast<size_t>(r) * cpr, cpr, lane);
   }
   __threadfence_system();
   __syncthreads();
@@ -222,15 +238,14 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpPeersDev P, cons
   const uint32_t epoch = own->epoch;
   const int cpr = P.ret_row_bytes / 16;
   const int rows = own->recv_count;
-  const long long total = static_cast<long long>(rows) * cpr;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(i / cpr), c = static_cast<int>(i - static_cast<long long>(r) * cpr);
+  const int lane = threadIdx.x & 31;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nwarps) {
     int s = 0;
     while (r >= g.recv_start[s + 1]) ++s;
     uint4* dst = reinterpret_cast<uint4*>(P.regions[s] + P.ret_off) +
-                 static_cast<size_t>(g.src_pos[s] + r - g.recv_start[s]) * cpr + c;
-    *dst = partials[static_cast<size_t>(r) * cpr + c];
+                 static_cast<size_t>(g.src_pos[s] + r - g.recv_start[s]) * cpr;
+    warp_copy_row(dst, partials + static_cast<size_t>(r) * cpr, cpr, lane);
   }
   __threadfence_system();
   __syncthreads();
