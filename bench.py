@@ -54,6 +54,10 @@ LAYER_FLOP_PER_TOKEN = 9 * (GU_FLOP_PER_ROW + DN_FLOP_PER_ROW)  # 8 routed + 1 s
 # (65 experts streamed).  Traffic grows with the number of experts streamed, so the
 # full launch's traffic is this ratio times its algorithmic bytes.
 GU_TRAFFIC_RATIO = (1.0408e9 + 7.37e6) / 1_013_841_920
+# dram__bytes_read.sum + dram__bytes_write.sum of the headline's gate/up launch (4096 FP8
+# tokens, 256 + 1 experts), one ncu capture of `bench.py --act fp8 --tokens 4096
+# --experts 256 --profile-small` (the same layer and routing as the N = 1 headline).
+GU_PREFILL_TRAFFIC = 4_554_863_360 + 72_959_744
 HEAD_T = 4096        # tokens per GPU of the headline
 CPU_SAMPLE_T = 512   # tokens per step of the CPU reference path
 SEED = 1234
@@ -279,7 +283,7 @@ def e2e(layer, x, steps, dist_on):
 
 
 
-def fp8_roofline(gemm_ms: float, rows: int, tf_peak: float, peak_src: str) -> dict:
+def fp8_roofline(gemm_ms: float, rows: int, tf_peak: float, peak_src: str, traffic=None) -> dict:
     """Gate/up launch against the tensor-core peak.  kind::mxf8f6f4 (E2M1 x E4M3)
     runs at the FP8 rate, twice the bf16 rate: the denominator is twice the
     measured dense bf16 peak (cuBLAS, MEASURED_PEAKS.json)."""
@@ -288,7 +292,7 @@ def fp8_roofline(gemm_ms: float, rows: int, tf_peak: float, peak_src: str) -> di
     peak = 2.0 * tf_peak
     return {"kernel": "moe_gemm_kernel (gate/up + SwiGLU + act_quant, tcgen05 kind::mxf8f6f4 block-scaled)",
             "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": None, "algorithmic_flops": flops,
+            "traffic": traffic, "algorithmic_flops": flops,
             "peak_source": f"2 x {peak_src} dense bf16 ({tf_peak:.1f} TF/s): the FP8 MMA rate is twice the bf16 rate",
             "frac_of_nominal_fp8_4500": achieved / 4500.0, "frac_of_nominal_fp4_9000": achieved / 9000.0}
 
@@ -403,7 +407,8 @@ def headline_single(args, local, hbm, tf_peak, peak_src, bank):
                   "graph": "one CUDA graph per layer step"},
         "clocks": clocks,
         "gpu_launches": layer_launches(HEAD_T, 1) * steps,
-        "roofline": fp8_roofline(stages["gemm_gate_up"], rows, tf_peak, peak_src),
+        "roofline": dict(fp8_roofline(stages["gemm_gate_up"], rows, tf_peak, peak_src, GU_PREFILL_TRAFFIC),
+                         traffic_source="ncu dram bytes of this launch (same layer, routing and tokens)"),
         "layer_tflops": flops / (ms * 1e-3) / 1e12,
         "stages_ms": stages,
         "e2e": {"value": HEAD_T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bi,
