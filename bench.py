@@ -78,15 +78,16 @@ def layer_launches(t: int, world: int) -> int:
     Router: tensor-core logits + top-k, plus the W split above 128 tokens.
     Layout: one CTA up to 1024 assignments, else count / scan / rank / finish.
     One GPU: router, layout, rows_quant, gate/up, down, combine.  Expert
-    parallel: router, dispatch (layout, pack, destination counts), exchange
-    (counts, send, wait), the shared expert and the received rows (per-row
-    metadata, layout, rows_quant, gate/up, down each), return (signal, wait),
-    combine."""
+    parallel (FP8, E4M3 rows): router, dispatch + exchange (layout, destination
+    counts, count exchange, quantise-and-send, wait), the shared expert
+    (per-row metadata, layout, rows_quant, gate/up, down) and the received
+    rows (per-row metadata, layout, placement, gate/up, down), return (signal,
+    wait), combine."""
     router = 3 if t > 128 else 2
     lay = lambda a: 4 if a > 1024 else 1  # noqa: E731
     if world == 1:
         return router + lay(t * 8) + 4
-    return router + (lay(t * 8) + 2) + 3 + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
+    return router + (lay(t * 8) + 4) + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
 
 
 def parse():

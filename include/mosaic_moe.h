@@ -343,6 +343,12 @@ MOSAIC_API int mosaic_moe_routed_slots(const mosaic_moe_dims* dims, const void* 
  * Send row (MOSAIC_EP_ROW_BYTES(H) bytes, 16-B aligned): H bf16 token values,
  * then int32 {local expert id, route weight (fp32 bits), source token, dest}. */
 #define MOSAIC_EP_ROW_BYTES(H) ((size_t)(H) * 2u + 16u)
+/* E4M3 exchange row (MOSAIC_ACT_FP8 layers over the peer-memory exchange with
+ * row_e4m3 = 1): the token row quantised as the layer quantises it
+ * (act_quant_ref: per 128 values a power-of-two scale, E4M3 codes), H code
+ * bytes, then the H/128 biased scale exponents (uint8, 2^(e-127)) padded with
+ * zeros to a multiple of 16 bytes, then the same 16-byte tail. */
+#define MOSAIC_EP_ROW_BYTES_E4M3(H) ((size_t)(H) + ((((size_t)(H) / 128u) + 15u) & ~(size_t)15u) + 16u)
 
 /* Layout + gather of one rank's assignments.  dims: the layer (tokens = this
  * rank's T, n_experts = global E, E % world == 0).  idx int64 [T, top_k],
@@ -414,6 +420,9 @@ typedef struct mosaic_ep_peers {
   int32_t wait_us;        /* budget of each device-side wait on a peer's flag, in microseconds
                              (0: about 2 s); a wait that runs out records MOSAIC_ERR_TIMEOUT in
                              this rank's region and the kernel returns */
+  int32_t row_e4m3;       /* 1: the exchange carries E4M3 rows (MOSAIC_EP_ROW_BYTES_E4M3; needs
+                             partial_f32 = 0 and H <= 16384), 0: bf16 rows (MOSAIC_EP_ROW_BYTES) */
+  int32_t reserved;       /* 0 */
   void* regions[MOSAIC_EP_MAX_WORLD];  /* rank r's region as mapped in this process (own at [rank]) */
 } mosaic_ep_peers;
 
@@ -422,7 +431,8 @@ MOSAIC_API int mosaic_ep_region_alloc(size_t bytes, void** region, uint8_t* ipc_
 MOSAIC_API int mosaic_ep_region_open(const uint8_t* ipc_handle64, void** peer_region);
 MOSAIC_API int mosaic_ep_region_close(void* peer_region);
 MOSAIC_API int mosaic_ep_region_free(void* region);
-/* Pointers into this rank's own region: receive rows [max_recv_rows][MOSAIC_EP_ROW_BYTES(H)],
+/* Pointers into this rank's own region: receive rows [max_recv_rows][row bytes] (MOSAIC_EP_ROW_BYTES(H),
+ * or MOSAIC_EP_ROW_BYTES_E4M3(H) with row_e4m3),
  * the device int32 received-row count, and the return buffer
  * [max_send_rows + max_tokens][H] (fp32 or bf16). */
 MOSAIC_API int mosaic_ep_region_view(const mosaic_ep_peers* peers, void** recv_rows, int32_t** recv_count,
@@ -430,13 +440,29 @@ MOSAIC_API int mosaic_ep_region_view(const mosaic_ep_peers* peers, void** recv_r
 MOSAIC_API int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void* send_rows, const int32_t* dest_counts,
                                        mosaic_stream_t stream);
 MOSAIC_API int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials, mosaic_stream_t stream);
+/* Dispatch fused with the exchange, for MOSAIC_ACT_FP8 layers with
+ * peers->row_e4m3 = 1: the layout of mosaic_ep_dispatch, then the count
+ * exchange, then every assignment's token row quantised (act_quant_ref, as
+ * the single-GPU layer does) straight into its owner's receive row as an E4M3
+ * row -- no send buffer, half the NVLink bytes of bf16 rows -- and the wait
+ * until every source's rows have landed here.  Replaces mosaic_ep_dispatch +
+ * mosaic_ep_exchange_rows; the rows received are what mosaic_ep_dispatch
+ * would have sent, quantised.  dims: the layer (tokens = this rank's T <=
+ * peers->max_tokens, n_experts = global E, hidden = peers->hidden); idx /
+ * weights as for mosaic_ep_dispatch; workspace: mosaic_moe_workspace_bytes(dims),
+ * kept for mosaic_ep_combine. */
+MOSAIC_API int mosaic_ep_dispatch_exchange(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers, const void* x,
+                                           const int64_t* idx, const float* weights, void* workspace,
+                                           size_t workspace_bytes, mosaic_stream_t stream);
 /* The expert pass on this rank's received rows with the return fused in: the
  * down GEMM's epilogue stores every partial straight into its source rank's
  * return buffer (NVLink stores overlapping the GEMM), then every source's
  * return flag is stamped and this rank waits for its own.  Replaces
  * mosaic_moe_expert_rows_dev + mosaic_ep_return_partials.  dims as for
  * mosaic_moe_expert_rows (n_experts = this rank's routed experts); workspace:
- * mosaic_moe_expert_rows_workspace_bytes(dims, peers->max_recv_rows). */
+ * mosaic_moe_expert_rows_workspace_bytes(dims, peers->max_recv_rows).  With
+ * peers->row_e4m3 the received E4M3 rows go into the GEMM's operand planes as
+ * they are (no second quantisation; dims->act_mode must be MOSAIC_ACT_FP8). */
 MOSAIC_API int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers,
                                             const mosaic_expert_bank* bank, void* workspace, size_t workspace_bytes,
                                             mosaic_stream_t stream);

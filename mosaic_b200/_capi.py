@@ -27,6 +27,12 @@ def ep_row_bytes(hidden: int) -> int:
     return 2 * hidden + 16
 
 
+def ep_row_bytes_e4m3(hidden: int) -> int:
+    """include/mosaic_moe.h MOSAIC_EP_ROW_BYTES_E4M3: H E4M3 codes, the H/128 scale
+    exponents padded to 16 bytes, the 16-byte tail."""
+    return hidden + ((hidden // 128 + 15) & ~15) + 16
+
+
 # include/mosaic_moe.h MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
 MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -76,6 +82,7 @@ EXPORTED = (
     "mosaic_ep_region_free",
     "mosaic_ep_region_view",
     "mosaic_ep_exchange_rows",
+    "mosaic_ep_dispatch_exchange",
     "mosaic_ep_return_partials",
     "mosaic_ep_expert_rows_return",
     "mosaic_moe_expert_rows_dev",
@@ -134,6 +141,8 @@ class EpPeersC(ctypes.Structure):
         ("hidden", ctypes.c_int32),
         ("partial_f32", ctypes.c_int32),
         ("wait_us", ctypes.c_int32),
+        ("row_e4m3", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
         ("regions", ctypes.c_void_p * EP_MAX_WORLD),
     ]
 
@@ -190,6 +199,8 @@ _SIGS = {
     "mosaic_ep_region_view": ([ctypes.POINTER(EpPeersC), ctypes.POINTER(ctypes.c_void_p),
                                ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "mosaic_ep_exchange_rows": ([ctypes.POINTER(EpPeersC), _P, _P, _P], ctypes.c_int),
+    "mosaic_ep_dispatch_exchange": ([ctypes.POINTER(MoEDims), ctypes.POINTER(EpPeersC), _P, _P, _P, _P, _SZ, _P],
+                                    ctypes.c_int),
     "mosaic_ep_return_partials": ([ctypes.POINTER(EpPeersC), _P, _P], ctypes.c_int),
     "mosaic_ep_expert_rows_return": ([ctypes.POINTER(MoEDims), ctypes.POINTER(EpPeersC), ctypes.POINTER(ExpertBankC),
                                       _P, _SZ, _P], ctypes.c_int),

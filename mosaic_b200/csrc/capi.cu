@@ -438,9 +438,10 @@ namespace {
 int expert_rows_impl(const mosaic_moe_dims* dims, int32_t rows, const int32_t* rows_dev, const void* x_rows,
                      int32_t ldx, const int32_t* ids, const float* weights, int32_t meta_stride, int32_t default_id,
                      const mosaic_expert_bank* bank, void* partials, void* workspace, size_t workspace_bytes,
-                     mosaic_stream_t stream, const EpPeersDev* ep = nullptr) {
+                     mosaic_stream_t stream, const EpPeersDev* ep = nullptr, int e4m3_row_bytes = 0) {
   if (!dims) return MOSAIC_ERR_SHAPE;
   if (rows < 0) return MOSAIC_ERR_SHAPE;
+  if (e4m3_row_bytes && dims->act_mode != MOSAIC_ACT_FP8) return MOSAIC_ERR_SHAPE;
   if (rows == 0) return MOSAIC_OK;
   if (dims->n_experts > 256) return MOSAIC_ERR_UNSUPPORTED;
   const mosaic_moe_dims r = rows_dims(dims, rows);
@@ -476,9 +477,15 @@ int expert_rows_impl(const mosaic_moe_dims* dims, int32_t rows, const int32_t* r
   lp.row_sorted = nullptr;
   if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   const bool hilo = r.act_mode == MOSAIC_ACT_BF16;
-  if (launch_rows_quant(x_rows, rows, rows_dev, r.hidden, ldx, 1, lp.row_of, -1, hilo ? 1 : 0, w.R_pad, lp.row_tile,
-                        lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), s) != cudaSuccess)
+  if (e4m3_row_bytes) {  // rows already quantised by the sender: into the operand planes as they are
+    if (launch_rows_place_e4m3(x_rows, e4m3_row_bytes, rows, rows_dev, r.hidden, lp.row_of, w.R_pad, lp.row_tile,
+                               lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), s) != cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+  } else if (launch_rows_quant(x_rows, rows, rows_dev, r.hidden, ldx, 1, lp.row_of, -1, hilo ? 1 : 0, w.R_pad,
+                               lp.row_tile, lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft),
+                               s) != cudaSuccess) {
     return MOSAIC_ERR_CUDA;
+  }
   // with k = 1 the packed row of input row t is sorted row row_of[t], and
   // row_token[sorted row] = t: partials land in input row order
   return run_gemms(&r, w, ws, lp, bank, dims->has_shared ? dims->n_experts : -1, lp.row_token, partials, s,
@@ -971,12 +978,17 @@ int check_peers(const mosaic_ep_peers* p) {
   if (p->max_recv_rows < 1 || p->max_send_rows < 1 || p->max_tokens < 1) return MOSAIC_ERR_SHAPE;
   if (p->hidden < 256 || p->hidden % 256) return MOSAIC_ERR_SHAPE;
   if (p->wait_us < 0) return MOSAIC_ERR_RANGE;
+  if ((p->row_e4m3 != 0 && p->row_e4m3 != 1) || p->reserved != 0) return MOSAIC_ERR_SHAPE;
+  if (p->row_e4m3 && p->partial_f32) return MOSAIC_ERR_SHAPE;  // E4M3 rows are the FP8 layer's
+  if (p->row_e4m3 && p->hidden > 16384) return MOSAIC_ERR_UNSUPPORTED;
   return MOSAIC_OK;
 }
 
-size_t ep_recv_bytes(const mosaic_ep_peers* p) {
-  return static_cast<size_t>(p->max_recv_rows) * MOSAIC_EP_ROW_BYTES(p->hidden);
+size_t ep_row_bytes(const mosaic_ep_peers* p) {
+  return p->row_e4m3 ? MOSAIC_EP_ROW_BYTES_E4M3(p->hidden) : MOSAIC_EP_ROW_BYTES(p->hidden);
 }
+
+size_t ep_recv_bytes(const mosaic_ep_peers* p) { return static_cast<size_t>(p->max_recv_rows) * ep_row_bytes(p); }
 
 int ep_ret_row_bytes(const mosaic_ep_peers* p) { return p->hidden * (p->partial_f32 ? 4 : 2); }
 
@@ -985,7 +997,7 @@ EpPeersDev ep_dev(const mosaic_ep_peers* p) {
   d.world = p->world;
   d.rank = p->rank;
   d.max_recv_rows = p->max_recv_rows;
-  d.row_bytes = static_cast<int>(MOSAIC_EP_ROW_BYTES(p->hidden));
+  d.row_bytes = static_cast<int>(ep_row_bytes(p));
   d.ret_row_bytes = ep_ret_row_bytes(p);
   d.recv_off = kEpHeaderBytes;
   d.ret_off = up256(kEpHeaderBytes + ep_recv_bytes(p));
@@ -1092,9 +1104,11 @@ int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_pe
   const int32_t* count = &reinterpret_cast<EpRegionHeader*>(own)->recv_count;
   const int rb = ep.row_bytes;
   const int h = peers->hidden;
-  st = expert_rows_impl(dims, peers->max_recv_rows, count, recv, rb / 2, reinterpret_cast<const int32_t*>(recv + 2 * h),
-                        reinterpret_cast<const float*>(recv + 2 * h + 4), rb / 4, 0, bank, nullptr, workspace,
-                        workspace_bytes, stream, &ep);
+  const bool e4m3 = peers->row_e4m3 != 0;
+  const int meta = e4m3 ? rb - 16 : 2 * h;  // byte offset of the row's tail
+  st = expert_rows_impl(dims, peers->max_recv_rows, count, recv, e4m3 ? rb : rb / 2,
+                        reinterpret_cast<const int32_t*>(recv + meta), reinterpret_cast<const float*>(recv + meta + 4),
+                        rb / 4, 0, bank, nullptr, workspace, workspace_bytes, stream, &ep, e4m3 ? rb : 0);
   if (st) return st;
   return launch_ep_signal_return(ep, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? MOSAIC_OK
                                                                                           : MOSAIC_ERR_CUDA;
@@ -1113,6 +1127,52 @@ int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials
                  cudaSuccess
              ? MOSAIC_OK
              : MOSAIC_ERR_CUDA;
+}
+
+int mosaic_ep_dispatch_exchange(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers, const void* x,
+                                const int64_t* idx, const float* weights, void* workspace, size_t workspace_bytes,
+                                mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  st = check_peers(peers);
+  if (st) return st;
+  st = check_regions(peers);
+  if (st) return st;
+  if (!x || !idx || !workspace) return MOSAIC_ERR_SHAPE;
+  if (!peers->row_e4m3 || dims->act_mode != MOSAIC_ACT_FP8 || dims->hidden != peers->hidden) return MOSAIC_ERR_SHAPE;
+  const int world = peers->world;
+  if (dims->n_experts % world) return MOSAIC_ERR_SHAPE;
+  if (dims->tokens > peers->max_tokens ||
+      static_cast<int64_t>(dims->tokens) * dims->top_k > static_cast<int64_t>(peers->max_send_rows))
+    return MOSAIC_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(idx, 8) || (weights && !aligned(weights, 4)) || !aligned(workspace, 256))
+    return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  const int sms = sm_count();
+  if (sms <= 0) return MOSAIC_ERR_CUDA;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  const int T = dims->tokens, k = dims->top_k, E = dims->n_experts;
+  LayoutParams lp{};
+  lp.idx = idx;
+  lp.weights = weights;
+  lp.T = T;
+  lp.k = k;
+  lp.E = E;
+  lp.with_shared = 0;
+  fill_layout(lp, w, ws);
+  lp.row_tile = nullptr;  // no GEMM tiles on the sending side
+  lp.row_pos = nullptr;
+  lp.tiles = nullptr;
+  if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  // the sender runs no GEMM, so the activation planes of the workspace are free
+  int* dest_counts = reinterpret_cast<int*>(ws + w.xq);
+  if (launch_ep_dispatch_send_e4m3(ep_dev(peers), x, dims->hidden, E, E / world, lp.offsets, lp.row_token,
+                                   lp.row_weight, dest_counts, sms, s) != cudaSuccess)
+    return MOSAIC_ERR_CUDA;
+  return MOSAIC_OK;
 }
 
 int mosaic_ep_combine(const mosaic_moe_dims* dims, const void* partials, const void* workspace, void* y,

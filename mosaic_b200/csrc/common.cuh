@@ -283,6 +283,22 @@ __device__ __forceinline__ int quant_block128(const float (&v)[8], uint8_t (&q)[
   return e;
 }
 
+// The same act_quant_ref block with 16 values per lane (the 128-block spans 8
+// aligned lanes): the block maximum is order-free, so every code and the
+// exponent equal quant_block128's.
+__device__ __forceinline__ int quant_block128_x16(const float (&v)[16], uint8_t (&q)[16]) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  const int e = pow2_scale_exp(m, 1e-4f);
+  const float inv = exp2i(-e);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) q[i] = f32_to_e4m3(fminf(fmaxf(v[i] * inv, -448.f), 448.f));
+  return e;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));

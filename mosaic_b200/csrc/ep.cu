@@ -258,6 +258,108 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpPeersDev P, cons
   }
 }
 
+// ------------------------------------------ E4M3 rows, quantised in flight ---
+// A warp per send row r (expert-sorted, hence grouped by owner): the token
+// row x[row_token[r]] is quantised per 128-value block (act_quant_ref, 8 lanes
+// x 16 values per block, 512 values per warp pass, two passes per loop trip)
+// and the codes are stored straight into the owner's receive row, 16 bytes
+// per lane.  The block exponents collect in shared memory and follow the
+// codes, then the meta tail {local expert, route weight bits, token, owner}.
+// No send buffer: x is read once per send row (from L2 after the first).
+constexpr int kSendWarps = 8;
+constexpr int kMaxKtPad = 128;  // H <= 16384
+
+__device__ __forceinline__ void quant_pass(uint8_t* __restrict__ dst, uint8_t* __restrict__ exps, int k0, bool in,
+                                           const float (&v)[16]) {
+  uint8_t q[16];
+  const int e = quant_block128_x16(v, q);  // every lane takes part in the block shuffles
+  if (in) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = q[4 * i] | (q[4 * i + 1] << 8) | (q[4 * i + 2] << 16) | (static_cast<uint32_t>(q[4 * i + 3]) << 24);
+    *reinterpret_cast<uint4*>(dst + k0) = make_uint4(w[0], w[1], w[2], w[3]);
+    if ((threadIdx.x & 7) == 0) exps[k0 >> 7] = static_cast<uint8_t>((e + 127) & 0xFF);
+  }
+}
+
+__device__ __forceinline__ void load16_bf16(const __nv_bfloat16* __restrict__ p, bool in, float (&v)[16]) {
+  if (in) {
+    float a[8], b[8];
+    load8_bf16(p, a);
+    load8_bf16(p + 8, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] = a[i];
+      v[8 + i] = b[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+  }
+}
+
+__global__ void __launch_bounds__(kSendWarps * 32)
+    ep_send_e4m3_kernel(const EpPeersDev P, const __nv_bfloat16* __restrict__ x, int H, int E, int E_local,
+                        const int* __restrict__ offsets, const int* __restrict__ row_token,
+                        const float* __restrict__ row_weight) {
+  __shared__ EpGeom g;
+  __shared__ int off_s[257];
+  __shared__ __align__(16) uint8_t exps_s[kSendWarps][kMaxKtPad];
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  if (threadIdx.x == 0) ep_geometry(P, own, g);
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) off_s[i] = offsets[i];
+  __syncthreads();
+  const uint32_t epoch = own->epoch;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = H / 128, kt_pad = (KT + 15) & ~15;
+  uint8_t* exps = exps_s[warp];
+  const int rows = g.send_start[P.world];
+  for (int r = blockIdx.x * kSendWarps + warp; r < rows; r += gridDim.x * kSendWarps) {
+    int d = 0;
+    while (r >= g.send_start[d + 1]) ++d;
+    if (!g.fits[d]) continue;
+    const int t = row_token[r];
+    const __nv_bfloat16* src = x + static_cast<size_t>(t) * H;
+    uint8_t* dst = P.regions[d] + P.recv_off + static_cast<size_t>(g.dest_off[d] + r - g.send_start[d]) * P.row_bytes;
+    for (int base = 0; base < H; base += 1024) {
+      const int k0 = base + lane * 16, k1 = k0 + 512;
+      float v0[16], v1[16];
+      load16_bf16(src + k0, k0 < H, v0);
+      load16_bf16(src + k1, k1 < H, v1);
+      quant_pass(dst, exps, k0, k0 < H, v0);
+      quant_pass(dst, exps, k1, k1 < H, v1);
+    }
+    for (int i = KT + lane; i < kt_pad; i += 32) exps[i] = 0;
+    __syncwarp();
+    if (lane < kt_pad / 16) reinterpret_cast<uint4*>(dst + H)[lane] = reinterpret_cast<const uint4*>(exps)[lane];
+    if (lane == 0) {
+      int lo = 0, hi = E;  // expert of sorted row r: offsets[lo] <= r < offsets[hi]
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (off_s[mid] <= r)
+          lo = mid;
+        else
+          hi = mid;
+      }
+      const int dest = lo / E_local;
+      *reinterpret_cast<uint4*>(dst + H + kt_pad) =
+          make_uint4(static_cast<uint32_t>(lo - dest * E_local), __float_as_uint(row_weight[r]),
+                     static_cast<uint32_t>(t), static_cast<uint32_t>(dest));
+    }
+    __syncwarp();  // exps is rewritten by the next row
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(&own->send_done, 1u) == gridDim.x - 1) {
+      own->send_done = 0;
+      __threadfence_system();
+      for (int d = 0; d < P.world; ++d) st_release_sys(&hdr_of(P, d)->data_flag[P.rank], epoch);
+    }
+  }
+}
+
 // One CTA, after the down GEMM wrote this rank's partials into the sources'
 // return buffers (its threads fenced them at system scope before exiting):
 // stamp every source's return flag.
@@ -306,6 +408,21 @@ cudaError_t launch_ep_exchange_rows(const EpPeersDev& P, const void* send_rows, 
                                     cudaStream_t stream) {
   ep_counts_kernel<<<1, 32, 0, stream>>>(P, dest_counts);
   ep_send_kernel<<<2 * sms, 256, 0, stream>>>(P, static_cast<const uint4*>(send_rows));
+  ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int H, int E, int E_local,
+                                         const int* offsets, const int* row_token, const float* row_weight,
+                                         int* dest_counts, int sms, cudaStream_t stream) {
+  const int kt_pad = (H / 128 + 15) & ~15;
+  if (H % 256 || kt_pad > kMaxKtPad || E > 256 || E_local < 1 ||
+      P.row_bytes != H + kt_pad + 16)
+    return cudaErrorInvalidValue;
+  ep_dest_counts_kernel<<<(P.world + 127) / 128, 128, 0, stream>>>(offsets, E_local, P.world, dest_counts);
+  ep_counts_kernel<<<1, 32, 0, stream>>>(P, dest_counts);
+  ep_send_e4m3_kernel<<<2 * sms, kSendWarps * 32, 0, stream>>>(P, static_cast<const __nv_bfloat16*>(x), H, E, E_local,
+                                                                offsets, row_token, row_weight);
   ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
   return cudaGetLastError();
 }

@@ -191,6 +191,13 @@ cudaError_t launch_emit_tiles(const int32_t* counts, int E, int block_m, int max
 cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int ldx, int k, const int* row_of,
                               int shared_base, int hilo, int R_pad, const int* row_tile, const int* row_pos,
                               uint8_t* xq, uint32_t* sft, cudaStream_t stream);
+// E4M3 exchange rows (codes [H], biased scale exponents [H/128] padded to 16
+// bytes, then the meta tail) -> the same packed planes and scale chunks as
+// launch_rows_quant in act_quant_ref mode: row r goes to packed row row_of[r]
+// (rows with row_of < 0 are skipped); with R_dev only the first *R_dev rows.
+cudaError_t launch_rows_place_e4m3(const void* rows, int row_bytes, int R, const int* R_dev, int H, const int* row_of,
+                                   int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
+                                   cudaStream_t stream);
 cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
 cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
 // halves = 2 interleaves the two row halves of each matrix (gate rows, up rows)
@@ -250,6 +257,14 @@ cudaError_t launch_ep_return_partials(const EpPeersDev& P, const void* partials,
 // After a down GEMM that wrote the partials straight into the sources' return
 // buffers: stamp every source's return flag, then wait for this rank's.
 cudaError_t launch_ep_signal_return(const EpPeersDev& P, cudaStream_t stream);
+// E4M3 rows without a send buffer: destination counts from the layout's
+// offsets (kept in dest_counts), the count exchange, then a warp per send row
+// quantises x[row_token[r]] (act_quant_ref) straight into its owner's receive
+// row, and the wait for every source's rows.  P.row_bytes must be
+// MOSAIC_EP_ROW_BYTES_E4M3(H).
+cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int H, int E, int E_local,
+                                         const int* offsets, const int* row_token, const float* row_weight,
+                                         int* dest_counts, int sms, cudaStream_t stream);
 
 // ---- combine (combine.cu)
 cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,

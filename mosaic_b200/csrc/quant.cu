@@ -135,6 +135,46 @@ __global__ void __launch_bounds__(kRqThreads) rows_quant_kernel(const __nv_bfloa
   }
 }
 
+// A warp per E4M3 exchange row: its codes go to packed row p = row_of[r] of
+// the K-tile-major plane (one 128-byte line per K-tile, four 16-byte loads in
+// flight per lane) and each block exponent, as act_quant_ref's scale word
+// (the exponent in all four bytes), into the token tile's scale chunk: what
+// rows_quant_kernel writes for the bf16 row in act_quant_ref mode.
+constexpr int kPlaceWarps = 8;
+
+__global__ void __launch_bounds__(kPlaceWarps * 32)
+    rows_place_e4m3_kernel(const uint8_t* __restrict__ rows, int row_bytes, int R, const int* __restrict__ R_dev,
+                           int H, const int* __restrict__ row_of, int R_pad, const int* __restrict__ row_tile,
+                           const int* __restrict__ row_pos, uint8_t* __restrict__ xq, uint32_t* __restrict__ sft) {
+  griddep_wait();  // the layout's row maps are visible
+  griddep_launch();
+  const int n = R_dev ? min(*R_dev, R) : R;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = H / 128, nv = H / 16;
+  for (int r = blockIdx.x * kPlaceWarps + warp; r < n; r += gridDim.x * kPlaceWarps) {
+    const int p = row_of[r];
+    if (p < 0) continue;
+    const uint8_t* row = rows + static_cast<size_t>(r) * row_bytes;
+    const uint4* src = reinterpret_cast<const uint4*>(row);
+    // 16-byte vector v holds K values [16v, 16v + 16): K-tile v / 8, line offset 16 (v % 8)
+    uint8_t* dst = xq + static_cast<size_t>(p) * 128;
+    const size_t plane = static_cast<size_t>(R_pad) * 128;
+    int v = lane;
+    for (; v + 96 < nv; v += 128) {
+      const uint4 a = src[v], b = src[v + 32], c = src[v + 64], d = src[v + 96];
+      *reinterpret_cast<uint4*>(dst + (v >> 3) * plane + (v & 7) * 16) = a;
+      *reinterpret_cast<uint4*>(dst + ((v + 32) >> 3) * plane + (v & 7) * 16) = b;
+      *reinterpret_cast<uint4*>(dst + ((v + 64) >> 3) * plane + (v & 7) * 16) = c;
+      *reinterpret_cast<uint4*>(dst + ((v + 96) >> 3) * plane + (v & 7) * 16) = d;
+    }
+    for (; v < nv; v += 32) *reinterpret_cast<uint4*>(dst + (v >> 3) * plane + (v & 7) * 16) = src[v];
+    const int tile = row_tile[p], pos = row_pos[p] & 0xFF;
+    for (int kt = lane; kt < KT; kt += 32)
+      sft[(static_cast<size_t>(tile) * KT + kt) * 128 + (pos & 31) * 4 + (pos >> 5)] =
+          static_cast<uint32_t>(row[H + kt]) * 0x01010101u;
+  }
+}
+
 // act_quant_ref: grid (M, ceil(K / 1024)), 128 threads.
 __global__ void __launch_bounds__(128) act_quant_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
                                                         uint8_t* __restrict__ q, float* __restrict__ scale) {
@@ -289,6 +329,20 @@ cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int
   const cudaError_t e = launch_k(rows_quant_kernel, dim3(gx, gy), dim3(kRqThreads), 0, stream,
                                  static_cast<const __nv_bfloat16*>(x), T, T_dev, H, ldx, k, row_of, shared_base, hilo,
                                  R_pad, row_tile, row_pos, xq, sft);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rows_place_e4m3(const void* rows, int row_bytes, int R, const int* R_dev, int H, const int* row_of,
+                                   int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
+                                   cudaStream_t stream) {
+  if (R <= 0) return cudaSuccess;
+  if (H % 128 || row_bytes % 16 || row_bytes < H + H / 128) return cudaErrorInvalidValue;
+  int grid = (R + kPlaceWarps - 1) / kPlaceWarps;
+  if (grid > 148 * 8) grid = 148 * 8;
+  const cudaError_t e = launch_k(rows_place_e4m3_kernel, dim3(grid), dim3(kPlaceWarps * 32), 0, stream,
+                                 static_cast<const uint8_t*>(rows), row_bytes, R, R_dev, H, row_of, R_pad, row_tile,
+                                 row_pos, xq, sft);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

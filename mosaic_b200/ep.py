@@ -144,14 +144,16 @@ class PeerExchange:
     regions are opened (plain IPC mappings, no multicast).  The regions hold
     the flags, the count matrix, the receive rows and the return partials of
     the device-driven exchange (``mosaic_ep_exchange_rows`` /
-    ``mosaic_ep_return_partials``).  Capacity: ``max_tokens`` tokens per rank;
+    ``mosaic_ep_return_partials``).  With ``row_e4m3`` (FP8 layers) the rows
+    are E4M3 rows quantised by the sender (``mosaic_ep_dispatch_exchange``).
+    Capacity: ``max_tokens`` tokens per rank;
     the receive side is sized for any routing.  ``wait_us`` bounds every
     device-side wait on another rank's flag; a wait that runs out records
     MOSAIC_ERR_TIMEOUT in this rank's region (``error()``) and the kernel returns.
     """
 
     def __init__(self, *, group=None, max_tokens: int, top_k: int, n_experts: int, hidden: int,
-                 partial_f32: bool, wait_us: int = 0):
+                 partial_f32: bool, wait_us: int = 0, row_e4m3: bool = False):
         lib = C.lib()
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -169,6 +171,8 @@ class PeerExchange:
         pe.hidden = hidden
         pe.partial_f32 = int(bool(partial_f32))
         pe.wait_us = int(wait_us)  # budget of each device-side wait on a peer (0: about 2 s)
+        pe.row_e4m3 = int(bool(row_e4m3))  # E4M3 exchange rows (FP8 layers), half the bytes of bf16 rows
+        self.row_e4m3 = bool(row_e4m3)
         nbytes = lib.mosaic_ep_region_bytes(ctypes.byref(pe))
         if nbytes == 0:
             raise ValueError("invalid peer-exchange geometry")
@@ -306,7 +310,8 @@ class ExpertParallelMoELayer(nn.Module):
             self._px = PeerExchange(group=self.group, max_tokens=self.max_tokens,
                                     top_k=max(self.cfg.num_experts_per_tok, self._k()),
                                     n_experts=self.cfg.n_routed_experts,
-                                    hidden=self.cfg.hidden_size, partial_f32=self.cfg.act_mode == "bf16")
+                                    hidden=self.cfg.hidden_size, partial_f32=self.cfg.act_mode == "bf16",
+                                    row_e4m3=self.cfg.act_mode == "fp8")
         return self._px
 
     def close(self) -> None:
@@ -404,10 +409,16 @@ class ExpertParallelMoELayer(nn.Module):
                            kern._ws_shared, xf.device)
         w, idx = self._route(xf, token_ids)
         dims = self._dims(t)
-        send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
         pe = ctypes.byref(px.peers)
-        C.check(lib.mosaic_ep_exchange_rows(pe, ops._ptr(send), ops._ptr(counts), ops._stream()),
-                "mosaic_ep_exchange_rows")
+        if px.row_e4m3:  # layout, counts, rows quantised straight into the owners' buffers
+            ws = kern._ws_dispatch.get(lib.mosaic_moe_workspace_bytes(ctypes.byref(dims)), xf.device)
+            C.check(lib.mosaic_ep_dispatch_exchange(ctypes.byref(dims), pe, ops._ptr(xf), ops._ptr(idx), ops._ptr(w),
+                                                    ops._ptr(ws), ws.numel(), ops._stream()),
+                    "mosaic_ep_dispatch_exchange")
+        else:
+            send, counts, ws = kern.dispatch(dims, self.world, xf, idx, w)
+            C.check(lib.mosaic_ep_exchange_rows(pe, ops._ptr(send), ops._ptr(counts), ops._stream()),
+                    "mosaic_ep_exchange_rows")
         # expert pass on the received rows; the down epilogue stores every partial
         # straight into its source's return buffer
         ws_rows = kern._ws_rows.get(lib.mosaic_moe_expert_rows_workspace_bytes(ctypes.byref(dl), px.max_recv_rows),

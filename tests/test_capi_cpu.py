@@ -195,3 +195,55 @@ def test_rms_norm_validation_before_launch():
     assert st == C.MOSAIC_ERR_RANGE
     st = lib.mosaic_rms_norm(fake + 8, fake, 4, 256, 1e-6, fake, None, None, None)
     assert st == C.MOSAIC_ERR_ALIGN
+
+
+def test_ep_row_sizes_match_header_and_region_geometry():
+    """MOSAIC_EP_ROW_BYTES(_E4M3) as the header defines them; an E4M3 region
+    holds max_recv_rows E4M3 rows; E4M3 rows with fp32 partials (a bf16
+    layer), a non-zero reserved field or H > 16384 are refused (0 bytes)."""
+    text = HEADER.read_text()
+    assert "#define MOSAIC_EP_ROW_BYTES_E4M3(H) ((size_t)(H) + ((((size_t)(H) / 128u) + 15u) & ~(size_t)15u) + 16u)" \
+        in text
+    assert C.ep_row_bytes_e4m3(7168) == 7248 and C.ep_row_bytes(7168) == 14352
+    assert C.ep_row_bytes_e4m3(512) == 544 and C.ep_row_bytes_e4m3(2048 + 128) == 2176 + 32 + 16
+    lib = C.lib()
+
+    def region(**kw):
+        pe = C.EpPeersC()
+        pe.world, pe.rank, pe.max_tokens, pe.hidden, pe.partial_f32 = 2, 0, 8, 7168, 0
+        pe.max_send_rows, pe.max_recv_rows = 64, 128
+        for k, v in kw.items():
+            setattr(pe, k, v)
+        return lib.mosaic_ep_region_bytes(ctypes.byref(pe))
+
+    bf16_rows, e4m3_rows = region(), region(row_e4m3=1)
+    assert bf16_rows - e4m3_rows == 128 * (C.ep_row_bytes(7168) - C.ep_row_bytes_e4m3(7168))
+    assert region(row_e4m3=1, partial_f32=1) == 0
+    assert region(row_e4m3=2) == 0 and region(reserved=1) == 0
+    assert region(row_e4m3=1, hidden=16384 + 256) == 0 and region(hidden=16384 + 256) > 0
+
+
+def test_ep_dispatch_exchange_validation_before_launch():
+    """The fused E4M3 dispatch refuses a bf16 layer, a bf16-row exchange and a
+    rank's tokens above the exchange capacity before any device call."""
+    from mosaic_b200 import MoEConfig
+
+    lib = C.lib()
+    fake = 1 << 20
+    pe = C.EpPeersC()
+    pe.world, pe.rank, pe.max_tokens, pe.hidden, pe.partial_f32, pe.row_e4m3 = 1, 0, 8, 512, 0, 1
+    pe.max_send_rows, pe.max_recv_rows = 32, 32
+    pe.regions[0] = fake
+    cfg = MoEConfig(hidden_size=512, moe_intermediate_size=256, n_routed_experts=32, num_experts_per_tok=4,
+                    n_group=1, topk_group=1, act_mode="fp8")
+
+    def call(d, p):
+        return lib.mosaic_ep_dispatch_exchange(ctypes.byref(d), ctypes.byref(p), fake, fake, fake, fake, 1 << 40,
+                                               None)
+
+    assert call(cfg.dims(9, True), pe) == C.MOSAIC_ERR_SHAPE  # 9 tokens > max_tokens 8
+    d_bf16 = MoEConfig(hidden_size=512, moe_intermediate_size=256, n_routed_experts=32, num_experts_per_tok=4,
+                       n_group=1, topk_group=1, act_mode="bf16").dims(8, True)
+    assert call(d_bf16, pe) == C.MOSAIC_ERR_SHAPE
+    pe.row_e4m3 = 0
+    assert call(cfg.dims(8, True), pe) == C.MOSAIC_ERR_SHAPE

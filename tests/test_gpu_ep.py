@@ -141,6 +141,61 @@ def test_ep_dispatch_rows_match_cpu_restatement():
     assert torch.equal(send.cpu(), cs)
 
 
+class _DevBytes:
+    """A uint8 view of device memory the C ABI owns (the exchange region)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+@pytest.mark.parametrize("hidden", [512, 768, 7168])
+def test_ep_e4m3_rows_equal_act_quant_of_the_send_rows(hidden):
+    """mosaic_ep_dispatch_exchange at world 1: the received E4M3 rows are, byte
+    for byte, the CPU restatement's send rows (expert order, same tails) with
+    the token values replaced by the oracle's act_quant_ref codes and biased
+    exponents (zero padding up to 16 bytes)."""
+    import ctypes
+
+    from mosaic_b200 import _capi as C
+    from mosaic_b200 import MoEConfig, ops, synthetic
+    from mosaic_b200.ep import PeerExchange
+    from oracle.formats import act_quant_ref
+    from tests.ep_cpu_kernels import CpuEPKernels
+
+    t, k, e = 77, 4, 32
+    cfg = MoEConfig(hidden_size=hidden, moe_intermediate_size=256, n_routed_experts=e, num_experts_per_tok=k,
+                    n_group=1, topk_group=1, act_mode="fp8")
+    x = synthetic.make_tokens(t, hidden, 31) * 3.0
+    g = torch.Generator().manual_seed(5)
+    idx = torch.stack([torch.randperm(e, generator=g)[:k] for _ in range(t)]).cuda()
+    w = torch.rand(t, k, generator=g).cuda()
+    d = cfg.dims(t, True)
+    px = PeerExchange(max_tokens=t, top_k=k, n_experts=e, hidden=hidden, partial_f32=False, row_e4m3=True)
+    try:
+        lib = C.lib()
+        ws = torch.empty(lib.mosaic_moe_workspace_bytes(ctypes.byref(d)), dtype=torch.uint8, device="cuda")
+        C.check(lib.mosaic_ep_dispatch_exchange(ctypes.byref(d), ctypes.byref(px.peers), ops._ptr(x), ops._ptr(idx),
+                                                ops._ptr(w), ops._ptr(ws), ws.numel(), ops._stream()),
+                "mosaic_ep_dispatch_exchange")
+        torch.cuda.synchronize()
+        assert px.error() == 0
+        rb = C.ep_row_bytes_e4m3(hidden)
+        got = torch.as_tensor(_DevBytes(px.recv_rows, t * k * rb), device="cuda").cpu().numpy().reshape(t * k, rb)
+    finally:
+        px.close()
+    send, _, meta = CpuEPKernels(None, None, cfg, {}).dispatch(d, 1, x.cpu(), idx.cpu(), w.cpu())
+    send = send.numpy()
+    q, sc = act_quant_ref(x.cpu().float().numpy())
+    tok = np.repeat(np.arange(t), k)[meta["order"]]
+    kt = hidden // 128
+    pad = (kt + 15) & ~15
+    want = np.zeros((t * k, rb), dtype=np.uint8)
+    want[:, :hidden] = q[tok]
+    want[:, hidden:hidden + kt] = (np.log2(sc[tok]).astype(np.int32) + 127).astype(np.uint8)
+    want[:, hidden + pad:] = send[:, 2 * hidden:]
+    assert np.array_equal(got, want)
+
+
 def test_expert_rows_rejects_bad_ids_on_device():
     from mosaic_b200 import _capi as C
     from mosaic_b200.ep import CudaEPKernels, shard_bank
