@@ -20,6 +20,7 @@ from .moe import (  # noqa: F401
     grouped_expert_forward,
 )
 from .ep import ExpertParallelMoELayer, PeerFailure, PeerHealth, expert_range, shard_bank  # noqa: F401
+from .pipeline import HostPipeline  # noqa: F401
 
 __all__ = [
     "ExactContractError",
@@ -27,6 +28,7 @@ __all__ = [
     "ExpertParallelMoELayer",
     "HashMoELayer",
     "HashRouter",
+    "HostPipeline",
     "MoEConfig",
     "MoELayer",
     "PeerFailure",
