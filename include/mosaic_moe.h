@@ -248,10 +248,12 @@ MOSAIC_API int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32
  *   y           bf16 [T, D] = RMSNorm(sum_m pre_m * x_m), the MoE input
  *   post        fp32 [T, hc], comb fp32 [T, hc, hc]: for mosaic_hc_post
  *   q, q_scale  E4M3 [T, D] and fp32 [T, D/128] = act_quant_ref(y), or both NULL
- * hc 1..4; D a multiple of 128 (x, y, q 16-byte aligned; fn, norm_weight too).
- * The workspace (256-B aligned, mosaic_hc_pre_norm_workspace_bytes) holds the
- * error word (mosaic_read_error), the split-K partials of the mixing products
- * and fn split into three bf16 parts for the tensor cores. */
+ * hc 1..4; D a multiple of 128, at most 16384 (MOSAIC_ERR_UNSUPPORTED above:
+ * the pre-mix row is held in registers); x, y, q 16-byte aligned; fn,
+ * norm_weight too.  The workspace (256-B aligned,
+ * mosaic_hc_pre_norm_workspace_bytes) holds the error word
+ * (mosaic_read_error), the split-K partials of the mixing products, fn split
+ * into three bf16 parts for the tensor cores and the tokens' pre-mix weights. */
 MOSAIC_API size_t mosaic_hc_pre_norm_workspace_bytes(int32_t T, int32_t D, int32_t hc);
 MOSAIC_API int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const float* scale,
                                   const float* norm_weight, int32_t T, int32_t D, int32_t hc, int32_t sinkhorn_iters,

@@ -716,14 +716,15 @@ int mosaic_prepack_scales(const uint8_t* scale, int32_t n_mats, int32_t rows, in
 // Workspace of mosaic_hc_pre_norm: [error word][partials][fn parts].
 struct HcWs {
   int splits;
-  size_t partial, parts, total;
+  size_t partial, parts, pre, total;
 };
 HcWs hc_ws(int T, int D, int hc, int sms) {
   HcWs w{};
   w.splits = hc_mix_tc_splits(T, hc * D, sms);
   w.partial = 256;
   w.parts = w.partial + up256(hc_partials_bytes(T, w.splits));
-  w.total = w.parts + up256(hc_fn_parts_bytes(hc * D));
+  w.pre = w.parts + up256(hc_fn_parts_bytes(hc * D));
+  w.total = w.pre + up256(static_cast<size_t>(T) * 4 * sizeof(float));
   return w;
 }
 
@@ -746,7 +747,7 @@ int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const 
   if (!aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
   const int sms = sm_count();
   if (sms <= 0) return MOSAIC_ERR_CUDA;
-  if (hc_pre_norm_smem_bytes(hc_tokens_per_cta(T, sms), D) > 227u * 1024u) return MOSAIC_ERR_UNSUPPORTED;
+  if (D > hc_max_d()) return MOSAIC_ERR_UNSUPPORTED;
   const HcWs w = hc_ws(T, D, hc, sms);
   if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -755,7 +756,7 @@ int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const 
   CUtensorMap tx, tf;
   int st = make_bf16_rows_map(&tx, x, T, KD);
   if (st) return st;
-  st = make_bf16_rows_map(&tf, ws + w.parts, 3 * 32, KD, 32);
+  st = make_bf16_rows_map(&tf, ws + w.parts, 3 * 32, KD, 3 * 32);  // one box: the three parts of a K slice
   if (st) return st;
   if (cudaMemsetAsync(ws, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   if (launch_hc_split_fn(fn, nmix, KD, ws + w.parts, sms, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
@@ -781,6 +782,7 @@ int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const 
   p.comb = comb;
   p.q = q;
   p.q_scale = q_scale;
+  p.pre = reinterpret_cast<float*>(ws + w.pre);
   cudaError_t e = launch_hc_pre_norm(p, sms, s);
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }

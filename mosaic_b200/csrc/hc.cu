@@ -8,14 +8,15 @@
 //   act_quant_ref           mosaicvm/kernels/fp4_source.py:110-129
 //   HyperConnections.post   mosaicvm/model/layers.py:269-271
 //
-// Three launches.  hc_split_fn_kernel and hc_mix_tc_kernel (hc_tc.cu) make the
+// Four launches.  hc_split_fn_kernel and hc_mix_tc_kernel (hc_tc.cu) make the
 // split-K partials of the mixing dot products x_flat . fn^T (x_flat [T, hc*D]
 // bf16, fn [(2+hc)*hc, hc*D]) and of the tokens' sums of squares on the tensor
-// cores.  hc_pre_norm_kernel (TT tokens per CTA) adds the partials in a fixed
-// order (deterministic), runs the Sinkhorn normalisation of the 4x4
-// combination (one warp per token), forms the pre-mix y = sum_m pre_m x_m
-// (bf16) in shared memory, then applies the RMSNorm (skipped without a norm
-// weight) and writes the MoE input (and its E4M3 act_quant).
+// cores.  hc_sinkhorn_kernel (one warp per token) adds the partials in a fixed
+// order (deterministic) and runs the Sinkhorn normalisation of the 4x4
+// combination; hc_premix_norm_kernel (one token per CTA at a time) forms the
+// pre-mix y = sum_m pre_m x_m (bf16) in registers, then applies the RMSNorm
+// (skipped without a norm weight) and writes the MoE input (and its E4M3
+// act_quant).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,147 +32,168 @@ constexpr int kRed = kMaxMix + 1;         // mixes + sum of squares per token
 
 __device__ __forceinline__ float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-template <int TT>
-__global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(HcParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* ybuf = reinterpret_cast<__nv_bfloat16*>(smem);                   // [TT][D]
-  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(TT) * p.D * 2);  // [warps][TT]
-  float* tot = red + kHcWarps * TT * kRed;                                          // [TT][kRed]
-  float* pre_s = tot + TT * kRed;                                                   // [TT][4]
+// ---- partial sums + Sinkhorn split: one warp per token.  Lane r ends up with
+// value r of the token (24 mixes, then the sum of squares at kMaxMix): for each
+// value, lane l adds splits l, l+32, ... in order and a butterfly adds the
+// lanes, so the order is fixed (deterministic).  Writes pre [T][4] (for the
+// pre-mix kernel), post and comb.
+constexpr int kSkWarps = 8;
+
+__global__ void __launch_bounds__(kSkWarps * 32) hc_sinkhorn_kernel(HcParams p) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kSkWarps + (threadIdx.x >> 5);
+  if (t >= p.T) return;  // the whole warp
+  const int hc = p.hc, KD = hc * p.D, nmix = (2 + hc) * hc;
+  // every value's partials of this lane's splits first (all loads in flight), then
+  // the 25 independent butterflies
+  float part[kRed];
+#pragma unroll
+  for (int r = 0; r < kRed; ++r) part[r] = 0.f;
+  for (int sp = lane; sp < p.splits; sp += 32) {
+    const float* src = p.partial + (static_cast<size_t>(sp) * p.T + t) * kRed;
+#pragma unroll
+    for (int r = 0; r < kRed; ++r)
+      if (r < nmix || r == kMaxMix) part[r] += src[r];
+  }
+  float mine = 0.f;
+#pragma unroll
+  for (int r = 0; r < kRed; ++r) {
+    const float s = warp_sum(part[r]);
+    if (lane == r) mine = s;
+  }
+  const float rs = 1.0f / sqrtf(__shfl_sync(0xFFFFFFFFu, mine, kMaxMix) / static_cast<float>(KD) + p.norm_eps);
+  const float m_post = __shfl_sync(0xFFFFFFFFu, mine, (hc + lane) & 31);
+  if (lane < hc) {
+    p.pre[static_cast<size_t>(t) * 4 + lane] = sigmoidf(mine * rs * p.scale[0] + p.base[lane]) + p.hc_eps;
+    p.post[static_cast<size_t>(t) * hc + lane] = 2.0f * sigmoidf(m_post * rs * p.scale[1] + p.base[hc + lane]);
+  }
+  // Sinkhorn: lane 4i+j (< 16) holds comb[i][j], rows are 4-lane groups (xor 1,
+  // 2), columns stride 4 (xor 4, 8)
+  const int ci = (lane >> 2) & 3, cj = lane & 3;
+  const bool on = lane < 16 && ci < hc && cj < hc;
+  const int r = 2 * hc + ci * hc + cj;
+  const float m_comb = __shfl_sync(0xFFFFFFFFu, mine, on ? r : 0);
+  const float v = on ? m_comb * rs * p.scale[2] + p.base[r] : -INFINITY;
+  float mx = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+  float c = on ? expf(v - mx) : 0.f;
+  float sum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+  sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+  c = on ? c / sum + p.hc_eps : 0.f;
+  // row / column normalisations: products with the reciprocal of each sum
+  for (int it = 1; it < p.iters; ++it) {
+    float rsum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+    rsum += __shfl_xor_sync(0xFFFFFFFFu, rsum, 2);
+    c *= 1.0f / (rsum + p.hc_eps);
+    float csum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 4);
+    csum += __shfl_xor_sync(0xFFFFFFFFu, csum, 8);
+    c *= 1.0f / (csum + p.hc_eps);
+  }
+  if (on) p.comb[(static_cast<size_t>(t) * hc + ci) * hc + cj] = c;
+}
+
+// ---- pre-mix + RMSNorm (+ act_quant): one token per CTA at a time
+// (grid-stride).  Each thread loads its PER 8-value chunks of all hc residual
+// rows up front (16-byte loads, all in flight together), forms y = sum_m
+// pre_m x_m (products rounded, summed in m order, bf16) in registers, and the
+// block adds the squares of y in a fixed order for the RMSNorm.
+template <int PER>
+__global__ void __launch_bounds__(kHcThreads, PER <= 4 ? 2 : 1) hc_premix_norm_kernel(HcParams p) {
+  __shared__ float red[kHcWarps];
+  __shared__ float rs_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hc = p.hc, D = p.D, KD = hc * D, nmix = (2 + hc) * hc;
+  const int hc = p.hc, D = p.D, KD = hc * D;
   const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
   __nv_bfloat16* yout = static_cast<__nv_bfloat16*>(p.y);
-  for (int t0 = blockIdx.x * TT; t0 < p.T; t0 += gridDim.x * TT) {
-    // ---- mixing dot products and sums of squares: the splits' partials.  Warp w
-    // reduces values w, w+8, ...; lane l adds splits l, l+32, ... in order and
-    // a butterfly adds the lanes, so the order is fixed (deterministic).
-    for (int i = warp; i < TT * kRed; i += kHcWarps) {
-      const int t = t0 + i / kRed, r = i % kRed;
-      float s = 0.f;
-      if (t < p.T && (r < nmix || r == kMaxMix))
-        for (int sp = lane; sp < p.splits; sp += 32) s += p.partial[(static_cast<size_t>(sp) * p.T + t) * kRed + r];
-      s = warp_sum(s);
-      if (lane == 0) tot[i] = s;
+  for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
+    const __nv_bfloat16* xt = x + static_cast<size_t>(t) * KD;
+    uint4 raw[PER][4];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int d = k * kHcChunk + tid * 8;
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+        if (d < D && m < hc) raw[k][m] = *reinterpret_cast<const uint4*>(xt + static_cast<size_t>(m) * D + d);
     }
-    __syncthreads();
-    // ---- Sinkhorn split: warp tt takes token tt; lane 4i+j (< 16) holds comb[i][j],
-    // rows are 4-lane groups (xor 1, 2), columns stride 4 (xor 4, 8)
-    if (warp < TT && t0 + warp < p.T) {
-      const int t = t0 + warp;
-      const float* mt = tot + warp * kRed;
-      const float rs = 1.0f / sqrtf(mt[kMaxMix] / static_cast<float>(KD) + p.norm_eps);
-      if (lane < hc) {
-        pre_s[warp * 4 + lane] = sigmoidf(mt[lane] * rs * p.scale[0] + p.base[lane]) + p.hc_eps;
-        p.post[static_cast<size_t>(t) * hc + lane] = 2.0f * sigmoidf(mt[hc + lane] * rs * p.scale[1] + p.base[hc + lane]);
-      }
-      const int ci = (lane >> 2) & 3, cj = lane & 3;
-      const bool on = lane < 16 && ci < hc && cj < hc;
-      const int r = 2 * hc + ci * hc + cj;
-      const float v = on ? mt[r] * rs * p.scale[2] + p.base[r] : -INFINITY;
-      float mx = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
-      float c = on ? expf(v - mx) : 0.f;
-      float sum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
-      sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-      c = on ? c / sum + p.hc_eps : 0.f;
-      // row / column normalisations: products with the reciprocal of each sum
-      for (int it = 1; it < p.iters; ++it) {
-        float rsum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
-        rsum += __shfl_xor_sync(0xFFFFFFFFu, rsum, 2);
-        c *= 1.0f / (rsum + p.hc_eps);
-        float csum = c + __shfl_xor_sync(0xFFFFFFFFu, c, 4);
-        csum += __shfl_xor_sync(0xFFFFFFFFu, csum, 8);
-        c *= 1.0f / (csum + p.hc_eps);
-      }
-      if (on) p.comb[(static_cast<size_t>(t) * hc + ci) * hc + cj] = c;
-    }
-    __syncthreads();
-    // ---- pass B: y = sum_m pre_m x_m (products rounded, summed in m order), bf16
-    float ss2[TT];
+    const float4 pre4 = *reinterpret_cast<const float4*>(p.pre + static_cast<size_t>(t) * 4);
+    const float pm[4] = {pre4.x, pre4.y, pre4.z, pre4.w};
+    float yv[PER][8];
+    float ss2 = 0.f;
 #pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      ss2[t] = 0.f;
-      if (t0 + t >= p.T) continue;
-      const __nv_bfloat16* xt = x + static_cast<size_t>(t0 + t) * KD;
-      for (int d = tid * 8; d < D; d += kHcChunk) {
-        float y[8], xv[8];
-        load8_bf16(xt + d, xv);
-        const float p0 = pre_s[t * 4];
+    for (int k = 0; k < PER; ++k) {
+      const int d = k * kHcChunk + tid * 8;
+      if (d < D) {
+        float y[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(p0, xv[i]);
-        for (int m = 1; m < hc; ++m) {
-          load8_bf16(xt + static_cast<size_t>(m) * D + d, xv);
-          const float pm = pre_s[t * 4 + m];
+        for (int m = 0; m < 4; ++m) {
+          if (m >= hc) break;
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[k][m]);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) y[i] = __fadd_rn(y[i], __fmul_rn(pm, xv[i]));
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h2[i]);
+            if (m == 0) {
+              y[2 * i] = __fmul_rn(pm[0], f.x);
+              y[2 * i + 1] = __fmul_rn(pm[0], f.y);
+            } else {
+              y[2 * i] = __fadd_rn(y[2 * i], __fmul_rn(pm[m], f.x));
+              y[2 * i + 1] = __fadd_rn(y[2 * i + 1], __fmul_rn(pm[m], f.y));
+            }
+          }
         }
-        __align__(16) __nv_bfloat16 yb[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          yb[i] = __float2bfloat16_rn(y[i]);
-          const float f = __bfloat162float(yb[i]);
-          ss2[t] = fmaf(f, f, ss2[t]);
+          yv[k][i] = __bfloat162float(__float2bfloat16_rn(y[i]));
+          ss2 = fmaf(yv[k][i], yv[k][i], ss2);
         }
-        *reinterpret_cast<uint4*>(ybuf + static_cast<size_t>(t) * D + d) = *reinterpret_cast<const uint4*>(yb);
       }
     }
-#pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      const float v = warp_sum(ss2[t]);
-      if (lane == 0) red[warp * TT + t] = v;
-    }
+    ss2 = warp_sum(ss2);
+    if (lane == 0) red[warp] = ss2;
     __syncthreads();
-    if (tid < TT) {
+    if (tid == 0) {
       float s = 0.f;
-      for (int w = 0; w < kHcWarps; ++w) s += red[w * TT + tid];
-      tot[tid] = 1.0f / sqrtf(s / static_cast<float>(D) + p.norm_eps);
+      for (int w = 0; w < kHcWarps; ++w) s += red[w];
+      rs_s = 1.0f / sqrtf(s / static_cast<float>(D) + p.norm_eps);
     }
     __syncthreads();
-    // ---- pass C: RMSNorm (x * rsqrt, then * weight), bf16, optional act_quant.
-    // Every lane runs the same iterations: quant_block128 shuffles across 16 lanes.
+    // ---- RMSNorm (y * rsqrt, then * weight), bf16, optional act_quant.  Every
+    // lane runs the same iterations: quant_block128 shuffles across 16 lanes.
+    const float r = rs_s;
     const int steps = (D + kHcChunk - 1) / kHcChunk;
 #pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      if (t0 + t >= p.T) continue;
-      const float r = tot[t];
-      for (int s = 0; s < steps; ++s) {
-        const int d = s * kHcChunk + tid * 8;
-        const bool valid = d < D;
-        float v[8];
-        if (valid) {
-          float yv[8];
-          load8_bf16(ybuf + static_cast<size_t>(t) * D + d, yv);
-          __align__(16) __nv_bfloat16 ob[8];
-          if (p.norm_w) {
-            const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d));
-            const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d + 4));
-            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    for (int k = 0; k < PER; ++k) {
+      if (k >= steps) break;
+      const int d = k * kHcChunk + tid * 8;
+      const bool valid = d < D;
+      float v[8];
+      if (valid) {
+        __align__(16) __nv_bfloat16 ob[8];
+        if (p.norm_w) {
+          const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d));
+          const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d + 4));
+          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(yv[i], r), w[i]));
-          } else {  // the pre-mix alone (HyperConnections.pre)
+          for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(yv[k][i], r), w[i]));
+        } else {  // the pre-mix alone (HyperConnections.pre)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(yv[i]);
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(ob[i]);
-          *reinterpret_cast<uint4*>(yout + static_cast<size_t>(t0 + t) * D + d) =
-              *reinterpret_cast<const uint4*>(ob);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = 0.f;
+          for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(yv[k][i]);
         }
-        if (p.q) {
-          uint8_t b[8];
-          const int e = quant_block128(v, b);
-          if (valid) {
-            *reinterpret_cast<uint2*>(p.q + static_cast<size_t>(t0 + t) * D + d) = pack8(b);
-            if ((lane & 15) == 0) p.q_scale[static_cast<size_t>(t0 + t) * (D / 128) + d / 128] = exp2i(e);
-          }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(ob[i]);
+        *reinterpret_cast<uint4*>(yout + static_cast<size_t>(t) * D + d) = *reinterpret_cast<const uint4*>(ob);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+      }
+      if (p.q) {
+        uint8_t b[8];
+        const int e = quant_block128(v, b);
+        if (valid) {
+          *reinterpret_cast<uint2*>(p.q + static_cast<size_t>(t) * D + d) = pack8(b);
+          if ((lane & 15) == 0) p.q_scale[static_cast<size_t>(t) * (D / 128) + d / 128] = exp2i(e);
         }
       }
     }
-    __syncthreads();  // ybuf / red / tot are reused by the next token group
   }
 }
 
@@ -294,40 +316,22 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const __nv_bfloa
 
 }  // namespace
 
-size_t hc_pre_norm_smem_bytes(int tt, int D) {
-  return static_cast<size_t>(tt) * D * 2 + sizeof(float) * (kHcWarps * tt * kRed + tt * kRed + tt * 4);
-}
-
-// One token per CTA: the per-token kernel reads nothing that tokens could share,
-// and small CTAs keep many loads in flight on every SM.
-int hc_tokens_per_cta(int T, int num_sms) {
-  (void)T;
-  (void)num_sms;
-  return 1;
-}
+int hc_max_d() { return kHcChunk * 8; }
 
 size_t hc_partials_bytes(int T, int splits) { return sizeof(float) * static_cast<size_t>(splits) * T * kRed; }
 
-cudaError_t launch_hc_pre_norm(const HcParams& p_in, int num_sms, cudaStream_t stream) {
-  const HcParams& p = p_in;
-  const int tt = hc_tokens_per_cta(p.T, num_sms);
-  const int groups = (p.T + tt - 1) / tt;
-  const int grid = groups < 16 * num_sms ? groups : 16 * num_sms;
-  const size_t smem = hc_pre_norm_smem_bytes(tt, p.D);
-#define MOSAIC_HC(TT)                                                                                     \
-  do {                                                                                                    \
-    cudaError_t e = cudaFuncSetAttribute(hc_pre_norm_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                         static_cast<int>(smem));                                         \
-    if (e != cudaSuccess) return e;                                                                       \
-    hc_pre_norm_kernel<TT><<<grid, kHcThreads, smem, stream>>>(p);                                        \
-  } while (0)
-  if (tt == 4)
-    MOSAIC_HC(4);
-  else if (tt == 2)
-    MOSAIC_HC(2);
+cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream) {
+  if (p.D > hc_max_d() || p.D % 8 || p.hc < 1 || p.hc > 4) return cudaErrorInvalidValue;
+  hc_sinkhorn_kernel<<<(p.T + kSkWarps - 1) / kSkWarps, kSkWarps * 32, 0, stream>>>(p);
+  // two CTAs of 256 threads per SM (the registers of the rows in flight; one above D = 8192)
+  const int per_sm = p.D <= 4 * kHcChunk ? 2 : 1;
+  const int grid = p.T < per_sm * num_sms ? p.T : per_sm * num_sms;
+  if (p.D <= 2 * kHcChunk)
+    hc_premix_norm_kernel<2><<<grid, kHcThreads, 0, stream>>>(p);
+  else if (p.D <= 4 * kHcChunk)
+    hc_premix_norm_kernel<4><<<grid, kHcThreads, 0, stream>>>(p);
   else
-    MOSAIC_HC(1);
-#undef MOSAIC_HC
+    hc_premix_norm_kernel<8><<<grid, kHcThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -6,21 +6,22 @@
 // the split-K partials of x_flat . fn^T and of sum(x_flat^2) that
 // hc_pre_norm_kernel (hc.cu) adds, scales and turns into pre / post / comb.
 //
-// The same scheme as the router logits (router_tc.cu): x is bf16, exact as an
-// MMA operand; fn is split into three bf16 parts (hi + mid + lo, 3 x 8
-// significand bits) by hc_split_fn_kernel into [3][32][hc*D] (rows past the
-// (2+hc)*hc mixes zero), and every 64-wide K slice is its own accumulation
-// chain of 12 MMAs (the tensor core's fp32 accumulation error grows with the
-// chain length), added in slice order in fp32 registers.
+// The same operand scheme as the router logits (router_tc.cu): x is bf16,
+// exact as an MMA operand; fn is split into three bf16 parts (hi + mid + lo,
+// 3 x 8 significand bits) by hc_split_fn_kernel into [3][32][hc*D] (rows past
+// the (2+hc)*hc mixes zero).
 //
-// Tokens are M (128 per CTA), the mixes N = 32.  An MMA costs its issuing
-// thread about the same time whatever N is, so one issuer would leave the
-// tensor core mostly idle at N = 32; four issuer warps (6-9) take the K slices
-// in turn (slice j on issuer j % 4), each with two 32-column TMEM buffers.
-// Warp 0 loads the slices with TMA (x box 64 x 128 tokens, three 64 x 32 part
-// boxes, 128-byte swizzle); warps 2-5 hold one token each per lane: they add
-// the token's squares from the staged x tile and, in slice order, each
-// slice's 24 mixes from TMEM, then write the token's partials.
+// Tokens are M (128 per CTA); the three parts side by side are N = 96, so one
+// MMA per 16-wide K step gives each token all three parts' dot products in
+// TMEM columns [0, 32), [32, 64), [64, 96).  The K slices (64 wide, one ring
+// stage each) form groups of four; a group is one accumulation chain of 16
+// MMAs (the tensor core's fp32 accumulation error grows with the chain
+// length), and the two issuer warps (6, 7) take the groups in turn, each with
+// two 96-column TMEM buffers.  Warp 0 loads the slices with TMA (x box 64 x 128
+// tokens, the parts box 64 x 96 rows, 128-byte swizzle); warps 2-5 hold one
+// token each per lane: they add the token's squares from the staged x tile
+// (every slice) and, in group order, each group's 24 mixes as (hi + mid) + lo
+// from TMEM, then write the token's partials.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -28,20 +29,23 @@ namespace mosaic {
 
 namespace {
 
-constexpr int kHtThreads = 320;  // warp 0 TMA, 1 TMEM, 2-5 sums, 6-9 MMA issuers
+constexpr int kHtThreads = 256;  // warp 0 TMA, 1 TMEM, 2-5 sums, 6-7 MMA issuers
 constexpr int kHtTok = 128;
 constexpr int kHtK = 64;
-constexpr int kHtN = 32;                         // mixes padded to the MMA N
+constexpr int kHtN = 32;                         // mixes padded to 32 per part
+constexpr int kHtNB = 3 * kHtN;                  // MMA N: the three parts
 constexpr int kHtXBytes = kHtTok * 128;          // 16 KB
-constexpr int kHtPartBytes = kHtN * 128;         // 4 KB
-constexpr int kHtStageBytes = kHtXBytes + 3 * kHtPartBytes;  // 28 KB
-constexpr int kHtIssuers = 4;
-// Slice j uses stage j % 8 and issuer j % 4, so stage s always feeds issuer
-// s % 4, which thereby waits on every phase of its stages' full barriers in
-// order (an issuer that skipped phases could match a parity two fills back).
-constexpr int kHtStages = 2 * kHtIssuers;
-static_assert(kHtStages % kHtIssuers == 0, "each stage must feed one issuer");
-constexpr uint32_t kHtTmemCols = kHtIssuers * 2 * kHtN;  // 256
+constexpr int kHtPartBytes = kHtNB * 128;        // 12 KB
+constexpr int kHtStageBytes = kHtXBytes + kHtPartBytes;  // 28 KB
+constexpr int kHtIssuers = 2;
+constexpr int kHtGroup = 4;  // slices per accumulation chain
+// Slice j sits in ring stage j % 8 and group j / 4, issuer (j / 4) % 2: stage s
+// always feeds issuer s / 4, which thereby waits on every phase of its stages'
+// full barriers in order (an issuer that skipped phases could match a parity
+// two fills back).
+constexpr int kHtStages = kHtGroup * kHtIssuers;
+static_assert(kHtStages == 8, "ring of 8 slices: stage s feeds issuer s / 4");
+constexpr uint32_t kHtTmemCols = 512;  // 2 issuers x 2 buffers x 96 columns, rounded up
 constexpr int kHtRed = 25;  // per token: 24 mixes + the sum of squares (hc.cu's layout)
 constexpr int kHtSsq = 24;
 
@@ -65,9 +69,9 @@ __device__ __forceinline__ void ht_mma_bf16(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
-// kind::f16 instruction descriptor: fp32 D, bf16 A and B (K-major), M = 128, N = 32.
+// kind::f16 instruction descriptor: fp32 D, bf16 A and B (K-major), M = 128, N = 96.
 __host__ __device__ __forceinline__ uint32_t ht_idesc() {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kHtN >> 3) << 17) |
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kHtNB >> 3) << 17) |
          (static_cast<uint32_t>(128 >> 4) << 24);
 }
 
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kHtThreads, 1)
         uint64_t* fb = &ctrl->full[s];
         mbar_arrive_expect_tx(fb, static_cast<uint32_t>(kHtStageBytes));  // whole boxes (rows past T read as 0)
         tma_load_2d(st, &tmap_x, fb, k0, t0);
-        for (int p = 0; p < 3; ++p) tma_load_2d(st + kHtXBytes + p * kHtPartBytes, &tmap_f, fb, k0, p * kHtN);
+        tma_load_2d(st + kHtXBytes, &tmap_f, fb, k0, 0);
       }
       __syncwarp();
     }
@@ -146,32 +150,35 @@ __global__ void __launch_bounds__(kHtThreads, 1)
     const int i = warp - 6;
     bool ok = true, issued = false;
     const uint32_t idesc = ht_idesc();
-    for (int j = i; j < nit; j += kHtIssuers) {
-      const int s = j % kHtStages;
-      const uint32_t ph = static_cast<uint32_t>(j / kHtStages) & 1u;
-      const int b = (j / kHtIssuers) & 1;
-      const uint32_t bph = static_cast<uint32_t>(j / (2 * kHtIssuers)) & 1u;
-      if (!mbar_wait(&ctrl->full[s], ph, abort) || !mbar_wait(&ctrl->acc_empty[i][b], bph ^ 1u, abort)) {
+    for (int g = i, n = 0; ok && g * kHtGroup < nit; g += kHtIssuers, ++n) {
+      const int b = n & 1;
+      const uint32_t bph = static_cast<uint32_t>(n >> 1) & 1u;
+      if (!mbar_wait(&ctrl->acc_empty[i][b], bph ^ 1u, abort)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t sa = smem_u32(smem + s * kHtStageBytes);
-        const uint32_t d = tmem + static_cast<uint32_t>((2 * i + b) * kHtN);
-#pragma unroll
-        for (uint32_t kb = 0; kb < 4; ++kb) {
-#pragma unroll
-          for (uint32_t p = 0; p < 3; ++p) {
-            const uint32_t sb = sa + kHtXBytes + p * kHtPartBytes;
-            ht_mma_bf16(d, desc_sw128(sa + kb * 32), desc_sw128(sb + kb * 32), idesc, (kb | p) ? 1u : 0u);
-          }
+      const uint32_t d = tmem + static_cast<uint32_t>((2 * i + b) * kHtNB);
+      const int j1 = min((g + 1) * kHtGroup, nit);
+      for (int j = g * kHtGroup; j < j1; ++j) {
+        const int s = j % kHtStages;
+        if (!mbar_wait(&ctrl->full[s], static_cast<uint32_t>(j / kHtStages) & 1u, abort)) {
+          ok = false;
+          break;
         }
-        tc_commit(&ctrl->empty[s]);
-        tc_commit(&ctrl->acc_full[i][b]);
-        issued = true;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = smem_u32(smem + s * kHtStageBytes);
+          const uint32_t sb = sa + kHtXBytes;
+          const uint32_t first = (j == g * kHtGroup) ? 1u : 0u;
+#pragma unroll
+          for (uint32_t kb = 0; kb < 4; ++kb)
+            ht_mma_bf16(d, desc_sw128(sa + kb * 32), desc_sw128(sb + kb * 32), idesc, (first && kb == 0) ? 0u : 1u);
+          tc_commit(&ctrl->empty[s]);
+          if (j == j1 - 1) tc_commit(&ctrl->acc_full[i][b]);
+          issued = true;
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (!ok) {
       if (lane == 0) set_error(err, MOSAIC_ERR_TIMEOUT);
@@ -218,19 +225,26 @@ __global__ void __launch_bounds__(kHtThreads, 1)
       // thread's generic reads of the tile before it
       fence_proxy_async_smem();
       mbar_arrive(&ctrl->empty[s]);
-      // slice j's mixes: issuer j % 4, buffer (j / 4) & 1
-      const int i = j % kHtIssuers, b = (j / kHtIssuers) & 1;
-      if (!mbar_wait(&ctrl->acc_full[i][b], static_cast<uint32_t>(j / (2 * kHtIssuers)) & 1u, abort)) {
+      if (j % kHtGroup != kHtGroup - 1 && j != nit - 1) continue;
+      // the group's mixes: issuer (j / 4) % 2, its buffer n & 1 for the issuer's n-th group
+      const int g = j / kHtGroup, i = g % kHtIssuers, n = g / kHtIssuers, b = n & 1;
+      if (!mbar_wait(&ctrl->acc_full[i][b], static_cast<uint32_t>(n >> 1) & 1u, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t r[2][16];
-      tmem_ld16(trow + static_cast<uint32_t>((2 * i + b) * kHtN), r[0]);
-      tmem_ld16(trow + static_cast<uint32_t>((2 * i + b) * kHtN + 16), r[1]);
+      const uint32_t col = trow + static_cast<uint32_t>((2 * i + b) * kHtNB);
+      uint32_t r[6][16];
+#pragma unroll
+      for (int c = 0; c < 6; ++c) tmem_ld16(col + 16u * c, r[c]);
       tmem_ld_wait();
 #pragma unroll
-      for (int m = 0; m < kHtSsq; ++m) acc[m] += __uint_as_float(r[m >> 4][m & 15]);
+      for (int m = 0; m < kHtSsq; ++m) {
+        const float hi = __uint_as_float(r[m >> 4][m & 15]);
+        const float mid = __uint_as_float(r[2 + (m >> 4)][m & 15]);
+        const float lo = __uint_as_float(r[4 + (m >> 4)][m & 15]);
+        acc[m] += (hi + mid) + lo;
+      }
       tc_fence_before();
       mbar_arrive(&ctrl->acc_empty[i][b]);
     }

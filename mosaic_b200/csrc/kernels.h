@@ -131,11 +131,12 @@ struct HcParams {
   float* q_scale;        // [T][D/128]
   float* partial;        // workspace: [splits][T][25] mixing partials (+ sum of squares)
   int splits;
+  float* pre;            // workspace: [T][4] pre-mix weights (Sinkhorn kernel -> pre-mix kernel)
 };
-size_t hc_pre_norm_smem_bytes(int tt, int D);
 size_t hc_partials_bytes(int T, int splits);
-int hc_tokens_per_cta(int T, int num_sms);
-// the per-token kernel: adds p.splits partials, Sinkhorn, pre-mix, RMSNorm (+ act_quant)
+int hc_max_d();  // largest D of the pre-mix kernel (the pre-mix is held in registers)
+// the per-token kernels: add p.splits partials and run the Sinkhorn split (a warp
+// per token), then pre-mix, RMSNorm (+ act_quant)
 cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream);
 // mixing partials on the tensor cores (hc_tc.cu): fn [nmix][KD] -> parts bf16
 // [3][32][KD]; x_flat [T][KD] and the parts as 128-byte-swizzled 64-wide maps
