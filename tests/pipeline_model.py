@@ -6,12 +6,16 @@ for CPU tests of their ordering: ``run`` models ``hc_mix_tc_kernel``
 
 - the producer waits ``empty[s]`` (parity of the previous use) and issues a
   stage fill that lands after a random delay (TMA complete_tx on ``full[s]``);
-- issuer ``i`` takes slices ``i, i + I, ...``; it waits ``full[s]`` and its
-  accumulator buffer's ``acc_empty``, issues, and its MMAs complete after a
-  random delay, arriving on ``empty[s]`` and ``acc_full`` (tcgen05.commit);
+- the slices form groups of ``group`` consecutive slices, one accumulation
+  chain each; issuer ``i`` takes groups ``i, i + I, ...``, using accumulator
+  buffer ``n & 1`` for its n-th group.  Per group it waits that buffer's
+  ``acc_empty``, then per slice ``full[s]``; its MMAs complete in issue order
+  after random delays, each arriving on ``empty[s]``, and the group's last
+  one on ``acc_full`` (tcgen05.commit);
 - each summing warp waits ``full[s]`` for every slice in order, reads the
-  staged x tile, arrives on ``empty[s]`` (32 arrivals), waits the slice's
-  ``acc_full``, reads it and arrives on ``acc_empty``.
+  staged x tile, arrives on ``empty[s]`` (32 arrivals); after a group's last
+  slice it waits the group's ``acc_full``, reads it and arrives on
+  ``acc_empty``.
 
 An mbarrier is a pending count and a phase counter; a parity wait for P
 succeeds when ``phase & 1 != P``, as ``mbarrier.try_wait.parity`` does.  The
@@ -52,7 +56,8 @@ class Barrier:
         return (self.phase & 1) != parity
 
 
-def run(stages: int, issuers: int, nit: int, seed: int, warps: int = 4, max_steps: int = 200_000) -> list:
+def run(stages: int, issuers: int, nit: int, seed: int, warps: int = 4, group: int = 1,
+        max_steps: int = 200_000) -> list:
     """One randomised execution; returns the list of violations (empty = clean)."""
     rnd = random.Random(seed)
     full = [Barrier(1) for _ in range(stages)]
@@ -82,25 +87,34 @@ def run(stages: int, issuers: int, nit: int, seed: int, warps: int = 4, max_step
             later(rnd.randint(1, 40), land)
             yield
 
+    n_groups = (nit + group - 1) // group
+    completed = set()  # slices whose MMAs completed
+    last_done = [0] * issuers
+
     def issuer(i):
-        for j in range(i, nit, issuers):
-            s = j % stages
-            b = (j // issuers) & 1
-            while not full[s].passed((j // stages) & 1):
+        for n, g in enumerate(range(i, n_groups, issuers)):
+            b = n & 1
+            while not acc_empty[i][b].passed(((n >> 1) & 1) ^ 1):
                 yield
-            while not acc_empty[i][b].passed(((j // (2 * issuers)) & 1) ^ 1):
-                yield
-            if content[s] != j:
-                errors.append(("MMA issued on another fill", j, s, content[s]))
-
-            def complete(s=s, j=j, i=i, b=b):
+            j1 = min((g + 1) * group, nit)
+            for j in range(g * group, j1):
+                s = j % stages
+                while not full[s].passed((j // stages) & 1):
+                    yield
                 if content[s] != j:
-                    errors.append(("MMA operand replaced before completion", j, s, content[s]))
-                empty[s].arrive()
-                acc_full[i][b].arrive()
+                    errors.append(("MMA issued on another fill", j, s, content[s]))
+                last_done[i] = max(clock[0], last_done[i]) + rnd.randint(1, 30)
 
-            later(rnd.randint(1, 30), complete)
-            yield
+                def complete(s=s, j=j, i=i, b=b, last=(j == j1 - 1)):
+                    if content[s] != j:
+                        errors.append(("MMA operand replaced before completion", j, s, content[s]))
+                    completed.add(j)
+                    empty[s].arrive()
+                    if last:
+                        acc_full[i][b].arrive()
+
+                events.append((last_done[i], rnd.random(), complete))
+                yield
 
     def summing_warp(w):
         for j in range(nit):
@@ -113,9 +127,15 @@ def run(stages: int, issuers: int, nit: int, seed: int, warps: int = 4, max_step
             if content[s] != j:
                 errors.append(("x tile replaced during the read", w, j, s, content[s]))
             empty[s].arrive(32)
-            i, b = j % issuers, (j // issuers) & 1
-            while not acc_full[i][b].passed((j // (2 * issuers)) & 1):
+            if j % group != group - 1 and j != nit - 1:
+                continue
+            g = j // group
+            i, n = g % issuers, g // issuers
+            b = n & 1
+            while not acc_full[i][b].passed((n >> 1) & 1):
                 yield
+            if any(jj not in completed for jj in range(g * group, j + 1)):
+                errors.append(("group read before its MMAs completed", w, g))
             acc_empty[i][b].arrive(32)
             yield
 
