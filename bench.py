@@ -79,7 +79,7 @@ def layer_launches(t: int, world: int) -> int:
     Layout: one CTA up to 1024 assignments, else count / scan / rank / finish.
     One GPU: router, layout, rows_quant, gate/up, down, combine.  Expert
     parallel (FP8, E4M3 rows): router, dispatch + exchange (layout, destination
-    counts, count exchange, quantise-and-send, wait), the shared expert
+    counts, token quantise, count exchange, send, wait), the shared expert
     (per-row metadata, layout, rows_quant, gate/up, down) and the received
     rows (per-row metadata, layout, placement, gate/up, down), return (signal,
     wait), combine."""
@@ -87,7 +87,7 @@ def layer_launches(t: int, world: int) -> int:
     lay = lambda a: 4 if a > 1024 else 1  # noqa: E731
     if world == 1:
         return router + lay(t * 8) + 4
-    return router + (lay(t * 8) + 4) + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
+    return router + (lay(t * 8) + 5) + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
 
 
 def parse():

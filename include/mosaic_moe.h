@@ -443,11 +443,12 @@ MOSAIC_API int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void*
                                        mosaic_stream_t stream);
 MOSAIC_API int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const void* partials, mosaic_stream_t stream);
 /* Dispatch fused with the exchange, for MOSAIC_ACT_FP8 layers with
- * peers->row_e4m3 = 1: the layout of mosaic_ep_dispatch, then the count
- * exchange, then every assignment's token row quantised (act_quant_ref, as
- * the single-GPU layer does) straight into its owner's receive row as an E4M3
- * row -- no send buffer, half the NVLink bytes of bf16 rows -- and the wait
- * until every source's rows have landed here.  Replaces mosaic_ep_dispatch +
+ * peers->row_e4m3 = 1: the layout of mosaic_ep_dispatch, every token row
+ * quantised once (act_quant_ref, as the single-GPU layer does) into scratch
+ * rows of the workspace, the count exchange, then each assignment's E4M3 row
+ * copied straight into its owner's receive row -- no send buffer, half the
+ * NVLink bytes of bf16 rows -- and the wait until every source's rows have
+ * landed here.  Replaces mosaic_ep_dispatch +
  * mosaic_ep_exchange_rows; the rows received are what mosaic_ep_dispatch
  * would have sent, quantised.  dims: the layer (tokens = this rank's T <=
  * peers->max_tokens, n_experts = global E, hidden = peers->hidden); idx /

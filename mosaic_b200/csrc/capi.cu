@@ -1169,10 +1169,12 @@ int mosaic_ep_dispatch_exchange(const mosaic_moe_dims* dims, const mosaic_ep_pee
   lp.row_pos = nullptr;
   lp.tiles = nullptr;
   if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
-  // the sender runs no GEMM, so the activation planes of the workspace are free
+  // the sender runs no GEMM, so the activation planes and the partial rows of
+  // the workspace are free: the destination counts and the E4M3 token rows
+  // (T x (H + pad) <= T x 2H bytes of the R x H partials)
   int* dest_counts = reinterpret_cast<int*>(ws + w.xq);
-  if (launch_ep_dispatch_send_e4m3(ep_dev(peers), x, dims->hidden, E, E / world, lp.offsets, lp.row_token,
-                                   lp.row_weight, dest_counts, sms, s) != cudaSuccess)
+  if (launch_ep_dispatch_send_e4m3(ep_dev(peers), x, T, dims->hidden, E, E / world, lp.offsets, lp.row_token,
+                                   lp.row_weight, dest_counts, ws + w.partial, sms, s) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
   return MOSAIC_OK;
 }

@@ -258,14 +258,14 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpPeersDev P, cons
   }
 }
 
-// ------------------------------------------ E4M3 rows, quantised in flight ---
-// A warp per send row r (expert-sorted, hence grouped by owner): the token
-// row x[row_token[r]] is quantised per 128-value block (act_quant_ref, 8 lanes
+// ----------------------------------------------------------- E4M3 rows ---
+// Each token row is quantised once per 128-value block (act_quant_ref, 8 lanes
 // x 16 values per block, 512 values per warp pass, two passes per loop trip)
-// and the codes are stored straight into the owner's receive row, 16 bytes
-// per lane.  The block exponents collect in shared memory and follow the
-// codes, then the meta tail {local expert, route weight bits, token, owner}.
-// No send buffer: x is read once per send row (from L2 after the first).
+// into an L2-resident scratch row: codes, then the block exponents (collected
+// in shared memory).  The send then copies a token's row into the owner's
+// receive row for every assignment of the token and adds the meta tail
+// {local expert, route weight bits, token, owner}.  No send buffer of
+// assignment rows is written.
 constexpr int kSendWarps = 8;
 constexpr int kMaxKtPad = 128;  // H <= 16384
 
@@ -299,29 +299,17 @@ __device__ __forceinline__ void load16_bf16(const __nv_bfloat16* __restrict__ p,
   }
 }
 
+// E4M3 rows quantised once per token: tq[t] = codes [H] | exponents [kt_pad]
+// (row stride H + kt_pad, 16-byte aligned), a warp per token.
 __global__ void __launch_bounds__(kSendWarps * 32)
-    ep_send_e4m3_kernel(const EpPeersDev P, const __nv_bfloat16* __restrict__ x, int H, int E, int E_local,
-                        const int* __restrict__ offsets, const int* __restrict__ row_token,
-                        const float* __restrict__ row_weight) {
-  __shared__ EpGeom g;
-  __shared__ int off_s[257];
+    ep_tokens_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int T, int H, uint8_t* __restrict__ tq) {
   __shared__ __align__(16) uint8_t exps_s[kSendWarps][kMaxKtPad];
-  EpRegionHeader* own = hdr_of(P, P.rank);
-  if (threadIdx.x == 0) ep_geometry(P, own, g);
-  for (int i = threadIdx.x; i <= E; i += blockDim.x) off_s[i] = offsets[i];
-  __syncthreads();
-  const uint32_t epoch = own->epoch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KT = H / 128, kt_pad = (KT + 15) & ~15;
+  const int KT = H / 128, kt_pad = (KT + 15) & ~15, stride = H + kt_pad;
   uint8_t* exps = exps_s[warp];
-  const int rows = g.send_start[P.world];
-  for (int r = blockIdx.x * kSendWarps + warp; r < rows; r += gridDim.x * kSendWarps) {
-    int d = 0;
-    while (r >= g.send_start[d + 1]) ++d;
-    if (!g.fits[d]) continue;
-    const int t = row_token[r];
+  for (int t = blockIdx.x * kSendWarps + warp; t < T; t += gridDim.x * kSendWarps) {
     const __nv_bfloat16* src = x + static_cast<size_t>(t) * H;
-    uint8_t* dst = P.regions[d] + P.recv_off + static_cast<size_t>(g.dest_off[d] + r - g.send_start[d]) * P.row_bytes;
+    uint8_t* dst = tq + static_cast<size_t>(t) * stride;
     for (int base = 0; base < H; base += 1024) {
       const int k0 = base + lane * 16, k1 = k0 + 512;
       float v0[16], v1[16];
@@ -333,6 +321,35 @@ __global__ void __launch_bounds__(kSendWarps * 32)
     for (int i = KT + lane; i < kt_pad; i += 32) exps[i] = 0;
     __syncwarp();
     if (lane < kt_pad / 16) reinterpret_cast<uint4*>(dst + H)[lane] = reinterpret_cast<const uint4*>(exps)[lane];
+    __syncwarp();  // exps is rewritten by the next token
+  }
+}
+
+// The owners' receive rows from the token rows of ep_tokens_e4m3_kernel: a warp
+// per send row copies its token's E4M3 row (four 16-byte loads in flight per
+// lane) and writes the meta tail; the last CTA stamps every owner's data flag.
+__global__ void __launch_bounds__(kSendWarps * 32)
+    ep_send_rows_e4m3_kernel(const EpPeersDev P, const uint8_t* __restrict__ tq, int H, int E, int E_local,
+                             const int* __restrict__ offsets, const int* __restrict__ row_token,
+                             const float* __restrict__ row_weight) {
+  __shared__ EpGeom g;
+  __shared__ int off_s[257];
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  if (threadIdx.x == 0) ep_geometry(P, own, g);
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) off_s[i] = offsets[i];
+  __syncthreads();
+  const uint32_t epoch = own->epoch;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = H / 128, kt_pad = (KT + 15) & ~15, stride = H + kt_pad;
+  const int rows = g.send_start[P.world];
+  for (int r = blockIdx.x * kSendWarps + warp; r < rows; r += gridDim.x * kSendWarps) {
+    int d = 0;
+    while (r >= g.send_start[d + 1]) ++d;
+    if (!g.fits[d]) continue;
+    const int t = row_token[r];
+    uint8_t* dst = P.regions[d] + P.recv_off + static_cast<size_t>(g.dest_off[d] + r - g.send_start[d]) * P.row_bytes;
+    warp_copy_row(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(tq + static_cast<size_t>(t) * stride),
+                  stride / 16, lane);
     if (lane == 0) {
       int lo = 0, hi = E;  // expert of sorted row r: offsets[lo] <= r < offsets[hi]
       while (hi - lo > 1) {
@@ -343,11 +360,10 @@ __global__ void __launch_bounds__(kSendWarps * 32)
           hi = mid;
       }
       const int dest = lo / E_local;
-      *reinterpret_cast<uint4*>(dst + H + kt_pad) =
+      *reinterpret_cast<uint4*>(dst + stride) =
           make_uint4(static_cast<uint32_t>(lo - dest * E_local), __float_as_uint(row_weight[r]),
                      static_cast<uint32_t>(t), static_cast<uint32_t>(dest));
     }
-    __syncwarp();  // exps is rewritten by the next row
   }
   __threadfence_system();
   __syncthreads();
@@ -412,17 +428,20 @@ cudaError_t launch_ep_exchange_rows(const EpPeersDev& P, const void* send_rows, 
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int H, int E, int E_local,
+cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int T, int H, int E, int E_local,
                                          const int* offsets, const int* row_token, const float* row_weight,
-                                         int* dest_counts, int sms, cudaStream_t stream) {
+                                         int* dest_counts, uint8_t* tq, int sms, cudaStream_t stream) {
   const int kt_pad = (H / 128 + 15) & ~15;
   if (H % 256 || kt_pad > kMaxKtPad || E > 256 || E_local < 1 ||
       P.row_bytes != H + kt_pad + 16)
     return cudaErrorInvalidValue;
   ep_dest_counts_kernel<<<(P.world + 127) / 128, 128, 0, stream>>>(offsets, E_local, P.world, dest_counts);
+  int gq = (T + kSendWarps - 1) / kSendWarps;
+  if (gq > 8 * sms) gq = 8 * sms;
+  ep_tokens_e4m3_kernel<<<gq, kSendWarps * 32, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, tq);
   ep_counts_kernel<<<1, 32, 0, stream>>>(P, dest_counts);
-  ep_send_e4m3_kernel<<<2 * sms, kSendWarps * 32, 0, stream>>>(P, static_cast<const __nv_bfloat16*>(x), H, E, E_local,
-                                                                offsets, row_token, row_weight);
+  ep_send_rows_e4m3_kernel<<<4 * sms, kSendWarps * 32, 0, stream>>>(P, tq, H, E, E_local, offsets, row_token,
+                                                                     row_weight);
   ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
   return cudaGetLastError();
 }

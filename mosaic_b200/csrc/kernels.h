@@ -259,13 +259,14 @@ cudaError_t launch_ep_return_partials(const EpPeersDev& P, const void* partials,
 // buffers: stamp every source's return flag, then wait for this rank's.
 cudaError_t launch_ep_signal_return(const EpPeersDev& P, cudaStream_t stream);
 // E4M3 rows without a send buffer: destination counts from the layout's
-// offsets (kept in dest_counts), the count exchange, then a warp per send row
-// quantises x[row_token[r]] (act_quant_ref) straight into its owner's receive
-// row, and the wait for every source's rows.  P.row_bytes must be
-// MOSAIC_EP_ROW_BYTES_E4M3(H).
-cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int H, int E, int E_local,
+// offsets (kept in dest_counts), every token row quantised once (act_quant_ref)
+// into tq [T][H + pad] (scratch, T * (H + 128) bytes is enough), the count
+// exchange, then a warp per send row copies its token's E4M3 row straight into
+// its owner's receive row, and the wait for every source's rows.
+// P.row_bytes must be MOSAIC_EP_ROW_BYTES_E4M3(H).
+cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int T, int H, int E, int E_local,
                                          const int* offsets, const int* row_token, const float* row_weight,
-                                         int* dest_counts, int sms, cudaStream_t stream);
+                                         int* dest_counts, uint8_t* tq, int sms, cudaStream_t stream);
 
 // ---- combine (combine.cu)
 cudaError_t launch_combine(const void* partial, int partial_f32, const int* row_sorted, int T, int k, int H,
