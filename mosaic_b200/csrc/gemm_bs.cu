@@ -121,28 +121,11 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Sum over the C accumulation chains (chain stride acc_w columns) of 16 columns,
-// adding the lo-plane columns (lo_off > 0: columns lo_off.. of the same chain).
-// Chains and planes are added in a fixed order, so the result is deterministic.
-__device__ __forceinline__ void tmem_sum16(uint32_t taddr, int C, uint32_t acc_w, int lo_off, float (&out)[16]) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) out[j] = 0.f;
-  for (int c = 0; c < C; ++c) {
-    uint32_t r[16], r2[16];
-    tmem_ld16(taddr + c * acc_w, r);
-    if (lo_off) tmem_ld16(taddr + c * acc_w + lo_off, r2);
-    tmem_ld_wait();
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float v = __uint_as_float(r[j]);
-      if (lo_off) v += __uint_as_float(r2[j]);
-      out[j] += v;
-    }
-  }
-}
-
-// tmem_sum16 of two column groups (the pair's blocks, half_off apart), with all
-// loads of a chain issued before one wait.
+// Sum over the C accumulation chains (chain stride acc_w columns) of 16 columns
+// of two column groups (the pair's blocks, half_off apart), adding the lo-plane
+// columns (lo_off > 0: columns lo_off.. of the same chain); all loads of a chain
+// are issued before one wait, and chains and planes are added in a fixed order,
+// so the result is deterministic.
 __device__ __forceinline__ void tmem_sum16x2(uint32_t taddr, uint32_t half_off, int C, uint32_t acc_w, int lo_off,
                                              float (&out0)[16], float (&out1)[16]) {
 #pragma unroll
