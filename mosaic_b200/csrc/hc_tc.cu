@@ -287,6 +287,9 @@ __global__ void hc_split_fn_kernel(const float* __restrict__ fn, int nmix, int K
 int hc_mix_tc_splits(int T, int KD, int num_sms) {
   const int tiles = (T + kHtTok - 1) / kHtTok;
   int s = num_sms / tiles;  // one wave of CTAs
+  // at most one split per lane of the Sinkhorn kernel's warp: every lane then
+  // loads its split's partials in one round
+  if (s > 32) s = 32;
   const int kt = KD / kHtK;
   if (s > kt) s = kt;
   return s < 1 ? 1 : s;

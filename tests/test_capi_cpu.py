@@ -169,14 +169,14 @@ def test_router_workspace_follows_the_split_plan():
 
 def test_hc_workspace_follows_the_split_plan():
     """Error block, split-K mixing partials [splits][T][25] (one wave of 128-token
-    tiles over 148 SMs, at most one 64-wide slice per split), fn's parts
-    [3][32][hc·D], the tokens' pre-mix weights [T][4]."""
+    tiles over 148 SMs, at most 32 splits and one 64-wide slice per split), fn's
+    parts [3][32][hc·D], the tokens' pre-mix weights [T][4]."""
     lib = C.lib()
     d, hc = 7168, 4
     up = lambda n: (n + 255) // 256 * 256  # noqa: E731
     parts = up(3 * 32 * hc * d * 2)
     ws = lib.mosaic_hc_pre_norm_workspace_bytes
-    assert ws(128, d, hc) == 256 + up(148 * 128 * 25 * 4) + parts + up(128 * 16)
+    assert ws(128, d, hc) == 256 + up(32 * 128 * 25 * 4) + parts + up(128 * 16)
     assert ws(8192, d, hc) == 256 + up(2 * 8192 * 25 * 4) + parts + up(8192 * 16)
     assert ws(1, 128, 1) == 256 + up(2 * 1 * 25 * 4) + up(3 * 32 * 128 * 2) + up(16)
 
