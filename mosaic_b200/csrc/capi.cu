@@ -130,6 +130,13 @@ int run_router(const void* x, const float* w, const float* bias, int T, int H, i
                void* parts, int splits, int* err, cudaStream_t stream, const RouteVariant* rv) {
   const RouteVariant r = rv ? *rv : RouteVariant{};
   const int sms = sm_count();
+  // small batches: one launch; err[1] (zeroed with the error word by every
+  // caller) counts the CTAs that finished their logits
+  if (!(r.hash && !r.tid2eid) && err && router_small_applies(T, H, E))
+    return launch_router_small(x, w, bias, T, H, E, top_k, n_group, topk_group, route_scale, norm, weights_out,
+                               idx_out, partial, err + 1, err, stream, rv) == cudaSuccess
+               ? MOSAIC_OK
+               : MOSAIC_ERR_CUDA;
   if (!(r.hash && !r.tid2eid) && sms > 0 && router_tc_applies(H, E)) {
     const bool use_parts = router_tc_parts(T, H, E, sms);
     if (use_parts && !parts) return MOSAIC_ERR_WORKSPACE;

@@ -97,6 +97,13 @@ struct RouteVariant {
 // Split-K factor of the router logits (tensor-core split count where
 // router_tc_applies, else the FMA kernels'); the partials are [splits][T][E].
 int router_splits(int T, int H, int E, int num_sms);
+// Small batches (1 <= T <= 8, H % 64 == 0): logits and top-k in one launch;
+// logits [T][E] scratch, arrivals an int the caller zeroes before the launch.
+bool router_small_applies(int T, int H, int E);
+cudaError_t launch_router_small(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
+                                int n_group, int topk_group, float route_scale, int norm, float* weights_out,
+                                int64_t* idx_out, float* logits, int* arrivals, int* err, cudaStream_t stream,
+                                const RouteVariant* variant);
 cudaError_t launch_router_topk(const float* partial, int splits, const float* bias, int T, int E, int top_k,
                                int n_group, int topk_group, float route_scale, int norm, float* weights_out,
                                int64_t* idx_out, int* err, cudaStream_t stream, const RouteVariant* variant);

@@ -244,42 +244,15 @@ constexpr int kTopkWays = 8;  // warps adding one token's splits when there are 
 // One warp per token selects; with ways = kTopkWays a block of that many warps
 // serves one token, warp w adding splits w, w + ways, ... and warp 0 adding
 // the warps' sums in order w = 0, 1, ... (a fixed order: deterministic).
+// Score function + bias, group limit, top-k (or the table lookup) and the
+// weight normalisation of token t from this lane's PER logits (experts
+// lane * PER + i); lane 0 writes the token's ids and weights.
 template <int PER>
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits, int ways,
-                                                          const float* __restrict__ bias, int T, int E, int top_k,
-                                                          int n_group, int topk_group, float route_scale,
-                                                          int norm, float* __restrict__ w_out,
-                                                          int64_t* __restrict__ idx_out, int* err, RouteVariant rv) {
-  griddep_wait();  // the logits kernel's partials are visible
-  griddep_launch();
-  __shared__ float red[kTopkWays][32 * 8];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int t = ways > 1 ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + warp;  // one token per warp / block
-  if (t >= T) return;
+__device__ __forceinline__ void topk_select(const float (&logit)[PER], int t, int lane, const float* __restrict__ bias,
+                                            int E, int top_k, int n_group, int topk_group, float route_scale,
+                                            int norm, float* __restrict__ w_out, int64_t* __restrict__ idx_out,
+                                            int* err, const RouteVariant& rv) {
   float s[PER], sel[PER];
-  float logit[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) logit[i] = 0.f;
-  // vector path: this lane's experts in range and every row start 16-byte aligned
-  const bool full = (lane + 1) * PER <= E && (PER % 4 == 0) && (E % 4 == 0);
-  const float* pp = partial + static_cast<size_t>(t) * E + lane * PER;
-  const size_t stride = static_cast<size_t>(T) * E;
-  if (ways > 1) {
-    add_splits<PER>(pp, stride, splits, warp, ways, full, lane, E, logit);
-#pragma unroll
-    for (int i = 0; i < PER; ++i) red[warp][lane * PER + i] = logit[i];
-    __syncthreads();
-    if (warp != 0) return;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      float v = 0.f;
-      for (int w = 0; w < ways; ++w) v += red[w][lane * PER + i];
-      logit[i] = v;
-    }
-  } else {
-    add_splits<PER>(pp, stride, splits, 0, 1, full, lane, E, logit);
-  }
   if (rv.score_func == MOSAIC_SCORE_SOFTMAX) {
     // max-shifted exponentials times the reciprocal of their sum
     float m = -INFINITY;
@@ -451,6 +424,133 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   }
 }
 
+template <int PER>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits, int ways,
+                                                          const float* __restrict__ bias, int T, int E, int top_k,
+                                                          int n_group, int topk_group, float route_scale,
+                                                          int norm, float* __restrict__ w_out,
+                                                          int64_t* __restrict__ idx_out, int* err, RouteVariant rv) {
+  griddep_wait();  // the logits kernel's partials are visible
+  griddep_launch();
+  __shared__ float red[kTopkWays][32 * 8];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int t = ways > 1 ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + warp;  // one token per warp / block
+  if (t >= T) return;
+  float logit[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) logit[i] = 0.f;
+  // vector path: this lane's experts in range and every row start 16-byte aligned
+  const bool full = (lane + 1) * PER <= E && (PER % 4 == 0) && (E % 4 == 0);
+  const float* pp = partial + static_cast<size_t>(t) * E + lane * PER;
+  const size_t stride = static_cast<size_t>(T) * E;
+  if (ways > 1) {
+    add_splits<PER>(pp, stride, splits, warp, ways, full, lane, E, logit);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) red[warp][lane * PER + i] = logit[i];
+    __syncthreads();
+    if (warp != 0) return;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      float v = 0.f;
+      for (int w = 0; w < ways; ++w) v += red[w][lane * PER + i];
+      logit[i] = v;
+    }
+  } else {
+    add_splits<PER>(pp, stride, splits, 0, 1, full, lane, E, logit);
+  }
+  topk_select<PER>(logit, t, lane, bias, E, top_k, n_group, topk_group, route_scale, norm, w_out, idx_out, err, rv);
+}
+
+// Small batches (T <= kSmallT): the logits and the top-k in one launch.  CTA c
+// takes experts 2c and 2c + 1; warp w takes expert 2c + (w & 1) over the H
+// quarter w / 2: fp32 FMAs over 4 consecutive k per lane (lane-strided by
+// 128), a butterfly over the lanes, then the quarters added in order (a fixed
+// order).  The logits go to logits[T][E]; the CTA that arrives last (an
+// arrival count the caller zeroes) runs the top-k of every token, a warp per
+// token.  The tensor-core path for these sizes is two launches of ~128 CTAs
+// with a split-K top-k.
+constexpr int kSmallT = 8;
+
+template <int PER>
+__global__ void __launch_bounds__(256, 1) router_small_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const float* __restrict__ w, const float* __restrict__ bias,
+                                                           int T, int H, int E, int top_k, int n_group,
+                                                           int topk_group, float route_scale, int norm,
+                                                           float* __restrict__ logits, int* __restrict__ arrivals,
+                                                           float* __restrict__ w_out, int64_t* __restrict__ idx_out,
+                                                           int* err, RouteVariant rv) {
+  griddep_wait();
+  griddep_launch();
+  __shared__ float part[8][kSmallT];
+  __shared__ int last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = 2 * blockIdx.x + (warp & 1);
+  const int hq = H / 4, k0 = (warp >> 1) * hq;
+  float acc[kSmallT];
+#pragma unroll
+  for (int t = 0; t < kSmallT; ++t) acc[t] = 0.f;
+  if (e < E) {
+    // kSmallU K steps of 128 per trip, every load of the trip issued before its FMAs
+    constexpr int kSmallU = 7;
+    const float* wr = w + static_cast<size_t>(e) * H + k0;
+    for (int kb = lane * 4; kb < hq; kb += 128 * kSmallU) {
+      float4 wv[kSmallU];
+#pragma unroll
+      for (int u = 0; u < kSmallU; ++u)
+        wv[u] = kb + 128 * u < hq ? *reinterpret_cast<const float4*>(wr + kb + 128 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+      // every token's loads of the trip in flight together (rows past T read row 0, unused)
+      uint2 raw[kSmallT][kSmallU];
+#pragma unroll
+      for (int t = 0; t < kSmallT; ++t) {
+        const __nv_bfloat16* xt = x + static_cast<size_t>(t < T ? t : 0) * H + k0 + kb;
+#pragma unroll
+        for (int u = 0; u < kSmallU; ++u)
+          raw[t][u] = kb + 128 * u < hq ? *reinterpret_cast<const uint2*>(xt + 128 * u) : make_uint2(0u, 0u);
+      }
+#pragma unroll
+      for (int t = 0; t < kSmallT; ++t) {
+#pragma unroll
+        for (int u = 0; u < kSmallU; ++u) {
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[t][u]);
+          const float2 a = __bfloat1622float2(h2[0]), b = __bfloat1622float2(h2[1]);
+          acc[t] = fmaf(a.x, wv[u].x, acc[t]);
+          acc[t] = fmaf(a.y, wv[u].y, acc[t]);
+          acc[t] = fmaf(b.x, wv[u].z, acc[t]);
+          acc[t] = fmaf(b.y, wv[u].w, acc[t]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kSmallT; ++t) {
+    const float v = warp_sum(acc[t]);
+    if (lane == 0) part[warp][t] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * T) {
+    const int h = threadIdx.x & 1, t = threadIdx.x >> 1;
+    const int ee = 2 * blockIdx.x + h;
+    if (ee < E) logits[static_cast<size_t>(t) * E + ee] = ((part[h][t] + part[2 + h][t]) + part[4 + h][t]) + part[6 + h][t];
+  }
+  __threadfence();  // this CTA's logits before its arrival
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(arrivals, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (warp < T) {
+    float logit[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e2 = lane * PER + i;
+      logit[i] = e2 < E ? __ldcg(logits + static_cast<size_t>(warp) * E + e2) : 0.f;
+    }
+    topk_select<PER>(logit, warp, lane, bias, E, top_k, n_group, topk_group, route_scale, norm, w_out, idx_out, err,
+                     rv);
+  }
+}
+
 // Table-less hash routing (layers.py:180-184): one expert per token,
 //   salt   = layer_idx * 2654435761 mod 2^31          (Python integers)
 //   hashed = ((int32(token) + salt) * 2654435761) mod 2^31
@@ -539,6 +639,34 @@ cudaError_t launch_router_topk(const float* partial, int splits, const float* bi
   else
     MOSAIC_TOPK(8);
 #undef MOSAIC_TOPK
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+bool router_small_applies(int T, int H, int E) { return T >= 1 && T <= kSmallT && H % 64 == 0 && E >= 1 && E <= 256; }
+
+cudaError_t launch_router_small(const void* x, const float* w, const float* bias, int T, int H, int E, int top_k,
+                                int n_group, int topk_group, float route_scale, int norm, float* weights_out,
+                                int64_t* idx_out, float* logits, int* arrivals, int* err, cudaStream_t stream,
+                                const RouteVariant* variant) {
+  if (!router_small_applies(T, H, E)) return cudaErrorInvalidValue;
+  const RouteVariant rv = variant ? *variant : RouteVariant{};
+  const dim3 grid((E + 1) / 2);
+  const int per = (E + 31) / 32;
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  cudaError_t e = cudaSuccess;
+#define MOSAIC_SMALL(P)                                                                                         \
+  e = launch_k(router_small_kernel<P>, grid, dim3(256), 0, stream, xb, w, bias, T, H, E, top_k, n_group, topk_group, \
+               route_scale, norm, logits, arrivals, weights_out, idx_out, err, rv)
+  if (per <= 1)
+    MOSAIC_SMALL(1);
+  else if (per <= 2)
+    MOSAIC_SMALL(2);
+  else if (per <= 4)
+    MOSAIC_SMALL(4);
+  else
+    MOSAIC_SMALL(8);
+#undef MOSAIC_SMALL
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
