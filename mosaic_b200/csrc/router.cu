@@ -11,10 +11,12 @@
 // the ids from a token-id table instead of the top-k, and without a table uses
 // the salted multiplicative hash of layers.py:180-184.
 //
-// The logits x . W^T come from the tensor cores (router_tc.cu) wherever
-// H % 64 == 0 and E % 16 == 0, else from the FMA kernels here; both write
-// deterministic split-K partials [splits][T][E] (every split sums its K
-// range in a fixed order).  router_topk_kernel (one warp per token, or 8 per
+// For T <= 8 (H % 64 == 0) router_small_kernel computes the logits with fp32
+// FMAs and runs the top-k in the same launch.  Otherwise the logits x . W^T
+// come from the tensor cores (router_tc.cu) wherever H % 64 == 0 and
+// E % 16 == 0, else from the FMA kernels here; both write deterministic
+// split-K partials [splits][T][E] (every split sums its K range in a fixed
+// order).  router_topk_kernel (one warp per token, or 8 per
 // token when there are many splits) adds the partials in a fixed order, so a
 // logit never depends on scheduling, then applies the score function + bias,
 // the group limit and the top-k (or the table lookup), and normalises the
