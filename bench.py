@@ -75,7 +75,8 @@ def headline_config(world: int) -> dict:
 def layer_launches(t: int, world: int) -> int:
     """Kernels one layer step launches (the C ABI's launch sequence).
 
-    Router: tensor-core logits + top-k, plus the W split above 128 tokens.
+    Router: one launch up to 8 tokens (logits and top-k together), else
+    tensor-core logits + top-k, plus the W split above 128 tokens.
     Layout: one CTA up to 1024 assignments, else count / scan / rank / finish.
     One GPU: router, layout, rows_quant, gate/up, down, combine.  Expert
     parallel (FP8, E4M3 rows): router, dispatch + exchange (layout, destination
@@ -83,7 +84,7 @@ def layer_launches(t: int, world: int) -> int:
     (per-row metadata, layout, rows_quant, gate/up, down) and the received
     rows (per-row metadata, layout, placement, gate/up, down), return (signal,
     wait), combine."""
-    router = 3 if t > 128 else 2
+    router = 1 if t <= 8 else (3 if t > 128 else 2)
     lay = lambda a: 4 if a > 1024 else 1  # noqa: E731
     if world == 1:
         return router + lay(t * 8) + 4
