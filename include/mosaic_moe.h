@@ -351,6 +351,12 @@ MOSAIC_API int mosaic_moe_routed_slots(const mosaic_moe_dims* dims, const void* 
  * bytes, then the H/128 biased scale exponents (uint8, 2^(e-127)) padded with
  * zeros to a multiple of 16 bytes, then the same 16-byte tail. */
 #define MOSAIC_EP_ROW_BYTES_E4M3(H) ((size_t)(H) + ((((size_t)(H) / 128u) + 15u) & ~(size_t)15u) + 16u)
+/* E4M3 unit row (row_e4m3 = 1 with unit_slots = K > 0): one row per (token,
+ * owning rank) instead of one per assignment.  The E4M3 row above, whose
+ * 16-byte tail becomes a header {slots used, source token, 0, 0}, then K
+ * 16-byte slots {local expert id (-1: unused), route weight (fp32 bits),
+ * return position (the assignment's row in the source's return buffer), 0}. */
+#define MOSAIC_EP_ROW_BYTES_E4M3_UNITS(H, K) (MOSAIC_EP_ROW_BYTES_E4M3(H) + 16u * (size_t)(K))
 
 /* Layout + gather of one rank's assignments.  dims: the layer (tokens = this
  * rank's T, n_experts = global E, E % world == 0).  idx int64 [T, top_k],
@@ -424,7 +430,10 @@ typedef struct mosaic_ep_peers {
                              this rank's region and the kernel returns */
   int32_t row_e4m3;       /* 1: the exchange carries E4M3 rows (MOSAIC_EP_ROW_BYTES_E4M3; needs
                              partial_f32 = 0 and H <= 16384), 0: bf16 rows (MOSAIC_EP_ROW_BYTES) */
-  int32_t reserved;       /* 0 */
+  int32_t unit_slots;     /* 0: a row per assignment; K in 1..8 (with row_e4m3 = 1): a row per
+                             (token, owning rank) with K slots (K >= min(top_k, experts per rank);
+                             MOSAIC_EP_ROW_BYTES_E4M3_UNITS), max_recv_rows counting such rows
+                             (world * T_max covers any routing) */
   void* regions[MOSAIC_EP_MAX_WORLD];  /* rank r's region as mapped in this process (own at [rank]) */
 } mosaic_ep_peers;
 
@@ -453,7 +462,11 @@ MOSAIC_API int mosaic_ep_return_partials(const mosaic_ep_peers* peers, const voi
  * would have sent, quantised.  dims: the layer (tokens = this rank's T <=
  * peers->max_tokens, n_experts = global E, hidden = peers->hidden); idx /
  * weights as for mosaic_ep_dispatch; workspace: mosaic_moe_workspace_bytes(dims),
- * kept for mosaic_ep_combine. */
+ * kept for mosaic_ep_combine.  With peers->unit_slots > 0 a token's row goes
+ * once to each rank that owns one of its experts, carrying those experts'
+ * ids, weights and return positions (at most min(top_k, E/world) slots; at
+ * 8 ranks and groups aligned with ranks, at most topk_group rows per token
+ * instead of top_k). */
 MOSAIC_API int mosaic_ep_dispatch_exchange(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers, const void* x,
                                            const int64_t* idx, const float* weights, void* workspace,
                                            size_t workspace_bytes, mosaic_stream_t stream);
@@ -466,6 +479,10 @@ MOSAIC_API int mosaic_ep_dispatch_exchange(const mosaic_moe_dims* dims, const mo
  * mosaic_moe_expert_rows_workspace_bytes(dims, peers->max_recv_rows).  With
  * peers->row_e4m3 the received E4M3 rows go into the GEMM's operand planes as
  * they are (no second quantisation; dims->act_mode must be MOSAIC_ACT_FP8). */
+/* Workspace of mosaic_ep_expert_rows_return for this exchange (dims as for it):
+ * mosaic_moe_expert_rows_workspace_bytes(dims, peers->max_recv_rows) for rows per
+ * assignment; with unit rows, room for max_recv_rows * unit_slots assignments. */
+MOSAIC_API size_t mosaic_ep_expert_rows_workspace_bytes(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers);
 MOSAIC_API int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers,
                                             const mosaic_expert_bank* bank, void* workspace, size_t workspace_bytes,
                                             mosaic_stream_t stream);

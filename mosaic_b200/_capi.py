@@ -33,6 +33,12 @@ def ep_row_bytes_e4m3(hidden: int) -> int:
     return hidden + ((hidden // 128 + 15) & ~15) + 16
 
 
+def ep_row_bytes_e4m3_units(hidden: int, slots: int) -> int:
+    """include/mosaic_moe.h MOSAIC_EP_ROW_BYTES_E4M3_UNITS: the E4M3 row (its tail
+    the unit header) and 16 bytes per slot."""
+    return ep_row_bytes_e4m3(hidden) + 16 * slots
+
+
 # include/mosaic_moe.h MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES
 MOSAIC_ROUTER_NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -83,6 +89,7 @@ EXPORTED = (
     "mosaic_ep_region_view",
     "mosaic_ep_exchange_rows",
     "mosaic_ep_dispatch_exchange",
+    "mosaic_ep_expert_rows_workspace_bytes",
     "mosaic_ep_return_partials",
     "mosaic_ep_expert_rows_return",
     "mosaic_moe_expert_rows_dev",
@@ -142,7 +149,7 @@ class EpPeersC(ctypes.Structure):
         ("partial_f32", ctypes.c_int32),
         ("wait_us", ctypes.c_int32),
         ("row_e4m3", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("unit_slots", ctypes.c_int32),
         ("regions", ctypes.c_void_p * EP_MAX_WORLD),
     ]
 
@@ -201,6 +208,7 @@ _SIGS = {
     "mosaic_ep_exchange_rows": ([ctypes.POINTER(EpPeersC), _P, _P, _P], ctypes.c_int),
     "mosaic_ep_dispatch_exchange": ([ctypes.POINTER(MoEDims), ctypes.POINTER(EpPeersC), _P, _P, _P, _P, _SZ, _P],
                                     ctypes.c_int),
+    "mosaic_ep_expert_rows_workspace_bytes": ([ctypes.POINTER(MoEDims), ctypes.POINTER(EpPeersC)], _SZ),
     "mosaic_ep_return_partials": ([ctypes.POINTER(EpPeersC), _P, _P], ctypes.c_int),
     "mosaic_ep_expert_rows_return": ([ctypes.POINTER(MoEDims), ctypes.POINTER(EpPeersC), ctypes.POINTER(ExpertBankC),
                                       _P, _SZ, _P], ctypes.c_int),

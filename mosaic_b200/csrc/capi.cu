@@ -290,7 +290,8 @@ void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
 int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const LayoutParams& lp,
               const mosaic_expert_bank* bank, int shared_expert, const int* out_row, void* partial_out,
               cudaStream_t stream, void* const* ev, const EpPeersDev* ep = nullptr,
-              const int* expert_slot = nullptr, int bank_slots = 0) {
+              const int* expert_slot = nullptr, int bank_slots = 0, const int* ep_row_rank = nullptr,
+              const int* ep_row_pos = nullptr) {
   const int n_map = expert_slot ? bank_slots : w.n_bank;  // bank entries the weight maps cover
   const int H = d->hidden, I = d->inter;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
@@ -356,6 +357,8 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
     gp.ep_world = ep->world;
     gp.ep_recv_start = own->recv_start;
     gp.ep_src_pos = own->src_pos;
+    gp.ep_row_rank = ep_row_rank;
+    gp.ep_row_pos = ep_row_pos;
     gp.ep_ret_off = ep->ret_off;
     for (int r = 0; r < ep->world; ++r) gp.ep_regions[r] = ep->regions[r];
   }
@@ -987,14 +990,49 @@ int check_peers(const mosaic_ep_peers* p) {
   if (p->max_recv_rows < 1 || p->max_send_rows < 1 || p->max_tokens < 1) return MOSAIC_ERR_SHAPE;
   if (p->hidden < 256 || p->hidden % 256) return MOSAIC_ERR_SHAPE;
   if (p->wait_us < 0) return MOSAIC_ERR_RANGE;
-  if ((p->row_e4m3 != 0 && p->row_e4m3 != 1) || p->reserved != 0) return MOSAIC_ERR_SHAPE;
+  if ((p->row_e4m3 != 0 && p->row_e4m3 != 1) || p->unit_slots < 0 || p->unit_slots > 8) return MOSAIC_ERR_SHAPE;
+  if (p->unit_slots && !p->row_e4m3) return MOSAIC_ERR_SHAPE;  // unit rows are E4M3 rows
   if (p->row_e4m3 && p->partial_f32) return MOSAIC_ERR_SHAPE;  // E4M3 rows are the FP8 layer's
   if (p->row_e4m3 && p->hidden > 16384) return MOSAIC_ERR_UNSUPPORTED;
   return MOSAIC_OK;
 }
 
 size_t ep_row_bytes(const mosaic_ep_peers* p) {
+  if (p->unit_slots) return MOSAIC_EP_ROW_BYTES_E4M3_UNITS(p->hidden, p->unit_slots);
   return p->row_e4m3 ? MOSAIC_EP_ROW_BYTES_E4M3(p->hidden) : MOSAIC_EP_ROW_BYTES(p->hidden);
+}
+
+// Receive-side workspace with unit rows: the per-row plan for U units of K
+// slots (U * K assignments), then the assignments' ids, weights, return ranks
+// and positions, and the return rank and position of every packed row.
+struct UnitsWs {
+  WsPlan plan;
+  size_t idx, w, a_rank, a_pos, row_rank, row_ret, total;
+};
+UnitsWs units_ws(const mosaic_moe_dims* r) {
+  UnitsWs u{};
+  u.plan = plan_ws(r, true);
+  const size_t A = static_cast<size_t>(r->tokens) * r->top_k;
+  size_t o = u.plan.total;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = up256(o + bytes);
+    return at;
+  };
+  u.idx = take(sizeof(int64_t) * A);
+  u.w = take(sizeof(float) * A);
+  u.a_rank = take(sizeof(int) * A);
+  u.a_pos = take(sizeof(int) * A);
+  u.row_rank = take(sizeof(int) * static_cast<size_t>(u.plan.R));
+  u.row_ret = take(sizeof(int) * static_cast<size_t>(u.plan.R));
+  u.total = o;
+  return u;
+}
+
+mosaic_moe_dims units_dims(const mosaic_moe_dims* d, const mosaic_ep_peers* p) {
+  mosaic_moe_dims r = rows_dims(d, p->max_recv_rows);
+  r.top_k = p->unit_slots;
+  return r;
 }
 
 size_t ep_recv_bytes(const mosaic_ep_peers* p) { return static_cast<size_t>(p->max_recv_rows) * ep_row_bytes(p); }
@@ -1097,6 +1135,15 @@ int mosaic_ep_exchange_rows(const mosaic_ep_peers* peers, const void* send_rows,
              : MOSAIC_ERR_CUDA;
 }
 
+size_t mosaic_ep_expert_rows_workspace_bytes(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers) {
+  if (!dims || check_peers(peers) != MOSAIC_OK) return 0;
+  if (!peers->unit_slots) return mosaic_moe_expert_rows_workspace_bytes(dims, peers->max_recv_rows);
+  if (dims->n_experts > 256) return 0;
+  const mosaic_moe_dims r = units_dims(dims, peers);
+  if (check_rows_dims(&r) != MOSAIC_OK) return 0;
+  return units_ws(&r).total;
+}
+
 int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_peers* peers,
                                  const mosaic_expert_bank* bank, void* workspace, size_t workspace_bytes,
                                  mosaic_stream_t stream) {
@@ -1114,6 +1161,49 @@ int mosaic_ep_expert_rows_return(const mosaic_moe_dims* dims, const mosaic_ep_pe
   const int rb = ep.row_bytes;
   const int h = peers->hidden;
   const bool e4m3 = peers->row_e4m3 != 0;
+  if (peers->unit_slots) {  // unit rows: expand every unit into its slots' packed rows
+    if (dims->act_mode != MOSAIC_ACT_FP8 || dims->n_experts > 256) return MOSAIC_ERR_SHAPE;
+    const mosaic_moe_dims r = units_dims(dims, peers);
+    st = check_rows_dims(&r);
+    if (st) return st;
+    st = check_bank(bank);
+    if (st) return st;
+    if (!workspace) return MOSAIC_ERR_SHAPE;
+    if (!aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+    const UnitsWs uw = units_ws(&r);
+    if (workspace_bytes < uw.total) return MOSAIC_ERR_WORKSPACE;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const WsPlan& w = uw.plan;
+    if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+    const int K = peers->unit_slots, U = peers->max_recv_rows;
+    int64_t* aidx = reinterpret_cast<int64_t*>(ws + uw.idx);
+    float* aw = reinterpret_cast<float*>(ws + uw.w);
+    int* arank = reinterpret_cast<int*>(ws + uw.a_rank);
+    int* apos = reinterpret_cast<int*>(ws + uw.a_pos);
+    int* rrank = reinterpret_cast<int*>(ws + uw.row_rank);
+    int* rret = reinterpret_cast<int*>(ws + uw.row_ret);
+    if (launch_ep_units_meta(ep, h, K, U, aidx, aw, arank, apos, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+    LayoutParams lp{};
+    lp.idx = aidx;
+    lp.weights = aw;
+    lp.T = U;
+    lp.k = K;
+    lp.E = r.n_experts;
+    lp.with_shared = 0;
+    fill_layout(lp, w, ws);
+    lp.T_dev = count;
+    lp.row_sorted = nullptr;
+    lp.pad_ok = 1;  // unused slots
+    if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+    if (launch_rows_place_units(recv, rb, U, count, h, K, lp.row_of, arank, apos, w.R_pad, lp.row_tile, lp.row_pos,
+                                ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), rrank, rret, s) != cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+    st = run_gemms(&r, w, ws, lp, bank, dims->has_shared ? dims->n_experts : -1, lp.row_token, nullptr, s, nullptr,
+                   &ep, nullptr, 0, rrank, rret);
+    if (st) return st;
+    return launch_ep_signal_return(ep, s) == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
+  }
   const int meta = e4m3 ? rb - 16 : 2 * h;  // byte offset of the row's tail
   st = expert_rows_impl(dims, peers->max_recv_rows, count, recv, e4m3 ? rb : rb / 2,
                         reinterpret_cast<const int32_t*>(recv + meta), reinterpret_cast<const float*>(recv + meta + 4),
@@ -1177,9 +1267,20 @@ int mosaic_ep_dispatch_exchange(const mosaic_moe_dims* dims, const mosaic_ep_pee
   lp.tiles = nullptr;
   if (launch_layout(lp, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   // the sender runs no GEMM, so the activation planes and the partial rows of
-  // the workspace are free: the destination counts and the E4M3 token rows
-  // (T x (H + pad) <= T x 2H bytes of the R x H partials)
+  // the workspace are free: the destination counts (and, with unit rows, the
+  // units' tokens [world][T]) and the E4M3 token rows (T x (H + pad) <= T x 2H
+  // bytes of the R x H partials)
   int* dest_counts = reinterpret_cast<int*>(ws + w.xq);
+  if (peers->unit_slots) {
+    const int E_local = E / world;
+    if (peers->unit_slots < (k < E_local ? k : E_local)) return MOSAIC_ERR_SHAPE;
+    int* unit_token = reinterpret_cast<int*>(ws + w.xq + 256);
+    if (launch_ep_dispatch_send_units(ep_dev(peers), x, T, dims->hidden, k, E_local, peers->unit_slots, idx,
+                                      weights, lp.row_of, dest_counts, unit_token, ws + w.partial, sms,
+                                      s) != cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+    return MOSAIC_OK;
+  }
   if (launch_ep_dispatch_send_e4m3(ep_dev(peers), x, T, dims->hidden, E, E / world, lp.offsets, lp.row_token,
                                    lp.row_weight, dest_counts, ws + w.partial, sms, s) != cudaSuccess)
     return MOSAIC_ERR_CUDA;

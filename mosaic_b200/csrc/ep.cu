@@ -418,6 +418,158 @@ __global__ void __launch_bounds__(kSendWarps * 32)
   }
 }
 
+// ------------------------------------------------------------ unit rows ---
+// A token's row goes once to each rank owning one of its experts.  CTA d lists
+// the tokens with an expert on rank d, in token order (a block-wide scan):
+// unit_token[d * T_stride + p] = token of d's unit p; dest_counts[d] = units.
+__global__ void __launch_bounds__(1024)
+    ep_units_kernel(const int64_t* __restrict__ idx, int T, int k, int E_local, int T_stride,
+                    int* __restrict__ unit_token, int* __restrict__ dest_counts) {
+  __shared__ int warp_pre[32];
+  __shared__ int tot_s, carry;
+  const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t lo = static_cast<int64_t>(d) * E_local, hi = lo + E_local;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int t0 = 0; t0 < T; t0 += 1024) {
+    const int t = t0 + tid;
+    int m = 0;
+    if (t < T)
+      for (int s = 0; s < k; ++s) {
+        const int64_t e = idx[static_cast<size_t>(t) * k + s];
+        if (e >= lo && e < hi) m = 1;
+      }
+    const unsigned b = __ballot_sync(0xFFFFFFFFu, m);
+    const int wpre = __popc(b & ((1u << lane) - 1u));
+    if (lane == 0) warp_pre[warp] = __popc(b);
+    __syncthreads();
+    if (warp == 0) {
+      const int v = warp_pre[lane];
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      warp_pre[lane] = incl - v;
+      if (lane == 31) tot_s = incl;
+    }
+    __syncthreads();
+    if (m) unit_token[static_cast<size_t>(d) * T_stride + carry + warp_pre[warp] + wpre] = t;
+    __syncthreads();
+    if (tid == 0) carry += tot_s;
+    __syncthreads();
+  }
+  if (tid == 0) dest_counts[d] = carry;
+}
+
+// Unit rows into the owners' receive rows (the bulk-store scheme of
+// ep_send_rows_e4m3_kernel): lane 0 bulk-loads the token's E4M3 row, lane s < k
+// writes the slot of assignment s when its expert is on the owner (slots
+// packed in slot order), the other slots up to K are marked unused, lane 0
+// writes the header {slots used, token}; one bulk store writes the row.
+__global__ void __launch_bounds__(kSendWarps * 32)
+    ep_send_units_kernel(const EpPeersDev P, const uint8_t* __restrict__ tq, int H, int T_stride, int k, int E_local,
+                         int K, const int64_t* __restrict__ idx, const float* __restrict__ weights,
+                         const int* __restrict__ row_of, const int* __restrict__ unit_token) {
+  extern __shared__ __align__(128) uint8_t sbuf[];
+  __shared__ EpGeom g;
+  __shared__ uint64_t lbar[kSendWarps];
+  __shared__ int abort_s;
+  EpRegionHeader* own = hdr_of(P, P.rank);
+  if (threadIdx.x == 0) {
+    ep_geometry(P, own, g);
+    for (int w = 0; w < kSendWarps; ++w) mbar_init(&lbar[w], 1);
+    abort_s = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint32_t epoch = own->epoch;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = H / 128, kt_pad = (KT + 15) & ~15, stride = H + kt_pad;
+  uint8_t* buf = sbuf + warp * ((P.row_bytes + 127) & ~127);
+  const int rows = g.send_start[P.world];
+  uint32_t ph = 0;
+  bool ok = true;
+  for (int q = blockIdx.x * kSendWarps + warp; ok && q < rows; q += gridDim.x * kSendWarps) {
+    int d = 0;
+    while (q >= g.send_start[d + 1]) ++d;
+    if (!g.fits[d]) continue;
+    const int pu = q - g.send_start[d];
+    const int t = unit_token[static_cast<size_t>(d) * T_stride + pu];
+    uint8_t* dst = P.regions[d] + P.recv_off + static_cast<size_t>(g.dest_off[d] + pu) * P.row_bytes;
+    if (lane == 0) {
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the buffer's last store has read it
+      mbar_arrive_expect_tx(&lbar[warp], static_cast<uint32_t>(stride));
+      bulk_load(buf, tq + static_cast<size_t>(t) * stride, static_cast<uint32_t>(stride), &lbar[warp]);
+      ok = mbar_wait(&lbar[warp], ph, &abort_s);
+      if (!ok) set_error(&own->err, MOSAIC_ERR_TIMEOUT);
+    }
+    ph ^= 1u;
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    if (!ok) break;
+    int e = -1;
+    if (lane < k) {
+      const int64_t v = idx[static_cast<size_t>(t) * k + lane];
+      const int64_t lo = static_cast<int64_t>(d) * E_local;
+      if (v >= lo && v < lo + E_local) e = static_cast<int>(v - lo);
+    }
+    const unsigned m = __ballot_sync(0xFFFFFFFFu, e >= 0);
+    const int c = __popc(m);
+    uint4* slot = reinterpret_cast<uint4*>(buf + stride + 16);
+    if (e >= 0) {
+      const size_t a = static_cast<size_t>(t) * k + lane;
+      slot[__popc(m & ((1u << lane) - 1u))] =
+          make_uint4(static_cast<uint32_t>(e), __float_as_uint(weights ? weights[a] : 1.0f),
+                     static_cast<uint32_t>(row_of[a]), 0u);
+    }
+    if (lane >= c && lane < K) slot[lane] = make_uint4(0xFFFFFFFFu, 0u, 0u, 0u);
+    if (lane == 0) *reinterpret_cast<uint4*>(buf + stride) = make_uint4(static_cast<uint32_t>(c), static_cast<uint32_t>(t), 0u, 0u);
+    fence_proxy_async_smem();  // every lane's generic writes before the bulk store reads the buffer
+    __syncwarp();
+    if (lane == 0) bulk_store(dst, buf, static_cast<uint32_t>(P.row_bytes));
+  }
+  if (lane == 0) {
+    if (!ok) {  // a load that never completed: no copy may still write into the buffer at exit
+      volatile int never = 0;
+      mbar_wait(&lbar[warp], ph ^ 1u, &never);
+    }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every store of this warp complete
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(&own->send_done, 1u) == gridDim.x - 1) {
+      own->send_done = 0;
+      __threadfence_system();
+      for (int d2 = 0; d2 < P.world; ++d2) st_release_sys(&hdr_of(P, d2)->data_flag[P.rank], epoch);
+    }
+  }
+}
+
+// Received unit rows -> assignments: slot j of unit u is assignment u * K + j
+// (id -1: unused), with its route weight, the source rank of the unit and the
+// assignment's row in the source's return buffer.
+__global__ void ep_units_meta_kernel(const EpPeersDev P, int stride, int K, int U_max, int64_t* __restrict__ idx,
+                                     float* __restrict__ w, int* __restrict__ a_rank, int* __restrict__ a_pos) {
+  griddep_wait();
+  griddep_launch();
+  const EpRegionHeader* own = hdr_of(P, P.rank);
+  const int n = min(own->recv_count, U_max);
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= n * K) return;
+  const int u = a / K, j = a - u * K;
+  const uint8_t* row = P.regions[P.rank] + P.recv_off + static_cast<size_t>(u) * P.row_bytes;
+  const uint4 sl = *reinterpret_cast<const uint4*>(row + stride + 16 + 16 * j);
+  idx[a] = static_cast<int64_t>(static_cast<int32_t>(sl.x));
+  w[a] = __uint_as_float(sl.y);
+  a_pos[a] = static_cast<int>(sl.z);
+  int s = 0;
+  while (s + 1 < P.world && u >= own->recv_start[s + 1]) ++s;
+  a_rank[a] = s;
+}
+
 // One CTA, after the down GEMM wrote this rank's partials into the sources'
 // return buffers (its threads fenced them at system scope before exiting):
 // stamp every source's return flag.
@@ -492,6 +644,42 @@ cudaError_t launch_ep_dispatch_send_e4m3(const EpPeersDev& P, const void* x, int
   ep_send_rows_e4m3_kernel<<<per_sm * sms, kSendWarps * 32, smem, stream>>>(P, tq, H, E, E_local, offsets, row_token,
                                                                              row_weight);
   ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_dispatch_send_units(const EpPeersDev& P, const void* x, int T, int H, int k, int E_local,
+                                          int K, const int64_t* idx, const float* weights, const int* row_of,
+                                          int* dest_counts, int* unit_token, uint8_t* tq, int sms,
+                                          cudaStream_t stream) {
+  const int kt_pad = (H / 128 + 15) & ~15;
+  if (H % 256 || kt_pad > kMaxKtPad || E_local < 1 || K < 1 || K > 8 || k < 1 || k > 8 ||
+      P.row_bytes != H + kt_pad + 16 + 16 * K)
+    return cudaErrorInvalidValue;
+  ep_units_kernel<<<P.world, 1024, 0, stream>>>(idx, T, k, E_local, T, unit_token, dest_counts);
+  int gq = (T + kSendWarps - 1) / kSendWarps;
+  if (gq > 8 * sms) gq = 8 * sms;
+  ep_tokens_e4m3_kernel<<<gq, kSendWarps * 32, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), T, H, tq);
+  ep_counts_kernel<<<1, 32, 0, stream>>>(P, dest_counts);
+  const int smem = kSendWarps * ((P.row_bytes + 127) & ~127);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  int per_sm = (220 * 1024) / (smem + 2048);
+  if (per_sm > 3) per_sm = 3;
+  cudaError_t e = cudaFuncSetAttribute(ep_send_units_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  ep_send_units_kernel<<<per_sm * sms, kSendWarps * 32, smem, stream>>>(P, tq, H, T, k, E_local, K, idx, weights,
+                                                                         row_of, unit_token);
+  ep_wait_kernel<<<1, 32, 0, stream>>>(P, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_units_meta(const EpPeersDev& P, int H, int K, int U_max, int64_t* idx, float* w, int* a_rank,
+                                 int* a_pos, cudaStream_t stream) {
+  const int stride = H + ((H / 128 + 15) & ~15);
+  const int n = U_max * K;
+  if (n <= 0) return cudaSuccess;
+  const cudaError_t e = launch_k(ep_units_meta_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, P, stride, K,
+                                 U_max, idx, w, a_rank, a_pos);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

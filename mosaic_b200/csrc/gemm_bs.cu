@@ -505,6 +505,9 @@ __global__ void __launch_bounds__(NT, 1)
         const int r = m.row0 + et;
         if (gu) {
           meta_w[et] = p.row_weight[r];
+        } else if (p.ep_row_pos) {  // unit rows: the return rank and row of packed row r
+          meta_r[et] = p.ep_row_rank[r];
+          meta_o[et] = p.ep_row_pos[r];
         } else {
           const int orow = p.out_row ? p.out_row[r] : r;
           if (p.ep_world) {  // receive row orow of source s goes to s's send position of it

@@ -69,6 +69,8 @@ struct GemmParams {
   int ep_world;       // 0: plain output
   const int* ep_recv_start;
   const int* ep_src_pos;
+  const int* ep_row_rank;  // unit rows: packed row r returns to rank ep_row_rank[r], row ep_row_pos[r]
+  const int* ep_row_pos;   // (null: from the receive geometry above)
   size_t ep_ret_off;
   uint8_t* ep_regions[MOSAIC_EP_MAX_WORLD];
   // expert offload: the weights of logical expert e are bank entry
@@ -182,6 +184,7 @@ struct LayoutParams {
   int* err;
   int* scratch;           // layout_scratch_ints(T, k, E) ints: the multi-CTA layout of
                           // batches above 1024 assignments (null: the single-CTA kernel)
+  int pad_ok;             // 1: negative ids are padding slots (no row, no error)
 };
 size_t layout_scratch_ints(int T, int k, int E);
 cudaError_t launch_layout(const LayoutParams& p, cudaStream_t stream);
@@ -206,6 +209,14 @@ cudaError_t launch_rows_quant(const void* x, int T, const int* T_dev, int H, int
 cudaError_t launch_rows_place_e4m3(const void* rows, int row_bytes, int R, const int* R_dev, int H, const int* row_of,
                                    int R_pad, const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
                                    cudaStream_t stream);
+// E4M3 unit rows (MOSAIC_EP_ROW_BYTES_E4M3_UNITS) -> the same planes and scale
+// chunks: unit u's codes to the packed row of each used slot (row_of[u*K + j]),
+// and row_rank / row_ret [R] = slot j's return rank and position (a_rank / a_pos
+// [U*K]) under that packed row; only the first *U_dev units.
+cudaError_t launch_rows_place_units(const void* rows, int row_bytes, int U, const int* U_dev, int H, int K,
+                                    const int* row_of, const int* a_rank, const int* a_pos, int R_pad,
+                                    const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
+                                    int* row_rank, int* row_ret, cudaStream_t stream);
 cudaError_t launch_act_quant(const void* x, int M, int K, uint8_t* q, float* scale, cudaStream_t stream);
 cudaError_t launch_pack_mxfp4(const float* w, int N, int K, uint8_t* packed, uint8_t* scale, cudaStream_t stream);
 // halves = 2 interleaves the two row halves of each matrix (gate rows, up rows)
@@ -265,6 +276,16 @@ cudaError_t launch_ep_return_partials(const EpPeersDev& P, const void* partials,
 // After a down GEMM that wrote the partials straight into the sources' return
 // buffers: stamp every source's return flag, then wait for this rank's.
 cudaError_t launch_ep_signal_return(const EpPeersDev& P, cudaStream_t stream);
+// Unit rows (P.row_bytes = MOSAIC_EP_ROW_BYTES_E4M3_UNITS(H, K)): the units per
+// owner (unit_token [world][T] scratch, dest_counts = units), the token
+// quantise into tq, the count exchange, the unit send and the wait.
+cudaError_t launch_ep_dispatch_send_units(const EpPeersDev& P, const void* x, int T, int H, int k, int E_local,
+                                          int K, const int64_t* idx, const float* weights, const int* row_of,
+                                          int* dest_counts, int* unit_token, uint8_t* tq, int sms,
+                                          cudaStream_t stream);
+// Received unit rows -> assignments idx / w / a_rank / a_pos [U_max * K] (id -1: unused slot).
+cudaError_t launch_ep_units_meta(const EpPeersDev& P, int H, int K, int U_max, int64_t* idx, float* w, int* a_rank,
+                                 int* a_pos, cudaStream_t stream);
 // E4M3 rows without a send buffer: destination counts from the layout's
 // offsets (kept in dest_counts), every token row quantised once (act_quant_ref)
 // into tq [T][H + pad] (scratch, T * (H + 128) bytes is enough), the count

@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(1024) layout_kernel(LayoutParams p, LayoutExtr
   for (int a = tid; a < A; a += 1024) {
     const int64_t e = p.idx[a];
     if (e < 0 || e >= E) {
-      set_error(p.err, MOSAIC_ERR_RANGE);
+      if (!(p.pad_ok && e < 0)) set_error(p.err, MOSAIC_ERR_RANGE);
       continue;
     }
     atomicAdd(&hist[static_cast<int>(e)], 1);
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(1024) layout_count_kernel(LayoutParams p, int 
     const int64_t v = p.idx[a];
     if (v >= 0 && v < E) {
       atomicAdd(&cnt[static_cast<int>(v)], 1);
-    } else {
+    } else if (!(p.pad_ok && v < 0)) {
       set_error(p.err, MOSAIC_ERR_RANGE);
     }
   }

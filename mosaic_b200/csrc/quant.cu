@@ -175,6 +175,57 @@ __global__ void __launch_bounds__(kPlaceWarps * 32)
   }
 }
 
+// Unit rows (one per token and owning rank, K slots): a warp per unit reads
+// each 16-byte code vector once and stores it to the packed row of every used
+// slot (row_of[u * K + j] >= 0), then the slots' scale words; lane j also
+// records slot j's return rank and position under its packed row, for the
+// down GEMM's epilogue.
+__global__ void __launch_bounds__(kPlaceWarps * 32)
+    rows_place_units_kernel(const uint8_t* __restrict__ rows, int row_bytes, int U, const int* __restrict__ U_dev,
+                            int H, int K, const int* __restrict__ row_of, const int* __restrict__ a_rank,
+                            const int* __restrict__ a_pos, int R_pad, const int* __restrict__ row_tile,
+                            const int* __restrict__ row_pos, uint8_t* __restrict__ xq, uint32_t* __restrict__ sft,
+                            int* __restrict__ row_rank, int* __restrict__ row_ret) {
+  griddep_wait();  // the layout's row maps are visible
+  griddep_launch();
+  const int n = U_dev ? min(*U_dev, U) : U;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = H / 128, nv = H / 16;
+  const size_t plane = static_cast<size_t>(R_pad) * 128;
+  for (int u = blockIdx.x * kPlaceWarps + warp; u < n; u += gridDim.x * kPlaceWarps) {
+    int my_r = -1;
+    if (lane < K) {
+      my_r = row_of[static_cast<size_t>(u) * K + lane];
+      if (my_r >= 0) {
+        row_rank[my_r] = a_rank[static_cast<size_t>(u) * K + lane];
+        row_ret[my_r] = a_pos[static_cast<size_t>(u) * K + lane];
+      }
+    }
+    int r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __shfl_sync(0xFFFFFFFFu, my_r, j);
+    const uint8_t* row = rows + static_cast<size_t>(u) * row_bytes;
+    const uint4* src = reinterpret_cast<const uint4*>(row);
+    for (int v = lane; v < nv; v += 32) {
+      const uint4 val = src[v];
+      const size_t off = (v >> 3) * plane + (v & 7) * 16;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < K && r[j] >= 0) *reinterpret_cast<uint4*>(xq + static_cast<size_t>(r[j]) * 128 + off) = val;
+    }
+    for (int kt = lane; kt < KT; kt += 32) {
+      const uint32_t word = static_cast<uint32_t>(row[H + kt]) * 0x01010101u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < K && r[j] >= 0) {
+          const int pos = row_pos[r[j]] & 0xFF;
+          sft[(static_cast<size_t>(row_tile[r[j]]) * KT + kt) * 128 + (pos & 31) * 4 + (pos >> 5)] = word;
+        }
+      }
+    }
+  }
+}
+
 // act_quant_ref: grid (M, ceil(K / 1024)), 128 threads.
 __global__ void __launch_bounds__(128) act_quant_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
                                                         uint8_t* __restrict__ q, float* __restrict__ scale) {
@@ -343,6 +394,21 @@ cudaError_t launch_rows_place_e4m3(const void* rows, int row_bytes, int R, const
   const cudaError_t e = launch_k(rows_place_e4m3_kernel, dim3(grid), dim3(kPlaceWarps * 32), 0, stream,
                                  static_cast<const uint8_t*>(rows), row_bytes, R, R_dev, H, row_of, R_pad, row_tile,
                                  row_pos, xq, sft);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rows_place_units(const void* rows, int row_bytes, int U, const int* U_dev, int H, int K,
+                                    const int* row_of, const int* a_rank, const int* a_pos, int R_pad,
+                                    const int* row_tile, const int* row_pos, uint8_t* xq, uint32_t* sft,
+                                    int* row_rank, int* row_ret, cudaStream_t stream) {
+  if (U <= 0) return cudaSuccess;
+  if (H % 128 || row_bytes % 16 || K < 1 || K > 8) return cudaErrorInvalidValue;
+  int grid = (U + kPlaceWarps - 1) / kPlaceWarps;
+  if (grid > 148 * 8) grid = 148 * 8;
+  const cudaError_t e = launch_k(rows_place_units_kernel, dim3(grid), dim3(kPlaceWarps * 32), 0, stream,
+                                 static_cast<const uint8_t*>(rows), row_bytes, U, U_dev, H, K, row_of, a_rank, a_pos,
+                                 R_pad, row_tile, row_pos, xq, sft, row_rank, row_ret);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

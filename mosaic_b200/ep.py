@@ -145,7 +145,9 @@ class PeerExchange:
     the flags, the count matrix, the receive rows and the return partials of
     the device-driven exchange (``mosaic_ep_exchange_rows`` /
     ``mosaic_ep_return_partials``).  With ``row_e4m3`` (FP8 layers) the rows
-    are E4M3 rows quantised by the sender (``mosaic_ep_dispatch_exchange``).
+    are E4M3 rows quantised by the sender (``mosaic_ep_dispatch_exchange``);
+    with ``unit_rows`` a token's row goes once to each rank that owns one of
+    its experts, listing those experts (E4M3 unit rows).
     Capacity: ``max_tokens`` tokens per rank;
     the receive side is sized for any routing.  ``wait_us`` bounds every
     device-side wait on another rank's flag; a wait that runs out records
@@ -153,7 +155,7 @@ class PeerExchange:
     """
 
     def __init__(self, *, group=None, max_tokens: int, top_k: int, n_experts: int, hidden: int,
-                 partial_f32: bool, wait_us: int = 0, row_e4m3: bool = False):
+                 partial_f32: bool, wait_us: int = 0, row_e4m3: bool = False, unit_rows: bool = False):
         lib = C.lib()
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -165,14 +167,17 @@ class PeerExchange:
         self.hidden = hidden
         pe = C.EpPeersC()
         pe.world, pe.rank = self.world, self.rank
-        pe.max_recv_rows = self.world * max_tokens * min(top_k, e_local)
+        # unit rows: one per (token, owning rank), each with min(top_k, e_local) slots
+        self.unit_slots = min(top_k, e_local) if unit_rows else 0
+        pe.max_recv_rows = self.world * max_tokens * (1 if unit_rows else min(top_k, e_local))
         pe.max_send_rows = max_tokens * top_k
         pe.max_tokens = max_tokens
         pe.hidden = hidden
         pe.partial_f32 = int(bool(partial_f32))
         pe.wait_us = int(wait_us)  # budget of each device-side wait on a peer (0: about 2 s)
-        pe.row_e4m3 = int(bool(row_e4m3))  # E4M3 exchange rows (FP8 layers), half the bytes of bf16 rows
-        self.row_e4m3 = bool(row_e4m3)
+        pe.row_e4m3 = int(bool(row_e4m3 or unit_rows))  # E4M3 exchange rows (FP8 layers): half the bytes of bf16
+        pe.unit_slots = self.unit_slots
+        self.row_e4m3 = bool(row_e4m3 or unit_rows)
         nbytes = lib.mosaic_ep_region_bytes(ctypes.byref(pe))
         if nbytes == 0:
             raise ValueError("invalid peer-exchange geometry")
@@ -275,9 +280,10 @@ class ExpertParallelMoELayer(nn.Module):
 
     def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None, exchange: str = "nccl",
                  max_tokens: int | None = None, peer_exchange: "PeerExchange | None" = None,
-                 layer_idx: int | None = None, health: "PeerHealth | None" = None):
+                 layer_idx: int | None = None, health: "PeerHealth | None" = None, unit_rows: bool = False):
         super().__init__()
         self.health = health
+        self.unit_rows = unit_rows  # p2p exchange of an FP8 layer: a row per (token, owning rank)
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.exchange = exchange
@@ -311,7 +317,8 @@ class ExpertParallelMoELayer(nn.Module):
                                     top_k=max(self.cfg.num_experts_per_tok, self._k()),
                                     n_experts=self.cfg.n_routed_experts,
                                     hidden=self.cfg.hidden_size, partial_f32=self.cfg.act_mode == "bf16",
-                                    row_e4m3=self.cfg.act_mode == "fp8")
+                                    row_e4m3=self.cfg.act_mode == "fp8",
+                                    unit_rows=self.unit_rows and self.cfg.act_mode == "fp8")
         return self._px
 
     def close(self) -> None:
@@ -320,7 +327,8 @@ class ExpertParallelMoELayer(nn.Module):
         self._px = None
 
     @classmethod
-    def from_layer(cls, layer, *, group=None, kernels=None, exchange: str = "nccl", max_tokens: int | None = None):
+    def from_layer(cls, layer, *, group=None, kernels=None, exchange: str = "nccl", max_tokens: int | None = None,
+                   unit_rows: bool = False):
         """EP layer of this rank from a full single-GPU ``MoELayer`` (same config,
         router weights and experts; the bank keeps its reference-layout copies)."""
         world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -330,7 +338,7 @@ class ExpertParallelMoELayer(nn.Module):
                            n_experts=layer.cfg.n_routed_experts, has_shared=b.has_shared)
         hr = getattr(layer, "hash_router", None)
         ep = cls(layer.cfg, local, group=group, kernels=kernels, exchange=exchange, max_tokens=max_tokens,
-                 layer_idx=None if hr is None else hr.layer_idx)
+                 layer_idx=None if hr is None else hr.layer_idx, unit_rows=unit_rows)
         if hr is not None:
             ep.hash_router.weight.data = hr.weight.data
             ep.hash_router.tid2eid = hr.tid2eid
@@ -421,8 +429,7 @@ class ExpertParallelMoELayer(nn.Module):
                     "mosaic_ep_exchange_rows")
         # expert pass on the received rows; the down epilogue stores every partial
         # straight into its source's return buffer
-        ws_rows = kern._ws_rows.get(lib.mosaic_moe_expert_rows_workspace_bytes(ctypes.byref(dl), px.max_recv_rows),
-                                    xf.device)
+        ws_rows = kern._ws_rows.get(lib.mosaic_ep_expert_rows_workspace_bytes(ctypes.byref(dl), pe), xf.device)
         b = self.bank.c_struct()
         C.check(lib.mosaic_ep_expert_rows_return(ctypes.byref(dl), pe, ctypes.byref(b), ops._ptr(ws_rows),
                                                  ws_rows.numel(), ops._stream()), "mosaic_ep_expert_rows_return")

@@ -20,17 +20,17 @@ def check_p2p(rank) -> bool:
     from mosaic_b200.ep import ExpertParallelMoELayer
 
     ok = True
-    for act_mode, t in (("bf16", 128), ("fp8", 256)):
+    for act_mode, t, units in (("bf16", 128, False), ("fp8", 256, False), ("fp8", 256, True)):
         layer, _ = synthetic.make_layer(tokens=1, seed=78, act_mode=act_mode, n_experts=64)
         x = synthetic.make_tokens(t, 7168, 2000 + rank)
-        ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=t)
+        ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=t, unit_rows=units)
         ref = layer(x)
         for _ in range(3):
             y = ep(x)
         torch.cuda.synchronize()
         if not torch.equal(y, ref):
             ok = False
-            print(f"rank {rank} p2p {act_mode}: eager mismatch", flush=True)
+            print(f"rank {rank} p2p {act_mode} units={units}: eager mismatch", flush=True)
         xs = x.clone()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
@@ -42,11 +42,11 @@ def check_p2p(rank) -> bool:
         torch.cuda.synchronize()
         if not torch.equal(ys, layer(x2)):
             ok = False
-            print(f"rank {rank} p2p {act_mode}: graph mismatch", flush=True)
+            print(f"rank {rank} p2p {act_mode} units={units}: graph mismatch", flush=True)
         err = ep.peer_exchange().error()
         if err:
             ok = False
-            print(f"rank {rank} p2p {act_mode}: device error {err}", flush=True)
+            print(f"rank {rank} p2p {act_mode} units={units}: device error {err}", flush=True)
         del g
         ep.close()
         del layer, ep

@@ -202,7 +202,8 @@ def test_rms_norm_validation_before_launch():
 def test_ep_row_sizes_match_header_and_region_geometry():
     """MOSAIC_EP_ROW_BYTES(_E4M3) as the header defines them; an E4M3 region
     holds max_recv_rows E4M3 rows; E4M3 rows with fp32 partials (a bf16
-    layer), a non-zero reserved field or H > 16384 are refused (0 bytes)."""
+    layer), unit slots outside 0..8 or without E4M3 rows, or H > 16384 are
+    refused (0 bytes); unit rows add 16 bytes per slot to an E4M3 row."""
     text = HEADER.read_text()
     assert "#define MOSAIC_EP_ROW_BYTES_E4M3(H) ((size_t)(H) + ((((size_t)(H) / 128u) + 15u) & ~(size_t)15u) + 16u)" \
         in text
@@ -221,7 +222,9 @@ def test_ep_row_sizes_match_header_and_region_geometry():
     bf16_rows, e4m3_rows = region(), region(row_e4m3=1)
     assert bf16_rows - e4m3_rows == 128 * (C.ep_row_bytes(7168) - C.ep_row_bytes_e4m3(7168))
     assert region(row_e4m3=1, partial_f32=1) == 0
-    assert region(row_e4m3=2) == 0 and region(reserved=1) == 0
+    assert region(row_e4m3=2) == 0 and region(unit_slots=9) == 0 and region(unit_slots=2) == 0
+    assert C.ep_row_bytes_e4m3_units(7168, 8) == 7248 + 128
+    assert region(row_e4m3=1, unit_slots=8) - e4m3_rows == 128 * 128
     assert region(row_e4m3=1, hidden=16384 + 256) == 0 and region(hidden=16384 + 256) > 0
 
 

@@ -242,14 +242,16 @@ def test_ep_two_gpus_rank_departure_seen_before_the_next_step():
     assert "rank 0 PEER_FAILURE_SEEN" in out, out[-3000:]
 
 
-@pytest.mark.parametrize("act_mode", ["bf16", "fp8"])
-def test_ep_p2p_world1_bit_identical_and_graph_capturable(act_mode):
+@pytest.mark.parametrize("act_mode,unit_rows", [("bf16", False), ("fp8", False), ("fp8", True)])
+def test_ep_p2p_world1_bit_identical_and_graph_capturable(act_mode, unit_rows):
     """The device-driven exchange path (own region only at world 1): eager
-    steps and CUDA-graph replays equal MoELayer bit for bit, no device error."""
+    steps and CUDA-graph replays equal MoELayer bit for bit, no device error.
+    With unit rows every token goes once to the one rank with all k of its
+    experts in its slots."""
     from mosaic_b200.ep import ExpertParallelMoELayer
 
     layer, x = _small_layer(act_mode, seed=13, t=64)
-    ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=64)
+    ep = ExpertParallelMoELayer.from_layer(layer, exchange="p2p", max_tokens=64, unit_rows=unit_rows)
     try:
         y_ref = layer(x)
         for _ in range(3):  # several steps: epochs advance, buffers are reused
