@@ -280,10 +280,11 @@ class ExpertParallelMoELayer(nn.Module):
 
     def __init__(self, cfg: MoEConfig, local_bank, *, group=None, kernels=None, exchange: str = "nccl",
                  max_tokens: int | None = None, peer_exchange: "PeerExchange | None" = None,
-                 layer_idx: int | None = None, health: "PeerHealth | None" = None, unit_rows: bool = False):
+                 layer_idx: int | None = None, health: "PeerHealth | None" = None, unit_rows: bool = True):
         super().__init__()
         self.health = health
-        self.unit_rows = unit_rows  # p2p exchange of an FP8 layer: a row per (token, owning rank)
+        # p2p exchange of an FP8 layer: a row per (token, owning rank) instead of one per assignment
+        self.unit_rows = unit_rows
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.exchange = exchange
@@ -328,7 +329,7 @@ class ExpertParallelMoELayer(nn.Module):
 
     @classmethod
     def from_layer(cls, layer, *, group=None, kernels=None, exchange: str = "nccl", max_tokens: int | None = None,
-                   unit_rows: bool = False):
+                   unit_rows: bool = True):
         """EP layer of this rank from a full single-GPU ``MoELayer`` (same config,
         router weights and experts; the bank keeps its reference-layout copies)."""
         world = dist.get_world_size(group) if dist.is_initialized() else 1
