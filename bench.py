@@ -79,16 +79,16 @@ def layer_launches(t: int, world: int) -> int:
     tensor-core logits + top-k, plus the W split above 128 tokens.
     Layout: one CTA up to 1024 assignments, else count / scan / rank / finish.
     One GPU: router, layout, rows_quant, gate/up, down, combine.  Expert
-    parallel (FP8, E4M3 rows): router, dispatch + exchange (layout, destination
-    counts, token quantise, count exchange, send, wait), the shared expert
-    (per-row metadata, layout, rows_quant, gate/up, down) and the received
-    rows (per-row metadata, layout, placement, gate/up, down), return (signal,
-    wait), combine."""
+    parallel (FP8, E4M3 unit rows): router, dispatch + exchange (layout, units
+    per owner, destination counts, token quantise, count exchange, send, wait),
+    the shared expert (per-row metadata, layout, rows_quant, gate/up, down) and
+    the received units (slot metadata, layout, placement, gate/up, down),
+    return (signal, wait), combine."""
     router = 1 if t <= 8 else (3 if t > 128 else 2)
     lay = lambda a: 4 if a > 1024 else 1  # noqa: E731
     if world == 1:
         return router + lay(t * 8) + 4
-    return router + (lay(t * 8) + 5) + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
+    return router + (lay(t * 8) + 6) + (lay(t) + 4) + (lay(t * 8) + 4) + 2 + 1
 
 
 def parse():
