@@ -855,6 +855,13 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
+        # each rank on its GPU's NUMA node, so its pinned e2e buffers are local
+        # (one GPU keeps every core: the CPU baseline runs there)
+        from mosaic_b200.pipeline import gpu_numa_cpus
+
+        cpus = gpu_numa_cpus(local)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, tf_peak, peak_src = peaks()
     if args.hc_only:

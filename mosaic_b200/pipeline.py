@@ -18,7 +18,36 @@ The layer is anything callable on a bf16 device tensor [T, H] that returns
 """
 from __future__ import annotations
 
+import os
+
 import torch
+
+
+def gpu_numa_cpus(device_index: int) -> set | None:
+    """The CPUs of the NUMA node the GPU's PCI device hangs off (Linux sysfs),
+    or None when that is unknown.  A process that binds to them
+    (``os.sched_setaffinity``) before pinning host memory gets its pinned
+    buffers on the GPU's node, so several GPUs' uploads and downloads do not
+    cross the socket interconnect."""
+    try:
+        p = torch.cuda.get_device_properties(device_index)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            if "-" in part:
+                a, b = part.split("-")
+                cpus.update(range(int(a), int(b) + 1))
+            elif part:
+                cpus.add(int(part))
+        return cpus & os.sched_getaffinity(0) or None
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return None
 
 
 class HostPipeline:
