@@ -662,6 +662,41 @@ def hc_bench(hbm, steps=20, warmup=3):
     return res
 
 
+def hc_post_bench(hbm, steps=20, warmup=3):
+    """The hyper-connection post-mix behind the MoE at the V3 hidden size,
+    hc = 4: out[t, m] = post[t, m] * y[t] + sum_n comb[t, m, n] * x[t, n].
+    Bytes: read y and the hc residual copies, write hc new copies."""
+    from mosaic_b200.hc import HyperConnections
+
+    d, hcm = 7168, 4
+    hc = HyperConnections(d, hc_mult=hcm).cuda()
+    res = {}
+    for t in (128, 8192):
+        g = torch.Generator(device="cuda").manual_seed(t + 1)
+        x = torch.randn(t, hcm, d, generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.randn(t, d, generator=g, device="cuda").to(torch.bfloat16)
+        post = torch.rand(t, hcm, generator=g, device="cuda") * 2
+        comb = torch.rand(t, hcm, hcm, generator=g, device="cuda")
+        comb = comb / comb.sum(-1, keepdim=True)
+        for _ in range(warmup):
+            hc.post(y, x, post, comb)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            hc.post(y, x, post, comb)
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        del graph
+        nbytes = t * (d * 2 + 2 * hcm * d * 2 + hcm * 4 + hcm * hcm * 4)
+        res[f"T{t}"] = {"ms": ms, "GBs": nbytes / (ms * 1e-3) / 1e9, "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm}
+    return res
+
 def router_bench(tokens, steps=20, warmup=3):
     """mosaic_router alone at the V3 router dims: logits on the tensor cores
     (split-K; the W split in-kernel up to T = 128) and the group-limited top 8.
@@ -865,7 +900,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300))
     hbm, tf_peak, peak_src = peaks()
     if args.hc_only:
-        emit({"hc_pre_norm": hc_bench(hbm)})
+        emit({"hc_pre_norm": hc_bench(hbm), "hc_post": hc_post_bench(hbm)})
         return
     if args.router_only:
         tokens = [args.tokens] if args.tokens else [1, 128, 2048, 8192]
@@ -906,6 +941,7 @@ def main():
             extra("offload", lambda: offload_bench(holder["layer"]))
         extra("prefill", lambda: prefill_extra(bank, tf_peak, peak_src))
         extra("hc_pre_norm", lambda: hc_bench(hbm))
+        extra("hc_post", lambda: hc_post_bench(hbm))
     emit(out)
 
 

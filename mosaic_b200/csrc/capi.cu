@@ -793,6 +793,7 @@ int mosaic_hc_pre_norm(const void* x, const float* fn, const float* base, const 
   p.q = q;
   p.q_scale = q_scale;
   p.pre = reinterpret_cast<float*>(ws + w.pre);
+  p.err = reinterpret_cast<int*>(ws);
   cudaError_t e = launch_hc_pre_norm(p, sms, s);
   return e == cudaSuccess ? MOSAIC_OK : MOSAIC_ERR_CUDA;
 }

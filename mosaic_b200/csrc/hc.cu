@@ -13,10 +13,12 @@
 // bf16, fn [(2+hc)*hc, hc*D]) and of the tokens' sums of squares on the tensor
 // cores.  hc_sinkhorn_kernel (one warp per token) adds the partials in a fixed
 // order (deterministic) and runs the Sinkhorn normalisation of the 4x4
-// combination; hc_premix_norm_kernel (one token per CTA at a time) forms the
-// pre-mix y = sum_m pre_m x_m (bf16) in registers, then applies the RMSNorm
-// (skipped without a norm weight) and writes the MoE input (and its E4M3
-// act_quant).
+// combination; hc_premix_ring_kernel (D <= 8192: token rows streamed into a
+// shared-memory ring by bulk copies, two 256-thread groups each on one token
+// at a time) or hc_premix_norm_kernel (larger D: one token per CTA, loaded
+// into registers) forms the pre-mix y = sum_m pre_m x_m (bf16), then applies
+// the RMSNorm (skipped without a norm weight) and writes the MoE input (and
+// its E4M3 act_quant).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -92,108 +94,272 @@ __global__ void __launch_bounds__(kSkWarps * 32) hc_sinkhorn_kernel(HcParams p) 
   if (on) p.comb[(static_cast<size_t>(t) * hc + ci) * hc + cj] = c;
 }
 
-// ---- pre-mix + RMSNorm (+ act_quant): one token per CTA at a time
-// (grid-stride).  Each thread loads its PER 8-value chunks of all hc residual
-// rows up front (16-byte loads, all in flight together), forms y = sum_m
-// pre_m x_m (products rounded, summed in m order, bf16) in registers, and the
-// block adds the squares of y in a fixed order for the RMSNorm.
-template <int PER>
-__global__ void __launch_bounds__(kHcThreads, PER <= 4 ? 2 : 1) hc_premix_norm_kernel(HcParams p) {
-  __shared__ float red[kHcWarps];
-  __shared__ float rs_s;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hc = p.hc, D = p.D, KD = hc * D;
-  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
+// Packed fp32 pairs (f32x2, sm_100): one instruction for both lanes, each
+// lane rounded to nearest like the scalar mul.rn / add.rn / fma.rn.
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 ffma2_rn(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// 16-byte load from shared memory (ld.shared: the short-latency path, not a
+// generic load that resolves to shared memory at run time)
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p))
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// named barrier that also ORs a predicate over its threads
+__device__ __forceinline__ bool named_bar_any(int id, int threads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ float4 pre_of(const HcParams& p, int t) {
+  return *reinterpret_cast<const float4*>(p.pre + static_cast<size_t>(t) * 4);
+}
+
+// ---- pre-mix + RMSNorm (+ act_quant) of token t by the whole CTA.  Each
+// thread takes its PER 8-value chunks of all hc residual rows of the token at
+// xt (global or shared memory; 16-byte loads, all issued together), forms
+// y = sum_m pre_m x_m (products rounded, summed in m order, bf16) in
+// registers, and the block adds the squares of y in a fixed order for the
+// RMSNorm.  The THREADS threads (tid 0 .. THREADS - 1) meet once, on named
+// barrier bar, after writing their warps' sums of squares to red; every thread
+// then adds the THREADS / 32 sums itself.  So that no thread overwrites a sum
+// another still reads, callers alternate between two red buffers from one
+// token to the next.  pre4: the token's pre-mix weights (p.pre[t]).
+// released() runs on every thread after the barrier, when all of them have
+// read xt.
+template <int THREADS, int PER, bool SMEM, class Hook>
+__device__ __forceinline__ void premix_token(const HcParams& p, int t, const __nv_bfloat16* __restrict__ xt,
+                                             const float4 pre4, float* red, int tid, int bar, Hook released) {
+  constexpr int kChunk = THREADS * 8;  // x_flat columns per step: 8 per thread
+  constexpr int kWarps = THREADS / 32;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int hc = p.hc, D = p.D;
   __nv_bfloat16* yout = static_cast<__nv_bfloat16*>(p.y);
-  for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
-    const __nv_bfloat16* xt = x + static_cast<size_t>(t) * KD;
-    uint4 raw[PER][4];
+  uint4 raw[PER][4];
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int d = k * kHcChunk + tid * 8;
+  for (int k = 0; k < PER; ++k) {
+    const int d = k * kChunk + tid * 8;
 #pragma unroll
-      for (int m = 0; m < 4; ++m)
-        if (d < D && m < hc) raw[k][m] = *reinterpret_cast<const uint4*>(xt + static_cast<size_t>(m) * D + d);
-    }
-    const float4 pre4 = *reinterpret_cast<const float4*>(p.pre + static_cast<size_t>(t) * 4);
-    const float pm[4] = {pre4.x, pre4.y, pre4.z, pre4.w};
-    float yv[PER][8];
-    float ss2 = 0.f;
+    for (int m = 0; m < 4; ++m)
+      if (d < D && m < hc) {
+        if (SMEM)
+          raw[k][m] = lds128(xt + static_cast<size_t>(m) * D + d);
+        else
+          raw[k][m] = *reinterpret_cast<const uint4*>(xt + static_cast<size_t>(m) * D + d);
+      }
+  }
+  // the arithmetic on pairs of values (packed f32x2 instructions, each lane
+  // rounded as the scalar operation would be)
+  const float2 pm[4] = {make_float2(pre4.x, pre4.x), make_float2(pre4.y, pre4.y), make_float2(pre4.z, pre4.z),
+                        make_float2(pre4.w, pre4.w)};
+  float2 yv[PER][4];
+  float2 ss = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int d = k * kHcChunk + tid * 8;
-      if (d < D) {
-        float y[8];
+  for (int k = 0; k < PER; ++k) {
+    const int d = k * kChunk + tid * 8;
+    if (d < D) {
+      float2 y[4];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          if (m >= hc) break;
-          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[k][m]);
+      for (int m = 0; m < 4; ++m) {
+        if (m >= hc) break;
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[k][m]);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __bfloat1622float2(h2[i]);
-            if (m == 0) {
-              y[2 * i] = __fmul_rn(pm[0], f.x);
-              y[2 * i + 1] = __fmul_rn(pm[0], f.y);
-            } else {
-              y[2 * i] = __fadd_rn(y[2 * i], __fmul_rn(pm[m], f.x));
-              y[2 * i + 1] = __fadd_rn(y[2 * i + 1], __fmul_rn(pm[m], f.y));
-            }
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          yv[k][i] = __bfloat162float(__float2bfloat16_rn(y[i]));
-          ss2 = fmaf(yv[k][i], yv[k][i], ss2);
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h2[i]);
+          y[i] = m == 0 ? fmul2_rn(pm[0], f) : fadd2_rn(y[i], fmul2_rn(pm[m], f));
         }
       }
-    }
-    ss2 = warp_sum(ss2);
-    if (lane == 0) red[warp] = ss2;
-    __syncthreads();
-    if (tid == 0) {
-      float s = 0.f;
-      for (int w = 0; w < kHcWarps; ++w) s += red[w];
-      rs_s = 1.0f / sqrtf(s / static_cast<float>(D) + p.norm_eps);
-    }
-    __syncthreads();
-    // ---- RMSNorm (y * rsqrt, then * weight), bf16, optional act_quant.  Every
-    // lane runs the same iterations: quant_block128 shuffles across 16 lanes.
-    const float r = rs_s;
-    const int steps = (D + kHcChunk - 1) / kHcChunk;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      if (k >= steps) break;
-      const int d = k * kHcChunk + tid * 8;
-      const bool valid = d < D;
-      float v[8];
+      for (int i = 0; i < 4; ++i) {
+        yv[k][i] = __bfloat1622float2(__floats2bfloat162_rn(y[i].x, y[i].y));
+        ss = ffma2_rn(yv[k][i], yv[k][i], ss);
+      }
+    }
+  }
+  float ss2 = warp_sum(ss.x + ss.y);
+  if (lane == 0) red[warp] = ss2;
+  // a shared-memory row's next fill is an async-proxy write: order this
+  // thread's generic reads of the row before it
+  if (SMEM) fence_proxy_async_smem();
+  named_bar(bar, THREADS);
+  released();
+  float sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) sum += red[w];
+  const float rs = 1.0f / sqrtf(sum / static_cast<float>(D) + p.norm_eps);
+  // ---- RMSNorm (y * rsqrt, then * weight), bf16, optional act_quant.  Every
+  // lane runs the same iterations: quant_block128 shuffles across 16 lanes.
+  const float r = rs;
+  const int steps = (D + kChunk - 1) / kChunk;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    if (k >= steps) break;
+    const int d = k * kChunk + tid * 8;
+    const bool valid = d < D;
+    float v[8];
+    if (valid) {
+      __align__(16) __nv_bfloat162 ob[4];
+      if (p.norm_w) {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d + 4));
+        const float2 w[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                             make_float2(w1.z, w1.w)};
+        const float2 r2 = make_float2(r, r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 o = fmul2_rn(fmul2_rn(yv[k][i], r2), w[i]);
+          ob[i] = __floats2bfloat162_rn(o.x, o.y);
+        }
+      } else {  // the pre-mix alone (HyperConnections.pre)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ob[i] = __floats2bfloat162_rn(yv[k][i].x, yv[k][i].y);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 o = __bfloat1622float2(ob[i]);
+        v[2 * i] = o.x;
+        v[2 * i + 1] = o.y;
+      }
+      *reinterpret_cast<uint4*>(yout + static_cast<size_t>(t) * D + d) = *reinterpret_cast<const uint4*>(ob);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    if (p.q) {
+      uint8_t b[8];
+      const int e = quant_block128(v, b);
       if (valid) {
-        __align__(16) __nv_bfloat16 ob[8];
-        if (p.norm_w) {
-          const float4 w0 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d));
-          const float4 w1 = __ldg(reinterpret_cast<const float4*>(p.norm_w + d + 4));
-          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(yv[k][i], r), w[i]));
-        } else {  // the pre-mix alone (HyperConnections.pre)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) ob[i] = __float2bfloat16_rn(yv[k][i]);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(ob[i]);
-        *reinterpret_cast<uint4*>(yout + static_cast<size_t>(t) * D + d) = *reinterpret_cast<const uint4*>(ob);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-      }
-      if (p.q) {
-        uint8_t b[8];
-        const int e = quant_block128(v, b);
-        if (valid) {
-          *reinterpret_cast<uint2*>(p.q + static_cast<size_t>(t) * D + d) = pack8(b);
-          if ((lane & 15) == 0) p.q_scale[static_cast<size_t>(t) * (D / 128) + d / 128] = exp2i(e);
-        }
+        *reinterpret_cast<uint2*>(p.q + static_cast<size_t>(t) * D + d) = pack8(b);
+        if ((lane & 15) == 0) p.q_scale[static_cast<size_t>(t) * (D / 128) + d / 128] = exp2i(e);
       }
     }
+  }
+}
+
+// Register variant, for D above the ring's 8192: one token per CTA at a time
+// (grid-stride), the row loaded straight into registers.
+template <int PER>
+__global__ void __launch_bounds__(kHcThreads, 1) hc_premix_norm_kernel(HcParams p) {
+  __shared__ float red[2][kHcWarps];
+  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
+  const size_t KD = static_cast<size_t>(p.hc) * p.D;
+  int j = 0;
+  for (int t = blockIdx.x; t < p.T; t += gridDim.x, ++j)
+    premix_token<kHcThreads, PER, false>(p, t, x + static_cast<size_t>(t) * KD, pre_of(p, t), red[j & 1],
+                                         static_cast<int>(threadIdx.x), 0, [] {});
+}
+
+// Ring variant, for token rows (hc x D bf16) that fit kHcRing times in shared
+// memory: one CTA per SM, two groups of 256 threads, group g taking the CTA's
+// tokens g, g + 2, ... (grid-stride over T).  Token i's row arrives in slot
+// i % kHcRing by a bulk copy (cp.async.bulk, one per row); once the group that
+// consumes token i has read it (the group's one barrier per token) it refills
+// the slot with token i + kHcRing, so rows stay in flight while both groups do
+// their arithmetic.  Token i completes a phase
+// of barrier full[i % (2 * kHcRing)]: each barrier's phases belong to one group
+// and are consumed in order, so a parity wait cannot match a stale phase.
+// Waits are bounded: a group that gives up records MOSAIC_ERR_TIMEOUT and
+// stops; at exit the CTA waits (bounded) for every copy still in flight.
+constexpr int kHcRing = 3;
+constexpr int kHcBars = 2 * kHcRing;
+constexpr int kHcGroupThreads = 256;
+constexpr int kHcRingThreads = 2 * kHcGroupThreads;
+constexpr int kHcRingChunk = kHcGroupThreads * 8;
+constexpr int kHcRingSmem = 225 * 1024;
+static_assert(kHcRing * 4 * 4 * kHcRingChunk * 2 <= kHcRingSmem, "three rows of hc 4 x D 8192 bf16");
+
+template <int PER>
+__global__ void __launch_bounds__(kHcRingThreads, 1) hc_premix_ring_kernel(HcParams p) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[kHcBars];
+  __shared__ int filled[kHcBars], consumed[kHcBars];
+  __shared__ float red[2][2][kHcGroupThreads / 32];  // [group][token parity][warp]
+  __shared__ int failed;
+  const int g = static_cast<int>(threadIdx.x) / kHcGroupThreads, gt = static_cast<int>(threadIdx.x) % kHcGroupThreads;
+  const int bar = 1 + g;  // named barrier of the group (0 is __syncthreads)
+  const size_t KD = static_cast<size_t>(p.hc) * p.D;
+  const uint32_t row_bytes = static_cast<uint32_t>(KD * 2);
+  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
+  const int n = static_cast<int>(blockIdx.x) < p.T ? (p.T - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+  auto token = [&](int i) { return static_cast<int>(blockIdx.x + static_cast<size_t>(i) * gridDim.x); };
+  auto fill = [&](int i) {  // token i of this CTA into slot i % kHcRing (one thread)
+    const int b = i % kHcBars;
+    ++filled[b];
+    mbar_arrive_expect_tx(&full[b], row_bytes);
+    bulk_load(ring + static_cast<size_t>(i % kHcRing) * row_bytes, x + static_cast<size_t>(token(i)) * KD, row_bytes,
+              &full[b]);
+  };
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < kHcBars; ++b) {
+      mbar_init(&full[b], 1);
+      filled[b] = consumed[b] = 0;
+    }
+    failed = 0;
+    fence_mbar_init();
+    for (int i = 0; i < kHcRing && i < n; ++i) fill(i);
+  }
+  __syncthreads();
+  volatile int never = 0;
+  // the pre-mix weights (an L2 read) one token ahead, off the token's critical path
+  float4 pre_next = g < n ? pre_of(p, token(g)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = g; i < n; i += 2) {
+    const int b = i % kHcBars;
+    const float4 pre4 = pre_next;
+    if (i + 2 < n) pre_next = pre_of(p, token(i + 2));
+    const bool ok = mbar_wait(&full[b], static_cast<uint32_t>(i / kHcBars) & 1u, &never);
+    if (named_bar_any(bar, kHcGroupThreads, !ok)) {  // the same decision on the group's threads
+      if (gt == 0) {
+        set_error(p.err, MOSAIC_ERR_TIMEOUT);
+        failed = 1;
+      }
+      break;
+    }
+    premix_token<kHcGroupThreads, PER, true>(
+        p, token(i), reinterpret_cast<const __nv_bfloat16*>(ring + static_cast<size_t>(i % kHcRing) * row_bytes), pre4,
+        red[g][(i >> 1) & 1], gt, bar, [&] {
+          if (gt == 0) {
+            ++consumed[b];
+            if (i + kHcRing < n) fill(i + kHcRing);
+          }
+        });
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && failed) {  // no copy may land in the CTA's shared memory after it exits
+    for (int b = 0; b < kHcBars; ++b)
+      if (filled[b] > consumed[b]) mbar_wait(&full[b], static_cast<uint32_t>(filled[b] - 1) & 1u, &never);
   }
 }
 
@@ -323,15 +489,23 @@ size_t hc_partials_bytes(int T, int splits) { return sizeof(float) * static_cast
 cudaError_t launch_hc_pre_norm(const HcParams& p, int num_sms, cudaStream_t stream) {
   if (p.D > hc_max_d() || p.D % 8 || p.hc < 1 || p.hc > 4) return cudaErrorInvalidValue;
   hc_sinkhorn_kernel<<<(p.T + kSkWarps - 1) / kSkWarps, kSkWarps * 32, 0, stream>>>(p);
-  // two CTAs of 256 threads per SM (the registers of the rows in flight; one above D = 8192)
-  const int per_sm = p.D <= 4 * kHcChunk ? 2 : 1;
-  const int grid = p.T < per_sm * num_sms ? p.T : per_sm * num_sms;
-  if (p.D <= 2 * kHcChunk)
-    hc_premix_norm_kernel<2><<<grid, kHcThreads, 0, stream>>>(p);
-  else if (p.D <= 4 * kHcChunk)
-    hc_premix_norm_kernel<4><<<grid, kHcThreads, 0, stream>>>(p);
-  else
-    hc_premix_norm_kernel<8><<<grid, kHcThreads, 0, stream>>>(p);
+  if (p.D <= 4 * kHcRingChunk) {  // D <= 8192: the ring (three rows of up to 4 x 8192 bf16 fit)
+    const size_t ring_bytes = static_cast<size_t>(kHcRing) * p.hc * p.D * 2;
+    const int grid = p.T < num_sms ? p.T : num_sms;
+    const bool two = p.D <= 2 * kHcRingChunk;
+    const void* fn = two ? reinterpret_cast<const void*>(hc_premix_ring_kernel<2>)
+                         : reinterpret_cast<const void*>(hc_premix_ring_kernel<4>);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ring_bytes));
+    if (e != cudaSuccess) return e;
+    if (two)
+      hc_premix_ring_kernel<2><<<grid, kHcRingThreads, ring_bytes, stream>>>(p);
+    else
+      hc_premix_ring_kernel<4><<<grid, kHcRingThreads, ring_bytes, stream>>>(p);
+    return cudaGetLastError();
+  }
+  // D in (8192, 16384]: the register kernel, one CTA of 256 threads per SM
+  const int grid = p.T < num_sms ? p.T : num_sms;
+  hc_premix_norm_kernel<8><<<grid, kHcThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

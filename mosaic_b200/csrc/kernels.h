@@ -141,6 +141,7 @@ struct HcParams {
   float* partial;        // workspace: [splits][T][25] mixing partials (+ sum of squares)
   int splits;
   float* pre;            // workspace: [T][4] pre-mix weights (Sinkhorn kernel -> pre-mix kernel)
+  int* err;              // device error word (bounded waits of the pre-mix ring)
 };
 size_t hc_partials_bytes(int T, int splits);
 int hc_max_d();  // largest D of the pre-mix kernel (the pre-mix is held in registers)

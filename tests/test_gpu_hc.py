@@ -97,6 +97,31 @@ def test_hc_pre_norm_v3_dims(t):
     _bf16_close(yn.float().cpu(), ref.float(), "y_norm")
 
 
+
+@pytest.mark.parametrize("t,hcm,d", [(130, 4, 12288), (150, 2, 16384), (151, 3, 8192), (2000, 1, 1024)])
+def test_hc_pre_norm_kernel_variants(t, hcm, d):
+    """Both pre-mix kernels: D <= 8192 takes the bulk-copy ring (hc 3 x D 8192
+    with four chunks per thread, and 2000 tokens of hc 1 x D 1024 that wrap
+    every CTA's ring of barriers many times, both groups of each CTA busy);
+    D 12288 and 16384 take the register kernel."""
+    from mosaic_b200.hc import ffn_pre_norm
+
+    x, fn, base, scale, norm_w, _ = make_hc_case(1, t, hcm, d, seed=70 + hcm)
+    hc, norm = _modules(hcm, d, 20, fn, base, scale, norm_w)
+    yn, post, comb, q, qs = ffn_pre_norm(x.cuda(), hc, norm, quant=True)
+    torch.cuda.synchronize()
+    from mosaic_b200 import ops
+
+    assert ops.read_error(hc.last_workspace) == 0
+    y_pre, post_r, comb_r = hc_pre(x, fn, base, scale, iters=20, eps=1e-6, norm_eps=1e-6)
+    ref = rms_norm(y_pre, norm_w, 1e-6)
+    np.testing.assert_allclose(post.cpu().numpy(), post_r.numpy(), rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(comb.cpu().numpy(), comb_r.numpy(), rtol=1e-4, atol=1e-6)
+    _bf16_close(yn.float().cpu(), ref.float(), "y_norm")
+    q_ref, s_ref = act_quant_ref(yn.float().cpu().numpy().reshape(-1, d))
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy().reshape(-1, d), q_ref)
+    assert np.array_equal(qs.cpu().numpy().reshape(-1, d // 128), s_ref)
+
 def test_hc_pre_norm_feeds_the_moe_layer():
     """The fused output drives a MoE layer exactly like the same bf16 tensor built on the host."""
     from mosaic_b200 import synthetic
