@@ -29,6 +29,8 @@
  *                               an invertible re-layout of the expert bank, scales only here)
  *   mosaic_moe_routed        <- mosaicvm/kernels/exact_moe.py:12-19 (exact_moe) /
  *                               mosaicvm/kernels/qpa_mma.py:681-784 (fused_moe_qpa)
+ *   mosaic_expert_gemm_gu /  <- mosaicvm/kernels/qpa_mma.py:750-772 (fused_moe_qpa's gate/up and
+ *   mosaic_expert_gemm_down     down calls of _run_two_queues, :787-830)
  *   mosaic_moe_forward       <- mosaicvm/model/layers.py:284-303 (MoELayer.forward)
  *   mosaic_moe_forward_ext   <- the same with mosaic_router_ext's routing, which with hash
  *                               routing is layers.py:394-405 (HashMoELayer.forward)
@@ -327,6 +329,28 @@ MOSAIC_API int mosaic_moe_routed_slots(const mosaic_moe_dims* dims, const void* 
                                        const float* expert_weights, const mosaic_expert_bank* bank,
                                        const int32_t* expert_slot, int32_t bank_slots, void* y, void* workspace,
                                        size_t workspace_bytes, mosaic_stream_t stream);
+
+/* mosaic_moe_routed in two calls, gate/up then down, in the order the
+ * reference runs its grouped kernels (_run_two_queues("gu") then
+ * _run_two_queues("down"), mosaicvm/kernels/qpa_mma.py:787-830, inside
+ * fused_moe_qpa, qpa_mma.py:681-784).  Same dims, bank and arguments as
+ * mosaic_moe_routed; workspace: mosaic_moe_workspace_bytes(dims), shared by
+ * the two calls.
+ * mosaic_expert_gemm_gu: layout of expert_ids / expert_weights (NULL = 1.0),
+ * gather and quantisation of the token rows, then the gate/up GEMM with the
+ * clamp, SwiGLU, route weight and act_quant_ref re-quantisation of z fused in
+ * its epilogue.  z, the tile list and the row maps stay in the workspace.
+ * mosaic_expert_gemm_down: the down GEMM over those z rows, then the ordered
+ * combine (ascending expert id in fp32, the shared expert last) into y bf16
+ * [T, H].  It must follow a mosaic_expert_gemm_gu call on the same stream
+ * with the same dims, bank and workspace, with no other call using that
+ * workspace in between.  The two calls give the bytes mosaic_moe_routed
+ * gives; the workspace error word keeps what the gate/up call recorded. */
+MOSAIC_API int mosaic_expert_gemm_gu(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,
+                                     const float* expert_weights, const mosaic_expert_bank* bank, void* workspace,
+                                     size_t workspace_bytes, mosaic_stream_t stream);
+MOSAIC_API int mosaic_expert_gemm_down(const mosaic_moe_dims* dims, const mosaic_expert_bank* bank, void* y,
+                                       void* workspace, size_t workspace_bytes, mosaic_stream_t stream);
 
 /* ---- Expert parallelism -------------------------------------------------
  * Rank d of `world` owns the contiguous experts [d*E/world, (d+1)*E/world)

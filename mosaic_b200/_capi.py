@@ -77,6 +77,8 @@ EXPORTED = (
     "mosaic_moe_forward_ext",
     "mosaic_moe_routed",
     "mosaic_moe_routed_slots",
+    "mosaic_expert_gemm_gu",
+    "mosaic_expert_gemm_down",
     "mosaic_ep_dispatch",
     "mosaic_moe_expert_rows_workspace_bytes",
     "mosaic_moe_expert_rows",
@@ -193,6 +195,10 @@ _SIGS = {
                           ctypes.c_int),
     "mosaic_moe_routed_slots": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _I, _P, _P, _SZ,
                                  _P], ctypes.c_int),
+    "mosaic_expert_gemm_gu": ([ctypes.POINTER(MoEDims), _P, _P, _P, ctypes.POINTER(ExpertBankC), _P, _SZ, _P],
+                              ctypes.c_int),
+    "mosaic_expert_gemm_down": ([ctypes.POINTER(MoEDims), ctypes.POINTER(ExpertBankC), _P, _P, _SZ, _P],
+                                ctypes.c_int),
     "mosaic_ep_dispatch": ([ctypes.POINTER(MoEDims), _I, _P, _P, _P, _P, _P, _P, _SZ, _P], ctypes.c_int),
     "mosaic_moe_expert_rows_workspace_bytes": ([ctypes.POINTER(MoEDims), _I], _SZ),
     "mosaic_moe_expert_rows": ([ctypes.POINTER(MoEDims), _I, _P, _I, _P, _P, _I, _I, ctypes.POINTER(ExpertBankC), _P,

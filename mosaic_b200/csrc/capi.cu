@@ -261,6 +261,12 @@ int check_bank(const mosaic_expert_bank* b) {
 // (idx, weights) already on the device.
 // ev (optional) = 7 events: before router, after router, layout, quantise,
 // gate/up, down, combine; slots 0-1 are recorded by the caller of run_experts.
+// Launch groups of the expert pass: layout + quantise + gate/up, and down +
+// combine.  The fused entry points run both; mosaic_expert_gemm_gu and
+// mosaic_expert_gemm_down run one each over a shared workspace.
+constexpr int kStageGateUp = 1;
+constexpr int kStageDown = 2;
+
 inline bool rec(void* const* ev, int i, cudaStream_t s) {
   return !ev || !ev[i] || cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s) == cudaSuccess;
 }
@@ -286,12 +292,14 @@ void fill_layout(LayoutParams& lp, const WsPlan& w, uint8_t* ws) {
 
 // Gate/up (+ SwiGLU, route weight, re-quantisation) then down over the packed
 // rows the layout and rows_quant left in the workspace.  Down partials go to
-// partial_out, row r at out_row[r] (out_row null: row r).
+// partial_out, row r at out_row[r] (out_row null: row r).  stages selects the
+// launches: a down-only pass reads the z rows and tile list an earlier
+// gate/up-only pass left in the same workspace.
 int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const LayoutParams& lp,
               const mosaic_expert_bank* bank, int shared_expert, const int* out_row, void* partial_out,
               cudaStream_t stream, void* const* ev, const EpPeersDev* ep = nullptr,
               const int* expert_slot = nullptr, int bank_slots = 0, const int* ep_row_rank = nullptr,
-              const int* ep_row_pos = nullptr) {
+              const int* ep_row_pos = nullptr, int stages = kStageGateUp | kStageDown) {
   const int n_map = expert_slot ? bank_slots : w.n_bank;  // bank entries the weight maps cover
   const int H = d->hidden, I = d->inter;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
@@ -335,8 +343,11 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
   gp.w_sf = bank->gu_sf;
   gp.zq = ws + w.zq;
   gp.z_sft = reinterpret_cast<uint32_t*>(ws + w.z_sft);
-  if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
-  if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
+  if (stages & kStageGateUp) {
+    if (launch_moe_gemm(tw, tx, gp, sms, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
+    if (!rec(ev, 4, stream)) return MOSAIC_ERR_CUDA;
+  }
+  if (!(stages & kStageDown)) return MOSAIC_OK;
 
   // down: pairs of hidden blocks (nb, nb + H/256), adjacent in the bank
   st = make_weight_map(&tw, bank->dn_tiled, n_map, H, I, 2);
@@ -372,10 +383,11 @@ int run_gemms(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const Layo
 int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const void* x, const int64_t* idx,
                 const float* weights, const mosaic_expert_bank* bank, void* y, cudaStream_t stream,
                 void* const* ev = nullptr, const int* expert_slot = nullptr, int bank_slots = 0,
-                bool after_kernel = false) {
+                bool after_kernel = false, int stages = kStageGateUp | kStageDown) {
   const int T = d->tokens, H = d->hidden, E = d->n_experts, k = d->top_k;
   const bool hilo = d->act_mode == MOSAIC_ACT_BF16;
   const int shared_base = d->has_shared ? T * k : -1;
+  const bool gate_up = (stages & kStageGateUp) != 0;
 
   LayoutParams lp{};
   lp.idx = idx;
@@ -388,22 +400,25 @@ int run_experts(const mosaic_moe_dims* d, const WsPlan& w, uint8_t* ws, const vo
   // layout -> quantise -> gate/up -> down -> combine: each kernel follows the
   // previous one in the stream, so they launch programmatically (the layout
   // only when the router's top-k precedes it); with stage events in between,
-  // none does
-  {
+  // none does, and neither does a down-only pass, whose first kernel follows
+  // whatever the caller queued
+  if (gate_up) {
     PdlScope pdl_layout(ev == nullptr && after_kernel);
     if (launch_layout(lp, stream) != cudaSuccess) return MOSAIC_ERR_CUDA;
   }
-  PdlScope pdl(ev == nullptr);
-  if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
-
-  if (launch_rows_quant(x, T, nullptr, H, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile, lp.row_pos,
-                        ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), stream) != cudaSuccess)
-    return MOSAIC_ERR_CUDA;
-  if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
+  PdlScope pdl(ev == nullptr && gate_up);
+  if (gate_up) {
+    if (!rec(ev, 2, stream)) return MOSAIC_ERR_CUDA;
+    if (launch_rows_quant(x, T, nullptr, H, H, k, lp.row_of, shared_base, hilo ? 1 : 0, w.R_pad, lp.row_tile,
+                          lp.row_pos, ws + w.xq, reinterpret_cast<uint32_t*>(ws + w.x_sft), stream) != cudaSuccess)
+      return MOSAIC_ERR_CUDA;
+    if (!rec(ev, 3, stream)) return MOSAIC_ERR_CUDA;
+  }
 
   const int st = run_gemms(d, w, ws, lp, bank, d->has_shared ? E : -1, nullptr, ws + w.partial, stream, ev, nullptr,
-                           expert_slot, bank_slots);
+                           expert_slot, bank_slots, nullptr, nullptr, stages);
   if (st) return st;
+  if (!(stages & kStageDown)) return MOSAIC_OK;
 
   if (launch_combine(ws + w.partial, w.partial_f32, lp.row_sorted, T, k, H, shared_base, y, stream) != cudaSuccess)
     return MOSAIC_ERR_CUDA;
@@ -922,6 +937,40 @@ int mosaic_moe_routed_slots(const mosaic_moe_dims* dims, const void* x, const in
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
   return run_experts(dims, w, ws, x, expert_ids, expert_weights, bank, y, s, nullptr, expert_slot, bank_slots);
+}
+
+int mosaic_expert_gemm_gu(const mosaic_moe_dims* dims, const void* x, const int64_t* expert_ids,
+                          const float* expert_weights, const mosaic_expert_bank* bank, void* workspace,
+                          size_t workspace_bytes, mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!x || !expert_ids || !workspace) return MOSAIC_ERR_SHAPE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(x, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemsetAsync(ws + w.err, 0, 16, s) != cudaSuccess) return MOSAIC_ERR_CUDA;
+  return run_experts(dims, w, ws, x, expert_ids, expert_weights, bank, nullptr, s, nullptr, nullptr, 0, false,
+                     kStageGateUp);
+}
+
+int mosaic_expert_gemm_down(const mosaic_moe_dims* dims, const mosaic_expert_bank* bank, void* y, void* workspace,
+                            size_t workspace_bytes, mosaic_stream_t stream) {
+  int st = check_dims(dims);
+  if (st) return st;
+  if (!y || !workspace) return MOSAIC_ERR_SHAPE;
+  st = check_bank(bank);
+  if (st) return st;
+  if (!aligned(y, 16) || !aligned(workspace, 256)) return MOSAIC_ERR_ALIGN;
+  const WsPlan w = plan_ws(dims);
+  if (workspace_bytes < w.total) return MOSAIC_ERR_WORKSPACE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  // the error word keeps what the gate/up call recorded
+  return run_experts(dims, w, ws, nullptr, nullptr, nullptr, bank, y, s, nullptr, nullptr, 0, false, kStageDown);
 }
 
 int mosaic_ep_dispatch(const mosaic_moe_dims* dims, int32_t world, const void* x, const int64_t* idx,

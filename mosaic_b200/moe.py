@@ -347,7 +347,10 @@ class HashMoELayer(MoELayer):
 
 
 def _routed(cfg: MoEConfig, x, expert_ids, expert_weights, bank: ExpertBank, *, include_shared: bool,
-            workspace: _Workspace | None = None):
+            workspace: _Workspace | None = None, split: bool = False):
+    """Routed experts through ``mosaic_moe_routed``; ``split`` runs the same
+    work as ``mosaic_expert_gemm_gu`` then ``mosaic_expert_gemm_down`` (the
+    reference's gate/up and down ``_run_two_queues`` calls, qpa_mma.py:750-772)."""
     if x.device.type != "cuda":
         raise ValueError("MoE expert path requires CUDA tensors")
     xf = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
@@ -360,6 +363,14 @@ def _routed(cfg: MoEConfig, x, expert_ids, expert_weights, bank: ExpertBank, *, 
     ws = (workspace or _Workspace()).get(dims, xf.device)
     y = torch.empty_like(xf)
     b = bank.c_struct()
+    if split:
+        st = C.lib().mosaic_expert_gemm_gu(ctypes.byref(dims), ops._ptr(xf), ops._ptr(ids), ops._ptr(w),
+                                           ctypes.byref(b), ops._ptr(ws), ws.numel(), ops._stream())
+        C.check(st, "mosaic_expert_gemm_gu")
+        st = C.lib().mosaic_expert_gemm_down(ctypes.byref(dims), ctypes.byref(b), ops._ptr(y), ops._ptr(ws),
+                                             ws.numel(), ops._stream())
+        C.check(st, "mosaic_expert_gemm_down")
+        return y
     st = C.lib().mosaic_moe_routed(ctypes.byref(dims), ops._ptr(xf), ops._ptr(ids), ops._ptr(w), ctypes.byref(b),
                                    ops._ptr(y), ops._ptr(ws), ws.numel(), ops._stream())
     C.check(st, "mosaic_moe_routed")

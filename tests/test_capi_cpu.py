@@ -88,6 +88,38 @@ def test_forward_validation_before_launch():
     assert lib.mosaic_moe_forward(*a) == C.MOSAIC_ERR_SHAPE
 
 
+def test_split_expert_gemm_validation_before_launch():
+    lib = C.lib()
+    bank = C.ExpertBankC()
+    fake = 1 << 20  # aligned, never dereferenced: validation fails first
+    bank.gu_tiled = bank.gu_sf = bank.dn_tiled = bank.dn_sf = fake
+    d = _dims()
+    gu = [ctypes.byref(d), fake, fake, fake, ctypes.byref(bank), fake, 1 << 40, None]
+    dn = [ctypes.byref(d), ctypes.byref(bank), fake, fake, 1 << 40, None]
+    for fn, args, x_at, ws_at, size_at in ((lib.mosaic_expert_gemm_gu, gu, 1, 5, 6),
+                                            (lib.mosaic_expert_gemm_down, dn, 2, 3, 4)):
+        a = list(args)
+        a[x_at] = None  # null x (gate/up) or y (down)
+        assert fn(*a) == C.MOSAIC_ERR_SHAPE
+        a = list(args)
+        a[x_at] = fake + 2
+        assert fn(*a) == C.MOSAIC_ERR_ALIGN
+        a = list(args)
+        a[ws_at] = fake + 128  # the workspace needs 256-B alignment
+        assert fn(*a) == C.MOSAIC_ERR_ALIGN
+        a = list(args)
+        a[size_at] = 16
+        assert fn(*a) == C.MOSAIC_ERR_WORKSPACE
+        a = list(args)
+        a[0] = None
+        assert fn(*a) == C.MOSAIC_ERR_SHAPE
+        bank.dn_sf = fake + 4
+        assert fn(*args) == C.MOSAIC_ERR_ALIGN
+        bank.dn_sf = fake
+    # the two calls size their workspace exactly as the fused call does
+    assert lib.mosaic_moe_workspace_bytes(ctypes.byref(d)) > 16
+
+
 def test_router_validation_before_launch():
     lib = C.lib()
     fake = 1 << 20

@@ -124,6 +124,35 @@ def test_bad_expert_ids_flagged(cases):
     assert ops.read_error(ws.buf) == 4  # MOSAIC_ERR_RANGE
 
 
+@pytest.mark.parametrize("mode", ["bf16", "fp8"])
+@pytest.mark.parametrize("name", list(MOE_CASES))
+def test_split_gate_up_down_calls_match_fused(cases, name, mode):
+    """mosaic_expert_gemm_gu then mosaic_expert_gemm_down (the reference's two
+    _run_two_queues calls) give the bytes of the fused mosaic_moe_routed, and the
+    gate/up call's device error word survives the down call."""
+    from mosaic_b200 import MoEConfig, ops
+    from mosaic_b200.moe import _routed, _Workspace
+
+    case, _, full = cases[name]
+    c = case["cfg"]
+    bank = gpu_bank(full, has_shared=False)
+    cfg = MoEConfig(hidden_size=c["H"], moe_intermediate_size=c["I"], n_routed_experts=c["E"],
+                    num_experts_per_tok=c["k"], n_group=1, topk_group=1, n_shared_experts=0,
+                    swiglu_limit=c["swiglu_limit"], act_mode=mode)
+    x, ids, w = case["x"].cuda(), case["idx"].cuda(), case["weights"].cuda()
+    fused = _routed(cfg, x, ids, w, bank, include_shared=False, workspace=_Workspace())
+    ws = _Workspace()
+    split = _routed(cfg, x, ids, w, bank, include_shared=False, workspace=ws, split=True)
+    torch.cuda.synchronize()
+    assert ops.read_error(ws.buf) == 0
+    assert torch.equal(split, fused)
+    bad = ids.clone()
+    bad[0, 0] = c["E"] + 3
+    _routed(cfg, x, bad, w, bank, include_shared=False, workspace=ws, split=True)
+    torch.cuda.synchronize()
+    assert ops.read_error(ws.buf) == 4  # MOSAIC_ERR_RANGE
+
+
 def test_host_validation_rejects(cases):
     from mosaic_b200 import MoEConfig, MoELayer
 
