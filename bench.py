@@ -108,6 +108,8 @@ def parse():
                    help="with --act: no extras, no CPU baseline, 2 profiled stage runs")
     p.add_argument("--hc-only", action="store_true",
                    help="only the hyper-connection pre-mix + RMSNorm timing (prints its JSON; for ncu captures)")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="only BASELINE config 3 (T = 8192 FP8, clipped Zipf(1.2) load; prints its JSON)")
     p.add_argument("--router-only", action="store_true",
                    help="only the router (V3: H 7168, E 256, groups 8/4, top 8) at T = 1, 128, 2048, 8192, "
                         "or at --tokens when given (prints its JSON; for ncu captures)")
@@ -901,6 +903,9 @@ def main():
     hbm, tf_peak, peak_src = peaks()
     if args.hc_only:
         emit({"hc_pre_norm": hc_bench(hbm), "hc_post": hc_post_bench(hbm)})
+        return
+    if args.prefill_only:
+        emit({"prefill": prefill_extra(synthetic.make_bank(7168, 2048, args.experts, SEED), tf_peak, peak_src)})
         return
     if args.router_only:
         tokens = [args.tokens] if args.tokens else [1, 128, 2048, 8192]
